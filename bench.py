@@ -1,0 +1,352 @@
+#!/usr/bin/env python
+"""bench.py: batch-1 int8 decode of the Qwen3-8B-shaped configuration on B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one decode token of the 36-layer model (8.51 GB of int8 weights and scales, a float16 KV cache) at positions
+2048 onward, after a 2048-token prompt has filled the cache. Weights are seeded synthetic N(0, 0.02) int8 (the
+reference's group-of-32 format); the prompt is seeded random ids. Prints one JSON line (rank 0):
+  value       decode tok/s of the whole job, device-timed (CUDA events on the engine's stream), each step's token and
+              position already in device memory; the 8.5 GB of weights (> the 126 MB L2) stream from HBM every step
+  e2e         the same through the engine's public call forward(token, pos): the token and position copied from
+              pinned host memory and the logits (151936 floats) copied back every step
+  roofline    the dominant kernel (the fused w1/w3 product: 2 x 12288 x 4096 int8 + scales, SwiGLU epilogue), its
+              algorithmic bytes a launch over its CUDA-event duration, against MEASURED_PEAKS.json's HBM copy GB/s
+  cpu_baseline  the CPU oracle (the reference kernels' arithmetic in C, OpenMP over rows) decoding the same model
+              on the host cores, a bounded sample of tokens (rank 0, N = 1)
+Under torchrun (N > 1) every rank runs its own replica on its GPU (the path does not shard without a tensor-parallel
+split, which is not built yet): scaling "weak", value = all ranks' tokens / the slowest rank's time.
+
+--impl reference: the reference's CPU implementation of the path, timed on the host cores: its kernels are
+AssemblyScript compiled to WASM and cannot run on this image (no Node, Bun or AssemblyScript), so the oracle's C
+restatement of them runs instead, on all host threads, on the same config and metric (rank 0 alone under torchrun).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (ROOT, os.path.join(ROOT, "pyodide-llm_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+
+METRIC = "int8 decode tok/s (batch 1) + prefill tok/s; GEMV HBM GB/s vs 8 TB/s peak"
+PROMPT = 2048
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(name):
+    """dram bytes a launch from the committed ncu summary of that kernel (profiles/<name>.md: 'traffic_bytes: N')."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes:"):
+                return int(float(line.split(":")[1]))
+    except Exception:
+        pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id=None):
+        self.bus_id = (bus_id or "").lower()
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait()
+        self.file.flush()
+        rows = [r.split(", ") for r in open(self.file.name).read().strip().splitlines() if r.count(",") >= 9]
+        os.unlink(self.file.name)
+        if self.bus_id:
+            mine = [r for r in rows if r[1].lower().endswith(self.bus_id[-12:])]
+            rows = mine or rows
+        if not rows:
+            return None
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[6 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][3]) if rows[0][3].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------------------------ the CPU oracle leg
+
+def oracle_decode(cfg, W, kc, vc, pos0, budget_s, most):
+    """The oracle's decode (all host threads) from pos0: tokens decoded and seconds taken (at least one token)."""
+    import oracle as O
+    oc = O.Config(dim=cfg.dim, hidden=cfg.hidden, layers=cfg.layers, heads=cfg.heads, kv_heads=cfg.kv_heads,
+                  head_size=cfg.head_size, vocab=cfg.vocab, seq_len=cfg.seq_len, qk_norm=int(cfg.qk_norm),
+                  relaxed=int(cfg.relaxed), half_kv=int(cfg.half_kv), eps=cfg.eps)
+    A = dict(W)
+    A.update(cq=None, ck=None, cv=None, co=None, c1=None, c2=None, c3=None, cls_c=None, kc=kc, vc=vc)
+    rng = np.random.default_rng(7)
+    done, t0 = 0, time.perf_counter()
+    while done < most and (done == 0 or time.perf_counter() - t0 < budget_s):
+        O.forward(oc, A, int(rng.integers(0, cfg.vocab)), pos0 + done)
+        done += 1
+    return done, time.perf_counter() - t0, O.threads()
+
+
+def reference_weights(cfg):
+    """Host weights for the reference arm, made without the GPU library: random int8 values and float32 scales of the
+    converter's layout (the CPU kernels' speed does not depend on the values), the cache's first PROMPT positions
+    random float16."""
+    rng = np.random.default_rng(0)
+    c = cfg
+
+    def q8(rows, cols):
+        return (np.frombuffer(rng.bytes(rows * cols), np.int8).reshape(rows, cols) // 8,
+                np.full((rows, cols // 32), 0.02 * 3 / 127, np.float32))
+
+    W = {}
+    for name, rows, cols in (("q", c.qdim, c.dim), ("k", c.kvdim, c.dim), ("v", c.kvdim, c.dim), ("o", c.dim, c.qdim),
+                             ("1", c.hidden, c.dim), ("2", c.dim, c.hidden), ("3", c.hidden, c.dim)):
+        w, s = q8(c.layers * rows, cols)
+        W["w" + name], W["s" + name] = w, s
+    W["emb"], W["emb_s"] = q8(c.vocab, c.dim)
+    W["cls"], W["cls_s"] = q8(c.vocab, c.dim)
+    for k, shape in (("att_norm", (c.layers, c.dim)), ("ffn_norm", (c.layers, c.dim)), ("final_norm", (c.dim,)),
+                     ("q_norm", (c.layers, c.head_size)), ("k_norm", (c.layers, c.head_size))):
+        W[k] = np.ones(shape, np.float32)
+    freqs = 1.0 / c.rope_theta ** (np.arange(0, c.head_size, 2, dtype=np.float64) / c.head_size)
+    angles = np.outer(np.arange(c.seq_len, dtype=np.float64), freqs)
+    W["cos_t"], W["sin_t"] = np.cos(angles).astype(np.float32), np.sin(angles).astype(np.float32)
+    n = c.layers * c.seq_len * c.kvdim
+    kc = np.zeros(n, np.uint16)
+    vc = np.zeros(n, np.uint16)
+    filled = (rng.normal(0, 1, c.kvdim * 4096).astype(np.float16)).view(np.uint16)
+    for l in range(c.layers):
+        at = l * c.seq_len * c.kvdim
+        for p in range(0, PROMPT, 4096 // 1):
+            m = min(4096, PROMPT - p) * c.kvdim
+            kc[at + p * c.kvdim: at + p * c.kvdim + m] = filled[:m]
+            vc[at + p * c.kvdim: at + p * c.kvdim + m] = filled[:m]
+    return W, kc, vc
+
+
+class ReferenceShape:
+    """configs[3]'s shape for the reference arm (kept apart from the GPU package, which that arm does not load)"""
+    dim, hidden, layers, heads, kv_heads, head_size, vocab, seq_len = 4096, 12288, 36, 32, 8, 128, 151936, 2560
+    qk_norm, rope_theta, eps, relaxed, half_kv = True, 1e6, 1e-6, False, True
+    qdim, kvdim = 32 * 128, 8 * 128
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return
+    W, kc, vc = reference_weights(cfg)
+    import oracle as O
+    # warm-up steps, then the timed ones: each a decode token at PROMPT + i; the number of timed tokens is bounded so
+    # the run ends within minutes (the count run is reported)
+    oracle_decode(cfg, W, kc, vc, PROMPT, 0.0, max(1, min(args.warmup, 1)))
+    n, secs, threads = oracle_decode(cfg, W, kc, vc, PROMPT + 1, 60.0, args.steps)
+    value = n / secs
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": n, "warmup": 1,
+            "ms_per_step": 1000 * secs / n, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "qwen3-8b-int8 batch-1 decode at positions 2048+ (BASELINE.json configs[3])",
+                       "model": "Qwen3-8B-shaped int8 (36 layers, 4096 hidden, 32/8 heads, 12288 FFN, 151936 vocab)",
+                       "global_batch": 1, "seq_len": PROMPT, "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": f"{n} decode tokens at positions {PROMPT + 1}.. of the full 36-layer model "
+                                       "(the reference's WASM kernels cannot run here: the C restatement of them)"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    del O
+
+
+# ------------------------------------------------------------------------------------------------ our arm
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--prompt", type=int, default=PROMPT)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    if args.impl == "reference":
+        return run_reference(args, ReferenceShape())
+    from pllm.forward import QWEN3_8B
+    cfg = QWEN3_8B
+
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
+
+    from pllm.device import Buffer
+    from pllm.forward import Engine
+    from pllm.lib import L, check
+
+    steps, warmup = args.steps, max(3, args.warmup)
+    prompt = args.prompt
+    assert prompt + warmup + steps <= cfg.seq_len, "positions past the cache"
+    eng = Engine(cfg, seed=0, device=local)
+    L.pllm_set_stream(eng.stream)
+    rng = np.random.default_rng(1 + rank)
+    ids = rng.integers(0, cfg.vocab, prompt + warmup + steps).astype(np.int32)
+    tp = np.stack([ids, np.arange(ids.size, dtype=np.int32)], axis=1).reshape(-1)
+    staged = Buffer.of(tp)  # every step's (token, position) in device memory before the timed region
+    ev = [L.pllm_event_create() for _ in range(2)]
+
+    def device_steps(first, count):
+        for i in range(first, first + count):
+            L.pllm_d2d(eng.B["tp"].ptr, staged.ptr + 8 * i, 8)
+            eng.launch_step()
+
+    def timed(fn):
+        L.pllm_sync()
+        if dist:
+            dist.barrier()
+        L.pllm_event_record(ev[0])
+        fn()
+        L.pllm_event_record(ev[1])
+        ms = L.pllm_event_ms(ev[0], ev[1])
+        check("timed region")
+        if dist:
+            import torch
+            t = torch.tensor([ms], device=f"cuda:{local}")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    eng.capture()
+    # the prompt: a decode step a token (the tensor-core prefill is not built yet), filling the cache
+    device_steps(0, 8)
+    prefill_ms = timed(lambda: device_steps(8, prompt - 8))
+    prefill_tps = (prompt - 8) / (prefill_ms / 1000) * world
+    device_steps(prompt, warmup)
+
+    try:
+        import torch
+        bus = torch.cuda.get_device_properties(local).pci_bus_id if hasattr(torch.cuda.get_device_properties(local), "pci_bus_id") else None
+    except Exception:
+        bus = None
+    clocks = Clocks(bus)
+    decode_ms = timed(lambda: device_steps(prompt + warmup, steps))
+    clock = clocks.stop()
+    value = steps * world / (decode_ms / 1000)
+
+    # end to end through the public call: token and position in from pinned memory, logits out, every step
+    e2e_steps = min(steps, cfg.seq_len - prompt - warmup - steps) or 0
+    e2e_first = prompt + warmup + steps
+    if e2e_steps < 8:  # rewind into the decode range (the cache's later positions are rewritten, as a new request)
+        e2e_first, e2e_steps = prompt + warmup, steps
+    e2e_ms = timed(lambda: [eng.forward(int(ids[i % ids.size]), i) for i in range(e2e_first, e2e_first + e2e_steps)])
+    e2e = e2e_steps * world / (e2e_ms / 1000)
+
+    # the dominant kernel alone: the fused w1 / w3 product of every layer (distinct weights: no L2 reuse)
+    c = cfg
+    B = eng.B
+    reps = 3
+
+    def w13_all():
+        for l in range(c.layers):
+            eng._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * c.hidden * c.dim, B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4,
+                      c.hidden, c.dim, B["x"].ptr, B["ffn_norm"].ptr + l * c.dim * 4, 1, 2, pair=c.hidden, pdl=False)
+
+    w13_all()
+    w13_ms = timed(lambda: [w13_all() for _ in range(reps)]) / (reps * c.layers)
+    w13_bytes = 2 * c.hidden * c.dim * 1.125 + c.dim * 4 * 2 + c.hidden * 4
+    peak, peak_kind = peaks()
+    achieved = w13_bytes / (w13_ms / 1000) / 1e9
+
+    # the other products' bandwidth (each over all layers, in isolation)
+    gemv = {"w13_swiglu": round(achieved, 1)}
+
+    def each(name, wq, ws, rows, cols, xin, norm, pro, epi):
+        def run():
+            for l in range(c.layers):
+                eng._gemv(B["qkv"].ptr if epi == 0 else B["x"].ptr, wq + l * rows * cols, ws + l * rows * (cols // 32) * 4,
+                          rows, cols, xin, norm, pro, epi, pdl=False)
+        run()
+        ms = timed(lambda: [run() for _ in range(reps)]) / (reps * c.layers)
+        gemv[name] = round(rows * cols * 1.125 / (ms / 1000) / 1e9, 1)
+
+    each("wqkv", B["wqkv"].ptr, B["sqkv"].ptr, eng.rows_qkv, c.dim, B["x"].ptr, B["att_norm"].ptr, 1, 0)
+    each("wo", B["wo"].ptr, B["so"].ptr, c.dim, c.qdim, B["att"].ptr, 0, 2, 1)
+    each("w2", B["w2"].ptr, B["s2"].ptr, c.dim, c.hidden, B["hb"].ptr, 0, 2, 1)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        W = eng.host_weights()
+        E = np.uint16
+        kc = B["kc"].download(E)
+        vc = B["vc"].download(E)
+        n, secs, threads = oracle_decode(cfg, W, kc, vc, prompt, 20.0, 8)
+        cpu = {"value": n / secs, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"{n} decode tokens at positions {prompt}.. of the same 36-layer model and cache (the C "
+                         "restatement of the reference kernels, OpenMP over rows and heads)"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": decode_ms / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "qwen3-8b-int8 batch-1 decode at positions 2048+ (BASELINE.json configs[3])",
+                   "model": "Qwen3-8B-shaped int8 (36 layers, 4096 hidden, 32/8 heads x 128, QK-norm, 12288 FFN, "
+                            "151936 vocab), float16 KV cache", "global_batch": world, "seq_len": prompt,
+                   "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                   "l2": "no flush: every step streams 8.51 GB of weights (> 126 MB L2)"},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": c.vocab * 4},
+        "prefill": {"value": prefill_tps, "unit": "tok/s", "method": "token by token through the decode graph"},
+        "gemv_gbs": gemv,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "kernel": "gemv_kernel<int8, 1 token, RMSNorm prologue, SwiGLU epilogue>",
+                     "bytes_per_launch": w13_bytes, "traffic": profile_traffic("gemv_q8_w13_qwen3-8b")},
+        "decode_roofline_frac": (c.weight_bytes() / (decode_ms / steps / 1000) / 1e9) / peak,
+        "gpu_launches": eng.launches_per_step * steps,
+        "clocks": clock,
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

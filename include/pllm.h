@@ -1,0 +1,201 @@
+/*
+ * pllm.h -- the C ABI of libpllm.so: takano32/pyodide-llm's kernel registry on a B200 (sm_100a).
+ *
+ * The registry functions keep the reference's names, argument order and argument meaning exactly (the exports of
+ * kernels/kernel.ts:23-43 and kernels/kernel_relaxed.ts:14-16, typed by src/runtime/jobs.ts:82-142 `Arguments`, with
+ * the address positions of src/runtime/jobs.ts:56-74 `ADDRESSES`). An address there (a WASM `usize`) is a
+ * `uint64_t` device pointer here; `i32` and `f32` stay `int32_t` and `float`. So a bun:ffi / ctypes binding of the
+ * reference's table binds this library unchanged: FFIType.u64 for an address, i32 and f32 for the rest.
+ *
+ * Differences from the reference's contract, all at the boundary:
+ *  - Memory: every address is device memory of the current device (pllm_alloc or any CUDA allocation). The
+ *    kernels allocate nothing and keep no state between calls (as kernels/README.md:365-370 requires of the
+ *    reference's), except the one status word of to_f16 / finite_f16.
+ *  - Ordering: a call enqueues its kernel on the current stream (pllm_set_stream; default: the legacy stream 0) and
+ *    returns; calls on one stream run in order. Only to_f16 and finite_f16 (which return a count) wait for the stream.
+ *  - Errors: the reference does not check its arguments (built --noAssert, kernels/build.py:13). Here a call whose
+ *    arguments the reference's kernel could not take (n not whole groups, r0 > r1, a null or misaligned address)
+ *    launches nothing and sets the sticky error that pllm_last_error returns; a failed launch sets it too.
+ *  - Alignment: int8 and ternary weights 32-byte aligned, binary 16, int6 8; quantized activations, their scales
+ *    and a tile's frame 16 bytes (pllm_alloc returns 256-byte aligned memory).
+ *  - Relaxed products (matmul_q8r, matmul_q6r, matmul_q8r_tile): the corrections wc are accepted and not read: the
+ *    activations' bias of 64 is taken off as they are loaded, which gives the same exact integer dot(w, q - 64) that
+ *    wc (int8_sums / six_sums of the same weights) gives the reference.
+ *  - Numbers: every group's int32 sum is the reference's to the bit (pllm_group_sums returns them). Float32 outputs
+ *    of the products and attention agree with the reference's within float32 rounding of a different summation order
+ *    (and of CUDA's expf against the reference's table-free exp); quantize_x, interleave, int8_sums, six_sums,
+ *    to_f16, from_f16, finite_f16, delta_rule are the reference's to the bit.
+ */
+#ifndef PLLM_H
+#define PLLM_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ===== the registry: activations (kernels/kernel/quantize.ts, kernels/kernel/matmul.ts) ===== */
+/* replaces quantize_x, kernels/kernel/quantize.ts:124 (jobs.ts:113): per group of 32, scale = max|x| / qmax,
+ * q = sat8(rne(x / scale) + bias); bias 0 (qmax 127, signed) or 64 (qmax 63, stored 1..127) */
+void quantize_x(uint64_t xq, uint64_t xs, uint64_t x, int32_t n, int32_t bias);
+/* replaces interleave, kernels/kernel/matmul.ts:129 (jobs.ts:105): the ternary / binary products' layout, in place;
+ * after the n / 32 scales at xs, n / 32 int32 minus-sums */
+void interleave(uint64_t xq, uint64_t xs, int32_t n);
+/* replaces int8_sums, kernels/kernel/matmul.ts:50 (jobs.ts:103) */
+void int8_sums(uint64_t out, uint64_t w, int32_t groups);
+/* replaces six_sums, kernels/kernel/matmul.ts:38 (jobs.ts:102) */
+void six_sums(uint64_t out, uint64_t w, int32_t groups);
+
+/* ===== the registry: products ===== */
+/* replaces matmul_q8, kernels/kernel/matmul.ts:77 (jobs.ts:104) */
+void matmul_q8(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, int32_t n, int32_t r0, int32_t r1);
+/* replaces matmul_q8r, kernels/relaxed/int8.ts:17 (jobs.ts:124) */
+void matmul_q8r(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, uint64_t wc, int32_t n, int32_t r0,
+                int32_t r1);
+/* replaces matmul_q8r_tile, kernels/relaxed/int8.ts:147 (jobs.ts:125): count tokens, xq / xs frame bytes apart,
+ * outputs os bytes apart */
+void matmul_q8r_tile(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, uint64_t wc, int32_t n,
+                     int32_t r0, int32_t r1, int32_t count, int32_t os, int32_t frame);
+/* replaces matmul_q6, kernels/kernel/matmul.ts:227 (jobs.ts:107) */
+void matmul_q6(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, int32_t n, int32_t r0, int32_t r1);
+/* replaces matmul_q6r, kernels/relaxed/six.ts:16 (jobs.ts:126) */
+void matmul_q6r(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, uint64_t wc, int32_t n, int32_t r0,
+                int32_t r1);
+/* replaces matmul_t2, kernels/kernel/matmul.ts:218 (jobs.ts:106); three must be 3 */
+void matmul_t2(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, int32_t n, int32_t r0, int32_t r1,
+               int32_t three);
+/* replaces matmul_t2r, kernels/relaxed/signs.ts:117 (jobs.ts:127) */
+void matmul_t2r(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, int32_t n, int32_t r0, int32_t r1,
+                int32_t three);
+/* replaces matmul_t2r_tile, kernels/relaxed/signs.ts:120 (jobs.ts:128) */
+void matmul_t2r_tile(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, int32_t n, int32_t r0,
+                     int32_t r1, int32_t count, int32_t os, int32_t frame, int32_t three);
+/* replaces matmul_b1, kernels/kernel/matmul.ts:222 (jobs.ts:138); two must be 2 */
+void matmul_b1(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, int32_t n, int32_t r0, int32_t r1,
+               int32_t two);
+/* replaces matmul_b1r, kernels/relaxed/signs.ts:123 (jobs.ts:139) */
+void matmul_b1r(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, int32_t n, int32_t r0, int32_t r1,
+                int32_t two);
+/* replaces matmul_b1r_tile, kernels/relaxed/signs.ts:126 (jobs.ts:140) */
+void matmul_b1r_tile(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, int32_t n, int32_t r0,
+                     int32_t r1, int32_t count, int32_t os, int32_t frame, int32_t two);
+/* replaces matmul_f32, kernels/kernel/matmul.ts:13 (jobs.ts:101) */
+void matmul_f32(uint64_t xout, uint64_t x, uint64_t w, int32_t n, int32_t r0, int32_t r1);
+
+/* ===== the registry: attention and float16 (kernels/kernel/attention.ts, kernels/kernel/halves.ts) ===== */
+/* replaces rope, kernels/kernel/attention.ts:7 (jobs.ts:93) */
+void rope(uint64_t v, uint64_t fcr, uint64_t fci, int32_t nh, int32_t hs, int32_t rot);
+/* replaces attention, kernels/kernel/attention.ts:28 (jobs.ts:94); att: nh (pos + 1) floats of scratch, whose
+ * contents after the call are not the probabilities */
+void attention(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t att, int32_t pos, int32_t nh, int32_t nkv,
+               int32_t hs, int32_t h0, int32_t h1);
+/* replaces attention_f16, kernels/kernel/attention.ts:34 (jobs.ts:95) */
+void attention_f16(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t att, int32_t pos, int32_t nh,
+                   int32_t nkv, int32_t hs, int32_t h0, int32_t h1);
+/* replaces attention_capped, kernels/kernel/attention.ts:40 (jobs.ts:96) */
+void attention_capped(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t att, int32_t pos, int32_t nh,
+                      int32_t nkv, int32_t hs, int32_t h0, int32_t h1, float cap);
+/* replaces attention_f16_capped, kernels/kernel/attention.ts:43 (jobs.ts:97) */
+void attention_f16_capped(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t att, int32_t pos, int32_t nh,
+                          int32_t nkv, int32_t hs, int32_t h0, int32_t h1, float cap);
+/* replaces to_f16, kernels/kernel/halves.ts:35 (jobs.ts:98): returns how many inputs were not finite (waits) */
+int32_t to_f16(uint64_t out, uint64_t x, int32_t n);
+/* replaces from_f16, kernels/kernel/halves.ts:72 (jobs.ts:99) */
+void from_f16(uint64_t out, uint64_t x, int32_t n);
+/* replaces finite_f16, kernels/kernel/halves.ts:82 (jobs.ts:100): 1 if all finite, else 0 (waits) */
+int32_t finite_f16(uint64_t x, int32_t n);
+
+/* ===== the registry: vector glue and stateful layers (kernels/kernel/activations.ts, kernels/kernel/stateful.ts) */
+/* replaces rmsnorm, kernels/kernel/activations.ts:8 (jobs.ts:83) */
+void rmsnorm(uint64_t out, uint64_t x, uint64_t w, int32_t n, float eps);
+/* replaces swiglu, kernels/kernel/activations.ts:77 (jobs.ts:86) */
+void swiglu(uint64_t out, uint64_t h1, uint64_t h3, int32_t n);
+/* replaces add_inplace, kernels/kernel/activations.ts:156 (jobs.ts:90) */
+void add_inplace(uint64_t x, uint64_t y, int32_t n);
+/* replaces gate, kernels/kernel/stateful.ts:12 (jobs.ts:120) */
+void gate(uint64_t out, uint64_t x, uint64_t g, int32_t n);
+/* replaces convolve, kernels/kernel/stateful.ts:49 (jobs.ts:121) */
+void convolve(uint64_t out, uint64_t taps, uint64_t rows, int32_t n, int32_t count);
+/* replaces short_conv, kernels/kernel/stateful.ts:70 (jobs.ts:122) */
+void short_conv(uint64_t out, uint64_t taps, uint64_t rows, uint64_t b, int32_t n, int32_t count);
+/* replaces delta_rule, kernels/kernel/stateful.ts:96 (jobs.ts:123) */
+void delta_rule(uint64_t out, uint64_t state, uint64_t next, uint64_t c, uint64_t work, int32_t kh, int32_t kd,
+                int32_t vd, int32_t vh, int32_t h0, int32_t h1);
+
+/* ===== device, memory, streams, graphs, errors (no counterpart in the reference: its kernels worked in one WASM
+ * memory the engine owned, src/runtime/forward/engine.ts:147-163) ===== */
+int32_t pllm_init(int32_t device);                     /* select the device (sm_100 only) and make its context */
+int32_t pllm_last_error(char *buf, int32_t len);       /* the sticky error code (0: none) and its message */
+void pllm_clear_error(void);
+int32_t pllm_num_sms_of_device(void);
+uint64_t pllm_alloc(uint64_t bytes);                   /* device memory, 256-byte aligned; 0 on failure */
+void pllm_free(uint64_t p);
+uint64_t pllm_alloc_host(uint64_t bytes);              /* pinned host memory */
+void pllm_free_host(uint64_t p);
+void pllm_h2d(uint64_t dst, const void *src, uint64_t bytes);   /* on the current stream */
+void pllm_d2h(void *dst, uint64_t src, uint64_t bytes);
+void pllm_d2d(uint64_t dst, uint64_t src, uint64_t bytes);
+void pllm_memset(uint64_t dst, int32_t value, uint64_t bytes);
+uint64_t pllm_stream_create(void);
+void pllm_stream_destroy(uint64_t s);
+void pllm_set_stream(uint64_t s);                      /* 0: the legacy default stream */
+uint64_t pllm_get_stream(void);
+int32_t pllm_sync(void);                               /* wait for the current stream */
+int32_t pllm_device_sync(void);
+int32_t pllm_graph_begin(void);                        /* record the calls that follow on the current stream */
+uint64_t pllm_graph_end(void);                         /* an executable graph of them (0 on failure) */
+int32_t pllm_graph_launch(uint64_t exec);
+void pllm_graph_destroy(uint64_t exec);
+uint64_t pllm_event_create(void);
+void pllm_event_record(uint64_t e);
+float pllm_event_ms(uint64_t a, uint64_t b);           /* waits for b */
+void pllm_event_destroy(uint64_t e);
+const char *pllm_version(void);
+
+/* ===== additions for a device-memory engine (no counterpart in the reference: its engine touched the memory from
+ * JavaScript between kernel calls, src/runtime/forward/tensors.ts:154-160, forward/cache.ts:117-141) ===== */
+/* the exact int32 sums of every (row, group of 32) of rows [r0, r1) against one token: the accumulators every
+ * product scales. fmt 0 int8, 1 int6, 2 ternary, 3 binary; bias 0 or 64 (int8 / int6) */
+void pllm_group_sums(uint64_t out, uint64_t xq, uint64_t xs, uint64_t wq, int32_t fmt, int32_t n, int32_t r0, int32_t r1,
+                     int32_t bias);
+/* count tokens quantized (x a frame of n floats apart, xq n bytes, xs n / 32 floats) */
+void pllm_quantize_tokens(uint64_t xq, uint64_t xs, uint64_t x, int32_t n, int32_t bias, int32_t count);
+/* to_f16 without waiting: the count of non-finite inputs is added to the device int32 at bad */
+void pllm_to_f16_async(uint64_t out, uint64_t x, int32_t n, uint64_t bad);
+/* rmsnorm of rows rows of n floats, stride floats apart, one weight (Qwen3's per-head q / k norms) */
+void pllm_rmsnorm_rows(uint64_t out, uint64_t x, uint64_t w, int32_t n, float eps, int32_t rows, int64_t stride);
+/* count tokens' int8 embedding rows (tokens: device int32[count], or 0 to take token), as tensors.ts:154-160 */
+void pllm_embed_q8(uint64_t x, uint64_t emb, uint64_t scales, uint64_t tokens, int32_t token, int32_t dim, int32_t count,
+                   int64_t stride);
+/* the fused decode product: fmt as pllm_group_sums; pro 0 quantized input (xq / xs), 1 RMSNorm(x, norm) then
+ * quantize_x, 2 quantize_x(x); epi 0 store, 1 add into out (the residual), 2 silu(row) * row + pair (the gated FFN);
+ * count tokens (strides: out and x in floats, xq and xs in bytes); pdl 1: launched as a programmatic dependent */
+void pllm_gemv(uint64_t out, int64_t out_stride, uint64_t xq, uint64_t xs, int64_t xq_stride, int64_t xs_stride,
+               uint64_t x, int64_t x_stride, uint64_t norm, float eps, int32_t bias, uint64_t wq, uint64_t ws,
+               int32_t fmt, int32_t n, int32_t r0, int32_t r1, int32_t count, int32_t pro, int32_t epi, int64_t pair,
+               int32_t pdl);
+/* q / k head norms (null weights: none), RoPE at the position, and k / v into the cache at it; the position is
+ * read from device memory at pos_dev (or pos if pos_dev is 0), so one recorded graph serves every position */
+void pllm_qk_rope_cache(uint64_t q, uint64_t k, uint64_t v, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t,
+                        uint64_t sin_t, uint64_t pos_dev, int32_t pos, uint64_t kc, uint64_t vc, int32_t nh,
+                        int32_t nkv, int32_t hs, int32_t rot, float eps, int32_t half, uint64_t bad, int32_t pdl);
+/* attention at the device position over a cache of capacity positions; scratch: pllm_attention_scratch_bytes */
+uint64_t pllm_attention_scratch_bytes(int32_t nh, int32_t hs, int32_t capacity, int32_t split_len);
+void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t scratch, uint64_t pos_dev,
+                        int32_t capacity, int32_t nh, int32_t nkv, int32_t hs, int32_t half, float cap,
+                        int32_t split_len, int32_t pdl);
+
+/* ===== seeded synthetic weights made on the device, for benchmarks and tests of model-sized shapes (no counterpart
+ * in the reference, whose tests make synthetic checkpoints in NumPy, tests/made_up.py:30) ===== */
+/* n float32 values N(mean, std) of (seed, index) */
+void pllm_synth_f32(uint64_t out, int64_t n, uint64_t seed, float mean, float std);
+/* rows x cols int8 weights: N(0, std) quantized group by group as engine/packing.py:40-45 quantizes */
+void pllm_synth_q8(uint64_t wq, uint64_t ws, int64_t rows, int32_t cols, uint64_t seed, float std);
+/* rows x cols ternary weights uniform on {-1, 0, +1} (packing.py:106-109's codes) and a float16 scale a row,
+ * N(mean, std) rounded to float16, repeated for each group of 128 */
+void pllm_synth_t2(uint64_t wq, uint64_t ws, int64_t rows, int32_t cols, uint64_t seed, float mean, float std);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,446 @@
+// attention.cu: RoPE, the cache write, and one token's attention over the cache (kernels/kernel/attention.ts).
+//   rope                       attention.ts:7-20
+//   attention, attention_f16   attention.ts:28-36 (attentionOf :87-211)
+//   attention_capped, attention_f16_capped   attention.ts:40-45
+// The cache is the reference's layout: a layer's keys (and values) [position][kv heads * head size], float32 or the
+// float16 bits halves.ts writes. Grouped-query: q head h reads kv head h / (nh / nkv).
+//
+// B200 form: split-KV ("flash decoding"). A CTA takes one kv head and a slice of the positions for all of that head's
+// query heads (the keys and values of the slice are read once for kvMul heads): scores in shared memory, a softmax
+// of the slice (its max and sum), and the weighted values. A second small kernel combines the slices' partial
+// results (max, sum, weighted values) per head. With one slice the first kernel writes the output itself.
+// The numbers differ from the reference's in the order of the float32 sums and in exp (CUDA's expf in place of the
+// reference's table-free one): the outputs agree within float32 rounding (the tests hold them to 1e-5 relative).
+//
+// The forward driver's calls read the position from device memory (pos_dev), so that one CUDA graph serves every
+// position; their grid covers the cache's capacity and the slices past the position return at once.
+#include "pllm_common.cuh"
+
+namespace {
+
+constexpr int ATT_THREADS = 128, ATT_WARPS = ATT_THREADS / 32;
+
+struct AttArgs {
+  float* out;
+  const float* q;
+  const void* kc;
+  const void* vc;
+  float* part;          // slices' partials: [nh][nsplit][hs + 2] (weighted values, max, sum)
+  const int* pos_dev;   // device position (or null: pos)
+  int pos, nh, nkv, hs, h0, h1;
+  int split_len;        // positions a slice
+  int nsplit;           // slices (the grid's y); with pos_dev, those past the position return
+  float cap;
+};
+
+template <bool HALF>
+__device__ __forceinline__ float kv_load(const void* base, long long i) {
+  if (HALF) return half_bits_to_float(reinterpret_cast<const uint16_t*>(base)[i]);
+  return reinterpret_cast<const float*>(base)[i];
+}
+
+// grid (nkv, nsplit); KVM: query heads a kv head; DPL: head dims a lane (hs <= 32 DPL)
+template <bool HALF, int KVM, int DPL>
+__global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttArgs a) {
+  extern __shared__ float sS[];  // [KVM][split_len] scores, then probabilities
+  __shared__ float sO[ATT_WARPS][KVM][DPL * 32];
+  __shared__ float sML[KVM][2];
+  pdl_wait();
+  const int pos = a.pos_dev ? *a.pos_dev : a.pos;
+  const int count = pos + 1;
+  const int kvh = blockIdx.x, split = blockIdx.y;
+  const int nsplit = a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
+  if (split >= nsplit) return;
+  const int p0 = split * a.split_len;
+  const int p1 = min(count, p0 + a.split_len);
+  const int len = p1 - p0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int hs = a.hs, kvdim = a.nkv * hs;
+  const int hbase = kvh * KVM;
+  const float isq = 1.0f / sqrtf((float)hs);
+  // this CTA's query heads in registers: head hbase + j, dims lane + 32 i
+  float qv[KVM][DPL];
+#pragma unroll
+  for (int j = 0; j < KVM; j++)
+#pragma unroll
+    for (int i = 0; i < DPL; i++) {
+      const int d = lane + 32 * i;
+      qv[j][i] = d < hs ? a.q[(long long)(hbase + j) * hs + d] : 0.0f;
+    }
+  // 1. scores
+  for (int t = warp; t < len; t += ATT_WARPS) {
+    const long long row = (long long)(p0 + t) * kvdim + (long long)kvh * hs;
+    float kv[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; i++) {
+      const int d = lane + 32 * i;
+      kv[i] = d < hs ? kv_load<HALF>(a.kc, row + d) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < KVM; j++) {
+      float s = 0.0f;
+#pragma unroll
+      for (int i = 0; i < DPL; i++) s = fmaf(qv[j][i], kv[i], s);
+      s = warp_sum(s) * isq;
+      if (a.cap > 0.0f) s = a.cap * tanhf(s / a.cap);
+      if (lane == 0) sS[j * a.split_len + t] = s;
+    }
+  }
+  __syncthreads();
+  // 2. the slice's softmax: its max and the sum of exp(s - max), a warp a head
+  for (int j = warp; j < KVM; j += ATT_WARPS) {
+    float m = -INFINITY;
+    for (int t = lane; t < len; t += 32) m = fmaxf(m, sS[j * a.split_len + t]);
+    m = warp_max(m);
+    float l = 0.0f;
+    for (int t = lane; t < len; t += 32) {
+      const float e = expf(sS[j * a.split_len + t] - m);
+      sS[j * a.split_len + t] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      sML[j][0] = m;
+      sML[j][1] = l;
+    }
+  }
+  __syncthreads();
+  // 3. the weighted values
+  float acc[KVM][DPL];
+#pragma unroll
+  for (int j = 0; j < KVM; j++)
+#pragma unroll
+    for (int i = 0; i < DPL; i++) acc[j][i] = 0.0f;
+  for (int t = warp; t < len; t += ATT_WARPS) {
+    const long long row = (long long)(p0 + t) * kvdim + (long long)kvh * hs;
+    float vv[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; i++) {
+      const int d = lane + 32 * i;
+      vv[i] = d < hs ? kv_load<HALF>(a.vc, row + d) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < KVM; j++) {
+      const float p = sS[j * a.split_len + t];
+#pragma unroll
+      for (int i = 0; i < DPL; i++) acc[j][i] = fmaf(p, vv[i], acc[j][i]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < KVM; j++)
+#pragma unroll
+    for (int i = 0; i < DPL; i++) sO[warp][j][lane + 32 * i] = acc[j][i];
+  __syncthreads();
+  for (int e = threadIdx.x; e < KVM * hs; e += ATT_THREADS) {
+    const int j = e / hs, d = e % hs;
+    const int h = hbase + j;
+    if (h < a.h0 || h >= a.h1) continue;
+    float o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < ATT_WARPS; w++) o += sO[w][j][d];
+    if (nsplit == 1) {
+      a.out[(long long)h * hs + d] = o / sML[j][1];
+    } else {
+      float* part = a.part + ((long long)h * a.nsplit + split) * (hs + 2);
+      part[d] = o;
+      if (d == 0) {
+        part[hs] = sML[j][0];
+        part[hs + 1] = sML[j][1];
+      }
+    }
+  }
+}
+
+// a block a head: the slices' partials combined
+__global__ void attention_combine_kernel(const AttArgs a) {
+  pdl_wait();
+  const int pos = a.pos_dev ? *a.pos_dev : a.pos;
+  const int count = pos + 1;
+  const int nsplit = a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
+  const int h = a.h0 + blockIdx.x;
+  if (nsplit == 1 || h >= a.h1) return;
+  const int hs = a.hs;
+  const float* part = a.part + (long long)h * a.nsplit * (hs + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; s++) M = fmaxf(M, part[s * (hs + 2) + hs]);
+  float L = 0.0f;
+  for (int s = 0; s < nsplit; s++) L += part[s * (hs + 2) + hs + 1] * expf(part[s * (hs + 2) + hs] - M);
+  const float inv = 1.0f / L;
+  for (int d = threadIdx.x; d < hs; d += blockDim.x) {
+    float o = 0.0f;
+    for (int s = 0; s < nsplit; s++) o += part[s * (hs + 2) + d] * expf(part[s * (hs + 2) + hs] - M);
+    a.out[(long long)h * hs + d] = o * inv;
+  }
+}
+
+template <bool HALF, int KVM>
+cudaError_t launch_split_kvm(const AttArgs& a, int dpl, size_t smem, dim3 grid, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(ATT_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = pllm_stream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+#define DPL_CASE(D)                                                                                       \
+  case D: {                                                                                               \
+    auto k = attention_split_kernel<HALF, KVM, D>;                                                        \
+    if (smem > 8 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);  \
+    return cudaLaunchKernelEx(&cfg, k, a);                                                                \
+  }
+  switch (dpl) {
+    DPL_CASE(1)
+    DPL_CASE(2)
+    DPL_CASE(4)
+    DPL_CASE(8)
+    default: return cudaErrorInvalidValue;
+  }
+#undef DPL_CASE
+}
+
+template <bool HALF>
+cudaError_t launch_split(const AttArgs& a, int kvm, int dpl, size_t smem, dim3 grid, bool pdl) {
+  switch (kvm) {
+    case 1: return launch_split_kvm<HALF, 1>(a, dpl, smem, grid, pdl);
+    case 2: return launch_split_kvm<HALF, 2>(a, dpl, smem, grid, pdl);
+    case 4: return launch_split_kvm<HALF, 4>(a, dpl, smem, grid, pdl);
+    case 8: return launch_split_kvm<HALF, 8>(a, dpl, smem, grid, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+void run_attention(const char* name, AttArgs a, bool half, bool pdl) {
+  const int kvm = a.nh / a.nkv;
+  const int dpl = a.hs <= 32 ? 1 : a.hs <= 64 ? 2 : a.hs <= 128 ? 4 : 8;
+  const size_t smem = (size_t)kvm * a.split_len * sizeof(float);
+  const dim3 grid(a.nkv, a.nsplit);
+  cudaError_t e = half ? launch_split<true>(a, kvm, dpl, smem, grid, pdl) : launch_split<false>(a, kvm, dpl, smem, grid, pdl);
+  if (e != cudaSuccess) {
+    pllm_fail(PLLM_ECUDA, "%s: launch failed: %s", name, cudaGetErrorString(e));
+    return;
+  }
+  if (a.nsplit > 1 || a.pos_dev) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.h1 - a.h0);
+    cfg.blockDim = dim3(a.hs >= 128 ? 128 : 64);
+    cfg.stream = pllm_stream();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, attention_combine_kernel, a);
+    if (e != cudaSuccess) pllm_fail(PLLM_ECUDA, "%s: combine launch failed: %s", name, cudaGetErrorString(e));
+  }
+}
+
+bool check_heads(const char* name, int nh, int nkv, int hs, int h0, int h1) {
+  if (nh <= 0 || nkv <= 0 || nh % nkv || hs <= 0 || hs > 256 || h0 < 0 || h1 < h0 || h1 > nh) {
+    pllm_fail(PLLM_EINVAL, "%s: nh %d nkv %d hs %d heads %d..%d", name, nh, nkv, hs, h0, h1);
+    return false;
+  }
+  const int kvm = nh / nkv;
+  if (kvm != 1 && kvm != 2 && kvm != 4 && kvm != 8) {
+    pllm_fail(PLLM_EINVAL, "%s: %d query heads a kv head (1, 2, 4 or 8 are built)", name, kvm);
+    return false;
+  }
+  return true;
+}
+
+// the registry's call: the slices' partials go to the reference's scratch att (nh (pos + 1) floats), so a slice
+// count is chosen whose partials fit in it
+void registry_attention(const char* name, uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t att, int pos,
+                        int nh, int nkv, int hs, int h0, int h1, float cap, bool half) {
+  if (!check_heads(name, nh, nkv, hs, h0, h1)) return;
+  PLLM_REQUIRE(pos >= 0, "%s: pos %d", name, pos);
+  if (h1 == h0) return;
+  const int count = pos + 1;
+  int nsplit = (count + 127) / 128;
+  const int fit = count / (hs + 2);
+  if (nsplit > fit) nsplit = fit;
+  if (nsplit < 1) nsplit = 1;
+  AttArgs a = {};
+  a.out = dptr<float>(out);
+  a.q = dptr<const float>(q);
+  a.kc = dptr<const void>(kc);
+  a.vc = dptr<const void>(vc);
+  a.part = dptr<float>(att);
+  a.pos = pos;
+  a.nh = nh;
+  a.nkv = nkv;
+  a.hs = hs;
+  a.h0 = h0;
+  a.h1 = h1;
+  a.nsplit = nsplit;
+  a.split_len = (count + nsplit - 1) / nsplit;
+  a.cap = cap;
+  run_attention(name, a, half, false);
+}
+
+__global__ void rope_kernel(float* v, const float* fcr, const float* fci, int nh, int hs, int turned) {
+  const int pairs = turned / 2;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < nh * pairs; e += gridDim.x * blockDim.x) {
+    const int h = e / pairs, i = e % pairs;
+    float* p = v + (long long)h * hs + 2 * i;
+    const float c = fcr[i], s = fci[i];
+    const float v0 = p[0], v1 = p[1];
+    p[0] = v0 * c - v1 * s;
+    p[1] = v0 * s + v1 * c;
+  }
+}
+
+// The forward driver's step between the q/k/v product and the attention: per head the RMSNorm of q and k (Qwen3's
+// q_norm / k_norm, forward/attention.ts:140-143; skipped where the weight is null), RoPE at the position
+// (attention.ts:7-20 with the tables' row of pos), and the key and value into the cache at pos (float16 by
+// halves.ts's rounding, or float32). Blocks: nh query heads, then nkv key heads, then nkv value heads.
+template <bool HALF>
+__global__ void qk_rope_cache_kernel(float* q, const float* k, const float* v, const float* qn, const float* kn,
+                                     const float* cos_t, const float* sin_t, const int* pos_dev, int pos, void* kc,
+                                     void* vc, int nh, int nkv, int hs, int rot, float eps, int* bad) {
+  pdl_wait();
+  if (pos_dev) pos = *pos_dev;
+  __shared__ float buf[512];
+  __shared__ float red[8];
+  const int b = blockIdx.x;
+  const int kind = b < nh ? 0 : (b < nh + nkv ? 1 : 2);
+  const int head = kind == 0 ? b : (kind == 1 ? b - nh : b - nh - nkv);
+  const float* src = kind == 0 ? q + (long long)head * hs : (kind == 1 ? k : v) + (long long)head * hs;
+  const float* w = kind == 0 ? qn : (kind == 1 ? kn : nullptr);
+  for (int d = threadIdx.x; d < hs; d += blockDim.x) buf[d] = src[d];
+  __syncthreads();
+  if (w) {
+    float s = 0.0f;
+    for (int d = threadIdx.x; d < hs; d += blockDim.x) s = fmaf(buf[d], buf[d], s);
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += red[i];
+    const float r = 1.0f / sqrtf(tot / (float)hs + eps);
+    __syncthreads();
+    for (int d = threadIdx.x; d < hs; d += blockDim.x) buf[d] = w[d] * (r * buf[d]);
+    __syncthreads();
+  }
+  if (kind < 2) {
+    const int turned = rot > 0 && rot < hs ? rot : hs;
+    const float* c = cos_t + (long long)pos * (hs / 2);
+    const float* s = sin_t + (long long)pos * (hs / 2);
+    for (int i = threadIdx.x; i < turned / 2; i += blockDim.x) {
+      const float v0 = buf[2 * i], v1 = buf[2 * i + 1];
+      buf[2 * i] = v0 * c[i] - v1 * s[i];
+      buf[2 * i + 1] = v0 * s[i] + v1 * c[i];
+    }
+    __syncthreads();
+  }
+  if (kind == 0) {
+    for (int d = threadIdx.x; d < hs; d += blockDim.x) q[(long long)head * hs + d] = buf[d];
+    return;
+  }
+  void* cache = kind == 1 ? kc : vc;
+  const long long at = (long long)pos * nkv * hs + (long long)head * hs;
+  int local = 0;
+  for (int d = threadIdx.x; d < hs; d += blockDim.x) {
+    if (HALF) reinterpret_cast<uint16_t*>(cache)[at + d] = float_to_half_bits(buf[d], &local);
+    else reinterpret_cast<float*>(cache)[at + d] = buf[d];
+  }
+  if (local && bad) atomicAdd(bad, local);
+}
+
+}  // namespace
+
+// ---- the registry
+
+PLLM_API void rope(uint64_t v, uint64_t fcr, uint64_t fci, int32_t nh, int32_t hs, int32_t rot) {
+  PLLM_REQUIRE(nh >= 0 && hs > 0 && hs % 2 == 0, "rope: nh %d hs %d", nh, hs);
+  if (!nh) return;
+  const int turned = rot > 0 && rot < hs ? rot : hs;
+  const int total = nh * (turned / 2);
+  rope_kernel<<<cdiv(total, 256), 256, 0, pllm_stream()>>>(dptr<float>(v), dptr<const float>(fcr),
+                                                          dptr<const float>(fci), nh, hs, turned);
+  PLLM_LAUNCHED("rope");
+}
+
+// att: the reference's scratch of nh (pos + 1) floats; here it holds the slices' partials, and what it holds after
+// the call is not the scores (the reference leaves the probabilities there; nothing of its engine reads them)
+PLLM_API void attention(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t att, int32_t pos, int32_t nh,
+                        int32_t nkv, int32_t hs, int32_t h0, int32_t h1) {
+  registry_attention("attention", out, q, kc, vc, att, pos, nh, nkv, hs, h0, h1, 0.0f, false);
+}
+PLLM_API void attention_f16(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t att, int32_t pos,
+                            int32_t nh, int32_t nkv, int32_t hs, int32_t h0, int32_t h1) {
+  registry_attention("attention_f16", out, q, kc, vc, att, pos, nh, nkv, hs, h0, h1, 0.0f, true);
+}
+PLLM_API void attention_capped(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t att, int32_t pos,
+                               int32_t nh, int32_t nkv, int32_t hs, int32_t h0, int32_t h1, float cap) {
+  PLLM_REQUIRE(cap > 0, "attention_capped: cap %g", cap);
+  registry_attention("attention_capped", out, q, kc, vc, att, pos, nh, nkv, hs, h0, h1, cap, false);
+}
+PLLM_API void attention_f16_capped(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t att, int32_t pos,
+                                   int32_t nh, int32_t nkv, int32_t hs, int32_t h0, int32_t h1, float cap) {
+  PLLM_REQUIRE(cap > 0, "attention_f16_capped: cap %g", cap);
+  registry_attention("attention_f16_capped", out, q, kc, vc, att, pos, nh, nkv, hs, h0, h1, cap, true);
+}
+
+// ---- the forward driver's calls (the position in device memory)
+
+// bytes of scratch pllm_attention_dev needs for a cache of capacity positions
+PLLM_API uint64_t pllm_attention_scratch_bytes(int32_t nh, int32_t hs, int32_t capacity, int32_t split_len) {
+  const long long nsplit = (capacity + split_len - 1) / split_len;
+  return (uint64_t)nh * nsplit * (hs + 2) * sizeof(float);
+}
+
+PLLM_API void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t scratch, uint64_t pos_dev,
+                                 int32_t capacity, int32_t nh, int32_t nkv, int32_t hs, int32_t half, float cap,
+                                 int32_t split_len, int32_t pdl) {
+  if (!check_heads("pllm_attention_dev", nh, nkv, hs, 0, nh)) return;
+  PLLM_REQUIRE(capacity > 0 && split_len > 0 && split_len <= 2048, "pllm_attention_dev: capacity %d split %d",
+               capacity, split_len);
+  AttArgs a = {};
+  a.out = dptr<float>(out);
+  a.q = dptr<const float>(q);
+  a.kc = dptr<const void>(kc);
+  a.vc = dptr<const void>(vc);
+  a.part = dptr<float>(scratch);
+  a.pos_dev = dptr<const int>(pos_dev);
+  a.nh = nh;
+  a.nkv = nkv;
+  a.hs = hs;
+  a.h0 = 0;
+  a.h1 = nh;
+  a.split_len = split_len;
+  a.nsplit = (capacity + split_len - 1) / split_len;
+  a.cap = cap;
+  run_attention("pllm_attention_dev", a, half != 0, pdl != 0);
+}
+
+PLLM_API void pllm_qk_rope_cache(uint64_t q, uint64_t k, uint64_t v, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t,
+                                 uint64_t sin_t, uint64_t pos_dev, int32_t pos, uint64_t kc, uint64_t vc, int32_t nh,
+                                 int32_t nkv, int32_t hs, int32_t rot, float eps, int32_t half, uint64_t bad,
+                                 int32_t pdl) {
+  PLLM_REQUIRE(nh > 0 && nkv > 0 && hs > 0 && hs <= 512 && hs % 2 == 0, "pllm_qk_rope_cache: nh %d nkv %d hs %d", nh,
+               nkv, hs);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nh + 2 * nkv);
+  cfg.blockDim = dim3(hs >= 128 ? 128 : 64);
+  cfg.stream = pllm_stream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e;
+  if (half)
+    e = cudaLaunchKernelEx(&cfg, qk_rope_cache_kernel<true>, dptr<float>(q), dptr<const float>(k), dptr<const float>(v),
+                           dptr<const float>(q_norm), dptr<const float>(k_norm), dptr<const float>(cos_t),
+                           dptr<const float>(sin_t), dptr<const int>(pos_dev), (int)pos, dptr<void>(kc), dptr<void>(vc),
+                           (int)nh, (int)nkv, (int)hs, (int)rot, eps, dptr<int>(bad));
+  else
+    e = cudaLaunchKernelEx(&cfg, qk_rope_cache_kernel<false>, dptr<float>(q), dptr<const float>(k),
+                           dptr<const float>(v), dptr<const float>(q_norm), dptr<const float>(k_norm),
+                           dptr<const float>(cos_t), dptr<const float>(sin_t), dptr<const int>(pos_dev), (int)pos,
+                           dptr<void>(kc), dptr<void>(vc), (int)nh, (int)nkv, (int)hs, (int)rot, eps, dptr<int>(bad));
+  if (e != cudaSuccess) pllm_fail(PLLM_ECUDA, "pllm_qk_rope_cache: %s", cudaGetErrorString(e));
+}

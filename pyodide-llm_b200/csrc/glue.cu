@@ -1,0 +1,191 @@
+// glue.cu: the vector work between the products and the stateful layers.
+//   rmsnorm       kernels/kernel/activations.ts:8-20
+//   swiglu        kernels/kernel/activations.ts:77-90
+//   add_inplace   kernels/kernel/activations.ts:156-158
+//   gate          kernels/kernel/stateful.ts:12-23
+//   convolve      kernels/kernel/stateful.ts:49-63
+//   short_conv    kernels/kernel/stateful.ts:70-86
+//   delta_rule    kernels/kernel/stateful.ts:96-151 (the same float32 operations in the same order: to the bit)
+//   pllm_embed_q8 the int8 embedding row as src/runtime/forward/tensors.ts:154-160 widens it (a device kernel where
+//                 the reference's engine wrote the row from JavaScript)
+#include "pllm_common.cuh"
+
+namespace {
+
+__global__ void rmsnorm_kernel(float* out, const float* x, const float* __restrict__ w, int n, float eps,
+                               long long stride) {
+  x += blockIdx.x * stride;
+  out += blockIdx.x * stride;
+  __shared__ float red[32];
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s = fmaf(x[i], x[i], s);
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += red[i];
+  const float r = 1.0f / sqrtf(tot / (float)n + eps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = w[i] * (r * x[i]);
+}
+
+__global__ void swiglu_kernel(float* out, const float* h1, const float* h3, int n) {
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
+    const float v = h1[j];
+    out[j] = (v / (1.0f + expf(-v))) * h3[j];
+  }
+}
+
+__global__ void add_kernel(float* x, const float* y, int n) {
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) x[j] = x[j] + y[j];
+}
+
+__global__ void gate_kernel(float* out, const float* x, const float* g, int n) {
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
+    out[j] = x[j] / (1.0f + expf(-g[j]));
+}
+
+__device__ __forceinline__ float taps_sum(const float* taps, const float* rows, int c, int n, int count) {
+  float acc = __fmul_rn(taps[c], rows[c]);  // oldest first, as NumPy adds them
+  for (int j = 1; j < count; j++) acc = __fadd_rn(acc, __fmul_rn(taps[(long long)j * n + c], rows[(long long)j * n + c]));
+  return acc;
+}
+
+__global__ void convolve_kernel(float* out, const float* taps, const float* rows, int n, int count) {
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < n; c += gridDim.x * blockDim.x) {
+    const float acc = taps_sum(taps, rows, c, n, count);
+    out[c] = acc / (1.0f + expf(-acc));
+  }
+}
+
+__global__ void short_conv_kernel(float* out, const float* taps, float* rows, const float* b, int n, int count) {
+  float* newest = rows + (long long)(count - 1) * n;
+  const float* gate = b + n;
+  const float* z = b + 2 * (long long)n;
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < n; c += gridDim.x * blockDim.x) {
+    newest[c] = __fmul_rn(b[c], z[c]);
+    out[c] = __fmul_rn(gate[c], taps_sum(taps, rows, c, n, count));
+  }
+}
+
+// one block a value head; thread j a column of the state. Two passes over the rows i (ascending, as the reference),
+// every operation rounded alone (no contraction), so the results are the reference's to the bit.
+__global__ void delta_rule_kernel(float* out, const float* __restrict__ state, float* __restrict__ next,
+                                  const float* __restrict__ c, float* work, int kh, int kd, int vd, int vh, int h0) {
+  const int h = h0 + blockIdx.x;
+  const int key = h / (vh / kh);
+  const float* q = c + (long long)key * kd;
+  const float* k = c + (long long)(kh + key) * kd;
+  const float* v = c + (long long)(2 * kh) * kd + (long long)h * vd;
+  const float beta = work[h], decay = work[vh + h];
+  float* delta = work + 2 * (long long)vh + (long long)h * vd;
+  const float* from = state + (long long)h * kd * vd;
+  float* to = next + (long long)h * kd * vd;
+  float* o = out + (long long)h * vd;
+  for (int j = threadIdx.x; j < vd; j += blockDim.x) {
+    float d = 0.0f;
+    for (int i = 0; i < kd; i++) d = __fadd_rn(d, __fmul_rn(k[i], __fmul_rn(from[(long long)i * vd + j], decay)));
+    d = __fmul_rn(__fsub_rn(v[j], d), beta);
+    delta[j] = d;
+    float acc = 0.0f;
+    for (int i = 0; i < kd; i++) {
+      const float s = __fadd_rn(__fmul_rn(from[(long long)i * vd + j], decay), __fmul_rn(k[i], d));
+      to[(long long)i * vd + j] = s;
+      acc = __fadd_rn(acc, __fmul_rn(q[i], s));
+    }
+    o[j] = acc;
+  }
+}
+
+__global__ void embed_q8_kernel(float* x, const int8_t* __restrict__ emb, const float* __restrict__ scales,
+                                const int32_t* __restrict__ tokens, int token, int dim, long long stride) {
+  const long long t = tokens ? tokens[blockIdx.y] : token;
+  float* xo = x + blockIdx.y * stride;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
+    const long long at = t * dim + i;
+    xo[i] = __fmul_rn((float)emb[at], scales[at / 32]);
+  }
+}
+
+unsigned grid_of(int n) {
+  unsigned g = cdiv((unsigned)(n > 0 ? n : 1), 256u);
+  const unsigned most = (unsigned)pllm_num_sms() * 4;
+  return g > most ? most : g;
+}
+
+}  // namespace
+
+PLLM_API void rmsnorm(uint64_t out, uint64_t x, uint64_t w, int32_t n, float eps) {
+  PLLM_REQUIRE(n > 0, "rmsnorm: n %d", n);
+  rmsnorm_kernel<<<1, 1024, 0, pllm_stream()>>>(dptr<float>(out), dptr<const float>(x), dptr<const float>(w), n, eps, 0);
+  PLLM_LAUNCHED("rmsnorm");
+}
+
+// rmsnorm of rows rows of n, stride apart (floats), all with the same weight: the per-head norms of q and k
+PLLM_API void pllm_rmsnorm_rows(uint64_t out, uint64_t x, uint64_t w, int32_t n, float eps, int32_t rows,
+                                int64_t stride) {
+  PLLM_REQUIRE(n > 0 && rows > 0, "pllm_rmsnorm_rows: n %d rows %d", n, rows);
+  rmsnorm_kernel<<<rows, n >= 1024 ? 1024 : ((n + 31) / 32) * 32, 0, pllm_stream()>>>(
+      dptr<float>(out), dptr<const float>(x), dptr<const float>(w), n, eps, stride);
+  PLLM_LAUNCHED("pllm_rmsnorm_rows");
+}
+
+PLLM_API void swiglu(uint64_t out, uint64_t h1, uint64_t h3, int32_t n) {
+  PLLM_REQUIRE(n >= 0, "swiglu: n %d", n);
+  if (!n) return;
+  swiglu_kernel<<<grid_of(n), 256, 0, pllm_stream()>>>(dptr<float>(out), dptr<const float>(h1), dptr<const float>(h3), n);
+  PLLM_LAUNCHED("swiglu");
+}
+
+PLLM_API void add_inplace(uint64_t x, uint64_t y, int32_t n) {
+  PLLM_REQUIRE(n >= 0, "add_inplace: n %d", n);
+  if (!n) return;
+  add_kernel<<<grid_of(n), 256, 0, pllm_stream()>>>(dptr<float>(x), dptr<const float>(y), n);
+  PLLM_LAUNCHED("add_inplace");
+}
+
+PLLM_API void gate(uint64_t out, uint64_t x, uint64_t g, int32_t n) {
+  PLLM_REQUIRE(n >= 0, "gate: n %d", n);
+  if (!n) return;
+  gate_kernel<<<grid_of(n), 256, 0, pllm_stream()>>>(dptr<float>(out), dptr<const float>(x), dptr<const float>(g), n);
+  PLLM_LAUNCHED("gate");
+}
+
+PLLM_API void convolve(uint64_t out, uint64_t taps, uint64_t rows, int32_t n, int32_t count) {
+  PLLM_REQUIRE(n >= 0 && count >= 1, "convolve: n %d count %d", n, count);
+  if (!n) return;
+  convolve_kernel<<<grid_of(n), 256, 0, pllm_stream()>>>(dptr<float>(out), dptr<const float>(taps),
+                                                       dptr<const float>(rows), n, count);
+  PLLM_LAUNCHED("convolve");
+}
+
+PLLM_API void short_conv(uint64_t out, uint64_t taps, uint64_t rows, uint64_t b, int32_t n, int32_t count) {
+  PLLM_REQUIRE(n >= 0 && count >= 2, "short_conv: n %d count %d", n, count);
+  if (!n) return;
+  short_conv_kernel<<<grid_of(n), 256, 0, pllm_stream()>>>(dptr<float>(out), dptr<const float>(taps),
+                                                         dptr<float>(rows), dptr<const float>(b), n, count);
+  PLLM_LAUNCHED("short_conv");
+}
+
+PLLM_API void delta_rule(uint64_t out, uint64_t state, uint64_t next, uint64_t c, uint64_t work, int32_t kh,
+                         int32_t kd, int32_t vd, int32_t vh, int32_t h0, int32_t h1) {
+  PLLM_REQUIRE(kh > 0 && vh > 0 && vh % kh == 0 && kd > 0 && vd > 0, "delta_rule: kh %d vh %d kd %d vd %d", kh, vh,
+               kd, vd);
+  PLLM_REQUIRE(h0 >= 0 && h1 >= h0 && h1 <= vh, "delta_rule: heads %d..%d of %d", h0, h1, vh);
+  PLLM_REQUIRE(state != next, "delta_rule: state and next must be apart (the reference writes next only)");
+  if (h1 == h0) return;
+  const int threads = vd >= 256 ? 256 : ((vd + 31) / 32) * 32;
+  delta_rule_kernel<<<h1 - h0, threads, 0, pllm_stream()>>>(dptr<float>(out), dptr<const float>(state),
+                                                           dptr<float>(next), dptr<const float>(c), dptr<float>(work),
+                                                           kh, kd, vd, vh, h0);
+  PLLM_LAUNCHED("delta_rule");
+}
+
+// count tokens' embedding rows (tokens: device int32[count], or 0 to take token) into x, stride floats apart
+PLLM_API void pllm_embed_q8(uint64_t x, uint64_t emb, uint64_t scales, uint64_t tokens, int32_t token, int32_t dim,
+                            int32_t count, int64_t stride) {
+  PLLM_REQUIRE(dim > 0 && dim % 32 == 0 && count > 0, "pllm_embed_q8: dim %d count %d", dim, count);
+  embed_q8_kernel<<<dim3(cdiv(dim, 256), count), 256, 0, pllm_stream()>>>(
+      dptr<float>(x), dptr<const int8_t>(emb), dptr<const float>(scales), dptr<const int32_t>(tokens), token, dim,
+      stride);
+  PLLM_LAUNCHED("pllm_embed_q8");
+}

@@ -1,0 +1,330 @@
+"""A decoder's forward pass on the device: the B200 counterpart of src/runtime/forward/engine.ts's createForward
+(run() :421-475; the attention layer forward/attention.ts:171-197; the gated FFN forward/ffn.ts:25-35) for the
+Llama / Qwen3 families of int8 models (Qwen3: q_norm / k_norm, forward/attention.ts:140-143).
+
+The engine's public calls are the reference's (engine.ts:549-702): forward(token, pos, need_logits) and
+forward_many(tokens, pos). What differs is where the memory is: the weights, the cache and the activations stay in
+device memory, and one decode step is recorded once as a CUDA graph of the library's kernels (the token and the
+position are read by the kernels from device memory, so the same graph serves every position). A step is:
+
+    embed (pllm_embed_q8: the int8 row times its scales, tensors.ts:154-160)
+    per layer:
+      q, k, v   = one product over the three matrices' rows, its input RMSNorm + quantize_x fused (pllm_gemv pro 1)
+      q/k norms, RoPE at pos, k and v into the cache (pllm_qk_rope_cache)
+      attention over positions 0..pos (pllm_attention_dev: split-KV)
+      x += wo . quantize_x(attention)      (pllm_gemv pro 2, epi 1: the residual add fused)
+      hb = silu(w1 . h) * (w3 . h), h = quantize_x(RMSNorm(x))  (pllm_gemv pro 1, epi 2: w1's and w3's rows in one)
+      x += w2 . quantize_x(hb)            (pllm_gemv pro 2, epi 1)
+    logits = wcls . quantize_x(RMSNorm(x))
+
+Every product's group sums are the reference kernels' exact integers; the float32 around them agrees with the
+reference's within rounding (the tests hold the logits to the oracle's within 1e-3 relative).
+"""
+from dataclasses import dataclass
+
+import numpy as np
+
+from .device import Buffer, Pinned, init
+from .lib import L, check
+
+F_Q8 = 0
+PRO_Q, PRO_RMS, PRO_QUANT = 0, 1, 2
+EPI_STORE, EPI_ADD, EPI_SWIGLU = 0, 1, 2
+
+
+@dataclass
+class Config:
+    dim: int
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_size: int
+    vocab: int
+    seq_len: int
+    qk_norm: bool = False
+    rope_theta: float = 10000.0
+    eps: float = 1e-5
+    relaxed: bool = False     # matmul_q8r's activations (bias 64, qmax 63) in place of matmul_q8's (qmax 127)
+    half_kv: bool = True      # a float16 cache (to_f16 / attention_f16), as engine.ts:191 chooses for int8 models
+
+    @property
+    def qdim(self):
+        return self.heads * self.head_size
+
+    @property
+    def kvdim(self):
+        return self.kv_heads * self.head_size
+
+    def weight_bytes(self):
+        """The bytes a decode step reads of the int8 matrices (values and float32 scales, 1.125 bytes a weight)."""
+        per_layer = (self.qdim + 2 * self.kvdim) * self.dim + self.dim * self.qdim + 3 * self.hidden * self.dim
+        return int((self.layers * per_layer + self.vocab * self.dim) * 1.125)
+
+
+# the BASELINE configurations (synthetic weights of these shapes)
+STORIES15M = Config(dim=288, hidden=768, layers=6, heads=6, kv_heads=6, head_size=48, vocab=32000, seq_len=256)
+QWEN3_8B = Config(dim=4096, hidden=12288, layers=36, heads=32, kv_heads=8, head_size=128, vocab=151936, seq_len=2560,
+                  qk_norm=True, rope_theta=1e6, eps=1e-6)
+
+
+def rope_tables(cfg):
+    """cos / sin of every position's angle of every pair of a head (float64, then float32), as the reference's
+    converter writes freq_cis_real / freq_cis_imag (engine/layers.py:372-377 rope_frequencies)."""
+    freqs = 1.0 / cfg.rope_theta ** (np.arange(0, cfg.head_size, 2, dtype=np.float64) / cfg.head_size)
+    angles = np.outer(np.arange(cfg.seq_len, dtype=np.float64), freqs)
+    return np.cos(angles).astype(np.float32), np.sin(angles).astype(np.float32)
+
+
+def quantize_rows(w):
+    """float32 rows -> (int8, float32 scales a group of 32): engine/packing.py's quantize (= quantize_x bias 0)."""
+    g = w.reshape(-1, 32)
+    scales = (np.abs(g).max(axis=1) / np.float32(127.0)).astype(np.float32)
+    inv = np.divide(np.float32(1.0), scales, out=np.zeros_like(scales), where=scales > 0)
+    return np.rint(g * inv[:, None]).astype(np.int8).reshape(w.shape), scales.reshape(w.shape[:-1] + (-1,))
+
+
+def synthetic_host_weights(cfg, seed=0, std=0.02):
+    """Host weights of a small model in the reference's int8 format (N(0, std) quantized; norms N(1, 0.1) as
+    tests/made_up.py:42 makes them): a dict by the oracle's field names."""
+    rng = np.random.default_rng(seed)
+    Lr, d, h, q, kv = cfg.layers, cfg.dim, cfg.hidden, cfg.qdim, cfg.kvdim
+    W = {}
+
+    def mat(name, shape):
+        w, s = quantize_rows(rng.normal(0, std, shape).astype(np.float32))
+        W["w" + name], W["s" + name] = w, s
+
+    mat("q", (Lr, q, d))
+    mat("k", (Lr, kv, d))
+    mat("v", (Lr, kv, d))
+    mat("o", (Lr, d, q))
+    mat("1", (Lr, h, d))
+    mat("2", (Lr, d, h))
+    mat("3", (Lr, h, d))
+    W["emb"], W["emb_s"] = quantize_rows(rng.normal(0, 1.0, (cfg.vocab, d)).astype(np.float32))
+    W["cls"], W["cls_s"] = quantize_rows(rng.normal(0, std, (cfg.vocab, d)).astype(np.float32))
+    W["att_norm"] = rng.normal(1, 0.1, (Lr, d)).astype(np.float32)
+    W["ffn_norm"] = rng.normal(1, 0.1, (Lr, d)).astype(np.float32)
+    W["final_norm"] = rng.normal(1, 0.1, d).astype(np.float32)
+    W["q_norm"] = rng.normal(1, 0.1, (Lr, cfg.head_size)).astype(np.float32) if cfg.qk_norm else None
+    W["k_norm"] = rng.normal(1, 0.1, (Lr, cfg.head_size)).astype(np.float32) if cfg.qk_norm else None
+    W["cos_t"], W["sin_t"] = rope_tables(cfg)
+    return W
+
+
+class Engine:
+    """One model's forward pass on the current device."""
+
+    SPLIT = 128  # positions a slice of the split-KV attention
+
+    def __init__(self, cfg, host=None, seed=0, device=0, graphs=True, pdl=True):
+        init(device)
+        self.cfg, self.graphs, self.pdl = cfg, graphs, pdl
+        c = cfg
+        self.rows_qkv = c.qdim + 2 * c.kvdim
+        self.bias = 64 if c.relaxed else 0
+        B = {}
+        ng = lambda cols: cols // 32  # noqa: E731
+        # the matrices, a layer's after another; q, k, v rows in one, w1 rows then w3 rows in one
+        B["wqkv"] = Buffer(c.layers * self.rows_qkv * c.dim)
+        B["sqkv"] = Buffer(c.layers * self.rows_qkv * ng(c.dim) * 4)
+        B["wo"] = Buffer(c.layers * c.dim * c.qdim)
+        B["so"] = Buffer(c.layers * c.dim * ng(c.qdim) * 4)
+        B["w13"] = Buffer(c.layers * 2 * c.hidden * c.dim)
+        B["s13"] = Buffer(c.layers * 2 * c.hidden * ng(c.dim) * 4)
+        B["w2"] = Buffer(c.layers * c.dim * c.hidden)
+        B["s2"] = Buffer(c.layers * c.dim * ng(c.hidden) * 4)
+        B["emb"] = Buffer(c.vocab * c.dim)
+        B["emb_s"] = Buffer(c.vocab * ng(c.dim) * 4)
+        B["cls"] = Buffer(c.vocab * c.dim)
+        B["cls_s"] = Buffer(c.vocab * ng(c.dim) * 4)
+        B["att_norm"] = Buffer(c.layers * c.dim * 4)
+        B["ffn_norm"] = Buffer(c.layers * c.dim * 4)
+        B["final_norm"] = Buffer(c.dim * 4)
+        B["q_norm"] = Buffer(c.layers * c.head_size * 4) if c.qk_norm else None
+        B["k_norm"] = Buffer(c.layers * c.head_size * 4) if c.qk_norm else None
+        B["cos_t"] = Buffer(c.seq_len * c.head_size // 2 * 4)
+        B["sin_t"] = Buffer(c.seq_len * c.head_size // 2 * 4)
+        E = 2 if c.half_kv else 4
+        B["kc"] = Buffer(c.layers * c.seq_len * c.kvdim * E).zero()
+        B["vc"] = Buffer(c.layers * c.seq_len * c.kvdim * E).zero()
+        # activations
+        B["x"] = Buffer(c.dim * 4)
+        B["qkv"] = Buffer(self.rows_qkv * 4)
+        B["att"] = Buffer(c.qdim * 4)
+        B["hb"] = Buffer(c.hidden * 4)
+        B["logits"] = Buffer(c.vocab * 4)
+        B["tp"] = Buffer(8).zero()      # the token and the position, read by the kernels
+        B["bad"] = Buffer(4).zero()     # non-finite keys / values written to a float16 cache (halves.ts:35)
+        B["scratch"] = Buffer(L.pllm_attention_scratch_bytes(c.heads, c.head_size, c.seq_len, self.SPLIT))
+        self.B = B
+        if host is not None:
+            self.load(host)
+        else:
+            self.synthesize(seed)
+        self.stream = L.pllm_stream_create()
+        self.tp_host = Pinned(2, np.int32)
+        self.logits_host = Pinned(c.vocab, np.float32)
+        self.graph = 0
+        check("Engine")
+
+    # ---- weights
+    def load(self, W):
+        """Host weights (synthetic_host_weights' dict, the reference's int8 layout) into the device layout."""
+        c, B = self.cfg, self.B
+        B["wqkv"].upload(np.concatenate([W["wq"], W["wk"], W["wv"]], axis=1))
+        B["sqkv"].upload(np.concatenate([W["sq"], W["sk"], W["sv"]], axis=1))
+        B["wo"].upload(W["wo"])
+        B["so"].upload(W["so"])
+        B["w13"].upload(np.concatenate([W["w1"], W["w3"]], axis=1))
+        B["s13"].upload(np.concatenate([W["s1"], W["s3"]], axis=1))
+        B["w2"].upload(W["w2"])
+        B["s2"].upload(W["s2"])
+        for k in ("emb", "emb_s", "cls", "cls_s", "att_norm", "ffn_norm", "final_norm", "cos_t", "sin_t"):
+            B[k].upload(W[k])
+        if c.qk_norm:
+            B["q_norm"].upload(W["q_norm"])
+            B["k_norm"].upload(W["k_norm"])
+        L.pllm_sync()
+        check("load")
+
+    def synthesize(self, seed):
+        """Seeded synthetic weights made on the device: N(0, 0.02) int8 matrices (the embedding N(0, 1)), norms
+        N(1, 0.1), the RoPE tables of the configuration."""
+        c, B = self.cfg, self.B
+        s = seed * 1000
+        for i, (w, sc, rows, cols) in enumerate([
+                ("wqkv", "sqkv", c.layers * self.rows_qkv, c.dim), ("wo", "so", c.layers * c.dim, c.qdim),
+                ("w13", "s13", c.layers * 2 * c.hidden, c.dim), ("w2", "s2", c.layers * c.dim, c.hidden),
+                ("cls", "cls_s", c.vocab, c.dim)]):
+            L.pllm_synth_q8(B[w].ptr, B[sc].ptr, rows, cols, s + i, 0.02)
+        L.pllm_synth_q8(B["emb"].ptr, B["emb_s"].ptr, c.vocab, c.dim, s + 10, 1.0)
+        for i, k in enumerate(("att_norm", "ffn_norm", "final_norm", "q_norm", "k_norm")):
+            if B[k] is not None:
+                L.pllm_synth_f32(B[k].ptr, B[k].nbytes // 4, s + 20 + i, 1.0, 0.1)
+        cos, sin = rope_tables(c)
+        B["cos_t"].upload(cos)
+        B["sin_t"].upload(sin)
+        L.pllm_sync()
+        check("synthesize")
+
+    def host_weights(self):
+        """The device weights back in the oracle's layout (for the CPU baseline and the checks)."""
+        c, B = self.cfg, self.B
+        d = lambda k, dt: B[k].download(dt)  # noqa: E731
+        W = {}
+        qkv = d("wqkv", np.int8).reshape(c.layers, self.rows_qkv, c.dim)
+        sqkv = d("sqkv", np.float32).reshape(c.layers, self.rows_qkv, c.dim // 32)
+        W["wq"], W["wk"], W["wv"] = np.split(qkv, [c.qdim, c.qdim + c.kvdim], axis=1)
+        W["sq"], W["sk"], W["sv"] = np.split(sqkv, [c.qdim, c.qdim + c.kvdim], axis=1)
+        W["wo"], W["so"] = d("wo", np.int8), d("so", np.float32)
+        w13 = d("w13", np.int8).reshape(c.layers, 2 * c.hidden, c.dim)
+        s13 = d("s13", np.float32).reshape(c.layers, 2 * c.hidden, c.dim // 32)
+        W["w1"], W["w3"] = w13[:, :c.hidden], w13[:, c.hidden:]
+        W["s1"], W["s3"] = s13[:, :c.hidden], s13[:, c.hidden:]
+        W["w2"], W["s2"] = d("w2", np.int8), d("s2", np.float32)
+        for k, dt in (("emb", np.int8), ("emb_s", np.float32), ("cls", np.int8), ("cls_s", np.float32),
+                      ("att_norm", np.float32), ("ffn_norm", np.float32), ("final_norm", np.float32),
+                      ("cos_t", np.float32), ("sin_t", np.float32)):
+            W[k] = d(k, dt)
+        W["q_norm"] = d("q_norm", np.float32) if c.qk_norm else None
+        W["k_norm"] = d("k_norm", np.float32) if c.qk_norm else None
+        return {k: (np.ascontiguousarray(v) if v is not None else None) for k, v in W.items()}
+
+    # ---- one step
+    def _gemv(self, out, wq, ws, rows, n, x, norm, pro, epi, pair=0, pdl=True):
+        c = self.cfg
+        L.pllm_gemv(out, 0, 0, 0, 0, 0, x, 0, norm, c.eps, self.bias, wq, ws, F_Q8, n, 0, rows, 1, pro, epi, pair,
+                    int(pdl and self.pdl))
+
+    @property
+    def launches_per_step(self):
+        """Kernels a step launches: the embedding, seven a layer (q/k/v product, norms + RoPE + cache, the attention's
+        two, the wo, w1/w3 and w2 products), the classifier."""
+        return 2 + 7 * self.cfg.layers
+
+    def _enqueue_step(self, need_logits=True):
+        c, B = self.cfg, self.B
+        tok, pos = B["tp"].ptr, B["tp"].ptr + 4
+        E = 2 if c.half_kv else 4
+        L.pllm_embed_q8(B["x"].ptr, B["emb"].ptr, B["emb_s"].ptr, tok, 0, c.dim, 1, c.dim)
+        for l in range(c.layers):
+            wqkv = B["wqkv"].ptr + l * self.rows_qkv * c.dim
+            sqkv = B["sqkv"].ptr + l * self.rows_qkv * (c.dim // 32) * 4
+            self._gemv(B["qkv"].ptr, wqkv, sqkv, self.rows_qkv, c.dim, B["x"].ptr, B["att_norm"].ptr + l * c.dim * 4,
+                       PRO_RMS, EPI_STORE)
+            kc = B["kc"].ptr + l * c.seq_len * c.kvdim * E
+            vc = B["vc"].ptr + l * c.seq_len * c.kvdim * E
+            qn = B["q_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
+            kn = B["k_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
+            q = B["qkv"].ptr
+            L.pllm_qk_rope_cache(q, q + c.qdim * 4, q + (c.qdim + c.kvdim) * 4, qn, kn, B["cos_t"].ptr, B["sin_t"].ptr,
+                                 pos, 0, kc, vc, c.heads, c.kv_heads, c.head_size, 0, c.eps, int(c.half_kv),
+                                 B["bad"].ptr, int(self.pdl))
+            L.pllm_attention_dev(B["att"].ptr, q, kc, vc, B["scratch"].ptr, pos, c.seq_len, c.heads, c.kv_heads,
+                                 c.head_size, int(c.half_kv), 0.0, self.SPLIT, int(self.pdl))
+            self._gemv(B["x"].ptr, B["wo"].ptr + l * c.dim * c.qdim, B["so"].ptr + l * c.dim * (c.qdim // 32) * 4,
+                       c.dim, c.qdim, B["att"].ptr, 0, PRO_QUANT, EPI_ADD)
+            self._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * c.hidden * c.dim,
+                       B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.hidden, c.dim, B["x"].ptr,
+                       B["ffn_norm"].ptr + l * c.dim * 4, PRO_RMS, EPI_SWIGLU, pair=c.hidden)
+            self._gemv(B["x"].ptr, B["w2"].ptr + l * c.dim * c.hidden, B["s2"].ptr + l * c.dim * (c.hidden // 32) * 4,
+                       c.dim, c.hidden, B["hb"].ptr, 0, PRO_QUANT, EPI_ADD)
+        if need_logits:
+            self._gemv(B["logits"].ptr, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim, B["x"].ptr, B["final_norm"].ptr,
+                       PRO_RMS, EPI_STORE)
+
+    def capture(self):
+        """Record one decode step (with logits) as a CUDA graph on the engine's stream."""
+        L.pllm_set_stream(self.stream)
+        if self.graph:
+            L.pllm_graph_destroy(self.graph)
+        if L.pllm_graph_begin() != 0:
+            check("graph begin")
+        self._enqueue_step(True)
+        self.graph = L.pllm_graph_end()
+        check("graph capture")
+        if not self.graph:
+            raise RuntimeError("graph capture failed")
+
+    def launch_step(self):
+        """Enqueue one step for the token and position already in device memory (no copies, no wait)."""
+        L.pllm_set_stream(self.stream)
+        if self.graphs:
+            if not self.graph:
+                self.capture()
+            L.pllm_graph_launch(self.graph)
+        else:
+            self._enqueue_step(True)
+
+    # ---- the engine's calls (forward/engine.ts:549-702)
+    def forward(self, token, pos, need_logits=True):
+        """One token at pos; the logits (a copy) when asked for."""
+        c = self.cfg
+        if not (0 <= pos < c.seq_len and 0 <= token < c.vocab):
+            raise ValueError(f"token {token} at {pos}: out of range")
+        L.pllm_set_stream(self.stream)
+        self.tp_host.array[0], self.tp_host.array[1] = token, pos
+        L.pllm_h2d(self.B["tp"].ptr, self.tp_host.ptr, 8)
+        self.launch_step()
+        if need_logits:
+            L.pllm_d2h(self.logits_host.ptr, self.B["logits"].ptr, c.vocab * 4)
+        L.pllm_sync()
+        check("forward")
+        return self.logits_host.array.copy() if need_logits else None
+
+    def forward_many(self, tokens, pos):
+        """Tokens at pos, pos + 1, ...: each computed as it would be alone (engine.ts:590); the last one's logits."""
+        out = None
+        for t, token in enumerate(tokens):
+            out = self.forward(int(token), pos + t, need_logits=(t == len(tokens) - 1))
+        return out
+
+    def close(self):
+        if self.graph:
+            L.pllm_graph_destroy(self.graph)
+            self.graph = 0
+        for b in self.B.values():
+            if b is not None:
+                b.free()

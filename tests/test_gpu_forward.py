@@ -1,0 +1,84 @@
+"""The device forward pass (pllm.forward.Engine: fused products, split-KV attention, one CUDA graph a step) against
+the oracle's forward (the reference kernels' arithmetic, oracle/pllm_oracle.c or_forward) on the same int8 weights:
+the logits within 1e-3 of the largest |logit| (the north star's line for int8 logits) at every position, the same
+greedy token, eager and graph launches equal."""
+import numpy as np
+import pytest
+
+import oracle as O
+from pllm.forward import Config, Engine, synthetic_host_weights
+
+pytestmark = pytest.mark.gpu
+
+SMALL_QWEN3 = Config(dim=256, hidden=512, layers=2, heads=8, kv_heads=2, head_size=64, vocab=1000, seq_len=300,
+                     qk_norm=True, rope_theta=1e6, eps=1e-6)
+STORIES = Config(dim=288, hidden=768, layers=6, heads=6, kv_heads=6, head_size=48, vocab=32000, seq_len=256)
+
+
+def oracle_arrays(cfg, W):
+    E = np.uint16 if cfg.half_kv else np.float32
+    A = {k: W[k] for k in ("wq", "wk", "wv", "wo", "w1", "w2", "w3", "sq", "sk", "sv", "so", "s1", "s2", "s3", "emb",
+                           "emb_s", "cls", "cls_s", "att_norm", "ffn_norm", "final_norm", "q_norm", "k_norm", "cos_t",
+                           "sin_t")}
+    A.update(cq=None, ck=None, cv=None, co=None, c1=None, c2=None, c3=None, cls_c=None)
+    A["kc"] = np.zeros(cfg.layers * cfg.seq_len * cfg.kvdim, E)
+    A["vc"] = np.zeros(cfg.layers * cfg.seq_len * cfg.kvdim, E)
+    return {k: (np.ascontiguousarray(v) if v is not None else None) for k, v in A.items()}
+
+
+def oracle_config(cfg):
+    return O.Config(dim=cfg.dim, hidden=cfg.hidden, layers=cfg.layers, heads=cfg.heads, kv_heads=cfg.kv_heads,
+                    head_size=cfg.head_size, vocab=cfg.vocab, seq_len=cfg.seq_len, qk_norm=int(cfg.qk_norm),
+                    relaxed=int(cfg.relaxed), half_kv=int(cfg.half_kv), eps=cfg.eps)
+
+
+@pytest.mark.parametrize("cfg", [SMALL_QWEN3, STORIES], ids=["qwen3-small", "stories15m"])
+@pytest.mark.parametrize("relaxed", [False, True])
+def test_forward_matches_oracle(cfg, relaxed):
+    from dataclasses import replace
+    cfg = replace(cfg, relaxed=relaxed)
+    W = synthetic_host_weights(cfg, seed=3)
+    eng = Engine(cfg, host=W)
+    A = oracle_arrays(cfg, W)
+    oc = oracle_config(cfg)
+    rng = np.random.default_rng(1)
+    tokens = rng.integers(0, cfg.vocab, 40)
+    agree = 0
+    for pos, tok in enumerate(tokens):
+        want = O.forward(oc, A, int(tok), pos)
+        got = eng.forward(int(tok), pos)
+        scale = np.abs(want).max()
+        assert np.abs(got - want).max() <= 1e-3 * scale, (pos, np.abs(got - want).max(), scale)
+        agree += int(np.argmax(got) == np.argmax(want))
+    assert agree >= len(tokens) - 1
+    eng.close()
+
+
+def test_graph_equals_eager():
+    cfg = SMALL_QWEN3
+    W = synthetic_host_weights(cfg, seed=5)
+    a, b = Engine(cfg, host=W, graphs=True), Engine(cfg, host=W, graphs=False, pdl=False)
+    for pos, tok in enumerate([3, 17, 999, 0, 42, 7]):
+        assert np.array_equal(a.forward(tok, pos), b.forward(tok, pos))
+    a.close()
+    b.close()
+
+
+def test_long_context_positions():
+    """Positions past a slice of the split-KV attention (128) and near the cache's end."""
+    cfg = SMALL_QWEN3
+    W = synthetic_host_weights(cfg, seed=8)
+    eng = Engine(cfg, host=W)
+    A = oracle_arrays(cfg, W)
+    oc = oracle_config(cfg)
+    rng = np.random.default_rng(2)
+    for pos in range(cfg.seq_len):
+        tok = int(rng.integers(0, cfg.vocab))
+        if pos in (0, 127, 128, 129, 255, 256, cfg.seq_len - 1):
+            want = O.forward(oc, A, tok, pos)
+            got = eng.forward(tok, pos)
+            assert np.abs(got - want).max() <= 1e-3 * np.abs(want).max(), pos
+        else:
+            O.forward(oc, A, tok, pos)
+            eng.forward(tok, pos, need_logits=False)
+    eng.close()

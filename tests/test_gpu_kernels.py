@@ -1,0 +1,399 @@
+"""Parity of every registry kernel of libpllm.so (called through the C ABI, device memory) with the CPU oracle on the
+same inputs: the reference's own kernel-test cases (tests/golden/golden.npz: int8-check.ts and ternary-check.ts
+inputs, edge weights and scales) and seeded random ones, plus the registry's contract (row ranges that write no row
+outside them, tiles equal to the token kernel, refused arguments).
+
+Bars: integer and byte work (quantize_x, interleave, the corrections, float16, every group's int32 sum, delta_rule)
+to the bit; float32 products within float32 rounding of a different summation order, bounded per row by
+8 * groups * 2^-24 * sum |group terms|; attention and the glue within 2e-5 relative (1e-4 for a float16 cache)."""
+import numpy as np
+import pytest
+
+import oracle as O
+from pllm.device import Buffer, init
+from pllm.lib import L, PllmError, check
+
+pytestmark = pytest.mark.gpu
+
+EPS = 2.0 ** -24
+
+
+@pytest.fixture(scope="module", autouse=True)
+def device():
+    init(0)
+    L.pllm_set_stream(0)
+    yield
+    L.pllm_device_sync()
+
+
+def dev(a):
+    return Buffer.of(np.ascontiguousarray(a))
+
+
+def get(b, dtype, count=None):
+    return b.download(dtype, count)
+
+
+def bits(a):
+    return np.asarray(a, np.float32).view(np.int32)
+
+
+def product_bound(G, ws, xs):
+    """The float32 error bound of sum_g G_g (ws_g xs_g) for each row: (8 groups) 2^-24 sum |terms|."""
+    terms = np.abs(G.astype(np.float64) * ws.astype(np.float64) * xs.astype(np.float64)[None, :])
+    return 8 * G.shape[1] * EPS * terms.sum(axis=1) + 1e-37
+
+
+# ---------------------------------------------------------------- activations
+
+@pytest.mark.parametrize("bias", [0, 64])
+def test_quantize_x_bit_exact(golden, bias):
+    for x in (golden["quant_x"], np.random.default_rng(1).normal(0, 3, 4096).astype(np.float32)):
+        xq, xs = dev(np.zeros(x.size, np.uint8)), dev(np.zeros(x.size // 32, np.float32))
+        L.quantize_x(xq.ptr, xs.ptr, dev(x).ptr, x.size, bias)
+        check("quantize_x")
+        wq, ws = O.quantize_x(x, bias)
+        assert np.array_equal(get(xq, np.uint8), wq)
+        assert np.array_equal(bits(get(xs, np.float32)), bits(ws))
+
+
+@pytest.mark.parametrize("groups", [1, 2, 3, 5, 9])
+def test_interleave_bit_exact(golden, groups):
+    k = f"tern_g{groups}_"
+    n = groups * 128
+    a, xs = golden[k + "a"], golden[k + "xs"]
+    xq = dev(a.view(np.uint8))
+    ext = dev(np.concatenate([xs, np.full(n // 32, -7, np.float32)]))
+    L.interleave(xq.ptr, ext.ptr, n)
+    check("interleave")
+    assert np.array_equal(get(xq, np.int8), golden[k + "il"])
+    e = get(ext, np.float32)
+    assert np.array_equal(e[n // 32:].view(np.int32), golden[k + "sums"])
+    assert np.array_equal(e[: n // 32], xs)
+
+
+def test_corrections_exact(golden):
+    for ng in (1, 9, 13, 81):
+        w8, w6 = golden[f"int8_ng{ng}_w8"], golden[f"int8_ng{ng}_w6"]
+        groups = w8.size // 32
+        out = dev(np.full(groups + 4, -7, np.int32))
+        L.int8_sums(out.ptr, dev(w8).ptr, groups)
+        got = get(out, np.int32)
+        assert np.array_equal(got[:groups], O.int8_sums(w8)) and np.all(got[groups:] == -7)
+        L.six_sums(out.ptr, dev(w6).ptr, groups)
+        assert np.array_equal(get(out, np.int32)[:groups], O.six_sums(w6))
+
+
+# ---------------------------------------------------------------- int8 / int6 products
+
+NGS = [1, 2, 3, 4, 5, 6, 7, 8, 9, 12, 13, 81]
+RANGES = [(0, 13), (0, 1), (0, 3), (12, 13), (1, 6), (3, 8), (5, 5), (4, 12)]
+
+
+@pytest.mark.parametrize("ng", NGS)
+def test_group_sums_bit_exact(golden, ng):
+    """The accumulators: every (row, group) int32 of int8 and int6 rows, plain and relaxed activations."""
+    k = f"int8_ng{ng}_"
+    n = ng * 32
+    w8, w6 = dev(golden[k + "w8"]), dev(golden[k + "w6"])
+    out = dev(np.zeros(13 * ng, np.int32))
+    for t in range(9):
+        for acts, bias in ((golden[k + "qp"][t].view(np.uint8), 0), (golden[k + "qr"][t], 64)):
+            xq = dev(acts)
+            xs = dev(np.zeros(2 * ng, np.float32))
+            L.pllm_group_sums(out.ptr, xq.ptr, xs.ptr, w8.ptr, 0, n, 0, 13, bias)
+            check("group sums")
+            assert np.array_equal(get(out, np.int32).reshape(13, ng), O.group_sums_q8(acts, golden[k + "w8"], bias))
+            L.pllm_group_sums(out.ptr, xq.ptr, xs.ptr, w6.ptr, 1, n, 0, 13, bias)
+            assert np.array_equal(get(out, np.int32).reshape(13, ng), O.group_sums_q6(acts, golden[k + "w6"], n, bias))
+
+
+@pytest.mark.parametrize("ng", NGS)
+def test_int8_int6_products(golden, ng):
+    """matmul_q8 / q8r / q6 / q6r on int8-check.ts's cases: every row range, nothing written outside it."""
+    k = f"int8_ng{ng}_"
+    n = ng * 32
+    w8h, w6h, wsh = golden[k + "w8"], golden[k + "w6"], golden[k + "ws"]
+    w8, w6, ws = dev(w8h), dev(w6h), dev(wsh)
+    wc8, wc6 = dev(O.int8_sums(w8h)), dev(O.six_sums(w6h))
+    out = dev(np.zeros(14, np.float32))
+    for t in range(9):
+        for plain in (True, False):
+            acts = golden[k + "qp"][t].view(np.uint8) if plain else golden[k + "qr"][t]
+            xsh = golden[k + "xp"][t] if plain else golden[k + "xr"][t]
+            xq, xs = dev(acts), dev(xsh)
+            bias = 0 if plain else 64
+            G8 = O.group_sums_q8(acts, w8h, bias)
+            G6 = O.group_sums_q6(acts, w6h, n, bias)
+            cases = [("q8", G8, lambda r0, r1: L.matmul_q8(out.ptr, xq.ptr, xs.ptr, w8.ptr, ws.ptr, n, r0, r1)
+                      if plain else L.matmul_q8r(out.ptr, xq.ptr, xs.ptr, w8.ptr, ws.ptr, wc8.ptr, n, r0, r1),
+                      (golden[k + "q8"] if plain else golden[k + "q8r"])[t]),
+                     ("q6", G6, lambda r0, r1: L.matmul_q6(out.ptr, xq.ptr, xs.ptr, w6.ptr, ws.ptr, n, r0, r1)
+                      if plain else L.matmul_q6r(out.ptr, xq.ptr, xs.ptr, w6.ptr, ws.ptr, wc6.ptr, n, r0, r1),
+                      (golden[k + "q6"] if plain else golden[k + "q6r"])[t])]
+            for name, G, call, want in cases:
+                bound = product_bound(G, wsh.reshape(13, ng), xsh)
+                for r0, r1 in RANGES:
+                    out.upload(np.full(14, -7, np.float32))
+                    call(r0, r1)
+                    check(name)
+                    got = get(out, np.float32)
+                    inside = np.arange(14)
+                    inside = (inside >= r0) & (inside < r1)
+                    assert np.all(got[~inside] == -7), (name, t, r0, r1)
+                    err = np.abs(got[:13][inside[:13]].astype(np.float64) - want[inside[:13]])
+                    assert np.all(err <= bound[inside[:13]]), (name, plain, t, r0, r1, err.max())
+
+
+def test_q8r_tile_equals_token_kernel(golden):
+    """relaxed/int8.ts:60-65: each (row, token) of the tile is matmul_q8r's number (here: to the bit on the GPU too),
+    for 1..9, 16 and 21 tokens, rows off the fours; nothing written outside the rows and tokens."""
+    k = "int8_ng13_"
+    n, frame, os_ = 13 * 32, 8192, 64
+    w8h = golden[k + "w8"]
+    w8, ws, wc = dev(w8h), dev(golden[k + "ws"]), dev(O.int8_sums(w8h))
+    rng = np.random.default_rng(9)
+    tokens = 21
+    qr = np.zeros((tokens, frame), np.uint8)
+    for t in range(tokens):
+        qr[t, :n] = golden[k + "qr"][t] if t < 9 else rng.integers(0, 128, n)
+        qr[t, 4096:4096 + 13 * 4] = golden[k + "xr"][t % 9].view(np.uint8)
+    frames = dev(qr)
+    alone = dev(np.zeros(16, np.float32))
+    outs = dev(np.zeros(tokens * os_ // 4, np.float32))
+    for count in list(range(1, 10)) + [16, 21]:
+        for r0, r1 in ((0, 13), (1, 6), (2, 13), (5, 5)):
+            outs.upload(np.full(tokens * os_ // 4, -7, np.float32))
+            L.matmul_q8r_tile(outs.ptr, frames.ptr, frames.ptr + 4096, w8.ptr, ws.ptr, wc.ptr, n, r0, r1, count, os_,
+                              frame)
+            check("matmul_q8r_tile")
+            got = get(outs, np.float32).reshape(tokens, os_ // 4)
+            for t in range(tokens):
+                alone.upload(np.full(16, -7, np.float32))
+                if t < count:
+                    L.matmul_q8r(alone.ptr, frames.ptr + t * frame, frames.ptr + t * frame + 4096, w8.ptr, ws.ptr,
+                                 wc.ptr, n, r0, r1)
+                assert np.array_equal(bits(got[t]), bits(get(alone, np.float32))), (count, r0, r1, t)
+
+
+# ---------------------------------------------------------------- ternary / binary
+
+@pytest.mark.parametrize("groups", [1, 2, 3, 4, 5, 7, 9])
+def test_ternary_binary_products(golden, groups):
+    k = f"tern_g{groups}_"
+    n = groups * 128
+    a, xsh = golden[k + "a"], golden[k + "xs"]
+    il, ext = O.interleave(a.view(np.uint8), xsh)
+    xq, xs = dev(il), dev(ext)
+    halves = dev(golden[k + "halves"])
+    out = dev(np.zeros(14, np.float32))
+    sums = dev(np.zeros(13 * n // 32, np.int32))
+    for binary, packed, want, fns in ((False, golden[k + "packed"], golden[k + "t2"], ("matmul_t2", "matmul_t2r")),
+                                      (True, golden[k + "bpacked"], golden[k + "b1"], ("matmul_b1", "matmul_b1r"))):
+        w = dev(packed)
+        G = O.group_sums_signs(il, ext, packed, n, binary)
+        L.pllm_group_sums(sums.ptr, xq.ptr, xs.ptr, w.ptr, 3 if binary else 2, n, 0, 13, 0)
+        check("group sums signs")
+        assert np.array_equal(get(sums, np.int32).reshape(13, -1), G)
+        d = O.from_f16(golden[k + "halves"]).reshape(13, groups)
+        terms = np.abs(G.astype(np.float64) * ext[: n // 32][None, :] * np.repeat(d, 4, axis=1))
+        bound = 8 * (n // 32) * EPS * terms.sum(axis=1) + 1e-37
+        for fn in fns:
+            for r0, r1 in RANGES:
+                out.upload(np.full(14, -7, np.float32))
+                getattr(L, fn)(out.ptr, xq.ptr, xs.ptr, w.ptr, halves.ptr, n, r0, r1, 2 if binary else 3)
+                check(fn)
+                got = get(out, np.float32)
+                sel = np.zeros(14, bool)
+                sel[r0:r1] = True
+                assert np.all(got[~sel] == -7)
+                assert np.all(np.abs(got[:13][sel[:13]] - want[sel[:13]]) <= bound[sel[:13]]), (fn, r0, r1)
+
+
+def test_signs_tiles_equal_token_kernel(golden):
+    k = "tern_g5_"
+    n, frame, os_ = 5 * 128, 4096, 64
+    a, xsh = golden[k + "a"], golden[k + "xs"]
+    rng = np.random.default_rng(4)
+    tokens = 11
+    buf = np.zeros((tokens, frame), np.uint8)
+    for t in range(tokens):
+        at = a if t == 0 else rng.integers(-128, 128, n).astype(np.int8)
+        il, ext = O.interleave(at.view(np.uint8), xsh)
+        buf[t, :n] = il
+        buf[t, 2048:2048 + ext.nbytes] = ext.view(np.uint8)
+    frames = dev(buf)
+    halves = dev(golden[k + "halves"])
+    for binary, packed, tile, one, code in ((False, golden[k + "packed"], "matmul_t2r_tile", "matmul_t2r", 3),
+                                            (True, golden[k + "bpacked"], "matmul_b1r_tile", "matmul_b1r", 2)):
+        w = dev(packed)
+        outs = dev(np.full(tokens * os_ // 4, -7, np.float32))
+        alone = dev(np.zeros(16, np.float32))
+        for count in (1, 3, 4, 7, 11):
+            outs.upload(np.full(tokens * os_ // 4, -7, np.float32))
+            getattr(L, tile)(outs.ptr, frames.ptr, frames.ptr + 2048, w.ptr, halves.ptr, n, 1, 12, count, os_, frame, code)
+            check(tile)
+            got = get(outs, np.float32).reshape(tokens, -1)
+            for t in range(tokens):
+                alone.upload(np.full(16, -7, np.float32))
+                if t < count:
+                    getattr(L, one)(alone.ptr, frames.ptr + t * frame, frames.ptr + t * frame + 2048, w.ptr, halves.ptr,
+                                    n, 1, 12, code)
+                assert np.array_equal(bits(got[t]), bits(get(alone, np.float32))), (tile, count, t)
+
+
+# ---------------------------------------------------------------- model-sized products (size-independent properties)
+
+@pytest.mark.parametrize("K,N", [(4096, 12288), (12288, 4096), (1024, 4608)])
+def test_large_products_against_oracle(K, N):
+    """BASELINE.json's product shapes: every output against the oracle's matmul_q8 within its float32 bound, the
+    group sums of 64 sampled rows to the bit, and the relaxed product's sums against the plain ones' integers."""
+    rng = np.random.default_rng(K + N)
+    from pllm.forward import quantize_rows
+    wq, ws = quantize_rows(rng.normal(0, 0.02, (N, K)).astype(np.float32))
+    x = rng.normal(0, 1, K).astype(np.float32)
+    W, S = dev(wq), dev(ws)
+    out = dev(np.zeros(N, np.float32))
+    for bias in (0, 64):
+        xqh, xsh = O.quantize_x(x, bias)
+        xq, xs = dev(xqh), dev(xsh)
+        if bias:
+            L.matmul_q8r(out.ptr, xq.ptr, xs.ptr, W.ptr, S.ptr, 0, K, 0, N)
+            want = O.matmul_q8r(xqh, xsh, wq, ws)
+        else:
+            L.matmul_q8(out.ptr, xq.ptr, xs.ptr, W.ptr, S.ptr, K, 0, N)
+            want = O.matmul_q8(xqh, xsh, wq, ws)
+        check("large product")
+        got = get(out, np.float32)
+        rows = rng.choice(N, 64, replace=False)
+        G = O.group_sums_q8(xqh, wq[rows], bias)
+        sums = dev(np.zeros(N * (K // 32), np.int32))
+        L.pllm_group_sums(sums.ptr, xq.ptr, xs.ptr, W.ptr, 0, K, 0, N, bias)
+        allG = get(sums, np.int32).reshape(N, K // 32)
+        assert np.array_equal(allG[rows], G)
+        bound = product_bound(allG, ws, xsh)
+        assert np.all(np.abs(got.astype(np.float64) - want) <= bound + 1e-7 * np.abs(want))
+        assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
+
+
+# ---------------------------------------------------------------- attention, rope, halves
+
+@pytest.mark.parametrize("half", [False, True])
+@pytest.mark.parametrize("nh,nkv,hs", [(8, 2, 128), (6, 6, 48), (16, 8, 64), (4, 4, 32)])
+@pytest.mark.parametrize("pos", [0, 3, 130, 700])
+def test_attention(half, nh, nkv, hs, pos):
+    rng = np.random.default_rng(pos * 31 + nh)
+    count = pos + 1
+    q = rng.normal(0, 1, nh * hs).astype(np.float32)
+    kc = rng.normal(0, 1, (count, nkv * hs)).astype(np.float32)
+    vc = rng.normal(0, 1, (count, nkv * hs)).astype(np.float32)
+    if half:
+        kc, _ = O.to_f16(kc)
+        vc, _ = O.to_f16(vc)
+    want, _ = O.attention(q, kc, vc, pos, nh, nkv, hs, half=half)
+    for cap in (0.0, 5.0):
+        if cap:
+            want, _ = O.attention(q, kc, vc, pos, nh, nkv, hs, half=half, cap=cap)
+        out = dev(np.full(nh * hs + 8, -7, np.float32))
+        att = dev(np.zeros(nh * count, np.float32))
+        K, V, Q = dev(kc), dev(vc), dev(q)
+        name = ("attention_f16" if half else "attention") + ("_capped" if cap else "")
+        args = [out.ptr, Q.ptr, K.ptr, V.ptr, att.ptr, pos, nh, nkv, hs, 0, nh] + ([cap] if cap else [])
+        getattr(L, name)(*args)
+        check(name)
+        got = get(out, np.float32)
+        assert np.all(got[nh * hs:] == -7)
+        np.testing.assert_allclose(got[: nh * hs], want, rtol=1e-4, atol=2e-5)
+    # a range of heads writes only those heads
+    out = dev(np.full(nh * hs, -7, np.float32))
+    L.attention_f16(out.ptr, Q.ptr, K.ptr, V.ptr, att.ptr, pos, nh, nkv, hs, 1, nh - 1) if half else \
+        L.attention(out.ptr, Q.ptr, K.ptr, V.ptr, att.ptr, pos, nh, nkv, hs, 1, nh - 1)
+    got = get(out, np.float32).reshape(nh, hs)
+    assert np.all(got[0] == -7) and np.all(got[-1] == -7)
+
+
+def test_rope_and_halves():
+    rng = np.random.default_rng(3)
+    nh, hs = 6, 48
+    v = rng.normal(0, 1, nh * hs).astype(np.float32)
+    c = rng.uniform(-1, 1, hs // 2).astype(np.float32)
+    s = rng.uniform(-1, 1, hs // 2).astype(np.float32)
+    V = dev(v)
+    L.rope(V.ptr, dev(c).ptr, dev(s).ptr, nh, hs, 0)
+    np.testing.assert_allclose(get(V, np.float32), O.rope(v, c, s, nh, hs), rtol=1e-6, atol=1e-6)
+    x = np.concatenate([rng.normal(0, 1, 3000), rng.normal(0, 1e-6, 500), rng.normal(0, 4e4, 500),
+                        [np.inf, -np.inf, np.nan, 65520.0, 2 ** -25, -0.0]]).astype(np.float32)
+    H = dev(np.zeros(x.size, np.uint16))
+    bad = L.to_f16(H.ptr, dev(x).ptr, x.size)
+    want, wbad = O.to_f16(x)
+    assert bad == wbad == 3
+    assert np.array_equal(get(H, np.uint16), want)
+    F = dev(np.zeros(x.size, np.float32))
+    L.from_f16(F.ptr, H.ptr, x.size)
+    assert np.array_equal(bits(get(F, np.float32)), bits(O.from_f16(want)))
+    assert L.finite_f16(H.ptr, x.size) == 0 and L.finite_f16(H.ptr, 3000) == 1
+
+
+# ---------------------------------------------------------------- glue and the stateful layers
+
+def test_glue():
+    rng = np.random.default_rng(11)
+    n = 1000
+    x, w, y = (rng.normal(0, 1, n).astype(np.float32) for _ in range(3))
+    out = dev(np.zeros(n, np.float32))
+    L.rmsnorm(out.ptr, dev(x).ptr, dev(w).ptr, n, 1e-5)
+    np.testing.assert_allclose(get(out, np.float32), O.rmsnorm(x, w, 1e-5), rtol=2e-6, atol=1e-7)
+    L.swiglu(out.ptr, dev(x).ptr, dev(y).ptr, n)
+    np.testing.assert_allclose(get(out, np.float32), O.swiglu(x, y), rtol=2e-6, atol=1e-7)
+    X = dev(x)
+    L.add_inplace(X.ptr, dev(y).ptr, n)
+    assert np.array_equal(get(X, np.float32), O.add_inplace(x, y))
+    L.gate(out.ptr, dev(x).ptr, dev(y).ptr, n)
+    np.testing.assert_allclose(get(out, np.float32), O.gate(x, y), rtol=2e-6, atol=1e-7)
+    taps, rows = rng.normal(0, 1, (4, n)).astype(np.float32), rng.normal(0, 1, (4, n)).astype(np.float32)
+    L.convolve(out.ptr, dev(taps).ptr, dev(rows).ptr, n, 4)
+    np.testing.assert_allclose(get(out, np.float32), O.convolve(taps, rows), rtol=2e-6, atol=1e-7)
+    b = rng.normal(0, 1, 3 * n).astype(np.float32)
+    R = dev(rows[:3])
+    L.short_conv(out.ptr, dev(taps[:3]).ptr, R.ptr, dev(b).ptr, n, 3)
+    want, wrows = O.short_conv(taps[:3], rows[:3], b)
+    assert np.array_equal(get(out, np.float32), want)
+    assert np.array_equal(get(R, np.float32).reshape(3, n), wrows)
+    wf = rng.normal(0, 0.1, (37, n)).astype(np.float32)
+    o = dev(np.zeros(37, np.float32))
+    L.matmul_f32(o.ptr, dev(x).ptr, dev(wf).ptr, n, 0, 37)
+    np.testing.assert_allclose(get(o, np.float32), O.matmul_f32(x, wf), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("kh,vh,kd,vd", [(2, 4, 16, 16), (16, 32, 128, 128), (1, 1, 4, 4)])
+def test_delta_rule_bit_exact(kh, vh, kd, vd):
+    """stateful.ts:96-151: the same float32 operations in the same order, so the same numbers to the bit; the state
+    is read, the new one written at next; a head range writes only its heads."""
+    rng = np.random.default_rng(kd + vh)
+    state = rng.normal(0, 0.5, vh * kd * vd).astype(np.float32)
+    c = rng.normal(0, 0.3, 2 * kh * kd + vh * vd).astype(np.float32)
+    work = np.concatenate([rng.uniform(0.1, 0.9, vh), rng.uniform(0.5, 1.0, vh), np.zeros(vh * vd)]).astype(np.float32)
+    want_out, want_next, want_work = O.delta_rule(state, c, work, kh, kd, vd, vh)
+    out, S, N, C, W = dev(np.zeros(vh * vd, np.float32)), dev(state), dev(np.zeros_like(state)), dev(c), dev(work)
+    L.delta_rule(out.ptr, S.ptr, N.ptr, C.ptr, W.ptr, kh, kd, vd, vh, 0, vh)
+    check("delta_rule")
+    assert np.array_equal(bits(get(out, np.float32)), bits(want_out))
+    assert np.array_equal(bits(get(N, np.float32)), bits(want_next))
+    assert np.array_equal(bits(get(W, np.float32)), bits(want_work))
+    assert np.array_equal(get(S, np.float32), state)
+
+
+# ---------------------------------------------------------------- the contract's refusals
+
+def test_bad_arguments_launch_nothing():
+    out = dev(np.full(4, -7, np.float32))
+    z = dev(np.zeros(64, np.uint8))
+    for call in (lambda: L.matmul_q8(out.ptr, z.ptr, z.ptr, z.ptr, z.ptr, 33, 0, 1),        # n not whole groups
+                 lambda: L.matmul_q8(out.ptr, z.ptr, z.ptr, z.ptr, z.ptr, 32, 2, 1),        # r1 < r0
+                 lambda: L.quantize_x(z.ptr, z.ptr, z.ptr, 32, 7),                          # a bias of neither
+                 lambda: L.matmul_t2(out.ptr, z.ptr, z.ptr, z.ptr, z.ptr, 128, 0, 1, 2),    # a wrong mask
+                 lambda: L.matmul_q8(out.ptr, z.ptr + 4, z.ptr, z.ptr, z.ptr, 32, 0, 1)):   # misaligned
+        call()
+        with pytest.raises(PllmError):
+            check("refused")
+    assert np.all(get(out, np.float32) == -7)
