@@ -69,8 +69,8 @@ class Clocks:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, bus_id=None):
-        self.bus_id = (bus_id or "").lower()
+    def __init__(self, bus=None):
+        self.bus_id = f":{bus:02x}:" if isinstance(bus, int) else ""
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -88,7 +88,7 @@ class Clocks:
         rows = [r.split(", ") for r in open(self.file.name).read().strip().splitlines() if r.count(",") >= 9]
         os.unlink(self.file.name)
         if self.bus_id:
-            mine = [r for r in rows if r[1].lower().endswith(self.bus_id[-12:])]
+            mine = [r for r in rows if self.bus_id in r[1].lower()]
             rows = mine or rows
         if not rows:
             return None
@@ -197,12 +197,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompt", type=int, default=PROMPT)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling only: the same shapes with fewer layers (a small case for ncu captures)")
     args = ap.parse_args()
 
     if args.impl == "reference":
         return run_reference(args, ReferenceShape())
+    from dataclasses import replace
+
     from pllm.forward import QWEN3_8B
-    cfg = QWEN3_8B
+    cfg = replace(QWEN3_8B, layers=args.layers) if args.layers else QWEN3_8B
 
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
@@ -326,7 +330,7 @@ def main():
         "config": {"workload": "qwen3-8b-int8 batch-1 decode at positions 2048+ (BASELINE.json configs[3])",
                    "model": "Qwen3-8B-shaped int8 (36 layers, 4096 hidden, 32/8 heads x 128, QK-norm, 12288 FFN, "
                             "151936 vocab), float16 KV cache", "global_batch": world, "seq_len": prompt,
-                   "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                   "parallelism": f"replicas x{world}" if world > 1 else "1 GPU", "layers": cfg.layers,
                    "l2": "no flush: every step streams 8.51 GB of weights (> 126 MB L2)"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": c.vocab * 4},
         "prefill": {"value": prefill_tps, "unit": "tok/s", "method": "token by token through the decode graph"},

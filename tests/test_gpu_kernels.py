@@ -18,6 +18,9 @@ pytestmark = pytest.mark.gpu
 EPS = 2.0 ** -24
 
 
+_alive = []  # the buffers of the running test: a temporary's memory must outlive the kernels that read it
+
+
 @pytest.fixture(scope="module", autouse=True)
 def device():
     init(0)
@@ -26,8 +29,17 @@ def device():
     L.pllm_device_sync()
 
 
+@pytest.fixture(autouse=True)
+def keep_buffers():
+    yield
+    L.pllm_device_sync()
+    _alive.clear()
+
+
 def dev(a):
-    return Buffer.of(np.ascontiguousarray(a))
+    b = Buffer.of(np.ascontiguousarray(a))
+    _alive.append(b)
+    return b
 
 
 def get(b, dtype, count=None):
@@ -39,9 +51,21 @@ def bits(a):
 
 
 def product_bound(G, ws, xs):
-    """The float32 error bound of sum_g G_g (ws_g xs_g) for each row: (8 groups) 2^-24 sum |terms|."""
-    terms = np.abs(G.astype(np.float64) * ws.astype(np.float64) * xs.astype(np.float64)[None, :])
-    return 8 * G.shape[1] * EPS * terms.sum(axis=1) + 1e-37
+    """The float32 error bound of sum_g G_g (ws_g xs_g) for each row: (8 groups) 2^-24 sum |terms|. G: the group
+    sums (rows, groups), or for matmul_q8 / q6 the four lanes each group is scaled in (rows, groups, 4): the
+    reference rounds each lane's product alone, so its error is of the lanes' size, not of their sum's."""
+    G = G.astype(np.float64)
+    mag = np.abs(G).sum(axis=2) if G.ndim == 3 else np.abs(G)
+    terms = mag * ws.astype(np.float64) * xs.astype(np.float64)[None, :]
+    return 8 * mag.shape[1] * EPS * terms.sum(axis=1) + 1e-37
+
+
+def lanes_q8(acts, w):
+    """matmul.ts:68-72 (dot32): lane k of a group holds products 2k, 2k+1, 2k+8, 2k+9 of each half: (rows, ng, 4)."""
+    rows, n = w.shape
+    p = w.reshape(rows, n // 32, 32).astype(np.int64) * acts.reshape(n // 32, 32).astype(np.int64)
+    idx = [[h + q for h in (0, 16) for q in (2 * k, 2 * k + 1, 2 * k + 8, 2 * k + 9)] for k in range(4)]
+    return np.stack([p[:, :, i].sum(axis=2) for i in idx], axis=2)
 
 
 # ---------------------------------------------------------------- activations
@@ -123,8 +147,12 @@ def test_int8_int6_products(golden, ng):
             xsh = golden[k + "xp"][t] if plain else golden[k + "xr"][t]
             xq, xs = dev(acts), dev(xsh)
             bias = 0 if plain else 64
-            G8 = O.group_sums_q8(acts, w8h, bias)
-            G6 = O.group_sums_q6(acts, w6h, n, bias)
+            if plain:
+                G8 = lanes_q8(acts.view(np.int8), w8h)
+                G6 = lanes_q8(acts.view(np.int8), O.widen6(w6h).reshape(13, n))
+            else:
+                G8 = O.group_sums_q8(acts, w8h, bias)
+                G6 = O.group_sums_q6(acts, w6h, n, bias)
             cases = [("q8", G8, lambda r0, r1: L.matmul_q8(out.ptr, xq.ptr, xs.ptr, w8.ptr, ws.ptr, n, r0, r1)
                       if plain else L.matmul_q8r(out.ptr, xq.ptr, xs.ptr, w8.ptr, ws.ptr, wc8.ptr, n, r0, r1),
                       (golden[k + "q8"] if plain else golden[k + "q8r"])[t]),
