@@ -94,7 +94,7 @@ class Clocks:
             return None
         sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[6 + i]})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": float(rows[0][3]) if rows[0][3].replace(".", "").isdigit() else None,
                 "reasons": reasons, "samples": len(rows)}
@@ -308,6 +308,22 @@ def main():
         ms = timed(lambda: [run() for _ in range(reps)]) / (reps * c.layers)
         gemv[name] = round(rows * cols * 1.125 / (ms / 1000) / 1e9, 1)
 
+    # the attention alone at the last decode position (36 layers' caches, 2 kernels a layer)
+    E = 2 if c.half_kv else 4
+
+    def attention_all():
+        for l in range(c.layers):
+            L.pllm_attention_dev(B["att"].ptr, B["qkv"].ptr, B["kc"].ptr + l * c.seq_len * c.kvdim * E,
+                                 B["vc"].ptr + l * c.seq_len * c.kvdim * E, B["scratch"].ptr, B["tp"].ptr + 4,
+                                 c.seq_len, c.heads, c.kv_heads, c.head_size, int(c.half_kv), 0.0, eng.SPLIT, 0)
+
+    attention_all()
+    att_ms = timed(lambda: [attention_all() for _ in range(reps)]) / (reps * c.layers)
+    last_pos = int(B["tp"].download(np.int32)[1])
+    att_bytes = 2 * (last_pos + 1) * c.kvdim * E
+    attention = {"us_per_layer": round(att_ms * 1000, 2), "position": last_pos,
+                 "gbs": round(att_bytes / (att_ms / 1000) / 1e9, 1)}
+
     each("wqkv", B["wqkv"].ptr, B["sqkv"].ptr, eng.rows_qkv, c.dim, B["x"].ptr, B["att_norm"].ptr, 1, 0)
     each("wo", B["wo"].ptr, B["so"].ptr, c.dim, c.qdim, B["att"].ptr, 0, 2, 1)
     each("w2", B["w2"].ptr, B["s2"].ptr, c.dim, c.hidden, B["hb"].ptr, 0, 2, 1)
@@ -335,6 +351,7 @@ def main():
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": c.vocab * 4},
         "prefill": {"value": prefill_tps, "unit": "tok/s", "method": "token by token through the decode graph"},
         "gemv_gbs": gemv,
+        "attention": attention,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "kernel": "gemv_kernel<int8, 1 token, RMSNorm prologue, SwiGLU epilogue>",
                      "bytes_per_launch": w13_bytes, "traffic": profile_traffic("gemv_q8_w13_qwen3-8b")},

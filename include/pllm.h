@@ -185,6 +185,15 @@ void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint
                         int32_t capacity, int32_t nh, int32_t nkv, int32_t hs, int32_t half, float cap,
                         int32_t split_len, int32_t pdl);
 
+/* a bounded device-side wait (an mbarrier of the bulk-copy product) gave up since the last call: PLLM_ETIMEOUT (3),
+ * else 0; reading it clears it */
+int32_t pllm_device_status(void);
+/* which decode-product kernel: 0 the bulk-copy pipeline where it applies (int8 weights, 1 or 2 tokens), 1 the
+ * register-streaming kernel always; returns the previous mode */
+int32_t pllm_set_gemv_mode(int32_t mode);
+/* the shared-memory bytes the bulk-copy product's ring of stages may take (32 KB..227 KB; default 200 KB) */
+int32_t pllm_set_stage_budget(int32_t bytes);
+
 /* ===== seeded synthetic weights made on the device, for benchmarks and tests of model-sized shapes (no counterpart
  * in the reference, whose tests make synthetic checkpoints in NumPy, tests/made_up.py:30) ===== */
 /* n float32 values N(mean, std) of (seed, index) */

@@ -1,0 +1,324 @@
+// gemv_tma.cu: the decode product as a bulk-copy pipeline (the forward driver's and the registry's int8 products at
+// one or two tokens).
+//
+// One CTA an SM, warp-specialized: a producer warp streams the CTA's rows of weights and their scales from HBM into
+// a ring of shared-memory stages with cp.async.bulk (the TMA's bulk engine; completion counted on an mbarrier per
+// stage, L2 evict-first: each weight byte is read once), and eight consumer warps take a row each of every stage:
+// dp4a of the row's groups of 32 against the activations (shared memory, made by the consumers in the prologue),
+// each group's exact int32 times the product of its two scales, summed in float32, reduced across the warp.
+//
+// The weights do not depend on the kernel ahead of this one in the stream, so the producer starts streaming before
+// the programmatic-dependent-launch wait; only the consumers wait (griddepcontrol.wait) before reading the
+// activations. Every wait on an mbarrier is bounded: past the bound the kernel records PLLM_ETIMEOUT in the device
+// status word and returns (the host reads it with pllm_device_status).
+//
+// A stage holds TR rows x KS columns (KS = K, or K cut into equal chunks of at most 8192): rows whole are one
+// contiguous copy of TR x K bytes (and one of TR x K/32 scales); rows cut into chunks are a copy a row.
+#include "gemv_common.cuh"
+
+__device__ int g_pllm_status = 0;  // a bounded wait gave up (PLLM_ETIMEOUT), read by pllm_device_status
+
+namespace {
+
+using namespace gemvk;
+
+constexpr int NC = 8;                 // consumer warps
+constexpr int TR = NC;                // row slots a stage
+constexpr int TMA_THREADS = (NC + 1) * 32;
+constexpr long long WAIT_BOUND = 1ll << 26;  // polls of an mbarrier before giving up (seconds: never in a run that works)
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// true once the phase of the given parity has completed; false (and the status word set) past the bound
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (long long i = 0; i < WAIT_BOUND; i++) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  atomicExch(&g_pllm_status, PLLM_ETIMEOUT);
+  return false;
+}
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, unsigned bytes, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory"); }
+struct ConsumerSync {
+  __device__ __forceinline__ void operator()() const { consumer_sync(); }
+};
+
+struct TmaPlan {
+  int stages;       // S
+  int ks;           // columns a chunk
+  int chunks;       // K / ks
+  int stage_bytes;  // TR * ks * 1.125, 128-aligned
+  int act_bytes;    // activations and their scales, 128-aligned
+};
+
+// this CTA's rows: [lo, hi) of [r0, r1), near-equal shares
+__device__ __forceinline__ void cta_rows(const GemvArgs& a, long long& lo, long long& hi) {
+  const long long rows = a.r1 - a.r0, G = gridDim.x, c = blockIdx.x;
+  const long long base = rows / G, rem = rows % G;
+  lo = a.r0 + c * base + (c < rem ? c : rem);
+  hi = lo + base + (c < rem ? 1 : 0);
+}
+
+// the rows of a tile: slots [0, n) (EPI_SWIGLU: pairs [0, n) in slots [0, n) and [TR/2, TR/2 + n))
+template <int EPI>
+__device__ __forceinline__ int tile_rows(long long t, long long hi) {
+  const long long per = EPI == EPI_SWIGLU ? TR / 2 : TR;
+  return (int)min(per, hi - t);
+}
+
+template <int MT, int PRO, int EPI>
+__global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs a, const TmaPlan p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int S = p.stages, KS = p.ks, chunks = p.chunks, K = a.K, ng = K / 32;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + S;
+  float* res = reinterpret_cast<float*>(smem + 16 * S);  // [2][TR][MT] row results (EPI_SWIGLU)
+  uint8_t* act = smem + ((16 * S + 2 * TR * MT * 4 + 127) & ~127);
+  int8_t* sq = reinterpret_cast<int8_t*>(act);
+  float* ss = reinterpret_cast<float*>(act + (size_t)MT * K);
+  uint8_t* stage0 = act + p.act_bytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  long long lo, hi;
+  cta_rows(a, lo, hi);
+  const long long per_tile = EPI == EPI_SWIGLU ? TR / 2 : TR;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NC);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == NC) {  // ---- the producer
+    if (lane == 0) {
+      uint64_t policy;
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+      long long it = 0;
+      for (long long t = lo; t < hi; t += per_tile) {
+        const int n = tile_rows<EPI>(t, hi);
+        for (int c = 0; c < chunks; c++, it++) {
+          const int slot = (int)(it % S);
+          const unsigned round = (unsigned)(it / S);
+          if (!mbar_wait(&empty[slot], (round & 1) ^ 1)) return;
+          uint8_t* w = stage0 + (size_t)slot * p.stage_bytes;
+          float* sc = reinterpret_cast<float*>(w + (size_t)TR * KS);
+          const int nrows = EPI == EPI_SWIGLU ? 2 * n : n;
+          mbar_expect_tx(&full[slot], (unsigned)(nrows * (KS + KS / 8)));
+          const int halves = EPI == EPI_SWIGLU ? 2 : 1;
+          for (int h = 0; h < halves; h++) {
+            const long long row0 = t + (h ? a.pair : 0);
+            const int slot0 = h ? TR / 2 : 0;
+            if (chunks == 1) {
+              bulk_copy(w + (size_t)slot0 * KS, a.wq + row0 * K, (unsigned)(n * K), &full[slot], policy);
+              bulk_copy(sc + (size_t)slot0 * (KS / 32), reinterpret_cast<const float*>(a.ws) + row0 * ng,
+                        (unsigned)(n * ng * 4), &full[slot], policy);
+            } else {
+              for (int r = 0; r < n; r++) {
+                bulk_copy(w + (size_t)(slot0 + r) * KS, a.wq + (row0 + r) * K + (long long)c * KS, (unsigned)KS,
+                          &full[slot], policy);
+                bulk_copy(sc + (size_t)(slot0 + r) * (KS / 32),
+                          reinterpret_cast<const float*>(a.ws) + (row0 + r) * ng + (long long)c * (KS / 32),
+                          (unsigned)(KS / 8), &full[slot], policy);
+              }
+            }
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // ---- the consumers
+  pdl_wait();
+  load_activations<F_Q8, MT, PRO, ConsumerSync>(a, sq, ss, nullptr);
+  consumer_sync();
+  pdl_launch_dependents();
+  const int swz = (lane >> 2) & 1;  // which half of its 32 bytes a lane reads first: no bank conflicts
+  long long it = 0;
+  int tiles = 0;
+  for (long long t = lo; t < hi; t += per_tile, tiles++) {
+    const int n = tile_rows<EPI>(t, hi);
+    const bool mine = EPI == EPI_SWIGLU ? ((warp % (TR / 2)) < n) : (warp < n);
+    float acc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; m++) acc[m] = 0.0f;
+    for (int c = 0; c < chunks; c++, it++) {
+      const int slot = (int)(it % S);
+      const unsigned round = (unsigned)(it / S);
+      if (!mbar_wait(&full[slot], round & 1)) return;
+      if (mine) {
+        const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * KS;
+        const float* sc = reinterpret_cast<const float*>(stage0 + (size_t)slot * p.stage_bytes + (size_t)TR * KS) +
+                          (size_t)warp * (KS / 32);
+        const int u0 = c * (KS / 32);
+        for (int u = lane; u < KS / 32; u += 32) {
+          const int4 wa = *reinterpret_cast<const int4*>(w + u * 32 + 16 * swz);
+          const int4 wb = *reinterpret_cast<const int4*>(w + u * 32 + 16 * (swz ^ 1));
+          const uint32_t wv[8] = {(uint32_t)(swz ? wb.x : wa.x), (uint32_t)(swz ? wb.y : wa.y),
+                                  (uint32_t)(swz ? wb.z : wa.z), (uint32_t)(swz ? wb.w : wa.w),
+                                  (uint32_t)(swz ? wa.x : wb.x), (uint32_t)(swz ? wa.y : wb.y),
+                                  (uint32_t)(swz ? wa.z : wb.z), (uint32_t)(swz ? wa.w : wb.w)};
+          const float s = sc[u];
+#pragma unroll
+          for (int m = 0; m < MT; m++) {
+            const int8_t* x = sq + (size_t)m * K + (size_t)(u0 + u) * 32;
+            const int4 xa = *reinterpret_cast<const int4*>(x + 16 * swz);
+            const int4 xb = *reinterpret_cast<const int4*>(x + 16 * (swz ^ 1));
+            const int G = dot32_words(wv, swz ? xb : xa, swz ? xa : xb);
+            acc[m] = fmaf((float)G, __fmul_rn(s, ss[m * ng + u0 + u]), acc[m]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (!mine) {
+      if (EPI == EPI_SWIGLU) consumer_sync();
+      continue;
+    }
+#pragma unroll
+    for (int m = 0; m < MT; m++) acc[m] = warp_sum(acc[m]);
+    if (EPI == EPI_SWIGLU) {
+      float* r = res + (tiles & 1) * TR * MT;
+      if (lane == 0)
+#pragma unroll
+        for (int m = 0; m < MT; m++) r[warp * MT + m] = acc[m];
+      consumer_sync();
+      if (warp < TR / 2 && lane < MT && lane < a.count) {
+        float h1 = r[warp * MT], h3 = r[(warp + TR / 2) * MT];
+#pragma unroll
+        for (int m = 1; m < MT; m++)
+          if (lane == m) {
+            h1 = r[warp * MT + m];
+            h3 = r[(warp + TR / 2) * MT + m];
+          }
+        a.out[lane * a.out_stride + t + warp] = (h1 / (1.0f + expf(-h1))) * h3;
+      }
+    } else if (lane < MT && lane < a.count) {
+      float v = acc[0];
+#pragma unroll
+      for (int m = 1; m < MT; m++)
+        if (lane == m) v = acc[m];
+      float* o = a.out + lane * a.out_stride + t + warp;
+      if (EPI == EPI_ADD) *o += v;
+      else *o = v;
+    }
+  }
+}
+
+template <int MT, int PRO, int EPI>
+bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl) {
+  auto kernel = gemv_tma_kernel<MT, PRO, EPI>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return false;
+  const long long rows = a.r1 - a.r0;
+  const long long per_tile = EPI == EPI_SWIGLU ? TR / 2 : TR;
+  long long grid = pllm_num_sms();
+  const long long tiles = (rows + per_tile - 1) / per_tile;
+  if (grid > tiles) grid = tiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(TMA_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = pllm_stream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a, p);
+  if (e != cudaSuccess) {
+    pllm_fail(PLLM_ECUDA, "gemv_tma launch: %s", cudaGetErrorString(e));
+    return true;  // failed, but not for want of a fit: do not fall back
+  }
+  return true;
+}
+
+}  // namespace
+
+namespace gemvk {
+
+// the stage budget: a stage ring of about this many bytes (a smaller one leaves room on the SM for the next
+// kernel's CTA)
+int g_tma_budget = 200 * 1024;
+// 0: the bulk-copy kernel wherever it applies; 1: the register-streaming kernel only (for comparisons)
+int g_gemv_mode = 0;
+
+// The bulk-copy product for int8 weights at 1 or 2 tokens; false where it does not apply (the caller then takes the
+// register-streaming kernel).
+bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl) {
+  if (g_gemv_mode == 1 || fmt != F_Q8 || a.count < 1 || a.count > 2) return false;
+  const int K = a.K;
+  if (K % 128 || ((uintptr_t)a.wq & 15) || ((uintptr_t)a.ws & 15)) return false;
+  TmaPlan p = {};
+  p.chunks = (K + 8191) / 8192;
+  while (K % (p.chunks * 128)) p.chunks++;
+  p.ks = K / p.chunks;
+  const int MT = a.count;
+  p.stage_bytes = (TR * p.ks + TR * (p.ks / 32) * 4 + 127) & ~127;
+  p.act_bytes = (int)((MT * (size_t)K + MT * (size_t)(K / 32) * 4 + 127) & ~127);
+  const int head = (16 * 8 + 2 * TR * MT * 4 + 127) & ~127;
+  int S = (g_tma_budget - p.act_bytes - head) / p.stage_bytes;
+  if (S > 8) S = 8;
+  if (S < 2) return false;
+  p.stages = S;
+  const size_t smem = (size_t)head + p.act_bytes + (size_t)S * p.stage_bytes;
+  if (smem > 227 * 1024) return false;
+#define CASE(M, P, E) \
+  if (MT == M && pro == P && epi == E) return launch<M, P, E>(a, p, smem, pdl);
+  CASE(1, PRO_Q, EPI_STORE) CASE(1, PRO_Q, EPI_ADD) CASE(1, PRO_Q, EPI_SWIGLU)
+  CASE(1, PRO_RMS, EPI_STORE) CASE(1, PRO_RMS, EPI_ADD) CASE(1, PRO_RMS, EPI_SWIGLU)
+  CASE(1, PRO_QUANT, EPI_STORE) CASE(1, PRO_QUANT, EPI_ADD) CASE(1, PRO_QUANT, EPI_SWIGLU)
+  CASE(2, PRO_Q, EPI_STORE) CASE(2, PRO_RMS, EPI_STORE) CASE(2, PRO_QUANT, EPI_ADD) CASE(2, PRO_RMS, EPI_SWIGLU)
+#undef CASE
+  return false;
+}
+
+}  // namespace gemvk
+
+// a bounded device-side wait gave up since the last call (PLLM_ETIMEOUT), or 0; reading it clears it
+PLLM_API int32_t pllm_device_status() {
+  int v = 0, zero = 0;
+  cudaMemcpyFromSymbol(&v, g_pllm_status, sizeof v);
+  if (v) cudaMemcpyToSymbol(g_pllm_status, &zero, sizeof zero);
+  return v;
+}
+
+// which decode-product kernel: 0 the bulk-copy pipeline where it applies (int8, 1 or 2 tokens), 1 the
+// register-streaming kernel always. Returns the previous mode.
+PLLM_API int32_t pllm_set_gemv_mode(int32_t mode) {
+  const int old = gemvk::g_gemv_mode;
+  if (mode == 0 || mode == 1) gemvk::g_gemv_mode = mode;
+  return old;
+}
+
+// the bytes of shared memory the bulk-copy product's stage ring may take (default 200 KB); a smaller ring leaves
+// room on each SM for the next kernel's CTA to start streaming early. Returns the previous value.
+PLLM_API int32_t pllm_set_stage_budget(int32_t bytes) {
+  const int old = gemvk::g_tma_budget;
+  if (bytes >= 32 * 1024 && bytes <= 227 * 1024) gemvk::g_tma_budget = bytes;
+  return old;
+}

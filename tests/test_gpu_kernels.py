@@ -272,14 +272,16 @@ def test_signs_tiles_equal_token_kernel(golden):
 
 # ---------------------------------------------------------------- model-sized products (size-independent properties)
 
+@pytest.mark.parametrize("mode", [0, 1], ids=["bulk-copy", "register"])
 @pytest.mark.parametrize("K,N", [(4096, 12288), (12288, 4096), (1024, 4608)])
-def test_large_products_against_oracle(K, N):
+def test_large_products_against_oracle(K, N, mode):
     """BASELINE.json's product shapes: every output against the oracle's matmul_q8 within its float32 bound, the
     group sums of 64 sampled rows to the bit, and the relaxed product's sums against the plain ones' integers."""
     rng = np.random.default_rng(K + N)
     from pllm.forward import quantize_rows
     wq, ws = quantize_rows(rng.normal(0, 0.02, (N, K)).astype(np.float32))
     x = rng.normal(0, 1, K).astype(np.float32)
+    old = L.pllm_set_gemv_mode(mode)
     W, S = dev(wq), dev(ws)
     out = dev(np.zeros(N, np.float32))
     for bias in (0, 64):
@@ -302,6 +304,7 @@ def test_large_products_against_oracle(K, N):
         bound = product_bound(allG, ws, xsh)
         assert np.all(np.abs(got.astype(np.float64) - want) <= bound + 1e-7 * np.abs(want))
         assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
+    L.pllm_set_gemv_mode(old)
 
 
 # ---------------------------------------------------------------- attention, rope, halves
@@ -425,3 +428,78 @@ def test_bad_arguments_launch_nothing():
         with pytest.raises(PllmError):
             check("refused")
     assert np.all(get(out, np.float32) == -7)
+
+
+# ---------------------------------------------------------------- the forward driver's fused products, both kernels
+
+@pytest.fixture(params=[0, 1], ids=["bulk-copy", "register"])
+def gemv_mode(request):
+    old = L.pllm_set_gemv_mode(request.param)
+    yield request.param
+    L.pllm_set_gemv_mode(old)
+
+
+@pytest.mark.parametrize("K,N", [(4096, 1000), (12288, 520), (384, 77)])
+@pytest.mark.parametrize("pro", [1, 2])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+@pytest.mark.parametrize("relaxed", [False, True])
+def test_fused_gemv(gemv_mode, K, N, pro, epi, relaxed):
+    """pllm_gemv's prologues (RMSNorm + quantize_x, quantize_x) and epilogues (store, residual add, SwiGLU of a row
+    pair) against the oracle's rmsnorm, quantize_x and matmul_q8 / q8r on the same numbers. The input is small
+    integers, so that its sum of squares is exact in any order and the quantized activations are the oracle's to the
+    byte; every group's integer is then exact and the outputs agree within float32 rounding."""
+    rng = np.random.default_rng(K + N + pro + 3 * epi)
+    from pllm.forward import quantize_rows
+    rows = 2 * N if epi == 2 else N
+    wq, ws = quantize_rows(rng.normal(0, 0.02, (rows, K)).astype(np.float32))
+    tokens = 2 if (N == 520 and epi != 1) else 1
+    x = rng.integers(-8, 9, (tokens, K)).astype(np.float32)
+    norm = rng.normal(1, 0.1, K).astype(np.float32)
+    eps, bias = 1e-6, (64 if relaxed else 0)
+    init = rng.normal(0, 1, (tokens, N)).astype(np.float32)
+    W, S, X, NW = dev(wq), dev(ws), dev(x), dev(norm)
+    out = dev(init)
+    L.pllm_gemv(out.ptr, N, 0, 0, 0, 0, X.ptr, K, NW.ptr if pro == 1 else 0, eps, bias, W.ptr, S.ptr, 0, K, 0, N,
+                tokens, pro, epi, N if epi == 2 else 0, 0)
+    check("pllm_gemv")
+    got = get(out, np.float32).reshape(tokens, N)
+    for t in range(tokens):
+        xb = O.rmsnorm(x[t], norm, eps) if pro == 1 else x[t]
+        xq, xs = O.quantize_x(xb, bias)
+        prod = (O.matmul_q8r(xq, xs, wq, ws) if relaxed else O.matmul_q8(xq, xs, wq, ws)).astype(np.float64)
+        G = O.group_sums_q8(xq, wq, bias)
+        bound = product_bound(G, ws, xs)
+        if epi == 0:
+            assert np.all(np.abs(got[t] - prod) <= bound), (t, np.abs(got[t] - prod).max())
+        elif epi == 1:
+            want = init[t].astype(np.float64) + prod
+            assert np.all(np.abs(got[t] - want) <= bound + 2 * EPS * np.abs(want))
+        else:
+            h1, h3 = prod[:N], prod[N:]
+            want = h1 / (1 + np.exp(-h1)) * h3
+            slack = (np.abs(h3) * bound[:N] + np.abs(h1) * bound[N:]) * 2 + 1e-6 * np.abs(want) + 1e-12
+            assert np.all(np.abs(got[t] - want) <= slack), (t, np.abs(got[t] - want).max())
+    assert L.pllm_device_status() == 0
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_registry_products_both_kernels(golden, mode):
+    """matmul_q8 / q8r through the bulk-copy kernel and the register one give the same numbers as each other within
+    float32 rounding, and the same as before on int8-check.ts's cases of 81 groups."""
+    old = L.pllm_set_gemv_mode(mode)
+    try:
+        k = "int8_ng81_"
+        n = 81 * 32
+        w8h, wsh = golden[k + "w8"], golden[k + "ws"]
+        # 81 groups is no multiple of 128 columns: the register kernel serves it in both modes
+        w8, ws = dev(w8h), dev(wsh)
+        out = dev(np.zeros(13, np.float32))
+        for t in range(9):
+            xq, xs = dev(golden[k + "qr"][t]), dev(golden[k + "xr"][t])
+            L.matmul_q8r(out.ptr, xq.ptr, xs.ptr, w8.ptr, ws.ptr, 0, n, 0, 13)
+            check("matmul_q8r")
+            G = O.group_sums_q8(golden[k + "qr"][t], w8h, 64)
+            bound = product_bound(G, wsh.reshape(13, 81), golden[k + "xr"][t])
+            assert np.all(np.abs(get(out, np.float32) - golden[k + "q8r"][t]) <= bound)
+    finally:
+        L.pllm_set_gemv_mode(old)
