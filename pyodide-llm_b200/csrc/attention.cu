@@ -33,18 +33,31 @@ struct AttArgs {
   float cap;
 };
 
+
+// grid (nkv, nsplit): one kv head's slice of positions for its KVM query heads. The slice is taken TILE positions at
+// a time: every thread first issues its 16-byte loads of the tile's keys and values (all of them in flight at once),
+// into shared memory (rows padded by 16 bytes: conflict-free 16-byte reads of a row by consecutive threads), then the
+// scores (a thread a position and head pair), an online softmax of the slice (running max and sum, the partial
+// output rescaled), and the weighted values (a thread a head dimension).
+constexpr int TILE = 64;
+
 template <bool HALF>
-__device__ __forceinline__ float kv_load(const void* base, long long i) {
-  if (HALF) return half_bits_to_float(reinterpret_cast<const uint16_t*>(base)[i]);
-  return reinterpret_cast<const float*>(base)[i];
+__device__ __forceinline__ float kv_elem(const uint8_t* row, int d) {
+  if (HALF) return half_bits_to_float(reinterpret_cast<const uint16_t*>(row)[d]);
+  return reinterpret_cast<const float*>(row)[d];
 }
 
-// grid (nkv, nsplit); KVM: query heads a kv head; DPL: head dims a lane (hs <= 32 DPL)
-template <bool HALF, int KVM, int DPL>
+template <bool HALF, int KVM>
 __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttArgs a) {
-  extern __shared__ float sS[];  // [KVM][split_len] scores, then probabilities
-  __shared__ float sO[ATT_WARPS][KVM][DPL * 32];
-  __shared__ float sML[KVM][2];
+  extern __shared__ __align__(16) uint8_t att_smem[];
+  constexpr int E = HALF ? 2 : 4;
+  const int hs = a.hs;
+  const int rowb = hs * E + 16;                      // a padded row of the tile, bytes
+  uint8_t* sK = att_smem;                            // [TILE][rowb]
+  uint8_t* sV = sK + TILE * rowb;                    // [TILE][rowb]
+  float* sq = reinterpret_cast<float*>(sV + TILE * rowb);  // [KVM][hs]
+  float* sp = sq + KVM * hs;                         // [KVM][TILE] scores, then probabilities
+  __shared__ float sM[KVM], sL[KVM], sScale[KVM];
   pdl_wait();
   const int pos = a.pos_dev ? *a.pos_dev : a.pos;
   const int count = pos + 1;
@@ -53,99 +66,133 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   if (split >= nsplit) return;
   const int p0 = split * a.split_len;
   const int p1 = min(count, p0 + a.split_len);
-  const int len = p1 - p0;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int hs = a.hs, kvdim = a.nkv * hs;
-  const int hbase = kvh * KVM;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kvdim = a.nkv * hs, hbase = kvh * KVM;
   const float isq = 1.0f / sqrtf((float)hs);
-  // this CTA's query heads in registers: head hbase + j, dims lane + 32 i
-  float qv[KVM][DPL];
+  for (int e = tid; e < KVM * hs; e += ATT_THREADS) sq[e] = a.q[(long long)hbase * hs + e];
+  if (tid < KVM) {
+    sM[tid] = -INFINITY;
+    sL[tid] = 0.0f;
+  }
+  // the running output: this thread's dims d = tid + ATT_THREADS i of every head
+  constexpr int DMAX = 2;  // hs <= 256
+  float acc[KVM][DMAX];
 #pragma unroll
   for (int j = 0; j < KVM; j++)
 #pragma unroll
-    for (int i = 0; i < DPL; i++) {
-      const int d = lane + 32 * i;
-      qv[j][i] = d < hs ? a.q[(long long)(hbase + j) * hs + d] : 0.0f;
-    }
-  // 1. scores
-  for (int t = warp; t < len; t += ATT_WARPS) {
-    const long long row = (long long)(p0 + t) * kvdim + (long long)kvh * hs;
-    float kv[DPL];
+    for (int i = 0; i < DMAX; i++) acc[j][i] = 0.0f;
+  const int chunks = hs * E / 16;                    // 16-byte pieces a row
+  const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.kc) + (long long)kvh * hs * E;
+  const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vc) + (long long)kvh * hs * E;
+  for (int t0 = p0; t0 < p1; t0 += TILE) {
+    const int len = min(TILE, p1 - t0);
+    __syncthreads();  // the previous tile's keys, values and probabilities are no longer read
+    // 1. the tile's keys and values: every load issued before any is used
+    constexpr int PER = 8;
+    for (int base = tid; base < len * chunks; base += ATT_THREADS * PER) {
+      int4 kv[PER], vv[PER];
 #pragma unroll
-    for (int i = 0; i < DPL; i++) {
-      const int d = lane + 32 * i;
-      kv[i] = d < hs ? kv_load<HALF>(a.kc, row + d) : 0.0f;
+      for (int u = 0; u < PER; u++) {
+        const int e = base + u * ATT_THREADS;
+        if (e < len * chunks) {
+          const int t = e / chunks, c = e % chunks;
+          const long long off = (long long)(t0 + t) * kvdim * E + c * 16;
+          kv[u] = __ldg(reinterpret_cast<const int4*>(kbase + off));
+          vv[u] = __ldg(reinterpret_cast<const int4*>(vbase + off));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < PER; u++) {
+        const int e = base + u * ATT_THREADS;
+        if (e < len * chunks) {
+          const int t = e / chunks, c = e % chunks;
+          *reinterpret_cast<int4*>(sK + t * rowb + c * 16) = kv[u];
+          *reinterpret_cast<int4*>(sV + t * rowb + c * 16) = vv[u];
+        }
+      }
     }
+    __syncthreads();
+    // 2. scores: a thread a (position, head) pair
+    for (int e = tid; e < KVM * TILE; e += ATT_THREADS) {
+      const int t = e % TILE, j = e / TILE;
+      float s = -INFINITY;
+      if (t < len) {
+        const uint8_t* row = sK + t * rowb;
+        const float* qj = sq + j * hs;
+        s = 0.0f;
+        for (int c = 0; c < chunks; c++) {  // 16 bytes of the row at a time: conflict-free across the threads' rows
+          const int4 w = *reinterpret_cast<const int4*>(row + c * 16);
+          const uint32_t u[4] = {(uint32_t)w.x, (uint32_t)w.y, (uint32_t)w.z, (uint32_t)w.w};
+          if (HALF) {
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+              s = fmaf(qj[c * 8 + 2 * k], half_bits_to_float((uint16_t)(u[k] & 0xffffu)), s);
+              s = fmaf(qj[c * 8 + 2 * k + 1], half_bits_to_float((uint16_t)(u[k] >> 16)), s);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; k++) s = fmaf(qj[c * 4 + k], __uint_as_float(u[k]), s);
+          }
+        }
+        s *= isq;
+        if (a.cap > 0.0f) s = a.cap * tanhf(s / a.cap);
+      }
+      sp[j * TILE + t] = s;
+    }
+    __syncthreads();
+    // 3. the online softmax: a warp a head
+    for (int j = warp; j < KVM; j += ATT_WARPS) {
+      float m = -INFINITY;
+      for (int t = lane; t < len; t += 32) m = fmaxf(m, sp[j * TILE + t]);
+      m = warp_max(m);
+      const float mnew = fmaxf(sM[j], m);
+      float l = 0.0f;
+      for (int t = lane; t < TILE; t += 32) {
+        const float p = t < len ? expf(sp[j * TILE + t] - mnew) : 0.0f;
+        sp[j * TILE + t] = p;
+        l += p;
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        const float scale = expf(sM[j] - mnew);  // 0 at the first tile (exp(-inf))
+        sScale[j] = scale;
+        sL[j] = sL[j] * scale + l;
+        sM[j] = mnew;
+      }
+    }
+    __syncthreads();
+    // 4. the weighted values: a thread a dimension
+#pragma unroll
+    for (int i = 0; i < DMAX; i++) {
+      const int d = tid + ATT_THREADS * i;
+      if (d >= hs) continue;
+#pragma unroll
+      for (int j = 0; j < KVM; j++) acc[j][i] *= sScale[j];
+      for (int t = 0; t < len; t++) {
+        const float v = kv_elem<HALF>(sV + t * rowb, d);
+#pragma unroll
+        for (int j = 0; j < KVM; j++) acc[j][i] = fmaf(sp[j * TILE + t], v, acc[j][i]);
+      }
+    }
+  }
+  // 5. the slice's output (one slice: the head's output itself)
+#pragma unroll
+  for (int i = 0; i < DMAX; i++) {
+    const int d = tid + ATT_THREADS * i;
+    if (d >= hs) continue;
 #pragma unroll
     for (int j = 0; j < KVM; j++) {
-      float s = 0.0f;
-#pragma unroll
-      for (int i = 0; i < DPL; i++) s = fmaf(qv[j][i], kv[i], s);
-      s = warp_sum(s) * isq;
-      if (a.cap > 0.0f) s = a.cap * tanhf(s / a.cap);
-      if (lane == 0) sS[j * a.split_len + t] = s;
-    }
-  }
-  __syncthreads();
-  // 2. the slice's softmax: its max and the sum of exp(s - max), a warp a head
-  for (int j = warp; j < KVM; j += ATT_WARPS) {
-    float m = -INFINITY;
-    for (int t = lane; t < len; t += 32) m = fmaxf(m, sS[j * a.split_len + t]);
-    m = warp_max(m);
-    float l = 0.0f;
-    for (int t = lane; t < len; t += 32) {
-      const float e = expf(sS[j * a.split_len + t] - m);
-      sS[j * a.split_len + t] = e;
-      l += e;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      sML[j][0] = m;
-      sML[j][1] = l;
-    }
-  }
-  __syncthreads();
-  // 3. the weighted values
-  float acc[KVM][DPL];
-#pragma unroll
-  for (int j = 0; j < KVM; j++)
-#pragma unroll
-    for (int i = 0; i < DPL; i++) acc[j][i] = 0.0f;
-  for (int t = warp; t < len; t += ATT_WARPS) {
-    const long long row = (long long)(p0 + t) * kvdim + (long long)kvh * hs;
-    float vv[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; i++) {
-      const int d = lane + 32 * i;
-      vv[i] = d < hs ? kv_load<HALF>(a.vc, row + d) : 0.0f;
-    }
-#pragma unroll
-    for (int j = 0; j < KVM; j++) {
-      const float p = sS[j * a.split_len + t];
-#pragma unroll
-      for (int i = 0; i < DPL; i++) acc[j][i] = fmaf(p, vv[i], acc[j][i]);
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < KVM; j++)
-#pragma unroll
-    for (int i = 0; i < DPL; i++) sO[warp][j][lane + 32 * i] = acc[j][i];
-  __syncthreads();
-  for (int e = threadIdx.x; e < KVM * hs; e += ATT_THREADS) {
-    const int j = e / hs, d = e % hs;
-    const int h = hbase + j;
-    if (h < a.h0 || h >= a.h1) continue;
-    float o = 0.0f;
-#pragma unroll
-    for (int w = 0; w < ATT_WARPS; w++) o += sO[w][j][d];
-    if (nsplit == 1) {
-      a.out[(long long)h * hs + d] = o / sML[j][1];
-    } else {
-      float* part = a.part + ((long long)h * a.nsplit + split) * (hs + 2);
-      part[d] = o;
-      if (d == 0) {
-        part[hs] = sML[j][0];
-        part[hs + 1] = sML[j][1];
+      const int h = hbase + j;
+      if (h < a.h0 || h >= a.h1) continue;
+      if (nsplit == 1) {
+        a.out[(long long)h * hs + d] = acc[j][i] / sL[j];
+      } else {
+        float* part = a.part + ((long long)h * a.nsplit + split) * (hs + 2);
+        part[d] = acc[j][i];
+        if (d == 0) {
+          part[hs] = sM[j];
+          part[hs + 1] = sL[j];
+        }
       }
     }
   }
@@ -174,7 +221,7 @@ __global__ void attention_combine_kernel(const AttArgs a) {
 }
 
 template <bool HALF, int KVM>
-cudaError_t launch_split_kvm(const AttArgs& a, int dpl, size_t smem, dim3 grid, bool pdl) {
+cudaError_t launch_split_kvm(const AttArgs& a, size_t smem, dim3 grid, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(ATT_THREADS);
@@ -185,39 +232,28 @@ cudaError_t launch_split_kvm(const AttArgs& a, int dpl, size_t smem, dim3 grid, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-#define DPL_CASE(D)                                                                                       \
-  case D: {                                                                                               \
-    auto k = attention_split_kernel<HALF, KVM, D>;                                                        \
-    if (smem > 8 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);  \
-    return cudaLaunchKernelEx(&cfg, k, a);                                                                \
-  }
-  switch (dpl) {
-    DPL_CASE(1)
-    DPL_CASE(2)
-    DPL_CASE(4)
-    DPL_CASE(8)
-    default: return cudaErrorInvalidValue;
-  }
-#undef DPL_CASE
+auto k = attention_split_kernel<HALF, KVM>;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  return cudaLaunchKernelEx(&cfg, k, a);
 }
 
 template <bool HALF>
-cudaError_t launch_split(const AttArgs& a, int kvm, int dpl, size_t smem, dim3 grid, bool pdl) {
+cudaError_t launch_split(const AttArgs& a, int kvm, size_t smem, dim3 grid, bool pdl) {
   switch (kvm) {
-    case 1: return launch_split_kvm<HALF, 1>(a, dpl, smem, grid, pdl);
-    case 2: return launch_split_kvm<HALF, 2>(a, dpl, smem, grid, pdl);
-    case 4: return launch_split_kvm<HALF, 4>(a, dpl, smem, grid, pdl);
-    case 8: return launch_split_kvm<HALF, 8>(a, dpl, smem, grid, pdl);
+    case 1: return launch_split_kvm<HALF, 1>(a, smem, grid, pdl);
+    case 2: return launch_split_kvm<HALF, 2>(a, smem, grid, pdl);
+    case 4: return launch_split_kvm<HALF, 4>(a, smem, grid, pdl);
+    case 8: return launch_split_kvm<HALF, 8>(a, smem, grid, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
 
 void run_attention(const char* name, AttArgs a, bool half, bool pdl) {
   const int kvm = a.nh / a.nkv;
-  const int dpl = a.hs <= 32 ? 1 : a.hs <= 64 ? 2 : a.hs <= 128 ? 4 : 8;
-  const size_t smem = (size_t)kvm * a.split_len * sizeof(float);
+  const size_t rowb = (size_t)a.hs * (half ? 2 : 4) + 16;
+  const size_t smem = 2 * TILE * rowb + (size_t)kvm * a.hs * 4 + (size_t)kvm * TILE * 4;
   const dim3 grid(a.nkv, a.nsplit);
-  cudaError_t e = half ? launch_split<true>(a, kvm, dpl, smem, grid, pdl) : launch_split<false>(a, kvm, dpl, smem, grid, pdl);
+  cudaError_t e = half ? launch_split<true>(a, kvm, smem, grid, pdl) : launch_split<false>(a, kvm, smem, grid, pdl);
   if (e != cudaSuccess) {
     pllm_fail(PLLM_ECUDA, "%s: launch failed: %s", name, cudaGetErrorString(e));
     return;
@@ -238,7 +274,7 @@ void run_attention(const char* name, AttArgs a, bool half, bool pdl) {
 }
 
 bool check_heads(const char* name, int nh, int nkv, int hs, int h0, int h1) {
-  if (nh <= 0 || nkv <= 0 || nh % nkv || hs <= 0 || hs > 256 || h0 < 0 || h1 < h0 || h1 > nh) {
+  if (nh <= 0 || nkv <= 0 || nh % nkv || hs <= 0 || hs > 256 || hs % 8 || h0 < 0 || h1 < h0 || h1 > nh) {
     pllm_fail(PLLM_EINVAL, "%s: nh %d nkv %d hs %d heads %d..%d", name, nh, nkv, hs, h0, h1);
     return false;
   }
@@ -256,6 +292,7 @@ void registry_attention(const char* name, uint64_t out, uint64_t q, uint64_t kc,
                         int nh, int nkv, int hs, int h0, int h1, float cap, bool half) {
   if (!check_heads(name, nh, nkv, hs, h0, h1)) return;
   PLLM_REQUIRE(pos >= 0, "%s: pos %d", name, pos);
+  PLLM_REQUIRE(!(kc & 15) && !(vc & 15), "%s: the cache must be 16-byte aligned", name);
   if (h1 == h0) return;
   const int count = pos + 1;
   int nsplit = (count + 127) / 128;

@@ -288,6 +288,17 @@ class Engine:
         if not self.graph:
             raise RuntimeError("graph capture failed")
 
+    def graph_of(self, enqueue):
+        """A CUDA graph of what enqueue() launches (on the engine's stream), for timing kernels without the host's
+        launch costs; release it with lib.L.pllm_graph_destroy."""
+        L.pllm_set_stream(self.stream)
+        if L.pllm_graph_begin() != 0:
+            check("graph begin")
+        enqueue()
+        g = L.pllm_graph_end()
+        check("graph capture")
+        return g
+
     def launch_step(self):
         """Enqueue one step for the token and position already in device memory (no copies, no wait)."""
         L.pllm_set_stream(self.stream)
