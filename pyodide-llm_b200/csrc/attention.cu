@@ -31,6 +31,7 @@ struct AttArgs {
   int split_len;        // positions a slice
   int nsplit;           // slices (the grid's y); with pos_dev, those past the position return
   float cap;
+  int* counters;        // [nkv] slices done, zero between calls; null: a second kernel combines the slices
 };
 
 
@@ -196,6 +197,31 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
       }
     }
   }
+  if (nsplit == 1 || !a.counters) return;
+  // 6. the last slice of this kv head to finish combines every slice's partials (no CTA waits for another: the
+  // others are done when the count reaches nsplit), and sets the count back to zero for the next call
+  __shared__ int last;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(&a.counters[kvh], 1) == nsplit - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int e = tid; e < KVM * hs; e += ATT_THREADS) {
+    const int j = e / hs, d = e % hs, h = hbase + j;
+    if (h < a.h0 || h >= a.h1) continue;
+    const float* part = a.part + (long long)h * a.nsplit * (hs + 2);
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < nsplit; s2++) M = fmaxf(M, __ldcg(part + s2 * (hs + 2) + hs));
+    float L = 0.0f, o = 0.0f;
+    for (int s2 = 0; s2 < nsplit; s2++) {
+      const float w = expf(__ldcg(part + s2 * (hs + 2) + hs) - M);
+      L = fmaf(__ldcg(part + s2 * (hs + 2) + hs + 1), w, L);
+      o = fmaf(__ldcg(part + s2 * (hs + 2) + d), w, o);
+    }
+    a.out[(long long)h * hs + d] = o / L;
+  }
+  if (tid == 0) a.counters[kvh] = 0;
 }
 
 // a block a head: the slices' partials combined
@@ -258,7 +284,7 @@ void run_attention(const char* name, AttArgs a, bool half, bool pdl) {
     pllm_fail(PLLM_ECUDA, "%s: launch failed: %s", name, cudaGetErrorString(e));
     return;
   }
-  if (a.nsplit > 1 || a.pos_dev) {
+  if ((a.nsplit > 1 || a.pos_dev) && !a.counters) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.h1 - a.h0);
     cfg.blockDim = dim3(a.hs >= 128 ? 128 : 64);
@@ -423,10 +449,14 @@ PLLM_API void attention_f16_capped(uint64_t out, uint64_t q, uint64_t kc, uint64
 
 // ---- the forward driver's calls (the position in device memory)
 
-// bytes of scratch pllm_attention_dev needs for a cache of capacity positions
-PLLM_API uint64_t pllm_attention_scratch_bytes(int32_t nh, int32_t hs, int32_t capacity, int32_t split_len) {
+// bytes of scratch pllm_attention_dev needs for a cache of capacity positions: the slices' partials, then a count a
+// kv head (the scratch must be zero when first used; every call leaves the counts at zero)
+static uint64_t partial_bytes(int nh, int hs, int capacity, int split_len) {
   const long long nsplit = (capacity + split_len - 1) / split_len;
-  return (uint64_t)nh * nsplit * (hs + 2) * sizeof(float);
+  return ((uint64_t)nh * nsplit * (hs + 2) * sizeof(float) + 255) & ~255ull;
+}
+PLLM_API uint64_t pllm_attention_scratch_bytes(int32_t nh, int32_t hs, int32_t capacity, int32_t split_len) {
+  return partial_bytes(nh, hs, capacity, split_len) + (uint64_t)nh * sizeof(int);
 }
 
 PLLM_API void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t scratch, uint64_t pos_dev,
@@ -450,6 +480,7 @@ PLLM_API void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t
   a.split_len = split_len;
   a.nsplit = (capacity + split_len - 1) / split_len;
   a.cap = cap;
+  a.counters = dptr<int>(scratch + partial_bytes(nh, hs, capacity, split_len));
   run_attention("pllm_attention_dev", a, half != 0, pdl != 0);
 }
 

@@ -243,8 +243,13 @@ void launch_fmt(int fmt, const GemvArgs& a, bool pdl) {
   switch (fmt) {
     case F_Q8: launch_tokens<F_Q8, PRO, EPI>(a, pdl); break;
     case F_Q6: launch_tokens<F_Q6, PRO, EPI>(a, pdl); break;
-    case F_T2: launch_tokens<F_T2, PRO, EPI>(a, pdl); break;
-    default: launch_tokens<F_B1, PRO, EPI>(a, pdl); break;
+    default:
+      // ternary and binary take interleaved activations, made by the caller (pllm_gemv refuses the others)
+      if constexpr (PRO == PRO_Q) {
+        if (fmt == F_T2) launch_tokens<F_T2, PRO, EPI>(a, pdl);
+        else launch_tokens<F_B1, PRO, EPI>(a, pdl);
+      }
+      break;
   }
 }
 

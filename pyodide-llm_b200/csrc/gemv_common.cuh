@@ -45,6 +45,58 @@ __host__ __device__ constexpr size_t smem_bytes(int K, int MT) {
 
 // The activations of MT tokens into shared memory, signed. PRO_Q copies the caller's (taking the bias of relaxed
 // activations off); PRO_RMS / PRO_QUANT make them here from float32: RMSNorm (optional), then quantize_x's steps.
+// One group of 32 held by a pair of threads (h: the lower or upper 16 values, as float4 x 4): RMSNorm's scaling
+// (PRO_RMS: w * (rs * x), activations.ts:19), quantize.ts:8-19's largest |x| a SIMD lane (value j in lane j % 4;
+// a NaN makes its lane NaN) and the lanes compared in order, then quantize_x's steps; the 16 signed bytes into sq and
+// the scale into ss. g past the groups: the pair computes on zeros and stores nothing (every thread of the warp
+// takes the shuffle).
+template <int PRO>
+__device__ __forceinline__ void quantize_pair(const GemvArgs& a, const float4* xv, const float4* wv, float rs, int g,
+                                              int h, int t, int8_t* sq, float* ss) {
+  const int K = a.K, ng = K / 32;
+  float u[16];
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    u[4 * k] = xv[k].x;
+    u[4 * k + 1] = xv[k].y;
+    u[4 * k + 2] = xv[k].z;
+    u[4 * k + 3] = xv[k].w;
+    if (PRO == PRO_RMS) {
+      u[4 * k] = wv[k].x * (rs * u[4 * k]);
+      u[4 * k + 1] = wv[k].y * (rs * u[4 * k + 1]);
+      u[4 * k + 2] = wv[k].z * (rs * u[4 * k + 2]);
+      u[4 * k + 3] = wv[k].w * (rs * u[4 * k + 3]);
+    }
+  }
+  float m[4];
+#pragma unroll
+  for (int l = 0; l < 4; l++)
+    m[l] = wasm_max(wasm_max(fabsf(u[l]), fabsf(u[l + 4])), wasm_max(fabsf(u[l + 8]), fabsf(u[l + 12])));
+#pragma unroll
+  for (int l = 0; l < 4; l++) m[l] = wasm_max(m[l], __shfl_xor_sync(0xffffffffu, m[l], 1));
+  float amax = m[0];
+  if (m[1] > amax) amax = m[1];
+  if (m[2] > amax) amax = m[2];
+  if (m[3] > amax) amax = m[3];
+  const float scale = __fdiv_rn(amax, a.bias == 0 ? 127.0f : 63.0f);
+  const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+  if (g >= ng) return;
+  uint32_t packed[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+      const int8_t q = (int8_t)(quantize_one(u[4 * k + b], inv, a.bias) - (int8_t)a.bias);  // signed
+      word |= (uint32_t)(uint8_t)q << (8 * b);
+    }
+    packed[k] = word;
+  }
+  *reinterpret_cast<int4*>(sq + (size_t)t * K + 32 * g + 16 * h) =
+      make_int4((int)packed[0], (int)packed[1], (int)packed[2], (int)packed[3]);
+  if (h == 0) ss[t * ng + g] = scale;
+}
+
 // The activations of MT tokens into shared memory by THREADS threads (the whole CTA, or the consumer warps of a
 // warp-specialized one: SYNC is their barrier).
 struct CtaSync {
@@ -79,30 +131,65 @@ __device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, 
       }
     }
   } else {
+    // A pair of threads a group of 32 (the lower thread its values 0..15, the upper 16..31), the groups taken 128 at a
+    // time: every float32 load of a token (and of the norm's weights) issued before any is used, held in registers.
     __shared__ float red[WARPS];
+    constexpr int RMAX = 3;  // rounds of 128 groups held in registers (K <= 12288); past them read again
+    const int pair = threadIdx.x >> 1, h = threadIdx.x & 1;
+    const int rounds = (ng + 127) / 128;
     for (int t = 0; t < MT; t++) {
       if (t >= a.count) break;
-      const float* x = a.x + t * a.x_stride;
+      const float4* x4 = reinterpret_cast<const float4*>(a.x + t * a.x_stride);
+      const float4* n4 = reinterpret_cast<const float4*>(a.norm);
+      float4 v[RMAX][4], w[RMAX][4];
+#pragma unroll
+      for (int r = 0; r < RMAX; r++) {
+        const int g = pair + 128 * r;
+        const bool in = r < rounds && g < ng;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          v[r][k] = in ? x4[(32 * g + 16 * h) / 4 + k] : make_float4(0.f, 0.f, 0.f, 0.f);
+          w[r][k] = (PRO == PRO_RMS && in) ? __ldg(n4 + (32 * g + 16 * h) / 4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
       float rs = 1.0f;
       if (PRO == PRO_RMS) {
         float s = 0.0f;
-        for (int i = threadIdx.x; i < K; i += THREADS) s = fmaf(x[i], x[i], s);
+#pragma unroll
+        for (int r = 0; r < RMAX; r++) {
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+              s = fmaf(v[r][k].x, v[r][k].x, fmaf(v[r][k].y, v[r][k].y, fmaf(v[r][k].z, v[r][k].z, fmaf(v[r][k].w, v[r][k].w, s))));
+        }
+        for (int r = RMAX; r < rounds; r++) {
+          const int g = pair + 128 * r;
+          if (g < ng)
+            for (int k = 0; k < 4; k++) {
+              const float4 u = x4[(32 * g + 16 * h) / 4 + k];
+              s = fmaf(u.x, u.x, fmaf(u.y, u.y, fmaf(u.z, u.z, fmaf(u.w, u.w, s))));
+            }
+        }
         s = warp_sum(s);
         if (lane == 0) red[warp] = s;
         sync();
         float tot = 0.0f;
 #pragma unroll
-        for (int w = 0; w < WARPS; w++) tot += red[w];
+        for (int i = 0; i < WARPS; i++) tot += red[i];
         rs = 1.0f / sqrtf(tot / (float)K + a.eps);
         sync();
       }
-      for (int g = warp; g < ng; g += WARPS) {
-        float v = x[g * 32 + lane];
-        if (PRO == PRO_RMS) v = a.norm[g * 32 + lane] * (rs * v);
-        float scale;
-        const int8_t q = quantize_group_warp(v, lane, a.bias, &scale);
-        sq[(size_t)t * K + g * 32 + lane] = (int8_t)(q - (int8_t)a.bias);  // signed, as the products take it
-        if (lane == 0) ss[t * ng + g] = scale;
+#pragma unroll
+      for (int r = 0; r < RMAX; r++) {
+        if (r < rounds) quantize_pair<PRO>(a, v[r], w[r], rs, pair + 128 * r, h, t, sq, ss);
+      }
+      for (int r = RMAX; r < rounds; r++) {
+        const int g = pair + 128 * r;
+        float4 xv[4], wv[4];
+        for (int k = 0; k < 4; k++) {
+          xv[k] = g < ng ? x4[(32 * g + 16 * h) / 4 + k] : make_float4(0.f, 0.f, 0.f, 0.f);
+          wv[k] = (PRO == PRO_RMS && g < ng) ? __ldg(n4 + (32 * g + 16 * h) / 4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        quantize_pair<PRO>(a, xv, wv, rs, g, h, t, sq, ss);
       }
     }
   }

@@ -116,7 +116,7 @@ def synthetic_host_weights(cfg, seed=0, std=0.02):
 class Engine:
     """One model's forward pass on the current device."""
 
-    SPLIT = 128  # positions a slice of the split-KV attention
+    SPLIT = 64  # positions a slice of the split-KV attention (one tile of keys and values a CTA)
 
     def __init__(self, cfg, host=None, seed=0, device=0, graphs=True, pdl=True):
         init(device)
@@ -157,7 +157,7 @@ class Engine:
         B["logits"] = Buffer(c.vocab * 4)
         B["tp"] = Buffer(8).zero()      # the token and the position, read by the kernels
         B["bad"] = Buffer(4).zero()     # non-finite keys / values written to a float16 cache (halves.ts:35)
-        B["scratch"] = Buffer(L.pllm_attention_scratch_bytes(c.heads, c.head_size, c.seq_len, self.SPLIT))
+        B["scratch"] = Buffer(L.pllm_attention_scratch_bytes(c.heads, c.head_size, c.seq_len, self.SPLIT)).zero()
         self.B = B
         if host is not None:
             self.load(host)
@@ -240,9 +240,9 @@ class Engine:
 
     @property
     def launches_per_step(self):
-        """Kernels a step launches: the embedding, seven a layer (q/k/v product, norms + RoPE + cache, the attention's
-        two, the wo, w1/w3 and w2 products), the classifier."""
-        return 2 + 7 * self.cfg.layers
+        """Kernels a step launches: the embedding, six a layer (q/k/v product, norms + RoPE + cache, the attention
+        with its slices' combine inside, the wo, w1/w3 and w2 products), the classifier."""
+        return 2 + 6 * self.cfg.layers
 
     def _enqueue_step(self, need_logits=True):
         c, B = self.cfg, self.B
