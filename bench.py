@@ -197,6 +197,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompt", type=int, default=PROMPT)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="profiling only: launch each kernel (no CUDA graph, no PDL)")
+    ap.add_argument("--no-micro", action="store_true", help="profiling only: skip the per-kernel timings")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: the same shapes with fewer layers (a small case for ncu captures)")
     args = ap.parse_args()
@@ -226,7 +228,7 @@ def main():
     steps, warmup = args.steps, max(3, args.warmup)
     prompt = args.prompt
     assert prompt + warmup + steps <= cfg.seq_len, "positions past the cache"
-    eng = Engine(cfg, seed=0, device=local)
+    eng = Engine(cfg, seed=0, device=local, graphs=not args.eager, pdl=not args.eager)
     L.pllm_set_stream(eng.stream)
     rng = np.random.default_rng(1 + rank)
     ids = rng.integers(0, cfg.vocab, prompt + warmup + steps).astype(np.int32)
@@ -255,7 +257,8 @@ def main():
             ms = float(t.item())
         return ms
 
-    eng.capture()
+    if not args.eager:
+        eng.capture()
     # the prompt: a decode step a token (the tensor-core prefill is not built yet), filling the cache
     device_steps(0, 8)
     prefill_ms = timed(lambda: device_steps(8, prompt - 8))
@@ -280,65 +283,69 @@ def main():
     e2e_ms = timed(lambda: [eng.forward(int(ids[i % ids.size]), i) for i in range(e2e_first, e2e_first + e2e_steps)])
     e2e = e2e_steps * world / (e2e_ms / 1000)
 
-    # the kernels alone, each family's 36 launches (every layer's weights: no L2 reuse) recorded as one CUDA graph
-    # and replayed, so that the host's launch costs are not in the times
-    c = cfg
-    B = eng.B
-    reps = 5
-    E = 2 if c.half_kv else 4
-
-    def graph_ms(enqueue, launches):
-        g = eng.graph_of(enqueue)
-        L.pllm_graph_launch(g)
-        ms = timed(lambda: [L.pllm_graph_launch(g) for _ in range(reps)]) / (reps * launches)
-        L.pllm_graph_destroy(g)
-        return ms
-
-    def w13_all():
-        for l in range(c.layers):
-            eng._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * c.hidden * c.dim, B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4,
-                      c.hidden, c.dim, B["x"].ptr, B["ffn_norm"].ptr + l * c.dim * 4, 1, 2, pair=c.hidden, pdl=False)
-
-    w13_ms = graph_ms(w13_all, c.layers)
-    w13_bytes = 2 * c.hidden * c.dim * 1.125 + c.dim * 4 * 2 + c.hidden * 4
+    gemv, gemv_us, attention, achieved, w13_bytes = {}, {}, {}, None, None
     peak, peak_kind = peaks()
-    achieved = w13_bytes / (w13_ms / 1000) / 1e9
-    gemv = {"w13_swiglu": round(achieved, 1)}
-    gemv_us = {"w13_swiglu": round(w13_ms * 1000, 2)}
+    c, B = cfg, eng.B
+    if not args.no_micro:
+        # the kernels alone, each family's 36 launches (every layer's weights: no L2 reuse) recorded as one CUDA graph
+        # and replayed, so that the host's launch costs are not in the times
+        c = cfg
+        B = eng.B
+        reps = 5
+        E = 2 if c.half_kv else 4
 
-    def each(name, wq, ws, rows, cols, xin, norm, pro, epi):
-        def run():
+        def graph_ms(enqueue, launches):
+            g = eng.graph_of(enqueue)
+            L.pllm_graph_launch(g)
+            ms = timed(lambda: [L.pllm_graph_launch(g) for _ in range(reps)]) / (reps * launches)
+            L.pllm_graph_destroy(g)
+            return ms
+
+        def w13_all():
             for l in range(c.layers):
-                eng._gemv(B["qkv"].ptr if epi == 0 else B["x"].ptr, wq + l * rows * cols, ws + l * rows * (cols // 32) * 4,
-                          rows, cols, xin, norm, pro, epi, pdl=False)
-        ms = graph_ms(run, c.layers)
-        gemv[name] = round(rows * cols * 1.125 / (ms / 1000) / 1e9, 1)
-        gemv_us[name] = round(ms * 1000, 2)
+                eng._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * c.hidden * c.dim, B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4,
+                          c.hidden, c.dim, B["x"].ptr, B["ffn_norm"].ptr + l * c.dim * 4, 1, 2, pair=c.hidden, pdl=False)
 
-    each("wqkv", B["wqkv"].ptr, B["sqkv"].ptr, eng.rows_qkv, c.dim, B["x"].ptr, B["att_norm"].ptr, 1, 0)
-    each("wo", B["wo"].ptr, B["so"].ptr, c.dim, c.qdim, B["att"].ptr, 0, 2, 1)
-    each("w2", B["w2"].ptr, B["s2"].ptr, c.dim, c.hidden, B["hb"].ptr, 0, 2, 1)
-    L.pllm_set_stream(eng.stream)
+        w13_ms = graph_ms(w13_all, c.layers)
+        w13_bytes = 2 * c.hidden * c.dim * 1.125 + c.dim * 4 * 2 + c.hidden * 4
+        peak, peak_kind = peaks()
+        achieved = w13_bytes / (w13_ms / 1000) / 1e9
+        gemv = {"w13_swiglu": round(achieved, 1)}
+        gemv_us = {"w13_swiglu": round(w13_ms * 1000, 2)}
 
-    def cls_run():
-        eng._gemv(B["logits"].ptr, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim, B["x"].ptr, B["final_norm"].ptr, 1, 0,
-                  pdl=False)
-    cls_ms = graph_ms(cls_run, 1)
-    gemv["cls"] = round(c.vocab * c.dim * 1.125 / (cls_ms / 1000) / 1e9, 1)
-    gemv_us["cls"] = round(cls_ms * 1000, 2)
+        def each(name, wq, ws, rows, cols, xin, norm, pro, epi):
+            def run():
+                for l in range(c.layers):
+                    eng._gemv(B["qkv"].ptr if epi == 0 else B["x"].ptr, wq + l * rows * cols, ws + l * rows * (cols // 32) * 4,
+                              rows, cols, xin, norm, pro, epi, pdl=False)
+            ms = graph_ms(run, c.layers)
+            gemv[name] = round(rows * cols * 1.125 / (ms / 1000) / 1e9, 1)
+            gemv_us[name] = round(ms * 1000, 2)
 
-    # the attention alone at the last decode position (36 layers' caches, 2 kernels a layer)
-    def attention_all():
-        for l in range(c.layers):
-            L.pllm_attention_dev(B["att"].ptr, B["qkv"].ptr, B["kc"].ptr + l * c.seq_len * c.kvdim * E,
-                                 B["vc"].ptr + l * c.seq_len * c.kvdim * E, B["scratch"].ptr, B["tp"].ptr + 4,
-                                 c.seq_len, c.heads, c.kv_heads, c.head_size, int(c.half_kv), 0.0, eng.SPLIT, 0)
+        each("wqkv", B["wqkv"].ptr, B["sqkv"].ptr, eng.rows_qkv, c.dim, B["x"].ptr, B["att_norm"].ptr, 1, 0)
+        each("wo", B["wo"].ptr, B["so"].ptr, c.dim, c.qdim, B["att"].ptr, 0, 2, 1)
+        each("w2", B["w2"].ptr, B["s2"].ptr, c.dim, c.hidden, B["hb"].ptr, 0, 2, 1)
+        L.pllm_set_stream(eng.stream)
 
-    att_ms = graph_ms(attention_all, c.layers)
-    last_pos = int(B["tp"].download(np.int32)[1])
-    att_bytes = 2 * (last_pos + 1) * c.kvdim * E
-    attention = {"us_per_layer": round(att_ms * 1000, 2), "position": last_pos,
-                 "gbs": round(att_bytes / (att_ms / 1000) / 1e9, 1)}
+        def cls_run():
+            eng._gemv(B["logits"].ptr, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim, B["x"].ptr, B["final_norm"].ptr, 1, 0,
+                      pdl=False)
+        cls_ms = graph_ms(cls_run, 1)
+        gemv["cls"] = round(c.vocab * c.dim * 1.125 / (cls_ms / 1000) / 1e9, 1)
+        gemv_us["cls"] = round(cls_ms * 1000, 2)
+
+        # the attention alone at the last decode position (36 layers' caches, 2 kernels a layer)
+        def attention_all():
+            for l in range(c.layers):
+                L.pllm_attention_dev(B["att"].ptr, B["qkv"].ptr, B["kc"].ptr + l * c.seq_len * c.kvdim * E,
+                                     B["vc"].ptr + l * c.seq_len * c.kvdim * E, B["scratch"].ptr, B["tp"].ptr + 4,
+                                     c.seq_len, c.heads, c.kv_heads, c.head_size, int(c.half_kv), 0.0, eng.SPLIT, 0)
+
+        att_ms = graph_ms(attention_all, c.layers)
+        last_pos = int(B["tp"].download(np.int32)[1])
+        att_bytes = 2 * (last_pos + 1) * c.kvdim * E
+        attention = {"us_per_layer": round(att_ms * 1000, 2), "position": last_pos,
+                     "gbs": round(att_bytes / (att_ms / 1000) / 1e9, 1)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -365,7 +372,8 @@ def main():
         "gemv_gbs": gemv,
         "gemv_us": gemv_us,
         "attention": attention,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak if achieved else None,
                      "peak_kind": peak_kind, "kernel": "gemv_kernel<int8, 1 token, RMSNorm prologue, SwiGLU epilogue>",
                      "bytes_per_launch": w13_bytes, "traffic": profile_traffic("gemv_q8_w13_qwen3-8b")},
         "decode_roofline_frac": (c.weight_bytes() / (decode_ms / steps / 1000) / 1e9) / peak,
