@@ -337,9 +337,11 @@ def main():
         # the attention alone at the last decode position (36 layers' caches, 2 kernels a layer)
         def attention_all():
             for l in range(c.layers):
-                L.pllm_attention_dev(B["att"].ptr, B["qkv"].ptr, B["kc"].ptr + l * c.seq_len * c.kvdim * E,
-                                     B["vc"].ptr + l * c.seq_len * c.kvdim * E, B["scratch"].ptr, B["tp"].ptr + 4,
-                                     c.seq_len, c.heads, c.kv_heads, c.head_size, int(c.half_kv), 0.0, eng.SPLIT, 0)
+                L.pllm_attention_step(B["att"].ptr, B["qkv"].ptr, B["kc"].ptr + l * c.seq_len * c.kvdim * E,
+                                      B["vc"].ptr + l * c.seq_len * c.kvdim * E, B["scratch"].ptr, B["tp"].ptr + 4,
+                                      c.seq_len, c.heads, c.kv_heads, c.head_size, int(c.half_kv), 0.0, eng.SPLIT,
+                                      B["q_norm"].ptr + l * c.head_size * 4, B["k_norm"].ptr + l * c.head_size * 4,
+                                      B["cos_t"].ptr, B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, 0)
 
         att_ms = graph_ms(attention_all, c.layers)
         last_pos = int(B["tp"].download(np.int32)[1])

@@ -179,6 +179,13 @@ void pllm_gemv(uint64_t out, int64_t out_stride, uint64_t xq, uint64_t xs, int64
 void pllm_qk_rope_cache(uint64_t q, uint64_t k, uint64_t v, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t,
                         uint64_t sin_t, uint64_t pos_dev, int32_t pos, uint64_t kc, uint64_t vc, int32_t nh,
                         int32_t nkv, int32_t hs, int32_t rot, float eps, int32_t half, uint64_t bad, int32_t pdl);
+/* the forward driver's attention step in one launch: the q / k head norms (null weights: none), RoPE at the device
+ * position, this position's key and value into the cache, and the attention over positions 0..pos; qkv: the q/k/v
+ * product's output (nh, nkv, nkv heads of hs); scratch: pllm_attention_scratch_bytes, zero before its first use */
+void pllm_attention_step(uint64_t out, uint64_t qkv, uint64_t kc, uint64_t vc, uint64_t scratch, uint64_t pos_dev,
+                         int32_t capacity, int32_t nh, int32_t nkv, int32_t hs, int32_t half, float cap,
+                         int32_t split_len, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t, uint64_t sin_t, int32_t rot,
+                         float eps, uint64_t bad, int32_t pdl);
 /* attention at the device position over a cache of capacity positions; scratch: pllm_attention_scratch_bytes */
 uint64_t pllm_attention_scratch_bytes(int32_t nh, int32_t hs, int32_t capacity, int32_t split_len);
 void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t scratch, uint64_t pos_dev,

@@ -48,8 +48,55 @@ __device__ __forceinline__ float kv_elem(const uint8_t* row, int d) {
   return reinterpret_cast<const float*>(row)[d];
 }
 
-template <bool HALF, int KVM>
-__global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttArgs a) {
+// What the forward driver's attention does before it reads the cache (FUSE): the per-head RMSNorm of q and k
+// (Qwen3's q_norm / k_norm, forward/attention.ts:140-143), RoPE at the position (kernels/kernel/attention.ts:7-20
+// with the tables' row of pos), and this position's key and value into the cache (halves.ts:35-67's rounding for a
+// float16 cache). Every CTA makes its own query heads; the CTA whose slice holds the position also makes the key and
+// value of its kv head, writes them to the cache and into its shared tile.
+struct Fuse {
+  const float* k;       // this token's keys (nkv heads) and values, as the q/k/v product wrote them
+  const float* v;
+  const float* qn;      // q_norm / k_norm (null: none)
+  const float* kn;
+  const float* cos_t;   // [capacity][hs / 2]
+  const float* sin_t;
+  float eps;
+  int rot;
+  int* bad;             // non-finite keys or values written to a float16 cache are counted here (may be null)
+};
+
+// a head of hs floats in shared memory, normalized (w: null for none) and turned at pos, by the CTA's threads
+__device__ __forceinline__ void norm_rope(float* x, const float* w, const Fuse& f, int hs, int pos, bool turn,
+                                          float* red) {
+  const int tid = threadIdx.x;
+  if (w) {
+    float s = 0.0f;
+    for (int d = tid; d < hs; d += ATT_THREADS) s = fmaf(x[d], x[d], s);
+    s = warp_sum(s);
+    if ((tid & 31) == 0) red[tid >> 5] = s;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int i = 0; i < ATT_WARPS; i++) tot += red[i];
+    const float r = 1.0f / sqrtf(tot / (float)hs + f.eps);
+    __syncthreads();
+    for (int d = tid; d < hs; d += ATT_THREADS) x[d] = w[d] * (r * x[d]);
+    __syncthreads();
+  }
+  if (turn) {
+    const int turned = f.rot > 0 && f.rot < hs ? f.rot : hs;
+    const float* c = f.cos_t + (long long)pos * (hs / 2);
+    const float* sn = f.sin_t + (long long)pos * (hs / 2);
+    for (int i = tid; i < turned / 2; i += ATT_THREADS) {
+      const float v0 = x[2 * i], v1 = x[2 * i + 1];
+      x[2 * i] = v0 * c[i] - v1 * sn[i];
+      x[2 * i + 1] = v0 * sn[i] + v1 * c[i];
+    }
+    __syncthreads();
+  }
+}
+
+template <bool HALF, int KVM, bool FUSE>
+__global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttArgs a, const Fuse f) {
   extern __shared__ __align__(16) uint8_t att_smem[];
   constexpr int E = HALF ? 2 : 4;
   const int hs = a.hs;
@@ -58,8 +105,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   uint8_t* sV = sK + TILE * rowb;                    // [TILE][rowb]
   float* sq = reinterpret_cast<float*>(sV + TILE * rowb);  // [KVM][hs]
   float* sp = sq + KVM * hs;                         // [KVM][TILE] scores, then probabilities
-  __shared__ float sM[KVM], sL[KVM], sScale[KVM];
-  pdl_wait();
+  float* sx = sp + KVM * TILE;                       // [2][hs] (FUSE) this position's key and value
+  __shared__ float sM[KVM], sL[KVM], sScale[KVM], red[ATT_WARPS];
+  // the position: written by the host before the step's first kernel, so readable before the dependency wait
   const int pos = a.pos_dev ? *a.pos_dev : a.pos;
   const int count = pos + 1;
   const int kvh = blockIdx.x, split = blockIdx.y;
@@ -70,25 +118,12 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kvdim = a.nkv * hs, hbase = kvh * KVM;
   const float isq = 1.0f / sqrtf((float)hs);
-  for (int e = tid; e < KVM * hs; e += ATT_THREADS) sq[e] = a.q[(long long)hbase * hs + e];
-  if (tid < KVM) {
-    sM[tid] = -INFINITY;
-    sL[tid] = 0.0f;
-  }
-  // the running output: this thread's dims d = tid + ATT_THREADS i of every head
-  constexpr int DMAX = 2;  // hs <= 256
-  float acc[KVM][DMAX];
-#pragma unroll
-  for (int j = 0; j < KVM; j++)
-#pragma unroll
-    for (int i = 0; i < DMAX; i++) acc[j][i] = 0.0f;
   const int chunks = hs * E / 16;                    // 16-byte pieces a row
   const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.kc) + (long long)kvh * hs * E;
   const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vc) + (long long)kvh * hs * E;
-  for (int t0 = p0; t0 < p1; t0 += TILE) {
-    const int len = min(TILE, p1 - t0);
-    __syncthreads();  // the previous tile's keys, values and probabilities are no longer read
-    // 1. the tile's keys and values: every load issued before any is used
+  // the tile's keys and values (positions before this token's: not the previous kernel's output), every load issued
+  // before any is used
+  auto load_tile = [&](int t0, int len) {
     constexpr int PER = 8;
     for (int base = tid; base < len * chunks; base += ATT_THREADS * PER) {
       int4 kv[PER], vv[PER];
@@ -98,8 +133,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
         if (e < len * chunks) {
           const int t = e / chunks, c = e % chunks;
           const long long off = (long long)(t0 + t) * kvdim * E + c * 16;
-          kv[u] = __ldg(reinterpret_cast<const int4*>(kbase + off));
-          vv[u] = __ldg(reinterpret_cast<const int4*>(vbase + off));
+          kv[u] = *reinterpret_cast<const int4*>(kbase + off);
+          vv[u] = *reinterpret_cast<const int4*>(vbase + off);
         }
       }
 #pragma unroll
@@ -109,6 +144,68 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
           const int t = e / chunks, c = e % chunks;
           *reinterpret_cast<int4*>(sK + t * rowb + c * 16) = kv[u];
           *reinterpret_cast<int4*>(sV + t * rowb + c * 16) = vv[u];
+        }
+      }
+    }
+  };
+  const int len0 = min(TILE, p1 - p0);
+  if (FUSE) load_tile(p0, len0);  // before the wait: it overlaps the q/k/v product's tail
+  pdl_wait();
+  for (int e = tid; e < KVM * hs; e += ATT_THREADS) sq[e] = a.q[(long long)hbase * hs + e];
+  if (tid < KVM) {
+    sM[tid] = -INFINITY;
+    sL[tid] = 0.0f;
+  }
+  const bool holds_pos = FUSE && p1 == count;
+  if (FUSE) {
+    __syncthreads();
+    for (int j = 0; j < KVM; j++) norm_rope(sq + j * hs, f.qn, f, hs, pos, true, red);
+    if (holds_pos) {  // this position's key (normalized, turned) and value, into the cache and the tile
+      for (int d = tid; d < hs; d += ATT_THREADS) {
+        sx[d] = f.k[(long long)kvh * hs + d];
+        sx[hs + d] = f.v[(long long)kvh * hs + d];
+      }
+      __syncthreads();
+      norm_rope(sx, f.kn, f, hs, pos, true, red);
+      int local = 0;
+      const int t = pos - p0;  // < TILE when the tile is the slice's first
+      for (int e = tid; e < 2 * hs; e += ATT_THREADS) {
+        const int d = e % hs;
+        uint8_t* cache = reinterpret_cast<uint8_t*>(const_cast<void*>(e < hs ? a.kc : a.vc)) + (long long)pos * kvdim * E +
+                         ((long long)kvh * hs + d) * E;
+        uint8_t* tile = (e < hs ? sK : sV) + (size_t)(t % TILE) * rowb + d * E;
+        if (HALF) {
+          const uint16_t hb = float_to_half_bits(sx[e], &local);
+          *reinterpret_cast<uint16_t*>(cache) = hb;
+          if (t < TILE) *reinterpret_cast<uint16_t*>(tile) = hb;
+        } else {
+          *reinterpret_cast<float*>(cache) = sx[e];
+          if (t < TILE) *reinterpret_cast<float*>(tile) = sx[e];
+        }
+      }
+      if (local && f.bad) atomicAdd(f.bad, local);
+    }
+  }
+  // the running output: this thread's dims d = tid + ATT_THREADS i of every head
+  constexpr int DMAX = 2;  // hs <= 256
+  float acc[KVM][DMAX];
+#pragma unroll
+  for (int j = 0; j < KVM; j++)
+#pragma unroll
+    for (int i = 0; i < DMAX; i++) acc[j][i] = 0.0f;
+  for (int t0 = p0; t0 < p1; t0 += TILE) {
+    const int len = min(TILE, p1 - t0);
+    if (t0 != p0 || !FUSE) {
+      __syncthreads();  // the previous tile's keys, values and probabilities are no longer read
+      load_tile(t0, len);
+      if (holds_pos && pos >= t0 && pos < t0 + len) {  // (a slice longer than a tile: this position's row again)
+        __syncthreads();
+        for (int e = tid; e < 2 * hs; e += ATT_THREADS) {
+          const int d = e % hs;
+          uint8_t* tile = (e < hs ? sK : sV) + (size_t)(pos - t0) * rowb + d * E;
+          int dummy = 0;
+          if (HALF) *reinterpret_cast<uint16_t*>(tile) = float_to_half_bits(sx[e], &dummy);
+          else *reinterpret_cast<float*>(tile) = sx[e];
         }
       }
     }
@@ -207,19 +304,35 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   __syncthreads();
   if (!last) return;
   __threadfence();
+  // the slices' maxima and sums first (all loads in flight), then each (head, dim) over the slices
+  float* sw = sp;  // [KVM][nsplit] weights exp(m_s - M), in the scores' room (the host sizes it for nsplit)
+  for (int e = tid; e < KVM * nsplit; e += ATT_THREADS) {
+    const int j = e / nsplit, s2 = e % nsplit;
+    sw[e] = __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * (hs + 2) + hs);
+  }
+  __syncthreads();
+  for (int j = warp; j < KVM; j += ATT_WARPS) {
+    float M = -INFINITY;
+    for (int s2 = lane; s2 < nsplit; s2 += 32) M = fmaxf(M, sw[j * nsplit + s2]);
+    M = warp_max(M);
+    float L = 0.0f;
+    for (int s2 = lane; s2 < nsplit; s2 += 32) {
+      const float w = expf(sw[j * nsplit + s2] - M);
+      sw[j * nsplit + s2] = w;
+      L = fmaf(__ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * (hs + 2) + hs + 1), w, L);
+    }
+    L = warp_sum(L);
+    if (lane == 0) sL[j] = L;
+  }
+  __syncthreads();
   for (int e = tid; e < KVM * hs; e += ATT_THREADS) {
     const int j = e / hs, d = e % hs, h = hbase + j;
     if (h < a.h0 || h >= a.h1) continue;
-    const float* part = a.part + (long long)h * a.nsplit * (hs + 2);
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < nsplit; s2++) M = fmaxf(M, __ldcg(part + s2 * (hs + 2) + hs));
-    float L = 0.0f, o = 0.0f;
-    for (int s2 = 0; s2 < nsplit; s2++) {
-      const float w = expf(__ldcg(part + s2 * (hs + 2) + hs) - M);
-      L = fmaf(__ldcg(part + s2 * (hs + 2) + hs + 1), w, L);
-      o = fmaf(__ldcg(part + s2 * (hs + 2) + d), w, o);
-    }
-    a.out[(long long)h * hs + d] = o / L;
+    const float* part = a.part + (long long)h * a.nsplit * (hs + 2) + d;
+    float o = 0.0f;
+#pragma unroll 8
+    for (int s2 = 0; s2 < nsplit; s2++) o = fmaf(__ldcg(part + (long long)s2 * (hs + 2)), sw[j * nsplit + s2], o);
+    a.out[(long long)h * hs + d] = o / sL[j];
   }
   if (tid == 0) a.counters[kvh] = 0;
 }
@@ -247,7 +360,7 @@ __global__ void attention_combine_kernel(const AttArgs a) {
 }
 
 template <bool HALF, int KVM>
-cudaError_t launch_split_kvm(const AttArgs& a, size_t smem, dim3 grid, bool pdl) {
+cudaError_t launch_split_kvm(const AttArgs& a, const Fuse* f, size_t smem, dim3 grid, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(ATT_THREADS);
@@ -258,28 +371,36 @@ cudaError_t launch_split_kvm(const AttArgs& a, size_t smem, dim3 grid, bool pdl)
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-auto k = attention_split_kernel<HALF, KVM>;
+if (f) {
+    auto k = attention_split_kernel<HALF, KVM, true>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return cudaLaunchKernelEx(&cfg, k, a, *f);
+  }
+  const Fuse none = {};
+  auto k = attention_split_kernel<HALF, KVM, false>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  return cudaLaunchKernelEx(&cfg, k, a);
+  return cudaLaunchKernelEx(&cfg, k, a, none);
 }
 
 template <bool HALF>
-cudaError_t launch_split(const AttArgs& a, int kvm, size_t smem, dim3 grid, bool pdl) {
+cudaError_t launch_split(const AttArgs& a, const Fuse* f, int kvm, size_t smem, dim3 grid, bool pdl) {
   switch (kvm) {
-    case 1: return launch_split_kvm<HALF, 1>(a, smem, grid, pdl);
-    case 2: return launch_split_kvm<HALF, 2>(a, smem, grid, pdl);
-    case 4: return launch_split_kvm<HALF, 4>(a, smem, grid, pdl);
-    case 8: return launch_split_kvm<HALF, 8>(a, smem, grid, pdl);
+    case 1: return launch_split_kvm<HALF, 1>(a, f, smem, grid, pdl);
+    case 2: return launch_split_kvm<HALF, 2>(a, f, smem, grid, pdl);
+    case 4: return launch_split_kvm<HALF, 4>(a, f, smem, grid, pdl);
+    case 8: return launch_split_kvm<HALF, 8>(a, f, smem, grid, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
 
-void run_attention(const char* name, AttArgs a, bool half, bool pdl) {
+void run_attention(const char* name, AttArgs a, bool half, bool pdl, const Fuse* f = nullptr) {
   const int kvm = a.nh / a.nkv;
   const size_t rowb = (size_t)a.hs * (half ? 2 : 4) + 16;
-  const size_t smem = 2 * TILE * rowb + (size_t)kvm * a.hs * 4 + (size_t)kvm * TILE * 4;
+  // the scores' room also holds the slices' weights in the combine (kvm * nsplit floats)
+  const size_t scores = (size_t)kvm * (a.nsplit > TILE ? a.nsplit : TILE) * 4;
+  const size_t smem = 2 * TILE * rowb + (size_t)kvm * a.hs * 4 + scores + 2 * (size_t)a.hs * 4;
   const dim3 grid(a.nkv, a.nsplit);
-  cudaError_t e = half ? launch_split<true>(a, kvm, smem, grid, pdl) : launch_split<false>(a, kvm, smem, grid, pdl);
+  cudaError_t e = half ? launch_split<true>(a, f, kvm, smem, grid, pdl) : launch_split<false>(a, f, kvm, smem, grid, pdl);
   if (e != cudaSuccess) {
     pllm_fail(PLLM_ECUDA, "%s: launch failed: %s", name, cudaGetErrorString(e));
     return;
@@ -482,6 +603,45 @@ PLLM_API void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t
   a.cap = cap;
   a.counters = dptr<int>(scratch + partial_bytes(nh, hs, capacity, split_len));
   run_attention("pllm_attention_dev", a, half != 0, pdl != 0);
+}
+
+// The forward driver's attention step, one launch: q / k head norms (null weights: none), RoPE at the position, this
+// position's key and value into the cache, and the attention over positions 0..pos; q, k, v: the q/k/v product's
+// output (nh, then nkv, then nkv heads of hs). The position is read from device memory (pos_dev).
+PLLM_API void pllm_attention_step(uint64_t out, uint64_t qkv, uint64_t kc, uint64_t vc, uint64_t scratch,
+                                  uint64_t pos_dev, int32_t capacity, int32_t nh, int32_t nkv, int32_t hs, int32_t half,
+                                  float cap, int32_t split_len, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t,
+                                  uint64_t sin_t, int32_t rot, float eps, uint64_t bad, int32_t pdl) {
+  if (!check_heads("pllm_attention_step", nh, nkv, hs, 0, nh)) return;
+  PLLM_REQUIRE(capacity > 0 && split_len > 0 && split_len <= 2048 && hs % 2 == 0 && pos_dev,
+               "pllm_attention_step: capacity %d split %d", capacity, split_len);
+  AttArgs a = {};
+  a.out = dptr<float>(out);
+  a.q = dptr<const float>(qkv);
+  a.kc = dptr<const void>(kc);
+  a.vc = dptr<const void>(vc);
+  a.part = dptr<float>(scratch);
+  a.pos_dev = dptr<const int>(pos_dev);
+  a.nh = nh;
+  a.nkv = nkv;
+  a.hs = hs;
+  a.h0 = 0;
+  a.h1 = nh;
+  a.split_len = split_len;
+  a.nsplit = (capacity + split_len - 1) / split_len;
+  a.cap = cap;
+  a.counters = dptr<int>(scratch + partial_bytes(nh, hs, capacity, split_len));
+  Fuse f = {};
+  f.k = dptr<const float>(qkv) + (long long)nh * hs;
+  f.v = f.k + (long long)nkv * hs;
+  f.qn = dptr<const float>(q_norm);
+  f.kn = dptr<const float>(k_norm);
+  f.cos_t = dptr<const float>(cos_t);
+  f.sin_t = dptr<const float>(sin_t);
+  f.eps = eps;
+  f.rot = rot;
+  f.bad = dptr<int>(bad);
+  run_attention("pllm_attention_step", a, half != 0, pdl != 0, &f);
 }
 
 PLLM_API void pllm_qk_rope_cache(uint64_t q, uint64_t k, uint64_t v, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t,

@@ -10,8 +10,7 @@ position are read by the kernels from device memory, so the same graph serves ev
     embed (pllm_embed_q8: the int8 row times its scales, tensors.ts:154-160)
     per layer:
       q, k, v   = one product over the three matrices' rows, its input RMSNorm + quantize_x fused (pllm_gemv pro 1)
-      q/k norms, RoPE at pos, k and v into the cache (pllm_qk_rope_cache)
-      attention over positions 0..pos (pllm_attention_dev: split-KV)
+      q/k norms, RoPE at pos, k and v into the cache, attention over 0..pos (pllm_attention_step: split-KV)
       x += wo . quantize_x(attention)      (pllm_gemv pro 2, epi 1: the residual add fused)
       hb = silu(w1 . h) * (w3 . h), h = quantize_x(RMSNorm(x))  (pllm_gemv pro 1, epi 2: w1's and w3's rows in one)
       x += w2 . quantize_x(hb)            (pllm_gemv pro 2, epi 1)
@@ -240,9 +239,9 @@ class Engine:
 
     @property
     def launches_per_step(self):
-        """Kernels a step launches: the embedding, six a layer (q/k/v product, norms + RoPE + cache, the attention
-        with its slices' combine inside, the wo, w1/w3 and w2 products), the classifier."""
-        return 2 + 6 * self.cfg.layers
+        """Kernels a step launches: the embedding, five a layer (the q/k/v product; the attention with the q / k
+        norms, RoPE, the cache write and its slices' combine inside; the wo, w1/w3 and w2 products), the classifier."""
+        return 2 + 5 * self.cfg.layers
 
     def _enqueue_step(self, need_logits=True):
         c, B = self.cfg, self.B
@@ -258,12 +257,9 @@ class Engine:
             vc = B["vc"].ptr + l * c.seq_len * c.kvdim * E
             qn = B["q_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
             kn = B["k_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
-            q = B["qkv"].ptr
-            L.pllm_qk_rope_cache(q, q + c.qdim * 4, q + (c.qdim + c.kvdim) * 4, qn, kn, B["cos_t"].ptr, B["sin_t"].ptr,
-                                 pos, 0, kc, vc, c.heads, c.kv_heads, c.head_size, 0, c.eps, int(c.half_kv),
-                                 B["bad"].ptr, int(self.pdl))
-            L.pllm_attention_dev(B["att"].ptr, q, kc, vc, B["scratch"].ptr, pos, c.seq_len, c.heads, c.kv_heads,
-                                 c.head_size, int(c.half_kv), 0.0, self.SPLIT, int(self.pdl))
+            L.pllm_attention_step(B["att"].ptr, B["qkv"].ptr, kc, vc, B["scratch"].ptr, pos, c.seq_len, c.heads,
+                                  c.kv_heads, c.head_size, int(c.half_kv), 0.0, self.SPLIT, qn, kn, B["cos_t"].ptr,
+                                  B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, int(self.pdl))
             self._gemv(B["x"].ptr, B["wo"].ptr + l * c.dim * c.qdim, B["so"].ptr + l * c.dim * (c.qdim // 32) * 4,
                        c.dim, c.qdim, B["att"].ptr, 0, PRO_QUANT, EPI_ADD)
             self._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * c.hidden * c.dim,

@@ -503,3 +503,58 @@ def test_registry_products_both_kernels(golden, mode):
             assert np.all(np.abs(get(out, np.float32) - golden[k + "q8r"][t]) <= bound)
     finally:
         L.pllm_set_gemv_mode(old)
+
+
+@pytest.mark.parametrize("half", [True, False])
+@pytest.mark.parametrize("nh,nkv,hs,qk", [(8, 2, 128, True), (6, 6, 48, False), (16, 8, 64, False)])
+def test_attention_step(half, nh, nkv, hs, qk):
+    """The driver's fused attention step against the oracle's steps on the same numbers: rmsnorm of every q and k
+    head (activations.ts:8-20), rope at pos (attention.ts:7-20), the key and value into the cache (halves.ts:35, to
+    the bit), attention over 0..pos (attention.ts:87-211); positions inside one slice, at the slices' edges and at
+    the cache's end; twice in a row (the slices' counts are left at zero)."""
+    rng = np.random.default_rng(nh * hs)
+    cap, split, eps = 300, 64, 1e-6
+    kvdim = nkv * hs
+    E = np.uint16 if half else np.float32
+    old = rng.normal(0, 1, (cap, kvdim)).astype(np.float32)
+    kc0 = O.to_f16(old)[0] if half else old.copy()
+    vc0 = O.to_f16(old[::-1].copy())[0] if half else old[::-1].copy()
+    qn = rng.normal(1, 0.1, hs).astype(np.float32) if qk else None
+    kn = rng.normal(1, 0.1, hs).astype(np.float32) if qk else None
+    ang = np.outer(np.arange(cap), 1.0 / 1e4 ** (np.arange(0, hs, 2) / hs))
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    C, S = dev(cos), dev(sin)
+    QN, KN = (dev(qn), dev(kn)) if qk else (None, None)
+    scratch = dev(np.zeros(L.pllm_attention_scratch_bytes(nh, hs, cap, split) // 4 + 1, np.float32))
+    bad = dev(np.zeros(1, np.int32))
+    for pos in (0, 5, 63, 64, 200, cap - 1):
+        qkv = rng.normal(0, 1, (nh + 2 * nkv) * hs).astype(np.float32)
+        KC, VC = dev(kc0.reshape(-1)), dev(vc0.reshape(-1))
+        P = dev(np.array([0, pos], np.int32))
+        out = dev(np.zeros(nh * hs, np.float32))
+        for _ in range(2):
+            L.pllm_attention_step(out.ptr, dev(qkv).ptr, KC.ptr, VC.ptr, scratch.ptr, P.ptr + 4, cap, nh, nkv, hs,
+                                  int(half), 0.0, split, QN.ptr if qk else 0, KN.ptr if qk else 0, C.ptr, S.ptr, 0,
+                                  eps, bad.ptr, 0)
+            check("pllm_attention_step")
+            q, k, v = qkv[: nh * hs], qkv[nh * hs: nh * hs + kvdim], qkv[nh * hs + kvdim:]
+            if qk:
+                q = np.concatenate([O.rmsnorm(q[h * hs:(h + 1) * hs], qn, eps) for h in range(nh)])
+                k = np.concatenate([O.rmsnorm(k[h * hs:(h + 1) * hs], kn, eps) for h in range(nkv)])
+            q = O.rope(q, cos[pos], sin[pos], nh, hs)
+            k = O.rope(k, cos[pos], sin[pos], nkv, hs)
+            kc, vc = kc0.copy(), vc0.copy()
+            kc[pos] = O.to_f16(k)[0] if half else k
+            vc[pos] = O.to_f16(v)[0] if half else v
+            got_k = get(KC, E).reshape(cap, kvdim)
+            got_v = get(VC, E).reshape(cap, kvdim)
+            if half:
+                assert np.array_equal(got_k[pos], kc[pos]) and np.array_equal(got_v[pos], vc[pos])
+            else:
+                np.testing.assert_allclose(got_k[pos], kc[pos], rtol=1e-6, atol=1e-6)
+                assert np.array_equal(got_v[pos], vc[pos])
+            assert np.array_equal(np.delete(got_k, pos, 0), np.delete(kc0, pos, 0))
+            want, _ = O.attention(q, kc[: pos + 1], vc[: pos + 1], pos, nh, nkv, hs, half=half)
+            np.testing.assert_allclose(get(out, np.float32), want, rtol=1e-4, atol=2e-5)
+    counts = get(scratch, np.int32)[-(nh + 1):]
+    assert np.all(counts == 0)
