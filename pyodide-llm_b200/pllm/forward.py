@@ -19,6 +19,7 @@ position are read by the kernels from device memory, so the same graph serves ev
 Every product's group sums are the reference kernels' exact integers; the float32 around them agrees with the
 reference's within rounding (the tests hold the logits to the oracle's within 1e-3 relative).
 """
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -119,6 +120,8 @@ class Engine:
 
     def __init__(self, cfg, host=None, seed=0, device=0, graphs=True, pdl=True):
         init(device)
+        if os.environ.get("PLLM_STAGE_BUDGET"):  # the bulk-copy product's stage ring, bytes (a tuning knob)
+            L.pllm_set_stage_budget(int(os.environ["PLLM_STAGE_BUDGET"]))
         self.cfg, self.graphs, self.pdl = cfg, graphs, pdl
         c = cfg
         self.rows_qkv = c.qdim + 2 * c.kvdim
