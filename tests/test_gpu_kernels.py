@@ -517,8 +517,8 @@ def test_attention_step(half, nh, nkv, hs, qk):
     kvdim = nkv * hs
     E = np.uint16 if half else np.float32
     old = rng.normal(0, 1, (cap, kvdim)).astype(np.float32)
-    kc0 = O.to_f16(old)[0] if half else old.copy()
-    vc0 = O.to_f16(old[::-1].copy())[0] if half else old[::-1].copy()
+    kc0 = O.to_f16(old)[0].reshape(cap, kvdim) if half else old.copy()
+    vc0 = O.to_f16(old[::-1].copy())[0].reshape(cap, kvdim) if half else old[::-1].copy()
     qn = rng.normal(1, 0.1, hs).astype(np.float32) if qk else None
     kn = rng.normal(1, 0.1, hs).astype(np.float32) if qk else None
     ang = np.outer(np.arange(cap), 1.0 / 1e4 ** (np.arange(0, hs, 2) / hs))
