@@ -304,7 +304,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   __syncthreads();
   if (!last) return;
   __threadfence();
-  // the slices' maxima and sums first (all loads in flight), then each (head, dim) over the slices
+  // the slices' maxima and sums first (all loads in flight), then their weighted values in chunks of slices staged
+  // in shared memory (the tile's room), each chunk's loads all issued before any is used
   float* sw = sp;  // [KVM][nsplit] weights exp(m_s - M), in the scores' room (the host sizes it for nsplit)
   for (int e = tid; e < KVM * nsplit; e += ATT_THREADS) {
     const int j = e / nsplit, s2 = e % nsplit;
@@ -324,15 +325,54 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
     L = warp_sum(L);
     if (lane == 0) sL[j] = L;
   }
-  __syncthreads();
-  for (int e = tid; e < KVM * hs; e += ATT_THREADS) {
-    const int j = e / hs, d = e % hs, h = hbase + j;
-    if (h < a.h0 || h >= a.h1) continue;
-    const float* part = a.part + (long long)h * a.nsplit * (hs + 2) + d;
-    float o = 0.0f;
-#pragma unroll 8
-    for (int s2 = 0; s2 < nsplit; s2++) o = fmaf(__ldcg(part + (long long)s2 * (hs + 2)), sw[j * nsplit + s2], o);
-    a.out[(long long)h * hs + d] = o / sL[j];
+  float o[KVM][DMAX];
+#pragma unroll
+  for (int j = 0; j < KVM; j++)
+#pragma unroll
+    for (int i = 0; i < DMAX; i++) o[j][i] = 0.0f;
+  const int row = hs + 2;                                    // floats a slice's partial
+  const int room = (int)((2 * TILE * rowb) / (KVM * row * 4));  // slices a chunk (sK and sV's bytes)
+  float* stage = reinterpret_cast<float*>(sK);
+  for (int c0 = 0; c0 < nsplit; c0 += room) {
+    const int cn = min(room, nsplit - c0);
+    __syncthreads();  // the previous chunk is read; sw and sL are written
+    const int per = cn * row;                                // floats a head's chunk (contiguous in part)
+    constexpr int PER = 8;
+    for (int base = tid; base < KVM * per; base += ATT_THREADS * PER) {
+      float v[PER];
+#pragma unroll
+      for (int u = 0; u < PER; u++) {
+        const int e = base + u * ATT_THREADS;
+        if (e < KVM * per) {
+          const int j = e / per, f2 = e % per;
+          v[u] = __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + c0) * row + f2);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < PER; u++) {
+        const int e = base + u * ATT_THREADS;
+        if (e < KVM * per) stage[e] = v[u];
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < DMAX; i++) {
+      const int d = tid + ATT_THREADS * i;
+      if (d >= hs) continue;
+#pragma unroll
+      for (int j = 0; j < KVM; j++)
+        for (int s2 = 0; s2 < cn; s2++) o[j][i] = fmaf(stage[j * per + s2 * row + d], sw[j * nsplit + c0 + s2], o[j][i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < DMAX; i++) {
+    const int d = tid + ATT_THREADS * i;
+    if (d >= hs) continue;
+#pragma unroll
+    for (int j = 0; j < KVM; j++) {
+      const int h = hbase + j;
+      if (h >= a.h0 && h < a.h1) a.out[(long long)h * hs + d] = o[j][i] / sL[j];
+    }
   }
   if (tid == 0) a.counters[kvh] = 0;
 }
