@@ -25,7 +25,7 @@ struct AttArgs {
   const float* q;
   const void* kc;
   const void* vc;
-  float* part;          // slices' partials: [nh][nsplit][hs + 2] (weighted values, max, sum)
+  float* part;          // slices' partials: [nh][nsplit][hs + 4] (weighted values, max, sum, 2 floats of pad)
   const int* pos_dev;   // device position (or null: pos)
   int pos, nh, nkv, hs, h0, h1;
   int split_len;        // positions a slice
@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
       if (nsplit == 1) {
         a.out[(long long)h * hs + d] = acc[j][i] / sL[j];
       } else {
-        float* part = a.part + ((long long)h * a.nsplit + split) * (hs + 2);
+        float* part = a.part + ((long long)h * a.nsplit + split) * (hs + 4);
         part[d] = acc[j][i];
         if (d == 0) {
           part[hs] = sM[j];
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   float* sw = sp;  // [KVM][nsplit] weights exp(m_s - M), in the scores' room (the host sizes it for nsplit)
   for (int e = tid; e < KVM * nsplit; e += ATT_THREADS) {
     const int j = e / nsplit, s2 = e % nsplit;
-    sw[e] = __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * (hs + 2) + hs);
+    sw[e] = __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * (hs + 4) + hs);
   }
   __syncthreads();
   for (int j = warp; j < KVM; j += ATT_WARPS) {
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
     for (int s2 = lane; s2 < nsplit; s2 += 32) {
       const float w = expf(sw[j * nsplit + s2] - M);
       sw[j * nsplit + s2] = w;
-      L = fmaf(__ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * (hs + 2) + hs + 1), w, L);
+      L = fmaf(__ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * (hs + 4) + hs + 1), w, L);
     }
     L = warp_sum(L);
     if (lane == 0) sL[j] = L;
@@ -330,28 +330,29 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   for (int j = 0; j < KVM; j++)
 #pragma unroll
     for (int i = 0; i < DMAX; i++) o[j][i] = 0.0f;
-  const int row = hs + 2;                                    // floats a slice's partial
+  const int row = hs + 4;                                    // floats a slice's partial (16-byte rows)
   const int room = (int)((2 * TILE * rowb) / (KVM * row * 4));  // slices a chunk (sK and sV's bytes)
   float* stage = reinterpret_cast<float*>(sK);
   for (int c0 = 0; c0 < nsplit; c0 += room) {
     const int cn = min(room, nsplit - c0);
     __syncthreads();  // the previous chunk is read; sw and sL are written
     const int per = cn * row;                                // floats a head's chunk (contiguous in part)
-    constexpr int PER = 8;
-    for (int base = tid; base < KVM * per; base += ATT_THREADS * PER) {
-      float v[PER];
+    const int per4 = per / 4;
+    constexpr int PER = 16;                                  // 16-byte loads a thread in flight
+    for (int base = tid; base < KVM * per4; base += ATT_THREADS * PER) {
+      float4 v[PER];
 #pragma unroll
       for (int u = 0; u < PER; u++) {
         const int e = base + u * ATT_THREADS;
-        if (e < KVM * per) {
-          const int j = e / per, f2 = e % per;
-          v[u] = __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + c0) * row + f2);
+        if (e < KVM * per4) {
+          const int j = e / per4, f4 = e % per4;
+          v[u] = __ldcg(reinterpret_cast<const float4*>(a.part + ((long long)(hbase + j) * a.nsplit + c0) * row) + f4);
         }
       }
 #pragma unroll
       for (int u = 0; u < PER; u++) {
         const int e = base + u * ATT_THREADS;
-        if (e < KVM * per) stage[e] = v[u];
+        if (e < KVM * per4) reinterpret_cast<float4*>(stage)[e] = v[u];
       }
     }
     __syncthreads();
@@ -386,15 +387,15 @@ __global__ void attention_combine_kernel(const AttArgs a) {
   const int h = a.h0 + blockIdx.x;
   if (nsplit == 1 || h >= a.h1) return;
   const int hs = a.hs;
-  const float* part = a.part + (long long)h * a.nsplit * (hs + 2);
+  const float* part = a.part + (long long)h * a.nsplit * (hs + 4);
   float M = -INFINITY;
-  for (int s = 0; s < nsplit; s++) M = fmaxf(M, part[s * (hs + 2) + hs]);
+  for (int s = 0; s < nsplit; s++) M = fmaxf(M, part[s * (hs + 4) + hs]);
   float L = 0.0f;
-  for (int s = 0; s < nsplit; s++) L += part[s * (hs + 2) + hs + 1] * expf(part[s * (hs + 2) + hs] - M);
+  for (int s = 0; s < nsplit; s++) L += part[s * (hs + 4) + hs + 1] * expf(part[s * (hs + 4) + hs] - M);
   const float inv = 1.0f / L;
   for (int d = threadIdx.x; d < hs; d += blockDim.x) {
     float o = 0.0f;
-    for (int s = 0; s < nsplit; s++) o += part[s * (hs + 2) + d] * expf(part[s * (hs + 2) + hs] - M);
+    for (int s = 0; s < nsplit; s++) o += part[s * (hs + 4) + d] * expf(part[s * (hs + 4) + hs] - M);
     a.out[(long long)h * hs + d] = o * inv;
   }
 }
@@ -474,16 +475,16 @@ bool check_heads(const char* name, int nh, int nkv, int hs, int h0, int h1) {
 }
 
 // the registry's call: the slices' partials go to the reference's scratch att (nh (pos + 1) floats), so a slice
-// count is chosen whose partials fit in it
+// count is chosen whose partials fit in it (and att must be 16-byte aligned)
 void registry_attention(const char* name, uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t att, int pos,
                         int nh, int nkv, int hs, int h0, int h1, float cap, bool half) {
   if (!check_heads(name, nh, nkv, hs, h0, h1)) return;
   PLLM_REQUIRE(pos >= 0, "%s: pos %d", name, pos);
-  PLLM_REQUIRE(!(kc & 15) && !(vc & 15), "%s: the cache must be 16-byte aligned", name);
+  PLLM_REQUIRE(!(kc & 15) && !(vc & 15) && !(att & 15), "%s: the cache and att must be 16-byte aligned", name);
   if (h1 == h0) return;
   const int count = pos + 1;
   int nsplit = (count + 127) / 128;
-  const int fit = count / (hs + 2);
+  const int fit = count / (hs + 4);
   if (nsplit > fit) nsplit = fit;
   if (nsplit < 1) nsplit = 1;
   AttArgs a = {};
@@ -614,7 +615,7 @@ PLLM_API void attention_f16_capped(uint64_t out, uint64_t q, uint64_t kc, uint64
 // kv head (the scratch must be zero when first used; every call leaves the counts at zero)
 static uint64_t partial_bytes(int nh, int hs, int capacity, int split_len) {
   const long long nsplit = (capacity + split_len - 1) / split_len;
-  return ((uint64_t)nh * nsplit * (hs + 2) * sizeof(float) + 255) & ~255ull;
+  return ((uint64_t)nh * nsplit * (hs + 4) * sizeof(float) + 255) & ~255ull;
 }
 PLLM_API uint64_t pllm_attention_scratch_bytes(int32_t nh, int32_t hs, int32_t capacity, int32_t split_len) {
   return partial_bytes(nh, hs, capacity, split_len) + (uint64_t)nh * sizeof(int);
