@@ -122,7 +122,8 @@ class Engine:
         init(device)
         if os.environ.get("PLLM_STAGE_BUDGET"):  # the bulk-copy product's stage ring, bytes (a tuning knob)
             L.pllm_set_stage_budget(int(os.environ["PLLM_STAGE_BUDGET"]))
-        self.cfg, self.graphs, self.pdl = cfg, graphs, pdl
+        self.cfg, self.graphs = cfg, graphs
+        self.pdl = pdl and not os.environ.get("PLLM_NO_PDL")  # (a switch for measuring what the early launches give)
         c = cfg
         self.rows_qkv = c.qdim + 2 * c.kvdim
         self.bias = 64 if c.relaxed else 0
