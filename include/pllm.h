@@ -201,6 +201,14 @@ int32_t pllm_set_gemv_mode(int32_t mode);
 /* the shared-memory bytes the bulk-copy product's ring of stages may take (32 KB..227 KB; default 200 KB) */
 int32_t pllm_set_stage_budget(int32_t bytes);
 
+/* attention_f16 for callers that cannot allocate device memory (no counterpart in the reference): the same
+ * arguments without att; the slices' partials live in a 4 MiB device array of the library's own, held by every GPU
+ * that loads the library until exit, shared by all calls (overlapping calls race), with nothing that must start at
+ * zero. Refused with an error where nh x ceil((pos + 1) / 128) x (hs + 4) floats exceed 1,048,576. The first call on
+ * a device looks up the array's address: make it before any stream capture. */
+void pllm_attention_f16_noalloc(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, int32_t pos, int32_t nh,
+                                int32_t nkv, int32_t hs, int32_t h0, int32_t h1);
+
 /* ===== seeded synthetic weights made on the device, for benchmarks and tests of model-sized shapes (no counterpart
  * in the reference, whose tests make synthetic checkpoints in NumPy, tests/made_up.py:30) ===== */
 /* n float32 values N(mean, std) of (seed, index) */

@@ -609,6 +609,73 @@ PLLM_API void attention_f16_capped(uint64_t out, uint64_t q, uint64_t kc, uint64
   registry_attention("attention_f16_capped", out, q, kc, vc, att, pos, nh, nkv, hs, h0, h1, cap, true);
 }
 
+// ---- the same attention for callers that cannot allocate device memory
+// Some callers cannot hand the attention a scratch buffer: they own a fixed device arena and may not allocate beside
+// it (as the reference's engine owns one linear memory and never allocates outside it), or they run where an
+// allocation is not allowed or would stall the device (a real-time decode loop, a plugin without access to the
+// process's allocator). This variant keeps the slices' partials in a file-scope device array instead: 4 MiB
+// (NOALLOC_FLOATS floats), held by every GPU that loads the library until the process exits. A call whose partials
+// (nh x slices x (hs + 4) floats, one slice per 128 positions) do not fit is refused with an error.
+// The array is shared by every call and keeps the last call's partials; nothing in it has to start at zero (each
+// call writes every partial it reads). Calls that overlap on the GPU (two streams, or two threads' streams) race on it.
+// The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device current);
+// make that first call before any stream capture.
+constexpr long long NOALLOC_FLOATS = 1ll << 20;
+static __device__ __align__(256) float g_noalloc_partials[NOALLOC_FLOATS];
+
+namespace {
+float* noalloc_partials() {
+  static float* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    pllm_fail(PLLM_ECUDA, "pllm_attention_f16_noalloc: no current device");
+    return nullptr;
+  }
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (e != cudaSuccess || !p) {
+      pllm_fail(PLLM_ECUDA, "pllm_attention_f16_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  return ptrs[dev];
+}
+}  // namespace
+
+PLLM_API void pllm_attention_f16_noalloc(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, int32_t pos, int32_t nh,
+                                         int32_t nkv, int32_t hs, int32_t h0, int32_t h1) {
+  const char* name = "pllm_attention_f16_noalloc";
+  if (!check_heads(name, nh, nkv, hs, h0, h1)) return;
+  PLLM_REQUIRE(pos >= 0, "%s: pos %d", name, pos);
+  PLLM_REQUIRE(!(kc & 15) && !(vc & 15), "%s: the cache must be 16-byte aligned", name);
+  const long long nsplit = ((long long)pos + 1 + 127) / 128;
+  const long long need = (long long)nh * nsplit * (hs + 4);
+  PLLM_REQUIRE(need <= NOALLOC_FLOATS,
+               "%s: %d heads of %d at position %d need %lld floats of partials, more than the %lld of the static "
+               "scratch (at most %lld positions for this shape)",
+               name, nh, hs, pos, need, NOALLOC_FLOATS, NOALLOC_FLOATS / ((long long)nh * (hs + 4)) * 128);
+  if (h1 == h0) return;
+  float* part = noalloc_partials();
+  if (!part) return;
+  AttArgs a = {};
+  a.out = dptr<float>(out);
+  a.q = dptr<const float>(q);
+  a.kc = dptr<const void>(kc);
+  a.vc = dptr<const void>(vc);
+  a.part = part;
+  a.pos = pos;
+  a.nh = nh;
+  a.nkv = nkv;
+  a.hs = hs;
+  a.h0 = h0;
+  a.h1 = h1;
+  a.nsplit = (int)nsplit;
+  a.split_len = 128;
+  run_attention(name, a, true, false);
+}
+
 // ---- the forward driver's calls (the position in device memory)
 
 // bytes of scratch pllm_attention_dev needs for a cache of capacity positions: the slices' partials, then a count a

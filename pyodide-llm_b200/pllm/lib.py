@@ -86,6 +86,7 @@ SIGNATURES = {
     "pllm_qk_rope_cache": ([U64, U64, U64, U64, U64, U64, U64, U64, I32, U64, U64, I32, I32, I32, I32, F32, I32, U64,
                             I32], None),
     "pllm_attention_scratch_bytes": ([I32, I32, I32, I32], U64),
+    "pllm_attention_f16_noalloc": ([U64, U64, U64, U64, I32, I32, I32, I32, I32, I32], None),
     "pllm_attention_step": ([U64, U64, U64, U64, U64, U64, I32, I32, I32, I32, I32, F32, I32, U64, U64, U64, U64, I32,
                              F32, U64, I32], None),
     "pllm_attention_dev": ([U64, U64, U64, U64, U64, U64, I32, I32, I32, I32, I32, F32, I32, I32], None),
