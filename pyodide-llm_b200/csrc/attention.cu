@@ -95,17 +95,51 @@ __device__ __forceinline__ void norm_rope(float* x, const float* w, const Fuse& 
   }
 }
 
+// tensor-core helpers (float16 caches): ldmatrix fragments and the m16n8k16 product with float32 accumulation
+__device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t r[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// x as the sum of two float16: hi = rn(x), lo = rn(x - hi) (the products of a float16 key or value with both are
+// exact in the float32 accumulation, so the sum keeps x to about 2^-22 of itself)
+__device__ __forceinline__ void split_half(float x, __half& hi, __half& lo) {
+  hi = __float2half_rn(x);
+  lo = __float2half_rn(x - __half2float(hi));
+}
+
 template <bool HALF, int KVM, bool FUSE>
 __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttArgs a, const Fuse f) {
   extern __shared__ __align__(16) uint8_t att_smem[];
   constexpr int E = HALF ? 2 : 4;
+  constexpr int HP = 8;                              // heads padded to the products' n = 8
   const int hs = a.hs;
-  const int rowb = hs * E + 16;                      // a padded row of the tile, bytes
+  const int rowb = hs * E + 16;                      // a padded row of the tile, bytes (16-byte rows, no conflicts)
   uint8_t* sK = att_smem;                            // [TILE][rowb]
   uint8_t* sV = sK + TILE * rowb;                    // [TILE][rowb]
   float* sq = reinterpret_cast<float*>(sV + TILE * rowb);  // [KVM][hs]
   float* sp = sq + KVM * hs;                         // [KVM][TILE] scores, then probabilities
   float* sx = sp + KVM * TILE;                       // [2][hs] (FUSE) this position's key and value
+  __half* sqh = reinterpret_cast<__half*>(sx + 2 * hs);  // [HP][hs] q's high halves (HALF), then its low halves
+  __half* sql = sqh + HP * hs;
+  __half* sph = sql + HP * hs;                       // [HP][TILE] probabilities' high halves, then low halves
+  __half* spl = sph + HP * TILE;
   __shared__ float sM[KVM], sL[KVM], sScale[KVM], red[ATT_WARPS];
   // the position: written by the host before the step's first kernel, so readable before the dependency wait
   const int pos = a.pos_dev ? *a.pos_dev : a.pos;
@@ -116,40 +150,30 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   const int p0 = split * a.split_len;
   const int p1 = min(count, p0 + a.split_len);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t4 = lane & 3;            // an mma fragment's row group and column pair
   const int kvdim = a.nkv * hs, hbase = kvh * KVM;
   const float isq = 1.0f / sqrtf((float)hs);
   const int chunks = hs * E / 16;                    // 16-byte pieces a row
   const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.kc) + (long long)kvh * hs * E;
   const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vc) + (long long)kvh * hs * E;
-  // the tile's keys and values (positions before this token's: not the previous kernel's output), every load issued
-  // before any is used
+  // the tile's keys and values by asynchronous 16-byte copies, all in flight at once (positions before this token's:
+  // not the previous kernel's output); the rows past the tile's length zeroed (a probability of 0 must meet a 0)
   auto load_tile = [&](int t0, int len) {
-    constexpr int PER = 8;
-    for (int base = tid; base < len * chunks; base += ATT_THREADS * PER) {
-      int4 kv[PER], vv[PER];
-#pragma unroll
-      for (int u = 0; u < PER; u++) {
-        const int e = base + u * ATT_THREADS;
-        if (e < len * chunks) {
-          const int t = e / chunks, c = e % chunks;
-          const long long off = (long long)(t0 + t) * kvdim * E + c * 16;
-          kv[u] = *reinterpret_cast<const int4*>(kbase + off);
-          vv[u] = *reinterpret_cast<const int4*>(vbase + off);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < PER; u++) {
-        const int e = base + u * ATT_THREADS;
-        if (e < len * chunks) {
-          const int t = e / chunks, c = e % chunks;
-          *reinterpret_cast<int4*>(sK + t * rowb + c * 16) = kv[u];
-          *reinterpret_cast<int4*>(sV + t * rowb + c * 16) = vv[u];
-        }
+    for (int e = tid; e < TILE * chunks; e += ATT_THREADS) {
+      const int t = e / chunks, c = e % chunks;
+      if (t < len) {
+        const long long off = (long long)(t0 + t) * kvdim * E + c * 16;
+        cp_async16(sK + t * rowb + c * 16, kbase + off);
+        cp_async16(sV + t * rowb + c * 16, vbase + off);
+      } else {
+        *reinterpret_cast<int4*>(sK + t * rowb + c * 16) = make_int4(0, 0, 0, 0);
+        *reinterpret_cast<int4*>(sV + t * rowb + c * 16) = make_int4(0, 0, 0, 0);
       }
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   };
   const int len0 = min(TILE, p1 - p0);
-  if (FUSE) load_tile(p0, len0);  // before the wait: it overlaps the q/k/v product's tail
+  load_tile(p0, len0);  // before the wait: it overlaps the kernel ahead's tail
   pdl_wait();
   for (int e = tid; e < KVM * hs; e += ATT_THREADS) sq[e] = a.q[(long long)hbase * hs + e];
   if (tid < KVM) {
@@ -157,10 +181,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
     sL[tid] = 0.0f;
   }
   const bool holds_pos = FUSE && p1 == count;
+  __syncthreads();
   if (FUSE) {
-    __syncthreads();
     for (int j = 0; j < KVM; j++) norm_rope(sq + j * hs, f.qn, f, hs, pos, true, red);
-    if (holds_pos) {  // this position's key (normalized, turned) and value, into the cache and the tile
+    if (holds_pos) {  // this position's key (normalized, turned) and value, into the cache
       for (int d = tid; d < hs; d += ATT_THREADS) {
         sx[d] = f.k[(long long)kvh * hs + d];
         sx[hs + d] = f.v[(long long)kvh * hs + d];
@@ -168,74 +192,104 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
       __syncthreads();
       norm_rope(sx, f.kn, f, hs, pos, true, red);
       int local = 0;
-      const int t = pos - p0;  // < TILE when the tile is the slice's first
       for (int e = tid; e < 2 * hs; e += ATT_THREADS) {
         const int d = e % hs;
         uint8_t* cache = reinterpret_cast<uint8_t*>(const_cast<void*>(e < hs ? a.kc : a.vc)) + (long long)pos * kvdim * E +
                          ((long long)kvh * hs + d) * E;
-        uint8_t* tile = (e < hs ? sK : sV) + (size_t)(t % TILE) * rowb + d * E;
-        if (HALF) {
-          const uint16_t hb = float_to_half_bits(sx[e], &local);
-          *reinterpret_cast<uint16_t*>(cache) = hb;
-          if (t < TILE) *reinterpret_cast<uint16_t*>(tile) = hb;
-        } else {
-          *reinterpret_cast<float*>(cache) = sx[e];
-          if (t < TILE) *reinterpret_cast<float*>(tile) = sx[e];
-        }
+        if (HALF) *reinterpret_cast<uint16_t*>(cache) = float_to_half_bits(sx[e], &local);
+        else *reinterpret_cast<float*>(cache) = sx[e];
       }
       if (local && f.bad) atomicAdd(f.bad, local);
     }
   }
-  // the running output: this thread's dims d = tid + ATT_THREADS i of every head
-  constexpr int DMAX = 2;  // hs <= 256
+  if (HALF) {  // q as two float16 halves a value, the padded heads zero
+    for (int e = tid; e < HP * hs; e += ATT_THREADS) {
+      const int j = e / hs;
+      __half hi = __float2half_rn(0.0f), lo = hi;
+      if (j < KVM) split_half(sq[e], hi, lo);
+      sqh[e] = hi;
+      sql[e] = lo;
+    }
+    for (int e = tid; e < HP * TILE; e += ATT_THREADS) {
+      sph[e] = __float2half_rn(0.0f);
+      spl[e] = __float2half_rn(0.0f);
+    }
+  }
+  // the running output. HALF: mma fragments of O^T (dims x heads), m-blocks of 16 dims warp, warp + 4, ...;
+  // else a thread a dimension d = tid + ATT_THREADS i of every head
+  constexpr int DMAX = 2;   // hs <= 256
+  constexpr int MBMAX = 4;  // hs / 16 / ATT_WARPS
   float acc[KVM][DMAX];
+  float oc[MBMAX][4];
 #pragma unroll
   for (int j = 0; j < KVM; j++)
 #pragma unroll
     for (int i = 0; i < DMAX; i++) acc[j][i] = 0.0f;
+#pragma unroll
+  for (int m = 0; m < MBMAX; m++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) oc[m][c] = 0.0f;
+  const int nmb = hs / 16;
   for (int t0 = p0; t0 < p1; t0 += TILE) {
     const int len = min(TILE, p1 - t0);
-    if (t0 != p0 || !FUSE) {
+    if (t0 != p0) {
       __syncthreads();  // the previous tile's keys, values and probabilities are no longer read
       load_tile(t0, len);
-      if (holds_pos && pos >= t0 && pos < t0 + len) {  // (a slice longer than a tile: this position's row again)
-        __syncthreads();
-        for (int e = tid; e < 2 * hs; e += ATT_THREADS) {
-          const int d = e % hs;
-          uint8_t* tile = (e < hs ? sK : sV) + (size_t)(pos - t0) * rowb + d * E;
-          int dummy = 0;
-          if (HALF) *reinterpret_cast<uint16_t*>(tile) = float_to_half_bits(sx[e], &dummy);
-          else *reinterpret_cast<float*>(tile) = sx[e];
-        }
-      }
     }
+    cp_async_wait_all();
     __syncthreads();
-    // 2. scores: a thread a (position, head) pair
-    for (int e = tid; e < KVM * TILE; e += ATT_THREADS) {
-      const int t = e % TILE, j = e / TILE;
-      float s = -INFINITY;
-      if (t < len) {
-        const uint8_t* row = sK + t * rowb;
-        const float* qj = sq + j * hs;
-        s = 0.0f;
-        for (int c = 0; c < chunks; c++) {  // 16 bytes of the row at a time: conflict-free across the threads' rows
-          const int4 w = *reinterpret_cast<const int4*>(row + c * 16);
-          const uint32_t u[4] = {(uint32_t)w.x, (uint32_t)w.y, (uint32_t)w.z, (uint32_t)w.w};
-          if (HALF) {
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-              s = fmaf(qj[c * 8 + 2 * k], half_bits_to_float((uint16_t)(u[k] & 0xffffu)), s);
-              s = fmaf(qj[c * 8 + 2 * k + 1], half_bits_to_float((uint16_t)(u[k] >> 16)), s);
-            }
-          } else {
-#pragma unroll
-            for (int k = 0; k < 4; k++) s = fmaf(qj[c * 4 + k], __uint_as_float(u[k]), s);
-          }
-        }
-        s *= isq;
-        if (a.cap > 0.0f) s = a.cap * tanhf(s / a.cap);
+    if (holds_pos && pos >= t0 && pos < t0 + len) {  // this position's row: the fresh key and value
+      for (int e = tid; e < 2 * hs; e += ATT_THREADS) {
+        const int d = e % hs;
+        uint8_t* tile = (e < hs ? sK : sV) + (size_t)(pos - t0) * rowb + d * E;
+        int dummy = 0;
+        if (HALF) *reinterpret_cast<uint16_t*>(tile) = float_to_half_bits(sx[e], &dummy);
+        else *reinterpret_cast<float*>(tile) = sx[e];
       }
-      sp[j * TILE + t] = s;
+      __syncthreads();
+    }
+    // 2. scores
+    if (HALF) {  // a warp 16 positions: S (positions x heads) = K (positions x dims) . q^T, the halves' two products
+      float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const uint8_t* arow = sK + (16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8) * rowb + (lane >> 4) * 16;
+      for (int kk = 0; kk < nmb; kk++) {
+        uint32_t af[4];
+        ldsm_x4(af, arow + kk * 32);
+        const int qo = g * hs + 16 * kk + 2 * t4;
+        mma16816(c, af, *reinterpret_cast<const uint32_t*>(sqh + qo), *reinterpret_cast<const uint32_t*>(sqh + qo + 8));
+        mma16816(c, af, *reinterpret_cast<const uint32_t*>(sql + qo), *reinterpret_cast<const uint32_t*>(sql + qo + 8));
+      }
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        const int t = 16 * warp + g + (r >> 1) * 8, j = 2 * t4 + (r & 1);
+        if (j < KVM) {
+          float v = -INFINITY;
+          if (t < len) {
+            v = c[r] * isq;
+            if (a.cap > 0.0f) v = a.cap * tanhf(v / a.cap);
+          }
+          sp[j * TILE + t] = v;
+        }
+      }
+    } else {  // a thread a (position, head) pair
+      for (int e = tid; e < KVM * TILE; e += ATT_THREADS) {
+        const int t = e % TILE, j = e / TILE;
+        float sc = -INFINITY;
+        if (t < len) {
+          const uint8_t* row = sK + t * rowb;
+          const float* qj = sq + j * hs;
+          sc = 0.0f;
+          for (int c = 0; c < chunks; c++) {
+            const int4 w = *reinterpret_cast<const int4*>(row + c * 16);
+            const uint32_t u[4] = {(uint32_t)w.x, (uint32_t)w.y, (uint32_t)w.z, (uint32_t)w.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) sc = fmaf(qj[c * 4 + k], __uint_as_float(u[k]), sc);
+          }
+          sc *= isq;
+          if (a.cap > 0.0f) sc = a.cap * tanhf(sc / a.cap);
+        }
+        sp[j * TILE + t] = sc;
+      }
     }
     __syncthreads();
     // 3. the online softmax: a warp a head
@@ -248,6 +302,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
       for (int t = lane; t < TILE; t += 32) {
         const float p = t < len ? expf(sp[j * TILE + t] - mnew) : 0.0f;
         sp[j * TILE + t] = p;
+        if (HALF) split_half(p, sph[j * TILE + t], spl[j * TILE + t]);
         l += p;
       }
       l = warp_sum(l);
@@ -259,39 +314,74 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
       }
     }
     __syncthreads();
-    // 4. the weighted values: a thread a dimension
+    // 4. the weighted values
+    if (HALF) {  // O^T (dims x heads) += V^T (dims x positions) . P^T (positions x heads), the halves' two products
+      const float s0 = 2 * t4 < KVM ? sScale[2 * t4] : 1.0f, s1 = 2 * t4 + 1 < KVM ? sScale[2 * t4 + 1] : 1.0f;
+#pragma unroll
+      for (int mi = 0; mi < MBMAX; mi++) {
+        const int mb = warp + ATT_WARPS * mi;
+        if (mb >= nmb) break;
+        oc[mi][0] *= s0;
+        oc[mi][1] *= s1;
+        oc[mi][2] *= s0;
+        oc[mi][3] *= s1;
+        const uint8_t* vrow = sV + ((lane & 7) + ((lane >> 4) & 1) * 8) * rowb + (16 * mb + ((lane >> 3) & 1) * 8) * 2;
+#pragma unroll
+        for (int ks = 0; ks < TILE / 16; ks++) {
+          uint32_t af[4];
+          ldsm_x4_trans(af, vrow + ks * 16 * rowb);
+          const int po = g * TILE + 16 * ks + 2 * t4;
+          mma16816(oc[mi], af, *reinterpret_cast<const uint32_t*>(sph + po), *reinterpret_cast<const uint32_t*>(sph + po + 8));
+          mma16816(oc[mi], af, *reinterpret_cast<const uint32_t*>(spl + po), *reinterpret_cast<const uint32_t*>(spl + po + 8));
+        }
+      }
+    } else {  // a thread a dimension
+#pragma unroll
+      for (int i = 0; i < DMAX; i++) {
+        const int d = tid + ATT_THREADS * i;
+        if (d >= hs) continue;
+#pragma unroll
+        for (int j = 0; j < KVM; j++) acc[j][i] *= sScale[j];
+        for (int t = 0; t < len; t++) {
+          const float v = kv_elem<HALF>(sV + t * rowb, d);
+#pragma unroll
+          for (int j = 0; j < KVM; j++) acc[j][i] = fmaf(sp[j * TILE + t], v, acc[j][i]);
+        }
+      }
+    }
+  }
+  // 5. the slice's output (one slice: the head's output itself)
+  auto put = [&](int j, int d, float v) {
+    const int h = hbase + j;
+    if (j >= KVM || h < a.h0 || h >= a.h1) return;
+    if (nsplit == 1) {
+      a.out[(long long)h * hs + d] = v / sL[j];
+    } else {
+      float* part = a.part + ((long long)h * a.nsplit + split) * (hs + 4);
+      part[d] = v;
+      if (d == 0) {
+        part[hs] = sM[j];
+        part[hs + 1] = sL[j];
+      }
+    }
+  };
+  if (HALF) {
+#pragma unroll
+    for (int mi = 0; mi < MBMAX; mi++) {
+      const int mb = warp + ATT_WARPS * mi;
+      if (mb >= nmb) break;
+      put(2 * t4, 16 * mb + g, oc[mi][0]);
+      put(2 * t4 + 1, 16 * mb + g, oc[mi][1]);
+      put(2 * t4, 16 * mb + g + 8, oc[mi][2]);
+      put(2 * t4 + 1, 16 * mb + g + 8, oc[mi][3]);
+    }
+  } else {
 #pragma unroll
     for (int i = 0; i < DMAX; i++) {
       const int d = tid + ATT_THREADS * i;
       if (d >= hs) continue;
 #pragma unroll
-      for (int j = 0; j < KVM; j++) acc[j][i] *= sScale[j];
-      for (int t = 0; t < len; t++) {
-        const float v = kv_elem<HALF>(sV + t * rowb, d);
-#pragma unroll
-        for (int j = 0; j < KVM; j++) acc[j][i] = fmaf(sp[j * TILE + t], v, acc[j][i]);
-      }
-    }
-  }
-  // 5. the slice's output (one slice: the head's output itself)
-#pragma unroll
-  for (int i = 0; i < DMAX; i++) {
-    const int d = tid + ATT_THREADS * i;
-    if (d >= hs) continue;
-#pragma unroll
-    for (int j = 0; j < KVM; j++) {
-      const int h = hbase + j;
-      if (h < a.h0 || h >= a.h1) continue;
-      if (nsplit == 1) {
-        a.out[(long long)h * hs + d] = acc[j][i] / sL[j];
-      } else {
-        float* part = a.part + ((long long)h * a.nsplit + split) * (hs + 4);
-        part[d] = acc[j][i];
-        if (d == 0) {
-          part[hs] = sM[j];
-          part[hs + 1] = sL[j];
-        }
-      }
+      for (int j = 0; j < KVM; j++) put(j, d, acc[j][i]);
     }
   }
   if (nsplit == 1 || !a.counters) return;
@@ -439,7 +529,8 @@ void run_attention(const char* name, AttArgs a, bool half, bool pdl, const Fuse*
   const size_t rowb = (size_t)a.hs * (half ? 2 : 4) + 16;
   // the scores' room also holds the slices' weights in the combine (kvm * nsplit floats)
   const size_t scores = (size_t)kvm * (a.nsplit > TILE ? a.nsplit : TILE) * 4;
-  const size_t smem = 2 * TILE * rowb + (size_t)kvm * a.hs * 4 + scores + 2 * (size_t)a.hs * 4;
+  const size_t halves = half ? (2 * 8 * (size_t)a.hs + 2 * 8 * TILE) * 2 : 0;
+  const size_t smem = 2 * TILE * rowb + (size_t)kvm * a.hs * 4 + scores + 2 * (size_t)a.hs * 4 + halves;
   const dim3 grid(a.nkv, a.nsplit);
   cudaError_t e = half ? launch_split<true>(a, f, kvm, smem, grid, pdl) : launch_split<false>(a, f, kvm, smem, grid, pdl);
   if (e != cudaSuccess) {
@@ -462,7 +553,7 @@ void run_attention(const char* name, AttArgs a, bool half, bool pdl, const Fuse*
 }
 
 bool check_heads(const char* name, int nh, int nkv, int hs, int h0, int h1) {
-  if (nh <= 0 || nkv <= 0 || nh % nkv || hs <= 0 || hs > 256 || hs % 8 || h0 < 0 || h1 < h0 || h1 > nh) {
+  if (nh <= 0 || nkv <= 0 || nh % nkv || hs <= 0 || hs > 256 || hs % 16 || h0 < 0 || h1 < h0 || h1 > nh) {
     pllm_fail(PLLM_EINVAL, "%s: nh %d nkv %d hs %d heads %d..%d", name, nh, nkv, hs, h0, h1);
     return false;
   }
