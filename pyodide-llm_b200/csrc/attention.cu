@@ -65,36 +65,6 @@ struct Fuse {
   int* bad;             // non-finite keys or values written to a float16 cache are counted here (may be null)
 };
 
-// a head of hs floats in shared memory, normalized (w: null for none) and turned at pos, by the CTA's threads
-__device__ __forceinline__ void norm_rope(float* x, const float* w, const Fuse& f, int hs, int pos, bool turn,
-                                          float* red) {
-  const int tid = threadIdx.x;
-  if (w) {
-    float s = 0.0f;
-    for (int d = tid; d < hs; d += ATT_THREADS) s = fmaf(x[d], x[d], s);
-    s = warp_sum(s);
-    if ((tid & 31) == 0) red[tid >> 5] = s;
-    __syncthreads();
-    float tot = 0.0f;
-    for (int i = 0; i < ATT_WARPS; i++) tot += red[i];
-    const float r = 1.0f / sqrtf(tot / (float)hs + f.eps);
-    __syncthreads();
-    for (int d = tid; d < hs; d += ATT_THREADS) x[d] = w[d] * (r * x[d]);
-    __syncthreads();
-  }
-  if (turn) {
-    const int turned = f.rot > 0 && f.rot < hs ? f.rot : hs;
-    const float* c = f.cos_t + (long long)pos * (hs / 2);
-    const float* sn = f.sin_t + (long long)pos * (hs / 2);
-    for (int i = tid; i < turned / 2; i += ATT_THREADS) {
-      const float v0 = x[2 * i], v1 = x[2 * i + 1];
-      x[2 * i] = v0 * c[i] - v1 * sn[i];
-      x[2 * i + 1] = v0 * sn[i] + v1 * c[i];
-    }
-    __syncthreads();
-  }
-}
-
 // tensor-core helpers (float16 caches): ldmatrix fragments and the m16n8k16 product with float32 accumulation
 __device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -124,6 +94,29 @@ __device__ __forceinline__ void split_half(float x, __half& hi, __half& lo) {
   lo = __float2half_rn(x - __half2float(hi));
 }
 
+// a head of hs floats in shared memory normalized (w: null for none) and turned at pos by one warp (no block-wide
+// barrier: the heads of a CTA go one a warp, side by side)
+__device__ __forceinline__ void norm_rope_warp(float* x, const float* w, const Fuse& f, int hs, int pos) {
+  const int lane = threadIdx.x & 31;
+  if (w) {
+    float s = 0.0f;
+    for (int d = lane; d < hs; d += 32) s = fmaf(x[d], x[d], s);
+    s = warp_sum(s);
+    const float r = 1.0f / sqrtf(s / (float)hs + f.eps);
+    for (int d = lane; d < hs; d += 32) x[d] = w[d] * (r * x[d]);
+    __syncwarp();
+  }
+  const int turned = f.rot > 0 && f.rot < hs ? f.rot : hs;
+  const float* c = f.cos_t + (long long)pos * (hs / 2);
+  const float* sn = f.sin_t + (long long)pos * (hs / 2);
+  for (int i = lane; i < turned / 2; i += 32) {
+    const float v0 = x[2 * i], v1 = x[2 * i + 1];
+    x[2 * i] = v0 * c[i] - v1 * sn[i];
+    x[2 * i + 1] = v0 * sn[i] + v1 * c[i];
+  }
+  __syncwarp();
+}
+
 template <bool HALF, int KVM, bool FUSE>
 __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttArgs a, const Fuse f) {
   extern __shared__ __align__(16) uint8_t att_smem[];
@@ -131,16 +124,16 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   constexpr int HP = 8;                              // heads padded to the products' n = 8
   const int hs = a.hs;
   const int rowb = hs * E + 16;                      // a padded row of the tile, bytes (16-byte rows, no conflicts)
-  uint8_t* sK = att_smem;                            // [TILE][rowb]
-  uint8_t* sV = sK + TILE * rowb;                    // [TILE][rowb]
-  float* sq = reinterpret_cast<float*>(sV + TILE * rowb);  // [KVM][hs]
+  const int tileb = TILE * rowb;
+  uint8_t* ring = att_smem;                          // [2 buffers][K tile, V tile]: 4 x tileb bytes
+  float* sq = reinterpret_cast<float*>(ring + 4 * tileb);  // [KVM][hs]
   float* sp = sq + KVM * hs;                         // [KVM][TILE] scores, then probabilities
   float* sx = sp + KVM * TILE;                       // [2][hs] (FUSE) this position's key and value
   __half* sqh = reinterpret_cast<__half*>(sx + 2 * hs);  // [HP][hs] q's high halves (HALF), then its low halves
   __half* sql = sqh + HP * hs;
   __half* sph = sql + HP * hs;                       // [HP][TILE] probabilities' high halves, then low halves
   __half* spl = sph + HP * TILE;
-  __shared__ float sM[KVM], sL[KVM], sScale[KVM], red[ATT_WARPS];
+  __shared__ float sM[KVM], sL[KVM], sScale[KVM];
   // the position: written by the host before the step's first kernel, so readable before the dependency wait
   const int pos = a.pos_dev ? *a.pos_dev : a.pos;
   const int count = pos + 1;
@@ -156,9 +149,12 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   const int chunks = hs * E / 16;                    // 16-byte pieces a row
   const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.kc) + (long long)kvh * hs * E;
   const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vc) + (long long)kvh * hs * E;
-  // the tile's keys and values by asynchronous 16-byte copies, all in flight at once (positions before this token's:
-  // not the previous kernel's output); the rows past the tile's length zeroed (a probability of 0 must meet a 0)
-  auto load_tile = [&](int t0, int len) {
+  // a tile's keys and values by asynchronous 16-byte copies, all in flight at once (positions before this token's:
+  // not the previous kernel's output); rows past the tile's length zeroed (a probability of 0 must meet a 0)
+  auto load_tile = [&](int t0, int buf) {
+    uint8_t* sK = ring + (size_t)(2 * buf) * tileb;
+    uint8_t* sV = sK + tileb;
+    const int len = min(TILE, p1 - t0);
     for (int e = tid; e < TILE * chunks; e += ATT_THREADS) {
       const int t = e / chunks, c = e % chunks;
       if (t < len) {
@@ -172,8 +168,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  const int len0 = min(TILE, p1 - p0);
-  load_tile(p0, len0);  // before the wait: it overlaps the kernel ahead's tail
+  load_tile(p0, 0);  // before the wait: it overlaps the kernel ahead's tail
+  if (p0 + TILE < p1) load_tile(p0 + TILE, 1);
   pdl_wait();
   for (int e = tid; e < KVM * hs; e += ATT_THREADS) sq[e] = a.q[(long long)hbase * hs + e];
   if (tid < KVM) {
@@ -181,16 +177,19 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
     sL[tid] = 0.0f;
   }
   const bool holds_pos = FUSE && p1 == count;
+  if (FUSE && holds_pos)
+    for (int d = tid; d < hs; d += ATT_THREADS) {
+      sx[d] = f.k[(long long)kvh * hs + d];
+      sx[hs + d] = f.v[(long long)kvh * hs + d];
+    }
   __syncthreads();
-  if (FUSE) {
-    for (int j = 0; j < KVM; j++) norm_rope(sq + j * hs, f.qn, f, hs, pos, true, red);
-    if (holds_pos) {  // this position's key (normalized, turned) and value, into the cache
-      for (int d = tid; d < hs; d += ATT_THREADS) {
-        sx[d] = f.k[(long long)kvh * hs + d];
-        sx[hs + d] = f.v[(long long)kvh * hs + d];
-      }
-      __syncthreads();
-      norm_rope(sx, f.kn, f, hs, pos, true, red);
+  if (FUSE) {  // the heads' norms and RoPE, a warp a head; the key's too where this slice holds the position
+    for (int j = warp; j < KVM + (holds_pos ? 1 : 0); j += ATT_WARPS) {
+      if (j < KVM) norm_rope_warp(sq + j * hs, f.qn, f, hs, pos);
+      else norm_rope_warp(sx, f.kn, f, hs, pos);
+    }
+    __syncthreads();
+    if (holds_pos) {  // this position's key and value into the cache
       int local = 0;
       for (int e = tid; e < 2 * hs; e += ATT_THREADS) {
         const int d = e % hs;
@@ -230,13 +229,14 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
 #pragma unroll
     for (int c = 0; c < 4; c++) oc[m][c] = 0.0f;
   const int nmb = hs / 16;
-  for (int t0 = p0; t0 < p1; t0 += TILE) {
+  int buf = 0;
+  for (int t0 = p0; t0 < p1; t0 += TILE, buf ^= 1) {
     const int len = min(TILE, p1 - t0);
-    if (t0 != p0) {
-      __syncthreads();  // the previous tile's keys, values and probabilities are no longer read
-      load_tile(t0, len);
-    }
-    cp_async_wait_all();
+    uint8_t* sK = ring + (size_t)(2 * buf) * tileb;
+    uint8_t* sV = sK + tileb;
+    // this tile's copies are done when at most the next tile's group is still in flight
+    if (t0 + TILE < p1) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else cp_async_wait_all();
     __syncthreads();
     if (holds_pos && pos >= t0 && pos < t0 + len) {  // this position's row: the fresh key and value
       for (int e = tid; e < 2 * hs; e += ATT_THREADS) {
@@ -349,6 +349,11 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
         }
       }
     }
+    // the tile after next into this buffer, once every warp is done with it
+    if (t0 + 2 * TILE < p1) {
+      __syncthreads();
+      load_tile(t0 + 2 * TILE, buf);
+    }
   }
   // 5. the slice's output (one slice: the head's output itself)
   auto put = [&](int j, int d, float v) {
@@ -386,7 +391,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   }
   if (nsplit == 1 || !a.counters) return;
   // 6. the last slice of this kv head to finish combines every slice's partials (no CTA waits for another: the
-  // others are done when the count reaches nsplit), and sets the count back to zero for the next call
+  // others are done when the count reaches nsplit), and sets the count back to zero for the next call. The partials
+  // of the kv head's query heads are contiguous: copied into shared memory by asynchronous 16-byte copies, as many
+  // slices at once as the tile ring holds (every copy of a chunk in flight together).
   __shared__ int last;
   __threadfence();
   __syncthreads();
@@ -394,65 +401,56 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   __syncthreads();
   if (!last) return;
   __threadfence();
-  // the slices' maxima and sums first (all loads in flight), then their weighted values in chunks of slices staged
-  // in shared memory (the tile's room), each chunk's loads all issued before any is used
+  const int row = hs + 4;                                    // floats a slice's partial (16-byte rows)
+  const int room = (int)((4 * (size_t)tileb) / ((size_t)KVM * row * 4));  // slices a chunk
+  float* stage = reinterpret_cast<float*>(ring);
   float* sw = sp;  // [KVM][nsplit] weights exp(m_s - M), in the scores' room (the host sizes it for nsplit)
-  for (int e = tid; e < KVM * nsplit; e += ATT_THREADS) {
-    const int j = e / nsplit, s2 = e % nsplit;
-    sw[e] = __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * (hs + 4) + hs);
-  }
-  __syncthreads();
-  for (int j = warp; j < KVM; j += ATT_WARPS) {
-    float M = -INFINITY;
-    for (int s2 = lane; s2 < nsplit; s2 += 32) M = fmaxf(M, sw[j * nsplit + s2]);
-    M = warp_max(M);
-    float L = 0.0f;
-    for (int s2 = lane; s2 < nsplit; s2 += 32) {
-      const float w = expf(sw[j * nsplit + s2] - M);
-      sw[j * nsplit + s2] = w;
-      L = fmaf(__ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * (hs + 4) + hs + 1), w, L);
-    }
-    L = warp_sum(L);
-    if (lane == 0) sL[j] = L;
-  }
   float o[KVM][DMAX];
 #pragma unroll
   for (int j = 0; j < KVM; j++)
 #pragma unroll
     for (int i = 0; i < DMAX; i++) o[j][i] = 0.0f;
-  const int row = hs + 4;                                    // floats a slice's partial (16-byte rows)
-  const int room = (int)((2 * TILE * rowb) / (KVM * row * 4));  // slices a chunk (sK and sV's bytes)
-  float* stage = reinterpret_cast<float*>(sK);
   for (int c0 = 0; c0 < nsplit; c0 += room) {
     const int cn = min(room, nsplit - c0);
-    __syncthreads();  // the previous chunk is read; sw and sL are written
-    const int per = cn * row;                                // floats a head's chunk (contiguous in part)
-    const int per4 = per / 4;
-    constexpr int PER = 16;                                  // 16-byte loads a thread in flight
-    for (int base = tid; base < KVM * per4; base += ATT_THREADS * PER) {
-      float4 v[PER];
-#pragma unroll
-      for (int u = 0; u < PER; u++) {
-        const int e = base + u * ATT_THREADS;
-        if (e < KVM * per4) {
-          const int j = e / per4, f4 = e % per4;
-          v[u] = __ldcg(reinterpret_cast<const float4*>(a.part + ((long long)(hbase + j) * a.nsplit + c0) * row) + f4);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < PER; u++) {
-        const int e = base + u * ATT_THREADS;
-        if (e < KVM * per4) reinterpret_cast<float4*>(stage)[e] = v[u];
-      }
+    const int per4 = cn * row / 4;                           // 16-byte pieces a head's chunk
+    __syncthreads();  // the previous chunk is read
+    for (int e = tid; e < KVM * per4; e += ATT_THREADS) {
+      const int j = e / per4, f4 = e % per4;
+      cp_async16(stage + 4 * e, a.part + ((long long)(hbase + j) * a.nsplit + c0) * row + 4 * f4);
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    cp_async_wait_all();
     __syncthreads();
+    if (c0 == 0) {  // the maxima and sums of every slice (the first chunk holds them when room >= nsplit; else from L2)
+      for (int j = warp; j < KVM; j += ATT_WARPS) {
+        float M = -INFINITY;
+        for (int s2 = lane; s2 < nsplit; s2 += 32) {
+          const float m = s2 < cn ? stage[(j * cn + s2) * row + hs]
+                                  : __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * row + hs);
+          sw[j * nsplit + s2] = m;
+          M = fmaxf(M, m);
+        }
+        M = warp_max(M);
+        float Ls = 0.0f;
+        for (int s2 = lane; s2 < nsplit; s2 += 32) {
+          const float w = expf(sw[j * nsplit + s2] - M);
+          sw[j * nsplit + s2] = w;
+          const float l = s2 < cn ? stage[(j * cn + s2) * row + hs + 1]
+                                  : __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * row + hs + 1);
+          Ls = fmaf(l, w, Ls);
+        }
+        Ls = warp_sum(Ls);
+        if (lane == 0) sL[j] = Ls;
+      }
+      __syncthreads();
+    }
 #pragma unroll
     for (int i = 0; i < DMAX; i++) {
       const int d = tid + ATT_THREADS * i;
       if (d >= hs) continue;
 #pragma unroll
       for (int j = 0; j < KVM; j++)
-        for (int s2 = 0; s2 < cn; s2++) o[j][i] = fmaf(stage[j * per + s2 * row + d], sw[j * nsplit + c0 + s2], o[j][i]);
+        for (int s2 = 0; s2 < cn; s2++) o[j][i] = fmaf(stage[(j * cn + s2) * row + d], sw[j * nsplit + c0 + s2], o[j][i]);
     }
   }
 #pragma unroll
@@ -530,7 +528,7 @@ void run_attention(const char* name, AttArgs a, bool half, bool pdl, const Fuse*
   // the scores' room also holds the slices' weights in the combine (kvm * nsplit floats)
   const size_t scores = (size_t)kvm * (a.nsplit > TILE ? a.nsplit : TILE) * 4;
   const size_t halves = half ? (2 * 8 * (size_t)a.hs + 2 * 8 * TILE) * 2 : 0;
-  const size_t smem = 2 * TILE * rowb + (size_t)kvm * a.hs * 4 + scores + 2 * (size_t)a.hs * 4 + halves;
+  const size_t smem = 4 * TILE * rowb + (size_t)kvm * a.hs * 4 + scores + 2 * (size_t)a.hs * 4 + halves;
   const dim3 grid(a.nkv, a.nsplit);
   cudaError_t e = half ? launch_split<true>(a, f, kvm, smem, grid, pdl) : launch_split<false>(a, f, kvm, smem, grid, pdl);
   if (e != cudaSuccess) {

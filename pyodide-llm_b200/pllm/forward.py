@@ -116,7 +116,7 @@ def synthetic_host_weights(cfg, seed=0, std=0.02):
 class Engine:
     """One model's forward pass on the current device."""
 
-    SPLIT = 64  # positions a slice of the split-KV attention (one tile of keys and values a CTA)
+    SPLIT = 128  # positions a slice of the split-KV attention (two tiles of 64 a CTA, double-buffered)
 
     def __init__(self, cfg, host=None, seed=0, device=0, graphs=True, pdl=True):
         init(device)
