@@ -108,8 +108,9 @@ def test_qwen3_8b_shape_matches_oracle(layers):
     synthetic weights, against the oracle's forward on the same weights, at the full widths with two layers and with
     all 36. Measured: where no quantize_x input lands across a rounding boundary the logits agree to ~4e-7; one that
     does flips one int8 activation, the next quantization then differs in ~160 of its 12,288 bytes, and the logits
-    move by ~5e-3 (two layers) to ~5e-2 (36 random layers). So the line is the reference's own for its GPU int8 path
-    against its CPU path: 2e-2 of the largest logit (36 layers: or the same greedy token)."""
+    move by ~5e-3 (two layers) to ~6e-2 (36 random layers, where the greedy token can change). So the line is the
+    reference's own for its GPU int8 path against its CPU path, 2e-2 of the largest logit, at two layers; at 36 a
+    relative distance of 0.1 (a fault moves the logits by their own order)."""
     from pllm.forward import QWEN3_8B
     from dataclasses import replace
     cfg = replace(QWEN3_8B, seq_len=64, layers=layers)
@@ -126,6 +127,6 @@ def test_qwen3_8b_shape_matches_oracle(layers):
               f"max-abs / max|logit| {peak:.2e}, argmax {np.argmax(got)} / {np.argmax(want)}")
         if layers <= 2:
             assert rel <= 2e-2 and peak <= 2e-2, (pos, rel, peak)
-        else:
-            assert peak <= 2e-2 or np.argmax(got) == np.argmax(want), (pos, rel, peak)
+        else:  # a fault (a matrix of another layer, a wrong scale) moves them by the order of the logits themselves
+            assert rel <= 0.1, (pos, rel, peak)
     eng.close()
