@@ -6,9 +6,11 @@
 // float16 bits halves.ts writes. Grouped-query: q head h reads kv head h / (nh / nkv).
 //
 // B200 form: split-KV ("flash decoding"). A CTA takes one kv head and a slice of the positions for all of that head's
-// query heads (the keys and values of the slice are read once for kvMul heads): scores in shared memory, a softmax
-// of the slice (its max and sum), and the weighted values. A second small kernel combines the slices' partial
-// results (max, sum, weighted values) per head. With one slice the first kernel writes the output itself.
+// query heads (the keys and values of the slice are read once for kvMul heads) and makes the slice's partial result
+// (max, sum, weighted values a head): float16 caches on the tensor cores, a warp per 16-position chunk with its own
+// online softmax; float32 caches by scalar float32 products over 64-position tiles. The last CTA of a kv head to
+// finish combines the slices (the forward driver's calls), or a second small kernel does (the registry's calls).
+// With one slice the first kernel writes the output itself.
 // The numbers differ from the reference's in the order of the float32 sums and in exp (CUDA's expf in place of the
 // reference's table-free one): the outputs agree within float32 rounding (the tests hold them to 1e-5 relative).
 //
@@ -34,19 +36,6 @@ struct AttArgs {
   int* counters;        // [nkv] slices done, zero between calls; null: a second kernel combines the slices
 };
 
-
-// grid (nkv, nsplit): one kv head's slice of positions for its KVM query heads. The slice is taken TILE positions at
-// a time: every thread first issues its 16-byte loads of the tile's keys and values (all of them in flight at once),
-// into shared memory (rows padded by 16 bytes: conflict-free 16-byte reads of a row by consecutive threads), then the
-// scores (a thread a position and head pair), an online softmax of the slice (running max and sum, the partial
-// output rescaled), and the weighted values (a thread a head dimension).
-constexpr int TILE = 64;
-
-template <bool HALF>
-__device__ __forceinline__ float kv_elem(const uint8_t* row, int d) {
-  if (HALF) return half_bits_to_float(reinterpret_cast<const uint16_t*>(row)[d]);
-  return reinterpret_cast<const float*>(row)[d];
-}
 
 // What the forward driver's attention does before it reads the cache (FUSE): the per-head RMSNorm of q and k
 // (Qwen3's q_norm / k_norm, forward/attention.ts:140-143), RoPE at the position (kernels/kernel/attention.ts:7-20
@@ -94,8 +83,97 @@ __device__ __forceinline__ void split_half(float x, __half& hi, __half& lo) {
   lo = __float2half_rn(x - __half2float(hi));
 }
 
-// a head of hs floats in shared memory normalized (w: null for none) and turned at pos by one warp (no block-wide
-// barrier: the heads of a CTA go one a warp, side by side)
+__device__ __forceinline__ uint32_t lds32(const __half* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// The last slice of a kv head to finish combines every slice's partials (no CTA waits for another: the others are
+// done when the count reaches nsplit) and sets the count back to zero for the next call. The partials of the kv
+// head's query heads are contiguous: copied into shared memory (stage, stage_bytes) by asynchronous 16-byte copies,
+// as many slices at once as it holds (every copy of a chunk in flight together). sw: KVM x nsplit floats for the
+// slices' weights exp(m_s - M); sL: KVM floats.
+template <int KVM, int THREADS>
+__device__ __forceinline__ void combine_slices(const AttArgs& a, int kvh, int nsplit, uint8_t* stage_mem,
+                                               size_t stage_bytes, float* sw, float* sL) {
+  __shared__ int last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __syncthreads();  // every partial of this CTA is written; one fence orders them before the count (cumulativity)
+  if (tid == 0) {
+    __threadfence();
+    last = atomicAdd(&a.counters[kvh], 1) == nsplit - 1;
+    __threadfence();
+  }
+  __syncthreads();
+  if (!last) return;
+  const int hs = a.hs, hbase = kvh * KVM;
+  const int row = hs + 4;  // floats a slice's partial (16-byte rows)
+  const int room = (int)(stage_bytes / ((size_t)KVM * row * 4));
+  float* stage = reinterpret_cast<float*>(stage_mem);
+  constexpr int PMAX = KVM * 256 / THREADS;  // (head, dimension) pairs a thread (hs <= 256)
+  float o[PMAX];
+#pragma unroll
+  for (int k = 0; k < PMAX; k++) o[k] = 0.0f;
+  for (int c0 = 0; c0 < nsplit; c0 += room) {
+    const int cn = min(room, nsplit - c0);
+    const int per4 = cn * row / 4;  // 16-byte pieces a head's chunk
+    __syncthreads();                // the previous chunk is read
+    for (int e = tid; e < KVM * per4; e += THREADS) {
+      const int j = e / per4, f4 = e % per4;
+      cp_async16(stage + 4 * e, a.part + ((long long)(hbase + j) * a.nsplit + c0) * row + 4 * f4);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    cp_async_wait_all();
+    __syncthreads();
+    if (c0 == 0) {  // the maxima and sums of every slice (the first chunk holds them when room >= nsplit; else L2)
+      for (int j = warp; j < KVM; j += THREADS / 32) {
+        float M = -INFINITY;
+        for (int s2 = lane; s2 < nsplit; s2 += 32) {
+          const float m = s2 < cn ? stage[(j * cn + s2) * row + hs]
+                                  : __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * row + hs);
+          sw[j * nsplit + s2] = m;
+          M = fmaxf(M, m);
+        }
+        M = warp_max(M);
+        float Ls = 0.0f;
+        for (int s2 = lane; s2 < nsplit; s2 += 32) {
+          const float w = expf(sw[j * nsplit + s2] - M);
+          sw[j * nsplit + s2] = w;
+          const float l = s2 < cn ? stage[(j * cn + s2) * row + hs + 1]
+                                  : __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * row + hs + 1);
+          Ls = fmaf(l, w, Ls);
+        }
+        Ls = warp_sum(Ls);
+        if (lane == 0) sL[j] = Ls;
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int k = 0; k < PMAX; k++) {
+      const int e = tid + THREADS * k;
+      if (e >= KVM * hs) break;
+      const int j = e / hs, d = e % hs;
+      float acc = o[k];
+      for (int s2 = 0; s2 < cn; s2++) acc = fmaf(stage[(j * cn + s2) * row + d], sw[j * nsplit + c0 + s2], acc);
+      o[k] = acc;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < PMAX; k++) {
+    const int e = tid + THREADS * k;
+    if (e >= KVM * hs) break;
+    const int j = e / hs, d = e % hs, h = hbase + j;
+    if (h >= a.h0 && h < a.h1) a.out[(long long)h * hs + d] = o[k] / sL[j];
+  }
+  if (tid == 0) a.counters[kvh] = 0;
+}
+
+// ---- float32 caches
+// grid (nkv, nsplit): one kv head's slice of positions for its KVM query heads, taken TILE positions at a time: every
+// thread first issues its 16-byte copies of the tile's keys and values (all of them in flight at once) into shared
+// memory (rows padded by 16 bytes: conflict-free 16-byte reads of a row by consecutive threads), then the scores (a
+// thread a position and head pair), an online softmax of the slice (running max and sum, the partial output
+// rescaled), and the weighted values (a thread a head dimension).
+constexpr int TILE = 64;
+
+// a head of hs floats in shared memory normalized (w: null for none) and turned at pos by one warp
 __device__ __forceinline__ void norm_rope_warp(float* x, const float* w, const Fuse& f, int hs, int pos) {
   const int lane = threadIdx.x & 31;
   if (w) {
@@ -117,23 +195,18 @@ __device__ __forceinline__ void norm_rope_warp(float* x, const float* w, const F
   __syncwarp();
 }
 
-template <bool HALF, int KVM, bool FUSE>
-__global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttArgs a, const Fuse f) {
+template <int KVM, bool FUSE>
+__global__ void __launch_bounds__(ATT_THREADS) attention_f32_kernel(const AttArgs a, const Fuse f) {
   extern __shared__ __align__(16) uint8_t att_smem[];
-  constexpr int E = HALF ? 2 : 4;
-  constexpr int HP = 8;                              // heads padded to the products' n = 8
   const int hs = a.hs;
-  const int rowb = hs * E + 16;                      // a padded row of the tile, bytes (16-byte rows, no conflicts)
+  const int rowb = hs * 4 + 16;                      // a padded row of the tile, bytes
   const int tileb = TILE * rowb;
   uint8_t* ring = att_smem;                          // [2 buffers][K tile, V tile]: 4 x tileb bytes
   float* sq = reinterpret_cast<float*>(ring + 4 * tileb);  // [KVM][hs]
-  float* sp = sq + KVM * hs;                         // [KVM][TILE] scores, then probabilities
-  float* sx = sp + KVM * TILE;                       // [2][hs] (FUSE) this position's key and value
-  __half* sqh = reinterpret_cast<__half*>(sx + 2 * hs);  // [HP][hs] q's high halves (HALF), then its low halves
-  __half* sql = sqh + HP * hs;
-  __half* sph = sql + HP * hs;                       // [HP][TILE] probabilities' high halves, then low halves
-  __half* spl = sph + HP * TILE;
+  float* sx = sq + KVM * hs;                         // [2][hs] (FUSE) this position's key and value
+  float* sp = sx + 2 * hs;                           // [KVM][TILE] scores, then probabilities; the combine's weights
   __shared__ float sM[KVM], sL[KVM], sScale[KVM];
+  pdl_launch_dependents();  // the next kernel waits for this one's completion; its CTAs may take the SMs this one leaves
   // the position: written by the host before the step's first kernel, so readable before the dependency wait
   const int pos = a.pos_dev ? *a.pos_dev : a.pos;
   const int count = pos + 1;
@@ -143,12 +216,11 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
   const int p0 = split * a.split_len;
   const int p1 = min(count, p0 + a.split_len);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, t4 = lane & 3;            // an mma fragment's row group and column pair
   const int kvdim = a.nkv * hs, hbase = kvh * KVM;
   const float isq = 1.0f / sqrtf((float)hs);
-  const int chunks = hs * E / 16;                    // 16-byte pieces a row
-  const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.kc) + (long long)kvh * hs * E;
-  const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vc) + (long long)kvh * hs * E;
+  const int chunks = hs / 4;                         // 16-byte pieces a row
+  const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.kc) + (long long)kvh * hs * 4;
+  const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vc) + (long long)kvh * hs * 4;
   // a tile's keys and values by asynchronous 16-byte copies, all in flight at once (positions before this token's:
   // not the previous kernel's output); rows past the tile's length zeroed (a probability of 0 must meet a 0)
   auto load_tile = [&](int t0, int buf) {
@@ -158,7 +230,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
     for (int e = tid; e < TILE * chunks; e += ATT_THREADS) {
       const int t = e / chunks, c = e % chunks;
       if (t < len) {
-        const long long off = (long long)(t0 + t) * kvdim * E + c * 16;
+        const long long off = (long long)(t0 + t) * kvdim * 4 + c * 16;
         cp_async16(sK + t * rowb + c * 16, kbase + off);
         cp_async16(sV + t * rowb + c * 16, vbase + off);
       } else {
@@ -189,46 +261,15 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
       else norm_rope_warp(sx, f.kn, f, hs, pos);
     }
     __syncthreads();
-    if (holds_pos) {  // this position's key and value into the cache
-      int local = 0;
+    if (holds_pos)  // this position's key and value into the cache
       for (int e = tid; e < 2 * hs; e += ATT_THREADS) {
-        const int d = e % hs;
-        uint8_t* cache = reinterpret_cast<uint8_t*>(const_cast<void*>(e < hs ? a.kc : a.vc)) + (long long)pos * kvdim * E +
-                         ((long long)kvh * hs + d) * E;
-        if (HALF) *reinterpret_cast<uint16_t*>(cache) = float_to_half_bits(sx[e], &local);
-        else *reinterpret_cast<float*>(cache) = sx[e];
+        float* cache = reinterpret_cast<float*>(const_cast<void*>(e < hs ? a.kc : a.vc));
+        cache[(long long)pos * kvdim + (long long)kvh * hs + e % hs] = sx[e];
       }
-      if (local && f.bad) atomicAdd(f.bad, local);
-    }
   }
-  if (HALF) {  // q as two float16 halves a value, the padded heads zero
-    for (int e = tid; e < HP * hs; e += ATT_THREADS) {
-      const int j = e / hs;
-      __half hi = __float2half_rn(0.0f), lo = hi;
-      if (j < KVM) split_half(sq[e], hi, lo);
-      sqh[e] = hi;
-      sql[e] = lo;
-    }
-    for (int e = tid; e < HP * TILE; e += ATT_THREADS) {
-      sph[e] = __float2half_rn(0.0f);
-      spl[e] = __float2half_rn(0.0f);
-    }
-  }
-  // the running output. HALF: mma fragments of O^T (dims x heads), m-blocks of 16 dims warp, warp + 4, ...;
-  // else a thread a dimension d = tid + ATT_THREADS i of every head
-  constexpr int DMAX = 2;   // hs <= 256
-  constexpr int MBMAX = 4;  // hs / 16 / ATT_WARPS
-  float acc[KVM][DMAX];
-  float oc[MBMAX][4];
+  float acc[KVM][2];  // a thread a dimension d = tid + ATT_THREADS i of every head (hs <= 256)
 #pragma unroll
-  for (int j = 0; j < KVM; j++)
-#pragma unroll
-    for (int i = 0; i < DMAX; i++) acc[j][i] = 0.0f;
-#pragma unroll
-  for (int m = 0; m < MBMAX; m++)
-#pragma unroll
-    for (int c = 0; c < 4; c++) oc[m][c] = 0.0f;
-  const int nmb = hs / 16;
+  for (int j = 0; j < KVM; j++) acc[j][0] = acc[j][1] = 0.0f;
   int buf = 0;
   for (int t0 = p0; t0 < p1; t0 += TILE, buf ^= 1) {
     const int len = min(TILE, p1 - t0);
@@ -239,60 +280,32 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
     else cp_async_wait_all();
     __syncthreads();
     if (holds_pos && pos >= t0 && pos < t0 + len) {  // this position's row: the fresh key and value
-      for (int e = tid; e < 2 * hs; e += ATT_THREADS) {
-        const int d = e % hs;
-        uint8_t* tile = (e < hs ? sK : sV) + (size_t)(pos - t0) * rowb + d * E;
-        int dummy = 0;
-        if (HALF) *reinterpret_cast<uint16_t*>(tile) = float_to_half_bits(sx[e], &dummy);
-        else *reinterpret_cast<float*>(tile) = sx[e];
-      }
+      for (int e = tid; e < 2 * hs; e += ATT_THREADS)
+        reinterpret_cast<float*>((e < hs ? sK : sV) + (size_t)(pos - t0) * rowb)[e % hs] = sx[e];
       __syncthreads();
     }
-    // 2. scores
-    if (HALF) {  // a warp 16 positions: S (positions x heads) = K (positions x dims) . q^T, the halves' two products
-      float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      const uint8_t* arow = sK + (16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8) * rowb + (lane >> 4) * 16;
-      for (int kk = 0; kk < nmb; kk++) {
-        uint32_t af[4];
-        ldsm_x4(af, arow + kk * 32);
-        const int qo = g * hs + 16 * kk + 2 * t4;
-        mma16816(c, af, *reinterpret_cast<const uint32_t*>(sqh + qo), *reinterpret_cast<const uint32_t*>(sqh + qo + 8));
-        mma16816(c, af, *reinterpret_cast<const uint32_t*>(sql + qo), *reinterpret_cast<const uint32_t*>(sql + qo + 8));
-      }
-#pragma unroll
-      for (int r = 0; r < 4; r++) {
-        const int t = 16 * warp + g + (r >> 1) * 8, j = 2 * t4 + (r & 1);
-        if (j < KVM) {
-          float v = -INFINITY;
-          if (t < len) {
-            v = c[r] * isq;
-            if (a.cap > 0.0f) v = a.cap * tanhf(v / a.cap);
-          }
-          sp[j * TILE + t] = v;
+    // scores: a thread a (position, head) pair
+    for (int e = tid; e < KVM * TILE; e += ATT_THREADS) {
+      const int t = e % TILE, j = e / TILE;
+      float sc = -INFINITY;
+      if (t < len) {
+        const uint8_t* row = sK + t * rowb;
+        const float* qj = sq + j * hs;
+        sc = 0.0f;
+        for (int c = 0; c < chunks; c++) {
+          const float4 w = *reinterpret_cast<const float4*>(row + c * 16);
+          sc = fmaf(qj[c * 4], w.x, sc);
+          sc = fmaf(qj[c * 4 + 1], w.y, sc);
+          sc = fmaf(qj[c * 4 + 2], w.z, sc);
+          sc = fmaf(qj[c * 4 + 3], w.w, sc);
         }
+        sc *= isq;
+        if (a.cap > 0.0f) sc = a.cap * tanhf(sc / a.cap);
       }
-    } else {  // a thread a (position, head) pair
-      for (int e = tid; e < KVM * TILE; e += ATT_THREADS) {
-        const int t = e % TILE, j = e / TILE;
-        float sc = -INFINITY;
-        if (t < len) {
-          const uint8_t* row = sK + t * rowb;
-          const float* qj = sq + j * hs;
-          sc = 0.0f;
-          for (int c = 0; c < chunks; c++) {
-            const int4 w = *reinterpret_cast<const int4*>(row + c * 16);
-            const uint32_t u[4] = {(uint32_t)w.x, (uint32_t)w.y, (uint32_t)w.z, (uint32_t)w.w};
-#pragma unroll
-            for (int k = 0; k < 4; k++) sc = fmaf(qj[c * 4 + k], __uint_as_float(u[k]), sc);
-          }
-          sc *= isq;
-          if (a.cap > 0.0f) sc = a.cap * tanhf(sc / a.cap);
-        }
-        sp[j * TILE + t] = sc;
-      }
+      sp[j * TILE + t] = sc;
     }
     __syncthreads();
-    // 3. the online softmax: a warp a head
+    // the online softmax: a warp a head
     for (int j = warp; j < KVM; j += ATT_WARPS) {
       float m = -INFINITY;
       for (int t = lane; t < len; t += 32) m = fmaxf(m, sp[j * TILE + t]);
@@ -302,7 +315,6 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
       for (int t = lane; t < TILE; t += 32) {
         const float p = t < len ? expf(sp[j * TILE + t] - mnew) : 0.0f;
         sp[j * TILE + t] = p;
-        if (HALF) split_half(p, sph[j * TILE + t], spl[j * TILE + t]);
         l += p;
       }
       l = warp_sum(l);
@@ -314,39 +326,17 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
       }
     }
     __syncthreads();
-    // 4. the weighted values
-    if (HALF) {  // O^T (dims x heads) += V^T (dims x positions) . P^T (positions x heads), the halves' two products
-      const float s0 = 2 * t4 < KVM ? sScale[2 * t4] : 1.0f, s1 = 2 * t4 + 1 < KVM ? sScale[2 * t4 + 1] : 1.0f;
+    // the weighted values: a thread a dimension
 #pragma unroll
-      for (int mi = 0; mi < MBMAX; mi++) {
-        const int mb = warp + ATT_WARPS * mi;
-        if (mb >= nmb) break;
-        oc[mi][0] *= s0;
-        oc[mi][1] *= s1;
-        oc[mi][2] *= s0;
-        oc[mi][3] *= s1;
-        const uint8_t* vrow = sV + ((lane & 7) + ((lane >> 4) & 1) * 8) * rowb + (16 * mb + ((lane >> 3) & 1) * 8) * 2;
+    for (int i = 0; i < 2; i++) {
+      const int d = tid + ATT_THREADS * i;
+      if (d >= hs) continue;
 #pragma unroll
-        for (int ks = 0; ks < TILE / 16; ks++) {
-          uint32_t af[4];
-          ldsm_x4_trans(af, vrow + ks * 16 * rowb);
-          const int po = g * TILE + 16 * ks + 2 * t4;
-          mma16816(oc[mi], af, *reinterpret_cast<const uint32_t*>(sph + po), *reinterpret_cast<const uint32_t*>(sph + po + 8));
-          mma16816(oc[mi], af, *reinterpret_cast<const uint32_t*>(spl + po), *reinterpret_cast<const uint32_t*>(spl + po + 8));
-        }
-      }
-    } else {  // a thread a dimension
+      for (int j = 0; j < KVM; j++) acc[j][i] *= sScale[j];
+      for (int t = 0; t < len; t++) {
+        const float v = reinterpret_cast<const float*>(sV + t * rowb)[d];
 #pragma unroll
-      for (int i = 0; i < DMAX; i++) {
-        const int d = tid + ATT_THREADS * i;
-        if (d >= hs) continue;
-#pragma unroll
-        for (int j = 0; j < KVM; j++) acc[j][i] *= sScale[j];
-        for (int t = 0; t < len; t++) {
-          const float v = kv_elem<HALF>(sV + t * rowb, d);
-#pragma unroll
-          for (int j = 0; j < KVM; j++) acc[j][i] = fmaf(sp[j * TILE + t], v, acc[j][i]);
-        }
+        for (int j = 0; j < KVM; j++) acc[j][i] = fmaf(sp[j * TILE + t], v, acc[j][i]);
       }
     }
     // the tile after next into this buffer, once every warp is done with it
@@ -355,115 +345,320 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_split_kernel(const AttA
       load_tile(t0 + 2 * TILE, buf);
     }
   }
-  // 5. the slice's output (one slice: the head's output itself)
-  auto put = [&](int j, int d, float v) {
-    const int h = hbase + j;
-    if (j >= KVM || h < a.h0 || h >= a.h1) return;
-    if (nsplit == 1) {
-      a.out[(long long)h * hs + d] = v / sL[j];
-    } else {
-      float* part = a.part + ((long long)h * a.nsplit + split) * (hs + 4);
-      part[d] = v;
-      if (d == 0) {
-        part[hs] = sM[j];
-        part[hs + 1] = sL[j];
-      }
-    }
-  };
-  if (HALF) {
+  // the slice's output (one slice: the head's output itself)
 #pragma unroll
-    for (int mi = 0; mi < MBMAX; mi++) {
-      const int mb = warp + ATT_WARPS * mi;
-      if (mb >= nmb) break;
-      put(2 * t4, 16 * mb + g, oc[mi][0]);
-      put(2 * t4 + 1, 16 * mb + g, oc[mi][1]);
-      put(2 * t4, 16 * mb + g + 8, oc[mi][2]);
-      put(2 * t4 + 1, 16 * mb + g + 8, oc[mi][3]);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < DMAX; i++) {
-      const int d = tid + ATT_THREADS * i;
-      if (d >= hs) continue;
-#pragma unroll
-      for (int j = 0; j < KVM; j++) put(j, d, acc[j][i]);
-    }
-  }
-  if (nsplit == 1 || !a.counters) return;
-  // 6. the last slice of this kv head to finish combines every slice's partials (no CTA waits for another: the
-  // others are done when the count reaches nsplit), and sets the count back to zero for the next call. The partials
-  // of the kv head's query heads are contiguous: copied into shared memory by asynchronous 16-byte copies, as many
-  // slices at once as the tile ring holds (every copy of a chunk in flight together).
-  __shared__ int last;
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) last = atomicAdd(&a.counters[kvh], 1) == nsplit - 1;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  const int row = hs + 4;                                    // floats a slice's partial (16-byte rows)
-  const int room = (int)((4 * (size_t)tileb) / ((size_t)KVM * row * 4));  // slices a chunk
-  float* stage = reinterpret_cast<float*>(ring);
-  float* sw = sp;  // [KVM][nsplit] weights exp(m_s - M), in the scores' room (the host sizes it for nsplit)
-  float o[KVM][DMAX];
-#pragma unroll
-  for (int j = 0; j < KVM; j++)
-#pragma unroll
-    for (int i = 0; i < DMAX; i++) o[j][i] = 0.0f;
-  for (int c0 = 0; c0 < nsplit; c0 += room) {
-    const int cn = min(room, nsplit - c0);
-    const int per4 = cn * row / 4;                           // 16-byte pieces a head's chunk
-    __syncthreads();  // the previous chunk is read
-    for (int e = tid; e < KVM * per4; e += ATT_THREADS) {
-      const int j = e / per4, f4 = e % per4;
-      cp_async16(stage + 4 * e, a.part + ((long long)(hbase + j) * a.nsplit + c0) * row + 4 * f4);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    cp_async_wait_all();
-    __syncthreads();
-    if (c0 == 0) {  // the maxima and sums of every slice (the first chunk holds them when room >= nsplit; else from L2)
-      for (int j = warp; j < KVM; j += ATT_WARPS) {
-        float M = -INFINITY;
-        for (int s2 = lane; s2 < nsplit; s2 += 32) {
-          const float m = s2 < cn ? stage[(j * cn + s2) * row + hs]
-                                  : __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * row + hs);
-          sw[j * nsplit + s2] = m;
-          M = fmaxf(M, m);
-        }
-        M = warp_max(M);
-        float Ls = 0.0f;
-        for (int s2 = lane; s2 < nsplit; s2 += 32) {
-          const float w = expf(sw[j * nsplit + s2] - M);
-          sw[j * nsplit + s2] = w;
-          const float l = s2 < cn ? stage[(j * cn + s2) * row + hs + 1]
-                                  : __ldcg(a.part + ((long long)(hbase + j) * a.nsplit + s2) * row + hs + 1);
-          Ls = fmaf(l, w, Ls);
-        }
-        Ls = warp_sum(Ls);
-        if (lane == 0) sL[j] = Ls;
-      }
-      __syncthreads();
-    }
-#pragma unroll
-    for (int i = 0; i < DMAX; i++) {
-      const int d = tid + ATT_THREADS * i;
-      if (d >= hs) continue;
-#pragma unroll
-      for (int j = 0; j < KVM; j++)
-        for (int s2 = 0; s2 < cn; s2++) o[j][i] = fmaf(stage[(j * cn + s2) * row + d], sw[j * nsplit + c0 + s2], o[j][i]);
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < DMAX; i++) {
+  for (int i = 0; i < 2; i++) {
     const int d = tid + ATT_THREADS * i;
     if (d >= hs) continue;
 #pragma unroll
     for (int j = 0; j < KVM; j++) {
       const int h = hbase + j;
-      if (h >= a.h0 && h < a.h1) a.out[(long long)h * hs + d] = o[j][i] / sL[j];
+      if (h < a.h0 || h >= a.h1) continue;
+      if (nsplit == 1) {
+        a.out[(long long)h * hs + d] = acc[j][i] / sL[j];
+      } else {
+        float* part = a.part + ((long long)h * a.nsplit + split) * (hs + 4);
+        part[d] = acc[j][i];
+        if (d == 0) {
+          part[hs] = sM[j];
+          part[hs + 1] = sL[j];
+        }
+      }
     }
   }
-  if (tid == 0) a.counters[kvh] = 0;
+  if (nsplit == 1 || !a.counters) return;
+  combine_slices<KVM, ATT_THREADS>(a, kvh, nsplit, ring, 4 * (size_t)tileb, sp, sL);
+}
+
+// ---- float16 caches
+// grid (nkv, nsplit), CH_WARPS warps. A CTA takes one kv head's slice of positions for its KVM query heads; the slice
+// is cut into chunks of 16 positions dealt to the warps in turn (warp w: chunks w, w + CH_WARPS, ...). Each warp copies
+// its chunks' keys and values into its own ring in shared memory (asynchronous 16-byte copies, the first ones issued
+// before the dependency wait: the cache rows before this token's are not the previous kernel's output) and keeps its
+// own online softmax (a running max and sum a head) and output over them, with no barrier shared with other warps:
+//   scores S (16 positions x 8 heads) = K . q^T,   output O^T (dims x heads) += V^T . P^T
+// on the tensor cores (mma m16n8k16, float32 accumulation), q and the probabilities each split into two float16
+// halves (hi + lo: their products with a float16 key or value are exact in the accumulation, so the sum keeps them to
+// about 2^-22 of themselves). The score fragment's columns (heads 2 t4, 2 t4 + 1) are the output fragment's columns,
+// so a thread rescales its own output with its own running maxima. The warps' parts are merged at the slice's end.
+constexpr int CH_WARPS = 8, CH_THREADS = 32 * CH_WARPS, CHUNK = 16;
+constexpr int HP = 8;    // heads padded to the products' n = 8
+constexpr int PST = 24;  // halves a head's row of a warp's probabilities (conflict-free fragment reads)
+
+template <int KVM, bool FUSE, int MBM>
+__global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const AttArgs a, const Fuse f, const int ring) {
+  extern __shared__ __align__(16) uint8_t att_smem[];
+  constexpr int DL = MBM / 2;                          // a lane's values of a head: d = lane + 32 i (hs <= 32 DL)
+  const int hs = a.hs, nmb = hs / 16;
+  const int rowb = hs * 2 + 16;                        // a padded row of a chunk, bytes (conflict-free ldmatrix)
+  const int chunkb = 2 * CHUNK * rowb;                 // a chunk's keys, then its values
+  const int qst = hs + 8;                              // halves a row of q's halves (conflict-free fragment reads)
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t4 = lane & 3;              // an mma fragment's row group and column pair
+  const int j0 = 2 * t4, j1 = 2 * t4 + 1;              // this thread's two head columns
+  uint8_t* myring = att_smem + (size_t)warp * ring * chunkb;
+  __half* sqh = reinterpret_cast<__half*>(att_smem + (size_t)CH_WARPS * ring * chunkb);  // [HP][qst] high halves
+  __half* sql = sqh + HP * qst;                                                          // and low halves
+  __half* sph = sql + HP * qst + warp * 2 * HP * PST;  // this warp's probabilities [HP][PST]: high, then low halves
+  __half* spl = sph + HP * PST;
+  uint16_t* sx = reinterpret_cast<uint16_t*>(sql + HP * qst + CH_WARPS * 2 * HP * PST);  // [2][hs] new key, value
+  float* sml = reinterpret_cast<float*>(sx + 2 * hs);  // [CH_WARPS][KVM][2] the warps' maxima and sums
+  float* sw = sml + CH_WARPS * KVM * 2;                // [KVM][nsplit] the combine's weights
+  __shared__ float sL[KVM];
+  pdl_launch_dependents();  // the next kernel waits for this one's completion; its CTAs may take the SMs this one leaves
+  // the position: written by the host before the step's first kernel, so readable before the dependency wait
+  const int pos = a.pos_dev ? *a.pos_dev : a.pos;
+  const int count = pos + 1;
+  const int kvh = blockIdx.x, split = blockIdx.y;
+  const int nsplit = a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
+  if (split >= nsplit) return;
+  const int p0 = split * a.split_len, p1 = min(count, p0 + a.split_len);
+  const int nchunk = (p1 - p0 + CHUNK - 1) / CHUNK;
+  const int mine = warp < nchunk ? (nchunk - 1 - warp) / CH_WARPS + 1 : 0;  // chunks of this warp
+  const int kvdim = a.nkv * hs, hbase = kvh * KVM, pieces = hs / 8;       // 16-byte pieces a row
+  const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.kc) + (long long)kvh * hs * 2;
+  const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vc) + (long long)kvh * hs * 2;
+  // this warp's i-th chunk into its ring slot i % ring; value rows past the chunk's length zeroed (a probability of
+  // 0 must meet a 0; key rows past it only make scores that are replaced by -inf)
+  auto load_chunk = [&](int i) {
+    uint8_t* sK = myring + (size_t)(i % ring) * chunkb;
+    uint8_t* sV = sK + CHUNK * rowb;
+    const int t0 = p0 + CHUNK * (warp + CH_WARPS * i);
+    const int len = min(CHUNK, p1 - t0);
+    for (int e = lane; e < CHUNK * pieces; e += 32) {
+      const int t = e / pieces, c = e % pieces;
+      if (t < len) {
+        const long long off = (long long)(t0 + t) * kvdim * 2 + c * 16;
+        cp_async16(sK + t * rowb + c * 16, kbase + off);
+        cp_async16(sV + t * rowb + c * 16, vbase + off);
+      } else {
+        *reinterpret_cast<int4*>(sV + t * rowb + c * 16) = make_int4(0, 0, 0, 0);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  for (int i = 0; i < ring && i < mine; i++) load_chunk(i);
+  for (int e = tid; e < (HP - KVM) * qst; e += CH_THREADS) {  // the padded heads' q: zero
+    sqh[KVM * qst + e] = __float2half_rn(0.0f);
+    sql[KVM * qst + e] = __float2half_rn(0.0f);
+  }
+  const bool holds_pos = FUSE && p1 == count;
+  // the head norms' weights and the RoPE tables' row of pos (not the previous kernel's output): read before the wait
+  const int turned = f.rot > 0 && f.rot < hs ? f.rot : hs;
+  float wq[DL], wk[DL], cs[DL], sn[DL];
+  if (FUSE) {
+    const float* crow = f.cos_t + (long long)pos * (hs / 2);
+    const float* srow = f.sin_t + (long long)pos * (hs / 2);
+#pragma unroll
+    for (int i = 0; i < DL; i++) {
+      const int d = lane + 32 * i;
+      wq[i] = d < hs && f.qn ? f.qn[d] : 1.0f;
+      wk[i] = d < hs && f.kn ? f.kn[d] : 1.0f;
+      cs[i] = d < turned ? crow[d >> 1] : 1.0f;
+      sn[i] = d < turned ? srow[d >> 1] : 0.0f;
+    }
+  }
+  pdl_wait();
+  // the query heads a warp each; where this slice holds the position, its key and value too (FUSE: the heads' RMSNorm
+  // over the lanes' strided sums, then RoPE on lane pairs)
+  for (int j = warp; j < KVM + (holds_pos ? 2 : 0); j += CH_WARPS) {
+    const float* src = j < KVM ? a.q + (long long)(hbase + j) * hs : (j == KVM ? f.k : f.v) + (long long)kvh * hs;
+    float x[DL];
+#pragma unroll
+    for (int i = 0; i < DL; i++) {
+      const int d = lane + 32 * i;
+      x[i] = d < hs ? src[d] : 0.0f;
+    }
+    if (FUSE && j <= KVM) {
+      if (j < KVM ? f.qn : f.kn) {
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < DL; i++) s = fmaf(x[i], x[i], s);
+        s = warp_sum(s);
+        const float r = 1.0f / sqrtf(s / (float)hs + f.eps);
+#pragma unroll
+        for (int i = 0; i < DL; i++) x[i] = (j < KVM ? wq[i] : wk[i]) * (r * x[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < DL; i++) {
+        const float o = __shfl_xor_sync(0xffffffffu, x[i], 1);  // the pair's other value
+        const int d = lane + 32 * i;
+        if (d < turned) x[i] = (d & 1) ? o * sn[i] + x[i] * cs[i] : x[i] * cs[i] - o * sn[i];
+      }
+    }
+    if (j < KVM) {  // q as two float16 halves
+#pragma unroll
+      for (int i = 0; i < DL; i++) {
+        const int d = lane + 32 * i;
+        if (d >= hs) continue;
+        __half hi, lo;
+        split_half(x[i], hi, lo);
+        sqh[j * qst + d] = hi;
+        sql[j * qst + d] = lo;
+      }
+    } else {  // this position's key (j == KVM) or value into the cache, and into the chunk that holds it
+      uint16_t* cache = reinterpret_cast<uint16_t*>(const_cast<void*>(j == KVM ? a.kc : a.vc)) +
+                        (long long)pos * kvdim + (long long)kvh * hs;
+      int local = 0;
+#pragma unroll
+      for (int i = 0; i < DL; i++) {
+        const int d = lane + 32 * i;
+        if (d >= hs) continue;
+        const uint16_t b = float_to_half_bits(x[i], &local);
+        cache[d] = b;
+        sx[(j - KVM) * hs + d] = b;
+      }
+      if (local && f.bad) atomicAdd(f.bad, local);
+    }
+  }
+  __syncthreads();
+  float M0 = -INFINITY, M1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // heads j0, j1: running max and (lane-partial) sum
+  float oc[MBM][4];
+#pragma unroll
+  for (int mb = 0; mb < MBM; mb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) oc[mb][c] = 0.0f;
+  const float isq = 1.0f / sqrtf((float)hs);
+  for (int i = 0; i < mine; i++) {
+    // this chunk's copies are done when at most the next chunk's group is still in flight
+    if (ring > 1 && i + 1 < mine) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else cp_async_wait_all();
+    __syncwarp();
+    uint8_t* sK = myring + (size_t)(i % ring) * chunkb;
+    uint8_t* sV = sK + CHUNK * rowb;
+    const int t0 = p0 + CHUNK * (warp + CH_WARPS * i);
+    const int len = min(CHUNK, p1 - t0);
+    if (holds_pos && pos >= t0 && pos < t0 + len) {  // this position's row: the fresh key and value
+      for (int e = lane; e < 2 * hs; e += 32)
+        reinterpret_cast<uint16_t*>((e < hs ? sK : sV) + (size_t)(pos - t0) * rowb)[e % hs] = sx[e];
+      __syncwarp();
+    }
+    // scores, the high and low halves' products in two accumulators
+    float ch[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const uint8_t* arow = sK + ((lane & 7) + ((lane >> 3) & 1) * 8) * rowb + (lane >> 4) * 16;
+#pragma unroll
+    for (int kk = 0; kk < MBM; kk++) {
+      if (kk >= nmb) break;
+      uint32_t af[4];
+      ldsm_x4(af, arow + kk * 32);
+      const int qo = g * qst + 16 * kk + 2 * t4;
+      mma16816(ch, af, lds32(sqh + qo), lds32(sqh + qo + 8));
+      mma16816(cl, af, lds32(sql + qo), lds32(sql + qo + 8));
+    }
+    float sc[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {  // rows g, g, g + 8, g + 8; columns j0, j1, j0, j1
+      float v = (ch[r] + cl[r]) * isq;
+      if (a.cap > 0.0f) v = a.cap * tanhf(v / a.cap);
+      sc[r] = g + (r >> 1) * 8 < len ? v : -INFINITY;
+    }
+    // the chunk's maxima over its 16 positions (the lanes of a column pair differ in g)
+    float m0 = fmaxf(sc[0], sc[2]), m1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+    }
+    const float n0 = fmaxf(M0, m0), n1 = fmaxf(M1, m1);
+    const float b0 = n0 == -INFINITY ? 0.0f : n0, b1 = n1 == -INFINITY ? 0.0f : n1;
+    const float r0 = expf(M0 - b0), r1 = expf(M1 - b1);  // 0 at the first chunk (exp(-inf))
+    M0 = n0;
+    M1 = n1;
+    const float q0 = expf(sc[0] - b0), q1 = expf(sc[1] - b1), q2 = expf(sc[2] - b0), q3 = expf(sc[3] - b1);
+    l0 = fmaf(l0, r0, q0 + q2);
+    l1 = fmaf(l1, r1, q1 + q3);
+    __half hi, lo;  // P as [head][position] halves, read back as the weighted values' B fragments
+    split_half(q0, hi, lo);
+    sph[j0 * PST + g] = hi;
+    spl[j0 * PST + g] = lo;
+    split_half(q1, hi, lo);
+    sph[j1 * PST + g] = hi;
+    spl[j1 * PST + g] = lo;
+    split_half(q2, hi, lo);
+    sph[j0 * PST + g + 8] = hi;
+    spl[j0 * PST + g + 8] = lo;
+    split_half(q3, hi, lo);
+    sph[j1 * PST + g + 8] = hi;
+    spl[j1 * PST + g + 8] = lo;
+    __syncwarp();
+    const uint32_t ph0 = lds32(sph + g * PST + 2 * t4), ph1 = lds32(sph + g * PST + 2 * t4 + 8);
+    const uint32_t pl0 = lds32(spl + g * PST + 2 * t4), pl1 = lds32(spl + g * PST + 2 * t4 + 8);
+    // the weighted values, 16 dimensions an m-block
+    const uint8_t* vrow = sV + ((lane & 7) + ((lane >> 4) & 1) * 8) * rowb + ((lane >> 3) & 1) * 16;
+#pragma unroll
+    for (int mb = 0; mb < MBM; mb++) {
+      if (mb >= nmb) break;
+      oc[mb][0] *= r0;
+      oc[mb][1] *= r1;
+      oc[mb][2] *= r0;
+      oc[mb][3] *= r1;
+      uint32_t af[4];
+      ldsm_x4_trans(af, vrow + mb * 32);
+      mma16816(oc[mb], af, ph0, ph1);
+      mma16816(oc[mb], af, pl0, pl1);
+    }
+    __syncwarp();  // the chunk's slot and the probabilities are read: both may be rewritten
+    if (i + ring < mine) load_chunk(i + ring);
+  }
+  // this warp's part: the sums over its row groups; output, maxima and sums to shared memory (its ring is free)
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  }
+  float* so = reinterpret_cast<float*>(myring);  // [KVM][hs + 4]
+#pragma unroll
+  for (int mb = 0; mb < MBM; mb++) {
+    if (mb >= nmb) break;
+    const int d = 16 * mb + g;
+    if (j0 < KVM) {
+      so[j0 * (hs + 4) + d] = oc[mb][0];
+      so[j0 * (hs + 4) + d + 8] = oc[mb][2];
+    }
+    if (j1 < KVM) {
+      so[j1 * (hs + 4) + d] = oc[mb][1];
+      so[j1 * (hs + 4) + d + 8] = oc[mb][3];
+    }
+  }
+  if (g == 0) {
+    if (j0 < KVM) {
+      sml[(warp * KVM + j0) * 2] = M0;
+      sml[(warp * KVM + j0) * 2 + 1] = l0;
+    }
+    if (j1 < KVM) {
+      sml[(warp * KVM + j1) * 2] = M1;
+      sml[(warp * KVM + j1) * 2 + 1] = l1;
+    }
+  }
+  __syncthreads();
+  // the warps' parts merged, a thread a (head, dimension) pair: the slice's output (one slice: the head's output)
+  for (int e = tid; e < KVM * hs; e += CH_THREADS) {
+    const int j = e / hs, d = e % hs, h = hbase + j;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < CH_WARPS; w++) mx = fmaxf(mx, sml[(w * KVM + j) * 2]);
+    const float base = mx == -INFINITY ? 0.0f : mx;
+    float o = 0.0f, l = 0.0f;
+#pragma unroll
+    for (int w = 0; w < CH_WARPS; w++) {
+      const float wt = expf(sml[(w * KVM + j) * 2] - base);  // 0 for a warp without chunks
+      o = fmaf(reinterpret_cast<const float*>(att_smem + (size_t)w * ring * chunkb)[j * (hs + 4) + d], wt, o);
+      l = fmaf(sml[(w * KVM + j) * 2 + 1], wt, l);
+    }
+    if (h < a.h0 || h >= a.h1) continue;
+    if (nsplit == 1) {
+      a.out[(long long)h * hs + d] = o / l;
+    } else {
+      float* part = a.part + ((long long)h * a.nsplit + split) * (hs + 4);
+      part[d] = o;
+      if (d == 0) {
+        part[hs] = mx;
+        part[hs + 1] = l;
+      }
+    }
+  }
+  if (nsplit == 1 || !a.counters) return;
+  combine_slices<KVM, CH_THREADS>(a, kvh, nsplit, att_smem, (size_t)CH_WARPS * ring * chunkb, sw, sL);
 }
 
 // a block a head: the slices' partials combined
@@ -488,63 +683,87 @@ __global__ void attention_combine_kernel(const AttArgs a) {
   }
 }
 
-template <bool HALF, int KVM>
-cudaError_t launch_split_kvm(const AttArgs& a, const Fuse* f, size_t smem, dim3 grid, bool pdl) {
+cudaLaunchConfig_t launch_config(dim3 grid, int threads, size_t smem, bool pdl, cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(ATT_THREADS);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = pllm_stream();
-  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-if (f) {
-    auto k = attention_split_kernel<HALF, KVM, true>;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    return cudaLaunchKernelEx(&cfg, k, a, *f);
-  }
-  const Fuse none = {};
-  auto k = attention_split_kernel<HALF, KVM, false>;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  return cudaLaunchKernelEx(&cfg, k, a, none);
+  return cfg;
 }
 
-template <bool HALF>
-cudaError_t launch_split(const AttArgs& a, const Fuse* f, int kvm, size_t smem, dim3 grid, bool pdl) {
-  switch (kvm) {
-    case 1: return launch_split_kvm<HALF, 1>(a, f, smem, grid, pdl);
-    case 2: return launch_split_kvm<HALF, 2>(a, f, smem, grid, pdl);
-    case 4: return launch_split_kvm<HALF, 4>(a, f, smem, grid, pdl);
-    case 8: return launch_split_kvm<HALF, 8>(a, f, smem, grid, pdl);
-    default: return cudaErrorInvalidValue;
+template <typename K, typename... Args>
+cudaError_t launch_with(K kernel, const cudaLaunchConfig_t& cfg, Args... args) {
+  if (cfg.dynamicSmemBytes > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
+    if (e != cudaSuccess) return e;
   }
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <int KVM>
+cudaError_t launch_f32(const AttArgs& a, const Fuse* f, const cudaLaunchConfig_t& cfg) {
+  if (f) return launch_with(attention_f32_kernel<KVM, true>, cfg, a, *f);
+  return launch_with(attention_f32_kernel<KVM, false>, cfg, a, Fuse{});
+}
+
+template <int KVM>
+cudaError_t launch_chunks(const AttArgs& a, const Fuse* f, const cudaLaunchConfig_t& cfg, int ring) {
+  const Fuse none = {};
+  if (a.hs <= 128) {
+    if (f) return launch_with(attention_chunk_kernel<KVM, true, 8>, cfg, a, *f, ring);
+    return launch_with(attention_chunk_kernel<KVM, false, 8>, cfg, a, none, ring);
+  }
+  if (f) return launch_with(attention_chunk_kernel<KVM, true, 16>, cfg, a, *f, ring);
+  return launch_with(attention_chunk_kernel<KVM, false, 16>, cfg, a, none, ring);
 }
 
 void run_attention(const char* name, AttArgs a, bool half, bool pdl, const Fuse* f = nullptr) {
   const int kvm = a.nh / a.nkv;
-  const size_t rowb = (size_t)a.hs * (half ? 2 : 4) + 16;
-  // the scores' room also holds the slices' weights in the combine (kvm * nsplit floats)
-  const size_t scores = (size_t)kvm * (a.nsplit > TILE ? a.nsplit : TILE) * 4;
-  const size_t halves = half ? (2 * 8 * (size_t)a.hs + 2 * 8 * TILE) * 2 : 0;
-  const size_t smem = 4 * TILE * rowb + (size_t)kvm * a.hs * 4 + scores + 2 * (size_t)a.hs * 4 + halves;
   const dim3 grid(a.nkv, a.nsplit);
-  cudaError_t e = half ? launch_split<true>(a, f, kvm, smem, grid, pdl) : launch_split<false>(a, f, kvm, smem, grid, pdl);
+  const size_t comb = a.counters ? (size_t)a.nsplit : 0;  // the combine's weights: kvm x nsplit floats
+  cudaLaunchAttribute attr[1];
+  cudaError_t e;
+  if (half) {
+    // two ring slots a warp where a warp has two chunks or more (hs <= 128: the slots fit beside each other)
+    const int per_warp = ((a.split_len + CHUNK - 1) / CHUNK + CH_WARPS - 1) / CH_WARPS;
+    const int ring = per_warp >= 2 && a.hs <= 128 ? 2 : 1;
+    const size_t rowb = (size_t)a.hs * 2 + 16;
+    const size_t smem = (size_t)CH_WARPS * ring * 2 * CHUNK * rowb + 2 * (size_t)HP * (a.hs + 8) * 2 +
+                        (size_t)CH_WARPS * 2 * HP * PST * 2 + 2 * (size_t)a.hs * 2 + (size_t)CH_WARPS * kvm * 2 * 4 +
+                        (size_t)kvm * comb * 4;
+    const cudaLaunchConfig_t cfg = launch_config(grid, CH_THREADS, smem, pdl, attr);
+    switch (kvm) {
+      case 1: e = launch_chunks<1>(a, f, cfg, ring); break;
+      case 2: e = launch_chunks<2>(a, f, cfg, ring); break;
+      case 4: e = launch_chunks<4>(a, f, cfg, ring); break;
+      case 8: e = launch_chunks<8>(a, f, cfg, ring); break;
+      default: e = cudaErrorInvalidValue;
+    }
+  } else {
+    const size_t rowb = (size_t)a.hs * 4 + 16;
+    const size_t scores = (size_t)kvm * ((size_t)TILE > comb ? (size_t)TILE : comb) * 4;
+    const size_t smem = 4 * TILE * rowb + (size_t)kvm * a.hs * 4 + 2 * (size_t)a.hs * 4 + scores;
+    const cudaLaunchConfig_t cfg = launch_config(grid, ATT_THREADS, smem, pdl, attr);
+    switch (kvm) {
+      case 1: e = launch_f32<1>(a, f, cfg); break;
+      case 2: e = launch_f32<2>(a, f, cfg); break;
+      case 4: e = launch_f32<4>(a, f, cfg); break;
+      case 8: e = launch_f32<8>(a, f, cfg); break;
+      default: e = cudaErrorInvalidValue;
+    }
+  }
   if (e != cudaSuccess) {
     pllm_fail(PLLM_ECUDA, "%s: launch failed: %s", name, cudaGetErrorString(e));
     return;
   }
   if ((a.nsplit > 1 || a.pos_dev) && !a.counters) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.h1 - a.h0);
-    cfg.blockDim = dim3(a.hs >= 128 ? 128 : 64);
-    cfg.stream = pllm_stream();
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    const cudaLaunchConfig_t cfg = launch_config(dim3(a.h1 - a.h0), a.hs >= 128 ? 128 : 64, 0, pdl, attr);
     e = cudaLaunchKernelEx(&cfg, attention_combine_kernel, a);
     if (e != cudaSuccess) pllm_fail(PLLM_ECUDA, "%s: combine launch failed: %s", name, cudaGetErrorString(e));
   }
