@@ -200,6 +200,10 @@ int32_t pllm_device_status(void);
 int32_t pllm_set_gemv_mode(int32_t mode);
 /* the shared-memory bytes the bulk-copy product's ring of stages may take (32 KB..227 KB; default 200 KB) */
 int32_t pllm_set_stage_budget(int32_t bytes);
+/* how the forward driver's float16 attention (pllm_attention_dev, pllm_attention_step) combines its parts: 1 (the
+ * default) one thread-block cluster a kv head over the whole cache, combined in distributed shared memory; 0 slices
+ * of split_len positions whose partials the last slice combines through the scratch; returns the previous mode */
+int32_t pllm_set_attention_mode(int32_t mode);
 
 /* attention_f16 for callers that cannot allocate device memory (no counterpart in the reference): the same
  * arguments without att; the slices' partials live in a 4 MiB device array of the library's own, held by every GPU

@@ -16,6 +16,8 @@
 //
 // The forward driver's calls read the position from device memory (pos_dev), so that one CUDA graph serves every
 // position; their grid covers the cache's capacity and the slices past the position return at once.
+#include <cooperative_groups.h>
+
 #include "pllm_common.cuh"
 
 namespace {
@@ -381,11 +383,15 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_f32_kernel(const AttArg
 // halves (hi + lo: their products with a float16 key or value are exact in the accumulation, so the sum keeps them to
 // about 2^-22 of themselves). The score fragment's columns (heads 2 t4, 2 t4 + 1) are the output fragment's columns,
 // so a thread rescales its own output with its own running maxima. The warps' parts are merged at the slice's end.
+// CS > 0 (the forward driver's calls): a thread-block cluster of CS CTAs a kv head takes all of its positions, the
+// chunks dealt to the cluster's CS x CH_WARPS warps in turn (grid (CS, nkv), cluster (CS, 1, 1)); each CTA merges its
+// warps, and the CTAs' parts are combined through distributed shared memory, each CTA making 1/CS of the output (the
+// cluster's CTAs run together, so they can wait for one another; no partials leave the SMs).
 constexpr int CH_WARPS = 8, CH_THREADS = 32 * CH_WARPS, CHUNK = 16;
 constexpr int HP = 8;    // heads padded to the products' n = 8
 constexpr int PST = 24;  // halves a head's row of a warp's probabilities (conflict-free fragment reads)
 
-template <int KVM, bool FUSE, int MBM>
+template <int KVM, bool FUSE, int MBM, int CS>
 __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const AttArgs a, const Fuse f, const int ring) {
   extern __shared__ __align__(16) uint8_t att_smem[];
   constexpr int DL = MBM / 2;                          // a lane's values of a head: d = lane + 32 i (hs <= 32 DL)
@@ -409,12 +415,15 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
   // the position: written by the host before the step's first kernel, so readable before the dependency wait
   const int pos = a.pos_dev ? *a.pos_dev : a.pos;
   const int count = pos + 1;
-  const int kvh = blockIdx.x, split = blockIdx.y;
-  const int nsplit = a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
+  const int kvh = CS ? blockIdx.y : blockIdx.x, split = CS ? 0 : blockIdx.y;
+  const int rank = CS ? blockIdx.x : 0;  // the CTA's rank in its cluster
+  const int nsplit = CS ? 1 : a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
   if (split >= nsplit) return;
-  const int p0 = split * a.split_len, p1 = min(count, p0 + a.split_len);
+  const int p0 = CS ? 0 : split * a.split_len, p1 = CS ? count : min(count, p0 + a.split_len);
+  constexpr int TW = (CS ? CS : 1) * CH_WARPS;  // the warps the chunks are dealt to
+  const int gw = rank * CH_WARPS + warp;       // this warp's turn
   const int nchunk = (p1 - p0 + CHUNK - 1) / CHUNK;
-  const int mine = warp < nchunk ? (nchunk - 1 - warp) / CH_WARPS + 1 : 0;  // chunks of this warp
+  const int mine = gw < nchunk ? (nchunk - 1 - gw) / TW + 1 : 0;  // chunks of this warp
   const int kvdim = a.nkv * hs, hbase = kvh * KVM, pieces = hs / 8;       // 16-byte pieces a row
   const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.kc) + (long long)kvh * hs * 2;
   const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.vc) + (long long)kvh * hs * 2;
@@ -423,7 +432,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
   auto load_chunk = [&](int i) {
     uint8_t* sK = myring + (size_t)(i % ring) * chunkb;
     uint8_t* sV = sK + CHUNK * rowb;
-    const int t0 = p0 + CHUNK * (warp + CH_WARPS * i);
+    const int t0 = p0 + CHUNK * (gw + TW * i);
     const int len = min(CHUNK, p1 - t0);
     for (int e = lane; e < CHUNK * pieces; e += 32) {
       const int t = e / pieces, c = e % pieces;
@@ -442,7 +451,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
     sqh[KVM * qst + e] = __float2half_rn(0.0f);
     sql[KVM * qst + e] = __float2half_rn(0.0f);
   }
-  const bool holds_pos = FUSE && p1 == count;
+  const bool holds_pos = FUSE && (CS ? (pos / CHUNK) % TW / CH_WARPS == rank : p1 == count);
   // the head norms' weights and the RoPE tables' row of pos (not the previous kernel's output): read before the wait
   const int turned = f.rot > 0 && f.rot < hs ? f.rot : hs;
   float wq[DL], wk[DL], cs[DL], sn[DL];
@@ -526,7 +535,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
     __syncwarp();
     uint8_t* sK = myring + (size_t)(i % ring) * chunkb;
     uint8_t* sV = sK + CHUNK * rowb;
-    const int t0 = p0 + CHUNK * (warp + CH_WARPS * i);
+    const int t0 = p0 + CHUNK * (gw + TW * i);
     const int len = min(CHUNK, p1 - t0);
     if (holds_pos && pos >= t0 && pos < t0 + len) {  // this position's row: the fresh key and value
       for (int e = lane; e < 2 * hs; e += 32)
@@ -631,7 +640,9 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
     }
   }
   __syncthreads();
-  // the warps' parts merged, a thread a (head, dimension) pair: the slice's output (one slice: the head's output)
+  // the warps' parts merged, a thread a (head, dimension) pair: the slice's output (one slice: the head's output);
+  // CS: the CTA's part, [KVM][hs] then KVM maxima and KVM sums, where q's halves were (no warp reads them now)
+  float* cpart = reinterpret_cast<float*>(sqh);
   for (int e = tid; e < KVM * hs; e += CH_THREADS) {
     const int j = e / hs, d = e % hs, h = hbase + j;
     float mx = -INFINITY;
@@ -645,6 +656,14 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
       o = fmaf(reinterpret_cast<const float*>(att_smem + (size_t)w * ring * chunkb)[j * (hs + 4) + d], wt, o);
       l = fmaf(sml[(w * KVM + j) * 2 + 1], wt, l);
     }
+    if (CS) {
+      cpart[e] = o;
+      if (d == 0) {
+        cpart[KVM * hs + j] = mx;
+        cpart[KVM * hs + KVM + j] = l;
+      }
+      continue;
+    }
     if (h < a.h0 || h >= a.h1) continue;
     if (nsplit == 1) {
       a.out[(long long)h * hs + d] = o / l;
@@ -656,6 +675,38 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
         part[hs + 1] = l;
       }
     }
+  }
+  if constexpr (CS > 0) {  // the cluster's parts combined: this CTA makes pairs [rank per, (rank + 1) per) from every CTA's part
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const int per = (KVM * hs + CS - 1) / CS;
+    const int e = rank * per + tid;
+    if (tid < per && e < KVM * hs) {
+      const int j = e / hs, d = e % hs;
+      float m[CS], l[CS], o[CS];
+#pragma unroll
+      for (int c = 0; c < CS; c++) {  // every load in flight together
+        const float* remote = cluster.map_shared_rank(cpart, c);
+        m[c] = remote[KVM * hs + j];
+        l[c] = remote[KVM * hs + KVM + j];
+        o[c] = remote[e];
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < CS; c++) mx = fmaxf(mx, m[c]);
+      const float base = mx == -INFINITY ? 0.0f : mx;
+      float os = 0.0f, ls = 0.0f;
+#pragma unroll
+      for (int c = 0; c < CS; c++) {
+        const float wt = expf(m[c] - base);  // 0 for a CTA without chunks
+        os = fmaf(o[c], wt, os);
+        ls = fmaf(l[c], wt, ls);
+      }
+      a.out[(long long)(hbase + j) * hs + d] = os / ls;
+    }
+    cluster.sync();  // no CTA leaves while another reads its shared memory
+    return;
   }
   if (nsplit == 1 || !a.counters) return;
   combine_slices<KVM, CH_THREADS>(a, kvh, nsplit, att_smem, (size_t)CH_WARPS * ring * chunkb, sw, sL);
@@ -716,12 +767,84 @@ template <int KVM>
 cudaError_t launch_chunks(const AttArgs& a, const Fuse* f, const cudaLaunchConfig_t& cfg, int ring) {
   const Fuse none = {};
   if (a.hs <= 128) {
-    if (f) return launch_with(attention_chunk_kernel<KVM, true, 8>, cfg, a, *f, ring);
-    return launch_with(attention_chunk_kernel<KVM, false, 8>, cfg, a, none, ring);
+    if (f) return launch_with(attention_chunk_kernel<KVM, true, 8, 0>, cfg, a, *f, ring);
+    return launch_with(attention_chunk_kernel<KVM, false, 8, 0>, cfg, a, none, ring);
   }
-  if (f) return launch_with(attention_chunk_kernel<KVM, true, 16>, cfg, a, *f, ring);
-  return launch_with(attention_chunk_kernel<KVM, false, 16>, cfg, a, none, ring);
+  if (f) return launch_with(attention_chunk_kernel<KVM, true, 16, 0>, cfg, a, *f, ring);
+  return launch_with(attention_chunk_kernel<KVM, false, 16, 0>, cfg, a, none, ring);
 }
+
+// One cluster size's launch (grid (CS, nkv), cluster (CS, 1, 1)), or (fits non-null) the number of such clusters
+// the device can hold at once.
+template <int CS, int KVM, bool FUSE, int MBM>
+cudaError_t launch_cluster_cs(const AttArgs& a, const Fuse& f, const cudaLaunchConfig_t& base, int ring, int* fits) {
+  auto k = attention_chunk_kernel<KVM, FUSE, MBM, CS>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)base.dynamicSmemBytes);
+  if (e == cudaSuccess && CS > 8) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = base;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1] = base.numAttrs ? base.attrs[0] : attr[0];  // the dependent-launch attribute, where asked for
+  cfg.gridDim = dim3(CS, a.nkv);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1 + (base.numAttrs ? 1 : 0);
+  if (fits) {
+    cfg.numAttrs = 1;
+    return cudaOccupancyMaxActiveClusters(fits, k, &cfg);
+  }
+  return cudaLaunchKernelEx(&cfg, k, a, f, ring);
+}
+
+// The cluster size for a configuration: 16 (a non-portable size) where the device holds all nkv such clusters at
+// once, else 8 where it holds one, else 0 (the slices' kernel). Found once a configuration (kernel, shared memory,
+// nkv) and device, before its first launch.
+template <int KVM, bool FUSE, int MBM>
+cudaError_t launch_cluster(const AttArgs& a, const Fuse& f, const cudaLaunchConfig_t& cfg, int ring, bool* launched) {
+  struct Choice {
+    int dev, nkv, hs;
+    size_t smem;
+    int cs;
+  };
+  static Choice cache[64];
+  static int used = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  int cs = -1;
+  for (int i = 0; i < used; i++)
+    if (cache[i].dev == dev && cache[i].nkv == a.nkv && cache[i].hs == a.hs && cache[i].smem == cfg.dynamicSmemBytes)
+      cs = cache[i].cs;
+  if (cs < 0) {
+    int n16 = 0, n8 = 0;
+    if (launch_cluster_cs<16, KVM, FUSE, MBM>(a, f, cfg, ring, &n16) != cudaSuccess) n16 = 0;
+    if (launch_cluster_cs<8, KVM, FUSE, MBM>(a, f, cfg, ring, &n8) != cudaSuccess) n8 = 0;
+    cudaGetLastError();  // a refused query leaves no error behind: the choice falls back
+    cs = n16 >= a.nkv ? 16 : n8 >= 1 ? 8 : 0;
+    if (used < 64) cache[used++] = Choice{dev, a.nkv, a.hs, cfg.dynamicSmemBytes, cs};
+  }
+  *launched = cs != 0;
+  if (cs == 16) return launch_cluster_cs<16, KVM, FUSE, MBM>(a, f, cfg, ring, nullptr);
+  if (cs == 8) return launch_cluster_cs<8, KVM, FUSE, MBM>(a, f, cfg, ring, nullptr);
+  return cudaSuccess;
+}
+
+template <int KVM>
+cudaError_t launch_clusters(const AttArgs& a, const Fuse* f, const cudaLaunchConfig_t& cfg, int ring, bool* launched) {
+  const Fuse none = {};
+  if (a.hs <= 128) {
+    if (f) return launch_cluster<KVM, true, 8>(a, *f, cfg, ring, launched);
+    return launch_cluster<KVM, false, 8>(a, none, cfg, ring, launched);
+  }
+  if (f) return launch_cluster<KVM, true, 16>(a, *f, cfg, ring, launched);
+  return launch_cluster<KVM, false, 16>(a, none, cfg, ring, launched);
+}
+
+// the forward driver's float16 attention by clusters (1) or by slices and a combine (0); pllm_set_attention_mode
+int g_cluster_attention = 1;
 
 void run_attention(const char* name, AttArgs a, bool half, bool pdl, const Fuse* f = nullptr) {
   const int kvm = a.nh / a.nkv;
@@ -730,14 +853,34 @@ void run_attention(const char* name, AttArgs a, bool half, bool pdl, const Fuse*
   cudaLaunchAttribute attr[1];
   cudaError_t e;
   if (half) {
+    const size_t rowb = (size_t)a.hs * 2 + 16;
+    auto smem_of = [&](int ring, size_t comb_floats) {
+      return (size_t)CH_WARPS * ring * 2 * CHUNK * rowb + 2 * (size_t)HP * (a.hs + 8) * 2 +
+             (size_t)CH_WARPS * 2 * HP * PST * 2 + 2 * (size_t)a.hs * 2 + (size_t)CH_WARPS * kvm * 2 * 4 +
+             (size_t)kvm * comb_floats * 4;
+    };
+    if (a.pos_dev && a.h0 == 0 && a.h1 == a.nh && g_cluster_attention) {
+      // the whole cache a cluster: two ring slots a warp (hs <= 128), no partials
+      const int ring = a.hs <= 128 ? 2 : 1;
+      const cudaLaunchConfig_t cfg = launch_config(grid, CH_THREADS, smem_of(ring, 0), pdl, attr);
+      bool launched = false;
+      switch (kvm) {
+        case 1: e = launch_clusters<1>(a, f, cfg, ring, &launched); break;
+        case 2: e = launch_clusters<2>(a, f, cfg, ring, &launched); break;
+        case 4: e = launch_clusters<4>(a, f, cfg, ring, &launched); break;
+        case 8: e = launch_clusters<8>(a, f, cfg, ring, &launched); break;
+        default: e = cudaErrorInvalidValue;
+      }
+      if (e != cudaSuccess) {
+        pllm_fail(PLLM_ECUDA, "%s: cluster launch failed: %s", name, cudaGetErrorString(e));
+        return;
+      }
+      if (launched) return;
+    }
     // two ring slots a warp where a warp has two chunks or more (hs <= 128: the slots fit beside each other)
     const int per_warp = ((a.split_len + CHUNK - 1) / CHUNK + CH_WARPS - 1) / CH_WARPS;
     const int ring = per_warp >= 2 && a.hs <= 128 ? 2 : 1;
-    const size_t rowb = (size_t)a.hs * 2 + 16;
-    const size_t smem = (size_t)CH_WARPS * ring * 2 * CHUNK * rowb + 2 * (size_t)HP * (a.hs + 8) * 2 +
-                        (size_t)CH_WARPS * 2 * HP * PST * 2 + 2 * (size_t)a.hs * 2 + (size_t)CH_WARPS * kvm * 2 * 4 +
-                        (size_t)kvm * comb * 4;
-    const cudaLaunchConfig_t cfg = launch_config(grid, CH_THREADS, smem, pdl, attr);
+    const cudaLaunchConfig_t cfg = launch_config(grid, CH_THREADS, smem_of(ring, comb), pdl, attr);
     switch (kvm) {
       case 1: e = launch_chunks<1>(a, f, cfg, ring); break;
       case 2: e = launch_chunks<2>(a, f, cfg, ring); break;
@@ -1058,6 +1201,14 @@ PLLM_API void pllm_attention_step(uint64_t out, uint64_t qkv, uint64_t kc, uint6
   f.rot = rot;
   f.bad = dptr<int>(bad);
   run_attention("pllm_attention_step", a, half != 0, pdl != 0, &f);
+}
+
+// 1: the forward driver's float16 attention by clusters (the default); 0: by slices and the last slice's combine.
+// Returns the previous mode.
+PLLM_API int32_t pllm_set_attention_mode(int32_t mode) {
+  const int old = g_cluster_attention;
+  if (mode == 0 || mode == 1) g_cluster_attention = mode;
+  return old;
 }
 
 PLLM_API void pllm_qk_rope_cache(uint64_t q, uint64_t k, uint64_t v, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t,
