@@ -205,6 +205,27 @@ int32_t pllm_set_stage_budget(int32_t bytes);
  * of split_len positions whose partials the last slice combines through the scratch; returns the previous mode */
 int32_t pllm_set_attention_mode(int32_t mode);
 
+/* ---- tensor-parallel decode over NVLink (no counterpart in the reference, whose engine splits rows across the
+ * CPU threads of one memory, src/runtime/forward/threads.ts): one process a GPU, a layer's two reductions (after wo
+ * and after w2) by peer stores into every rank's exchange region (mapped by CUDA IPC) and bounded waits */
+/* a rank's exchange of world ranks (<= 8), dim floats a reduction, layers layers; 0 on failure */
+uint64_t pllm_tp_open(int32_t world, int32_t rank, int32_t dim, int32_t layers);
+/* the exchange region's IPC handle (64 bytes at out) for the other ranks; 0 or an error code */
+int32_t pllm_tp_handle(uint64_t tp, void* out);
+/* every rank's handle (world x 64 bytes, rank order): maps the other ranks' regions; 0 or an error code */
+int32_t pllm_tp_connect(uint64_t tp, const void* handles);
+/* unmaps the other ranks' regions and frees this one (once every rank is done) */
+void pllm_tp_close(uint64_t tp);
+/* the first kernel of a step: counts the steps the reductions' marks are made from */
+void pllm_tp_step(uint64_t tp);
+/* a tensor-parallel step's int8 product of one token, rows 0..rows: pro 1 RMSNorm + quantize_x, 2 quantize_x, 3 x +
+ * every rank's partial of reduction use (in rank order) written to x_out, then RMSNorm + quantize_x; epi 0 store, 2
+ * the gated FFN's silu(row) * row + pair, 3 the rows sent to every rank as this rank's partial of reduction use (wo of
+ * layer l: use 2 l; w2: 2 l + 1). A wait for the other ranks gives up after 2 s (pllm_device_status: 3). */
+void pllm_gemv_tp(uint64_t out, uint64_t x, uint64_t x_out, uint64_t norm, float eps, int32_t bias, uint64_t wq,
+                  uint64_t ws, int32_t n, int32_t rows, int32_t pro, int32_t epi, int64_t pair, int32_t pdl,
+                  uint64_t tp, int32_t use);
+
 /* attention_f16 for callers that cannot allocate device memory (no counterpart in the reference): the same
  * arguments without att; the slices' partials live in a 4 MiB device array of the library's own, held by every GPU
  * that loads the library until exit, shared by all calls (overlapping calls race), with nothing that must start at
@@ -219,6 +240,10 @@ void pllm_attention_f16_noalloc(uint64_t out, uint64_t q, uint64_t kc, uint64_t 
 void pllm_synth_f32(uint64_t out, int64_t n, uint64_t seed, float mean, float std);
 /* rows x cols int8 weights: N(0, std) quantized group by group as engine/packing.py:40-45 quantizes */
 void pllm_synth_q8(uint64_t wq, uint64_t ws, int64_t rows, int32_t cols, uint64_t seed, float std);
+/* the block rows x cols at (row0, col0) of the matrix pllm_synth_q8 makes with full_cols columns (the same bytes):
+ * a tensor-parallel rank's share of a synthetic matrix */
+void pllm_synth_q8_block(uint64_t wq, uint64_t ws, int64_t rows, int32_t cols, uint64_t seed, float std, int64_t row0,
+                         int64_t col0, int64_t full_cols);
 /* rows x cols ternary weights uniform on {-1, 0, +1} (packing.py:106-109's codes) and a float16 scale a row,
  * N(mean, std) rounded to float16, repeated for each group of 128 */
 void pllm_synth_t2(uint64_t wq, uint64_t ws, int64_t rows, int32_t cols, uint64_t seed, float mean, float std);

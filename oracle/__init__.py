@@ -67,7 +67,8 @@ def _declare(L):
 
 
 def _p(a):
-    return a.ctypes.data if a is not None else None
+    # a pointer that holds the array (a temporary made by _c lives until the call returns)
+    return a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
 
 
 def _c(a, dtype):

@@ -8,8 +8,24 @@
 namespace gemvk {
 
 enum Fmt { F_Q8 = 0, F_Q6 = 1, F_T2 = 2, F_B1 = 3 };
-enum Pro { PRO_Q = 0, PRO_RMS = 1, PRO_QUANT = 2 };
-enum Epi { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+enum Pro { PRO_Q = 0, PRO_RMS = 1, PRO_QUANT = 2, PRO_RMS_SUM = 3 };
+enum Epi { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_SEND = 3 };
+
+// A tensor-parallel rank's side of one reduction over NVLink (exchange.cu): the row-parallel product (wo, w2: each
+// rank's share of K) sends its rows to every rank's receive region (EPI_SEND) and counts its CTAs done there; the
+// next product's prologue (PRO_RMS_SUM) waits for every rank's count, makes x + the ranks' partials (in rank order,
+// so every rank gets the same bits), writes that to x_out (CTA 0) and takes RMSNorm and quantize_x of it.
+constexpr int TP_MAX = 8;
+struct Xchg {
+  float* dst[TP_MAX];        // EPI_SEND: rank p's receive slot of this rank, this parity ([dim] floats)
+  unsigned* sig[TP_MAX];     // EPI_SEND: rank p's count of this rank's CTAs done, this parity
+  const float* src;          // PRO_RMS_SUM: this rank's receive region of this parity, [world][dim]
+  const unsigned* cnt;       // PRO_RMS_SUM: this rank's counts of this parity, [world]
+  const unsigned* step;      // this rank's step counter (pllm_tp_step: 1 in the first step)
+  float* x_out;              // PRO_RMS_SUM: x + the partials
+  int world;
+  unsigned per_step, k, ncta;  // a count is complete at ((step - 1) per_step + k + 1) ncta
+};
 
 struct GemvArgs {
   float* out;              // out + t * out_stride (floats) + row
@@ -102,8 +118,27 @@ __device__ __forceinline__ void quantize_pair(const GemvArgs& a, const float4* x
 struct CtaSync {
   __device__ __forceinline__ void operator()() const { __syncthreads(); }
 };
+// x's float4 number i of token t: PRO_RMS_SUM adds the ranks' partials in rank order (read from L2: other GPUs wrote
+// them) and CTA 0 stores the sum to x_out
+template <int PRO>
+__device__ __forceinline__ float4 x_vec(const GemvArgs& a, const Xchg* xg, int t, int i) {
+  float4 v = reinterpret_cast<const float4*>(a.x + t * a.x_stride)[i];
+  if constexpr (PRO == PRO_RMS_SUM) {
+    for (int p = 0; p < xg->world; p++) {
+      const float4 r = __ldcg(reinterpret_cast<const float4*>(xg->src) + (size_t)p * (a.K / 4) + i);
+      v.x += r.x;
+      v.y += r.y;
+      v.z += r.z;
+      v.w += r.w;
+    }
+    if (blockIdx.x == 0) reinterpret_cast<float4*>(xg->x_out)[i] = v;
+  }
+  return v;
+}
+
 template <int FMT, int MT, int PRO, class SYNC = CtaSync>
-__device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, float* ss, int32_t* sm) {
+__device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, float* ss, int32_t* sm,
+                                                 const Xchg* xg = nullptr) {
   const SYNC sync;
   const int K = a.K, ng = K / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -137,9 +172,9 @@ __device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, 
     constexpr int RMAX = 3;  // rounds of 128 groups held in registers (K <= 12288); past them read again
     const int pair = threadIdx.x >> 1, h = threadIdx.x & 1;
     const int rounds = (ng + 127) / 128;
+    constexpr bool NORM = PRO == PRO_RMS || PRO == PRO_RMS_SUM;
     for (int t = 0; t < MT; t++) {
       if (t >= a.count) break;
-      const float4* x4 = reinterpret_cast<const float4*>(a.x + t * a.x_stride);
       const float4* n4 = reinterpret_cast<const float4*>(a.norm);
       float4 v[RMAX][4], w[RMAX][4];
 #pragma unroll
@@ -148,12 +183,12 @@ __device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, 
         const bool in = r < rounds && g < ng;
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-          v[r][k] = in ? x4[(32 * g + 16 * h) / 4 + k] : make_float4(0.f, 0.f, 0.f, 0.f);
-          w[r][k] = (PRO == PRO_RMS && in) ? __ldg(n4 + (32 * g + 16 * h) / 4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[r][k] = in ? x_vec<PRO>(a, xg, t, (32 * g + 16 * h) / 4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+          w[r][k] = (NORM && in) ? __ldg(n4 + (32 * g + 16 * h) / 4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
       float rs = 1.0f;
-      if (PRO == PRO_RMS) {
+      if (NORM) {
         float s = 0.0f;
 #pragma unroll
         for (int r = 0; r < RMAX; r++) {
@@ -165,7 +200,7 @@ __device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, 
           const int g = pair + 128 * r;
           if (g < ng)
             for (int k = 0; k < 4; k++) {
-              const float4 u = x4[(32 * g + 16 * h) / 4 + k];
+              const float4 u = x_vec<PRO>(a, xg, t, (32 * g + 16 * h) / 4 + k);
               s = fmaf(u.x, u.x, fmaf(u.y, u.y, fmaf(u.z, u.z, fmaf(u.w, u.w, s))));
             }
         }
@@ -178,18 +213,19 @@ __device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, 
         rs = 1.0f / sqrtf(tot / (float)K + a.eps);
         sync();
       }
+      constexpr int QP = NORM ? PRO_RMS : PRO;
 #pragma unroll
       for (int r = 0; r < RMAX; r++) {
-        if (r < rounds) quantize_pair<PRO>(a, v[r], w[r], rs, pair + 128 * r, h, t, sq, ss);
+        if (r < rounds) quantize_pair<QP>(a, v[r], w[r], rs, pair + 128 * r, h, t, sq, ss);
       }
       for (int r = RMAX; r < rounds; r++) {
         const int g = pair + 128 * r;
         float4 xv[4], wv[4];
         for (int k = 0; k < 4; k++) {
-          xv[k] = g < ng ? x4[(32 * g + 16 * h) / 4 + k] : make_float4(0.f, 0.f, 0.f, 0.f);
-          wv[k] = (PRO == PRO_RMS && g < ng) ? __ldg(n4 + (32 * g + 16 * h) / 4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+          xv[k] = g < ng ? x_vec<PRO>(a, xg, t, (32 * g + 16 * h) / 4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+          wv[k] = (NORM && g < ng) ? __ldg(n4 + (32 * g + 16 * h) / 4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        quantize_pair<PRO>(a, xv, wv, rs, g, h, t, sq, ss);
+        quantize_pair<QP>(a, xv, wv, rs, g, h, t, sq, ss);
       }
     }
   }
@@ -200,8 +236,11 @@ __device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, 
 }
 
 
-// gemv_tma.cu: the bulk-copy pipeline for int8 at 1 or 2 tokens; false where it does not apply
-bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl);
+// gemv_tma.cu: the bulk-copy pipeline for int8 at 1 or 2 tokens; false where it does not apply (xg: the exchange of
+// PRO_RMS_SUM / EPI_SEND, which only this kernel takes)
+bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg* xg = nullptr);
+// the CTAs gemv_tma launches for rows r0..r1 (EPI_SEND's producers: their count is what a PRO_RMS_SUM waits for)
+int gemv_tma_grid(long long rows, int epi);
 extern int g_gemv_mode;
 extern int g_tma_budget;
 

@@ -26,6 +26,34 @@ constexpr int NC = 8;                 // consumer warps
 constexpr int TR = NC;                // row slots a stage
 constexpr int TMA_THREADS = (NC + 1) * 32;
 constexpr long long WAIT_BOUND = 1ll << 26;  // polls of an mbarrier before giving up (seconds: never in a run that works)
+constexpr unsigned long long XCHG_WAIT_NS = 2000000000ull;  // the wait for the other ranks' partials: 2 s at most
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// PRO_RMS_SUM: thread s (< world) of the consumers waits until rank s's count of CTAs done reaches this reduction's
+// mark (system-scope acquire: the counts and the partials are written by other GPUs); past 2 s it records
+// PLLM_ETIMEOUT and goes on (the partials it then reads are wrong, and the host sees the status)
+__device__ __forceinline__ void wait_partials(const Xchg& xg) {
+  if (threadIdx.x < xg.world) {
+    const unsigned step = *xg.step;
+    const unsigned mark = ((step - 1u) * xg.per_step + xg.k + 1u) * xg.ncta;
+    const unsigned* c = xg.cnt + threadIdx.x;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+      if ((int)(v - mark) >= 0) break;
+      if (global_ns() - t0 > XCHG_WAIT_NS) {
+        atomicExch(&g_pllm_status, PLLM_ETIMEOUT);
+        break;
+      }
+    }
+  }
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -89,7 +117,7 @@ __device__ __forceinline__ int tile_rows(long long t, long long hi) {
 }
 
 template <int MT, int PRO, int EPI>
-__global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs a, const TmaPlan p) {
+__global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs a, const TmaPlan p, const Xchg xg) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages, KS = p.ks, chunks = p.chunks, K = a.K, ng = K / 32;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -152,11 +180,17 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
     return;
   }
 
-  // ---- the consumers
+  // ---- the consumers (a wait that gives up makes the warp skip its work from then on, but it still meets every
+  // barrier of the consumers, so that none of them waits for it)
   pdl_wait();
-  load_activations<F_Q8, MT, PRO, ConsumerSync>(a, sq, ss, nullptr);
+  if (PRO == PRO_RMS_SUM) {
+    wait_partials(xg);
+    consumer_sync();
+  }
+  load_activations<F_Q8, MT, PRO, ConsumerSync>(a, sq, ss, nullptr, &xg);
   consumer_sync();
   pdl_launch_dependents();
+  bool ok = true;
   const int swz = (lane >> 2) & 1;  // which half of its 32 bytes a lane reads first: no bank conflicts
   long long it = 0;
   int tiles = 0;
@@ -169,8 +203,8 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
     for (int c = 0; c < chunks; c++, it++) {
       const int slot = (int)(it % S);
       const unsigned round = (unsigned)(it / S);
-      if (!mbar_wait(&full[slot], round & 1)) return;
-      if (mine) {
+      if (ok) ok = mbar_wait(&full[slot], round & 1);
+      if (mine && ok) {
         const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * KS;
         const float* sc = reinterpret_cast<const float*>(stage0 + (size_t)slot * p.stage_bytes + (size_t)TR * KS) +
                           (size_t)warp * (KS / 32);
@@ -224,21 +258,29 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
       for (int m = 1; m < MT; m++)
         if (lane == m) v = acc[m];
       float* o = a.out + lane * a.out_stride + t + warp;
-      if (EPI == EPI_ADD) *o += v;
-      else *o = v;
+      if (EPI == EPI_SEND) {
+        for (int r = 0; r < xg.world; r++) xg.dst[r][t + warp] = v;
+      } else if (EPI == EPI_ADD) {
+        *o += v;
+      } else {
+        *o = v;
+      }
+    }
+  }
+  if (EPI == EPI_SEND) {  // this CTA's rows are at every rank: count it there (one fence orders the warps' stores)
+    consumer_sync();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int r = 0; r < xg.world; r++) atomicAdd_system(xg.sig[r], 1u);
     }
   }
 }
 
 template <int MT, int PRO, int EPI>
-bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl) {
+bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl, const Xchg& xg) {
   auto kernel = gemv_tma_kernel<MT, PRO, EPI>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return false;
-  const long long rows = a.r1 - a.r0;
-  const long long per_tile = EPI == EPI_SWIGLU ? TR / 2 : TR;
-  long long grid = pllm_num_sms();
-  const long long tiles = (rows + per_tile - 1) / per_tile;
-  if (grid > tiles) grid = tiles;
+  const long long grid = gemv_tma_grid(a.r1 - a.r0, EPI);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(TMA_THREADS);
@@ -249,7 +291,7 @@ bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a, p, xg);
   if (e != cudaSuccess) {
     pllm_fail(PLLM_ECUDA, "gemv_tma launch: %s", cudaGetErrorString(e));
     return true;  // failed, but not for want of a fit: do not fall back
@@ -267,10 +309,19 @@ int g_tma_budget = 200 * 1024;
 // 0: the bulk-copy kernel wherever it applies; 1: the register-streaming kernel only (for comparisons)
 int g_gemv_mode = 0;
 
+int gemv_tma_grid(long long rows, int epi) {
+  const long long per_tile = epi == EPI_SWIGLU ? TR / 2 : TR;
+  const long long tiles = (rows + per_tile - 1) / per_tile;
+  const long long sms = pllm_num_sms();
+  return (int)(tiles < sms ? tiles : sms);
+}
+
 // The bulk-copy product for int8 weights at 1 or 2 tokens; false where it does not apply (the caller then takes the
 // register-streaming kernel).
-bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl) {
-  if (g_gemv_mode == 1 || fmt != F_Q8 || a.count < 1 || a.count > 2) return false;
+bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg* xg) {
+  const bool tp = pro == PRO_RMS_SUM || epi == EPI_SEND;
+  if (tp != (xg != nullptr)) return false;
+  if (g_gemv_mode == 1 || fmt != F_Q8 || a.count < 1 || a.count > 2 || (tp && a.count != 1)) return false;
   const int K = a.K;
   if (K % 128 || ((uintptr_t)a.wq & 15) || ((uintptr_t)a.ws & 15)) return false;
   TmaPlan p = {};
@@ -287,12 +338,15 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl) {
   p.stages = S;
   const size_t smem = (size_t)head + p.act_bytes + (size_t)S * p.stage_bytes;
   if (smem > 227 * 1024) return false;
+  const Xchg none = {};
+  const Xchg& x = xg ? *xg : none;
 #define CASE(M, P, E) \
-  if (MT == M && pro == P && epi == E) return launch<M, P, E>(a, p, smem, pdl);
+  if (MT == M && pro == P && epi == E) return launch<M, P, E>(a, p, smem, pdl, x);
   CASE(1, PRO_Q, EPI_STORE) CASE(1, PRO_Q, EPI_ADD) CASE(1, PRO_Q, EPI_SWIGLU)
   CASE(1, PRO_RMS, EPI_STORE) CASE(1, PRO_RMS, EPI_ADD) CASE(1, PRO_RMS, EPI_SWIGLU)
   CASE(1, PRO_QUANT, EPI_STORE) CASE(1, PRO_QUANT, EPI_ADD) CASE(1, PRO_QUANT, EPI_SWIGLU)
   CASE(2, PRO_Q, EPI_STORE) CASE(2, PRO_RMS, EPI_STORE) CASE(2, PRO_QUANT, EPI_ADD) CASE(2, PRO_RMS, EPI_SWIGLU)
+  CASE(1, PRO_RMS_SUM, EPI_STORE) CASE(1, PRO_RMS_SUM, EPI_SWIGLU) CASE(1, PRO_QUANT, EPI_SEND)
 #undef CASE
   return false;
 }

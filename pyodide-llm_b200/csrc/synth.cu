@@ -28,12 +28,16 @@ __global__ void synth_f32_kernel(float* out, long long n, uint64_t seed, float m
     out[i] = mean + std * normal_of(seed, (uint64_t)i);
 }
 
-// a warp a group of 32: N(0, std) values, quantized (bias 0: the converter's int8)
-__global__ void synth_q8_kernel(int8_t* wq, float* ws, long long groups, uint64_t seed, float std) {
+// a warp a group of 32: N(0, std) values, quantized (bias 0: the converter's int8). The block's element (r, c) is
+// element (row0 + r, col0 + c) of a matrix of full_cols columns, so a block is a slice of the whole matrix's bytes.
+__global__ void synth_q8_kernel(int8_t* wq, float* ws, long long groups, int cols, long long row0, long long col0,
+                                long long full_cols, uint64_t seed, float std) {
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const int per_row = cols / 32;
   for (long long g = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); g < groups; g += warps) {
-    const float v = std * normal_of(seed, (uint64_t)(g * 32 + lane));
+    const long long r = g / per_row, c = (g % per_row) * 32 + lane;
+    const float v = std * normal_of(seed, (uint64_t)((row0 + r) * full_cols + col0 + c));
     float s;
     const int8_t q = quantize_group_warp(v, lane, 0, &s);
     wq[g * 32 + lane] = q;
@@ -75,12 +79,22 @@ PLLM_API void pllm_synth_f32(uint64_t out, int64_t n, uint64_t seed, float mean,
   PLLM_LAUNCHED("pllm_synth_f32");
 }
 
-PLLM_API void pllm_synth_q8(uint64_t wq, uint64_t ws, int64_t rows, int32_t cols, uint64_t seed, float std) {
-  PLLM_REQUIRE(rows >= 0 && cols > 0 && cols % 32 == 0, "pllm_synth_q8: rows %lld cols %d", (long long)rows, cols);
+PLLM_API void pllm_synth_q8_block(uint64_t wq, uint64_t ws, int64_t rows, int32_t cols, uint64_t seed, float std,
+                                  int64_t row0, int64_t col0, int64_t full_cols) {
+  PLLM_REQUIRE(rows >= 0 && cols > 0 && cols % 32 == 0 && row0 >= 0 && col0 >= 0 && col0 % 32 == 0 &&
+                   full_cols % 32 == 0 && col0 + cols <= full_cols,
+               "pllm_synth_q8_block: rows %lld cols %d at (%lld, %lld) of %lld", (long long)rows, cols, (long long)row0,
+               (long long)col0, (long long)full_cols);
   const long long groups = rows * (cols / 32);
   if (!groups) return;
-  synth_q8_kernel<<<grid_n(groups * 32), 256, 0, pllm_stream()>>>(dptr<int8_t>(wq), dptr<float>(ws), groups, seed, std);
-  PLLM_LAUNCHED("pllm_synth_q8");
+  synth_q8_kernel<<<grid_n(groups * 32), 256, 0, pllm_stream()>>>(dptr<int8_t>(wq), dptr<float>(ws), groups, cols,
+                                                                   row0, col0, full_cols, seed, std);
+  PLLM_LAUNCHED("pllm_synth_q8_block");
+}
+
+PLLM_API void pllm_synth_q8(uint64_t wq, uint64_t ws, int64_t rows, int32_t cols, uint64_t seed, float std) {
+  PLLM_REQUIRE(rows >= 0 && cols > 0 && cols % 32 == 0, "pllm_synth_q8: rows %lld cols %d", (long long)rows, cols);
+  pllm_synth_q8_block(wq, ws, rows, cols, seed, std, 0, 0, cols);
 }
 
 PLLM_API void pllm_synth_t2(uint64_t wq, uint64_t ws, int64_t rows, int32_t cols, uint64_t seed, float mean, float std) {

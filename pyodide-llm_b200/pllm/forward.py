@@ -16,6 +16,11 @@ position are read by the kernels from device memory, so the same graph serves ev
       x += w2 . quantize_x(hb)            (pllm_gemv pro 2, epi 1)
     logits = wcls . quantize_x(RMSNorm(x))
 
+With an exchange (pllm.tp.Exchange: tensor parallelism, one process a GPU) each rank holds its share of the matrices
+(pllm.tp.Shard) and its heads' cache; wo and w2 send their partials to every rank (pllm_gemv_tp epi 3) instead of
+adding them to x, and the next product sums them into x in its prologue (pro 3), x alternating between two buffers
+(the prologue's CTAs all read one while the first writes the other). The logits are the rank's vocab rows.
+
 Every product's group sums are the reference kernels' exact integers; the float32 around them agrees with the
 reference's within rounding (the tests hold the logits to the oracle's within 1e-3 relative).
 """
@@ -26,10 +31,11 @@ import numpy as np
 
 from .device import Buffer, Pinned, init
 from .lib import L, check
+from .tp import Shard
 
 F_Q8 = 0
-PRO_Q, PRO_RMS, PRO_QUANT = 0, 1, 2
-EPI_STORE, EPI_ADD, EPI_SWIGLU = 0, 1, 2
+PRO_Q, PRO_RMS, PRO_QUANT, PRO_RMS_SUM = 0, 1, 2, 3
+EPI_STORE, EPI_ADD, EPI_SWIGLU, EPI_SEND = 0, 1, 2, 3
 
 
 @dataclass
@@ -118,30 +124,32 @@ class Engine:
 
     SPLIT = 128  # positions a slice of the split-KV attention (two tiles of 64 a CTA, double-buffered)
 
-    def __init__(self, cfg, host=None, seed=0, device=0, graphs=True, pdl=True):
+    def __init__(self, cfg, host=None, seed=0, device=0, graphs=True, pdl=True, exchange=None):
         init(device)
+        self.xg = exchange
+        self.shard = s = Shard(cfg, exchange.rank, exchange.world) if exchange else Shard(cfg)
         if os.environ.get("PLLM_STAGE_BUDGET"):  # the bulk-copy product's stage ring, bytes (a tuning knob)
             L.pllm_set_stage_budget(int(os.environ["PLLM_STAGE_BUDGET"]))
         self.cfg, self.graphs = cfg, graphs
         self.pdl = pdl and not os.environ.get("PLLM_NO_PDL")  # (a switch for measuring what the early launches give)
         c = cfg
-        self.rows_qkv = c.qdim + 2 * c.kvdim
+        self.rows_qkv = s.rows_qkv
         self.bias = 64 if c.relaxed else 0
         B = {}
         ng = lambda cols: cols // 32  # noqa: E731
-        # the matrices, a layer's after another; q, k, v rows in one, w1 rows then w3 rows in one
+        # the matrices (this rank's share), a layer's after another; q, k, v rows in one, w1 rows then w3 rows in one
         B["wqkv"] = Buffer(c.layers * self.rows_qkv * c.dim)
         B["sqkv"] = Buffer(c.layers * self.rows_qkv * ng(c.dim) * 4)
-        B["wo"] = Buffer(c.layers * c.dim * c.qdim)
-        B["so"] = Buffer(c.layers * c.dim * ng(c.qdim) * 4)
-        B["w13"] = Buffer(c.layers * 2 * c.hidden * c.dim)
-        B["s13"] = Buffer(c.layers * 2 * c.hidden * ng(c.dim) * 4)
-        B["w2"] = Buffer(c.layers * c.dim * c.hidden)
-        B["s2"] = Buffer(c.layers * c.dim * ng(c.hidden) * 4)
+        B["wo"] = Buffer(c.layers * c.dim * s.qdim)
+        B["so"] = Buffer(c.layers * c.dim * ng(s.qdim) * 4)
+        B["w13"] = Buffer(c.layers * 2 * s.hidden * c.dim)
+        B["s13"] = Buffer(c.layers * 2 * s.hidden * ng(c.dim) * 4)
+        B["w2"] = Buffer(c.layers * c.dim * s.hidden)
+        B["s2"] = Buffer(c.layers * c.dim * ng(s.hidden) * 4)
         B["emb"] = Buffer(c.vocab * c.dim)
         B["emb_s"] = Buffer(c.vocab * ng(c.dim) * 4)
-        B["cls"] = Buffer(c.vocab * c.dim)
-        B["cls_s"] = Buffer(c.vocab * ng(c.dim) * 4)
+        B["cls"] = Buffer(s.vocab * c.dim)
+        B["cls_s"] = Buffer(s.vocab * ng(c.dim) * 4)
         B["att_norm"] = Buffer(c.layers * c.dim * 4)
         B["ffn_norm"] = Buffer(c.layers * c.dim * 4)
         B["final_norm"] = Buffer(c.dim * 4)
@@ -150,17 +158,18 @@ class Engine:
         B["cos_t"] = Buffer(c.seq_len * c.head_size // 2 * 4)
         B["sin_t"] = Buffer(c.seq_len * c.head_size // 2 * 4)
         E = 2 if c.half_kv else 4
-        B["kc"] = Buffer(c.layers * c.seq_len * c.kvdim * E).zero()
-        B["vc"] = Buffer(c.layers * c.seq_len * c.kvdim * E).zero()
+        B["kc"] = Buffer(c.layers * c.seq_len * s.kvdim * E).zero()
+        B["vc"] = Buffer(c.layers * c.seq_len * s.kvdim * E).zero()
         # activations
         B["x"] = Buffer(c.dim * 4)
+        B["x1"] = Buffer(c.dim * 4) if exchange else None  # the residual's other buffer (tensor-parallel)
         B["qkv"] = Buffer(self.rows_qkv * 4)
-        B["att"] = Buffer(c.qdim * 4)
-        B["hb"] = Buffer(c.hidden * 4)
-        B["logits"] = Buffer(c.vocab * 4)
+        B["att"] = Buffer(s.qdim * 4)
+        B["hb"] = Buffer(s.hidden * 4)
+        B["logits"] = Buffer(s.vocab * 4)
         B["tp"] = Buffer(8).zero()      # the token and the position, read by the kernels
         B["bad"] = Buffer(4).zero()     # non-finite keys / values written to a float16 cache (halves.ts:35)
-        B["scratch"] = Buffer(L.pllm_attention_scratch_bytes(c.heads, c.head_size, c.seq_len, self.SPLIT)).zero()
+        B["scratch"] = Buffer(L.pllm_attention_scratch_bytes(s.heads, c.head_size, c.seq_len, self.SPLIT)).zero()
         self.B = B
         if host is not None:
             self.load(host)
@@ -168,14 +177,17 @@ class Engine:
             self.synthesize(seed)
         self.stream = L.pllm_stream_create()
         self.tp_host = Pinned(2, np.int32)
-        self.logits_host = Pinned(c.vocab, np.float32)
+        self.logits_host = Pinned(s.vocab, np.float32)
         self.graph = 0
         check("Engine")
 
     # ---- weights
     def load(self, W):
-        """Host weights (synthetic_host_weights' dict, the reference's int8 layout) into the device layout."""
+        """Host weights (synthetic_host_weights' dict, the reference's int8 layout) into the device layout (this rank's
+        share of them with an exchange)."""
         c, B = self.cfg, self.B
+        if self.xg:
+            W = self.shard.host_share(W)
         B["wqkv"].upload(np.concatenate([W["wq"], W["wk"], W["wv"]], axis=1))
         B["sqkv"].upload(np.concatenate([W["sq"], W["sk"], W["sv"]], axis=1))
         B["wo"].upload(W["wo"])
@@ -197,11 +209,14 @@ class Engine:
         N(1, 0.1), the RoPE tables of the configuration."""
         c, B = self.cfg, self.B
         s = seed * 1000
-        for i, (w, sc, rows, cols) in enumerate([
-                ("wqkv", "sqkv", c.layers * self.rows_qkv, c.dim), ("wo", "so", c.layers * c.dim, c.qdim),
-                ("w13", "s13", c.layers * 2 * c.hidden, c.dim), ("w2", "s2", c.layers * c.dim, c.hidden),
-                ("cls", "cls_s", c.vocab, c.dim)]):
-            L.pllm_synth_q8(B[w].ptr, B[sc].ptr, rows, cols, s + i, 0.02)
+        if self.xg:
+            self._synthesize_share(s)
+        else:
+            for i, (w, sc, rows, cols) in enumerate([
+                    ("wqkv", "sqkv", c.layers * self.rows_qkv, c.dim), ("wo", "so", c.layers * c.dim, c.qdim),
+                    ("w13", "s13", c.layers * 2 * c.hidden, c.dim), ("w2", "s2", c.layers * c.dim, c.hidden),
+                    ("cls", "cls_s", c.vocab, c.dim)]):
+                L.pllm_synth_q8(B[w].ptr, B[sc].ptr, rows, cols, s + i, 0.02)
         L.pllm_synth_q8(B["emb"].ptr, B["emb_s"].ptr, c.vocab, c.dim, s + 10, 1.0)
         for i, k in enumerate(("att_norm", "ffn_norm", "final_norm", "q_norm", "k_norm")):
             if B[k] is not None:
@@ -212,20 +227,40 @@ class Engine:
         L.pllm_sync()
         check("synthesize")
 
+    def _synthesize_share(self, s):
+        """This rank's blocks of the matrices synthesize() makes whole (the same bytes: pllm_synth_q8_block)."""
+        c, B, sh = self.cfg, self.B, self.shard
+        blk = lambda w, sc, row, nrows, cols, row0, col0, full, seed: L.pllm_synth_q8_block(  # noqa: E731
+            B[w].ptr + row * cols, B[sc].ptr + row * (cols // 32) * 4, nrows, cols, seed, 0.02, row0, col0, full)
+        R = c.qdim + 2 * c.kvdim  # a layer's q/k/v rows in the whole model
+        for l in range(c.layers):
+            at = l * self.rows_qkv
+            blk("wqkv", "sqkv", at, sh.qdim, c.dim, l * R + sh.q_rows().start, 0, c.dim, s)
+            blk("wqkv", "sqkv", at + sh.qdim, sh.kvdim, c.dim, l * R + c.qdim + sh.kv_rows().start, 0, c.dim, s)
+            blk("wqkv", "sqkv", at + sh.qdim + sh.kvdim, sh.kvdim, c.dim,
+                l * R + c.qdim + c.kvdim + sh.kv_rows().start, 0, c.dim, s)
+            at = l * 2 * sh.hidden
+            blk("w13", "s13", at, sh.hidden, c.dim, l * 2 * c.hidden + sh.hidden_rows().start, 0, c.dim, s + 2)
+            blk("w13", "s13", at + sh.hidden, sh.hidden, c.dim, l * 2 * c.hidden + c.hidden + sh.hidden_rows().start,
+                0, c.dim, s + 2)
+        blk("wo", "so", 0, c.layers * c.dim, sh.qdim, 0, sh.q_rows().start, c.qdim, s + 1)
+        blk("w2", "s2", 0, c.layers * c.dim, sh.hidden, 0, sh.hidden_rows().start, c.hidden, s + 3)
+        blk("cls", "cls_s", 0, sh.vocab, c.dim, sh.vocab_rows().start, 0, c.dim, s + 4)
+
     def host_weights(self):
         """The device weights back in the oracle's layout (for the CPU baseline and the checks)."""
-        c, B = self.cfg, self.B
+        c, B, sh = self.cfg, self.B, self.shard
         d = lambda k, dt: B[k].download(dt)  # noqa: E731
         W = {}
         qkv = d("wqkv", np.int8).reshape(c.layers, self.rows_qkv, c.dim)
         sqkv = d("sqkv", np.float32).reshape(c.layers, self.rows_qkv, c.dim // 32)
-        W["wq"], W["wk"], W["wv"] = np.split(qkv, [c.qdim, c.qdim + c.kvdim], axis=1)
-        W["sq"], W["sk"], W["sv"] = np.split(sqkv, [c.qdim, c.qdim + c.kvdim], axis=1)
+        W["wq"], W["wk"], W["wv"] = np.split(qkv, [sh.qdim, sh.qdim + sh.kvdim], axis=1)
+        W["sq"], W["sk"], W["sv"] = np.split(sqkv, [sh.qdim, sh.qdim + sh.kvdim], axis=1)
         W["wo"], W["so"] = d("wo", np.int8), d("so", np.float32)
-        w13 = d("w13", np.int8).reshape(c.layers, 2 * c.hidden, c.dim)
-        s13 = d("s13", np.float32).reshape(c.layers, 2 * c.hidden, c.dim // 32)
-        W["w1"], W["w3"] = w13[:, :c.hidden], w13[:, c.hidden:]
-        W["s1"], W["s3"] = s13[:, :c.hidden], s13[:, c.hidden:]
+        w13 = d("w13", np.int8).reshape(c.layers, 2 * sh.hidden, c.dim)
+        s13 = d("s13", np.float32).reshape(c.layers, 2 * sh.hidden, c.dim // 32)
+        W["w1"], W["w3"] = w13[:, :sh.hidden], w13[:, sh.hidden:]
+        W["s1"], W["s3"] = s13[:, :sh.hidden], s13[:, sh.hidden:]
         W["w2"], W["s2"] = d("w2", np.int8), d("s2", np.float32)
         for k, dt in (("emb", np.int8), ("emb_s", np.float32), ("cls", np.int8), ("cls_s", np.float32),
                       ("att_norm", np.float32), ("ffn_norm", np.float32), ("final_norm", np.float32),
@@ -245,9 +280,11 @@ class Engine:
     def launches_per_step(self):
         """Kernels a step launches: the embedding, five a layer (the q/k/v product; the attention with the q / k
         norms, RoPE, the cache write and its slices' combine inside; the wo, w1/w3 and w2 products), the classifier."""
-        return 2 + 5 * self.cfg.layers
+        return 2 + 5 * self.cfg.layers + (1 if self.xg else 0)
 
     def _enqueue_step(self, need_logits=True):
+        if self.xg:
+            return self._enqueue_tp_step(need_logits)
         c, B = self.cfg, self.B
         tok, pos = B["tp"].ptr, B["tp"].ptr + 4
         E = 2 if c.half_kv else 4
@@ -274,6 +311,46 @@ class Engine:
         if need_logits:
             self._gemv(B["logits"].ptr, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim, B["x"].ptr, B["final_norm"].ptr,
                        PRO_RMS, EPI_STORE)
+
+    def _enqueue_tp_step(self, need_logits=True):
+        """One tensor-parallel step: reduction 2 l after layer l's wo (summed into x1 by its w1/w3 product), 2 l + 1
+        after its w2 (summed into x by the next layer's q/k/v product, or the classifier's)."""
+        c, B, sh, xg = self.cfg, self.B, self.shard, self.xg.h
+        tok, pos = B["tp"].ptr, B["tp"].ptr + 4
+        E = 2 if c.half_kv else 4
+        pdl = int(self.pdl)
+        x0, x1 = B["x"].ptr, B["x1"].ptr
+        L.pllm_tp_step(xg)
+        L.pllm_embed_q8(x0, B["emb"].ptr, B["emb_s"].ptr, tok, 0, c.dim, 1, c.dim)
+        for l in range(c.layers):
+            wqkv = B["wqkv"].ptr + l * self.rows_qkv * c.dim
+            sqkv = B["sqkv"].ptr + l * self.rows_qkv * (c.dim // 32) * 4
+            norm = B["att_norm"].ptr + l * c.dim * 4
+            if l == 0:
+                L.pllm_gemv_tp(B["qkv"].ptr, x0, 0, norm, c.eps, self.bias, wqkv, sqkv, c.dim, self.rows_qkv,
+                               PRO_RMS, EPI_STORE, 0, pdl, xg, 0)
+            else:
+                L.pllm_gemv_tp(B["qkv"].ptr, x1, x0, norm, c.eps, self.bias, wqkv, sqkv, c.dim, self.rows_qkv,
+                               PRO_RMS_SUM, EPI_STORE, 0, pdl, xg, 2 * l - 1)
+            kc = B["kc"].ptr + l * c.seq_len * sh.kvdim * E
+            vc = B["vc"].ptr + l * c.seq_len * sh.kvdim * E
+            qn = B["q_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
+            kn = B["k_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
+            L.pllm_attention_step(B["att"].ptr, B["qkv"].ptr, kc, vc, B["scratch"].ptr, pos, c.seq_len, sh.heads,
+                                  sh.kv_heads, c.head_size, int(c.half_kv), 0.0, self.SPLIT, qn, kn, B["cos_t"].ptr,
+                                  B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, pdl)
+            L.pllm_gemv_tp(0, B["att"].ptr, 0, 0, c.eps, self.bias, B["wo"].ptr + l * c.dim * sh.qdim,
+                           B["so"].ptr + l * c.dim * (sh.qdim // 32) * 4, sh.qdim, c.dim, PRO_QUANT, EPI_SEND, 0, pdl,
+                           xg, 2 * l)
+            L.pllm_gemv_tp(B["hb"].ptr, x0, x1, B["ffn_norm"].ptr + l * c.dim * 4, c.eps, self.bias,
+                           B["w13"].ptr + l * 2 * sh.hidden * c.dim, B["s13"].ptr + l * 2 * sh.hidden * (c.dim // 32) * 4,
+                           c.dim, sh.hidden, PRO_RMS_SUM, EPI_SWIGLU, sh.hidden, pdl, xg, 2 * l)
+            L.pllm_gemv_tp(0, B["hb"].ptr, 0, 0, c.eps, self.bias, B["w2"].ptr + l * c.dim * sh.hidden,
+                           B["s2"].ptr + l * c.dim * (sh.hidden // 32) * 4, sh.hidden, c.dim, PRO_QUANT, EPI_SEND, 0,
+                           pdl, xg, 2 * l + 1)
+        # the classifier sums the last reduction whether or not the logits are wanted (every rank takes every step)
+        L.pllm_gemv_tp(B["logits"].ptr, x1, x0, B["final_norm"].ptr, c.eps, self.bias, B["cls"].ptr, B["cls_s"].ptr,
+                       c.dim, sh.vocab, PRO_RMS_SUM, EPI_STORE, 0, pdl, xg, 2 * c.layers - 1)
 
     def capture(self):
         """Record one decode step (with logits) as a CUDA graph on the engine's stream."""
@@ -320,7 +397,7 @@ class Engine:
         L.pllm_h2d(self.B["tp"].ptr, self.tp_host.ptr, 8)
         self.launch_step()
         if need_logits:
-            L.pllm_d2h(self.logits_host.ptr, self.B["logits"].ptr, c.vocab * 4)
+            L.pllm_d2h(self.logits_host.ptr, self.B["logits"].ptr, self.shard.vocab * 4)
         L.pllm_sync()
         check("forward")
         return self.logits_host.array.copy() if need_logits else None

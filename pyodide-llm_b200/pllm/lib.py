@@ -96,6 +96,13 @@ SIGNATURES = {
     "pllm_set_attention_mode": ([I32], I32),
     "pllm_synth_f32": ([U64, I64, U64, F32, F32], None),
     "pllm_synth_q8": ([U64, U64, I64, I32, U64, F32], None),
+    "pllm_synth_q8_block": ([U64, U64, I64, I32, U64, F32, I64, I64, I64], None),
+    "pllm_tp_open": ([I32, I32, I32, I32], U64),
+    "pllm_tp_handle": ([U64, P], I32),
+    "pllm_tp_connect": ([U64, P], I32),
+    "pllm_tp_close": ([U64], None),
+    "pllm_tp_step": ([U64], None),
+    "pllm_gemv_tp": ([U64, U64, U64, U64, F32, I32, U64, U64, I32, I32, I32, I32, I64, I32, U64, I32], None),
     "pllm_synth_t2": ([U64, U64, I64, I32, U64, F32, F32], None),
 }
 
