@@ -14,8 +14,9 @@ reference's group-of-32 format); the prompt is seeded random ids. Prints one JSO
               algorithmic bytes a launch over its CUDA-event duration, against MEASURED_PEAKS.json's HBM copy GB/s
   cpu_baseline  the CPU oracle (the reference kernels' arithmetic in C, OpenMP over rows) decoding the same model
               on the host cores, a bounded sample of tokens (rank 0, N = 1)
-Under torchrun (N > 1) every rank runs its own replica on its GPU (the path does not shard without a tensor-parallel
-split, which is not built yet): scaling "weak", value = all ranks' tokens / the slowest rank's time.
+Under torchrun (N > 1) the ranks decode one stream together, tensor-parallel (pllm.tp: each GPU holds 1/N of every
+matrix and its heads' cache; the two reductions a layer go over NVLink in the products' epilogues and prologues):
+scaling "strong" (the work of a token is fixed), value = tokens / the slowest rank's time.
 
 --impl reference: the reference's CPU implementation of the path, timed on the host cores: its kernels are
 AssemblyScript compiled to WASM and cannot run on this image (no Node, Bun or AssemblyScript), so the oracle's C
@@ -213,24 +214,26 @@ def main():
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
     dist = None
-    if world > 1:
-        import datetime
-
-        import torch
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
-
-    from pllm.device import Buffer
+    from pllm.device import Buffer, init
     from pllm.forward import Engine
     from pllm.lib import L, check
+    from pllm.tp import Exchange
+    init(local)
+    xg = None
+    if world > 1:  # host plumbing only (handles, barriers, the max of the ranks' times): the data path is NVLink
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+        xg = Exchange(cfg, rank, world)
 
     steps, warmup = args.steps, max(3, args.warmup)
     prompt = args.prompt
     assert prompt + warmup + steps <= cfg.seq_len, "positions past the cache"
-    eng = Engine(cfg, seed=0, device=local, graphs=not args.eager, pdl=not args.eager)
+    eng = Engine(cfg, seed=0, device=local, graphs=not args.eager, pdl=not args.eager, exchange=xg)
+    sh = eng.shard
     L.pllm_set_stream(eng.stream)
-    rng = np.random.default_rng(1 + rank)
+    rng = np.random.default_rng(1)  # one stream: the same ids on every rank
     ids = rng.integers(0, cfg.vocab, prompt + warmup + steps).astype(np.int32)
     tp = np.stack([ids, np.arange(ids.size, dtype=np.int32)], axis=1).reshape(-1)
     staged = Buffer.of(tp)  # every step's (token, position) in device memory before the timed region
@@ -252,7 +255,7 @@ def main():
         check("timed region")
         if dist:
             import torch
-            t = torch.tensor([ms], device=f"cuda:{local}")
+            t = torch.tensor([ms], dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
         return ms
@@ -262,7 +265,7 @@ def main():
     # the prompt: a decode step a token (the tensor-core prefill is not built yet), filling the cache
     device_steps(0, 8)
     prefill_ms = timed(lambda: device_steps(8, prompt - 8))
-    prefill_tps = (prompt - 8) / (prefill_ms / 1000) * world
+    prefill_tps = (prompt - 8) / (prefill_ms / 1000)
     device_steps(prompt, warmup)
 
     try:
@@ -273,7 +276,7 @@ def main():
     clocks = Clocks(bus)
     decode_ms = timed(lambda: device_steps(prompt + warmup, steps))
     clock = clocks.stop()
-    value = steps * world / (decode_ms / 1000)
+    value = steps / (decode_ms / 1000)
 
     # end to end through the public call: token and position in from pinned memory, logits out, every step
     e2e_steps = min(steps, cfg.seq_len - prompt - warmup - steps) or 0
@@ -281,7 +284,7 @@ def main():
     if e2e_steps < 8:  # rewind into the decode range (the cache's later positions are rewritten, as a new request)
         e2e_first, e2e_steps = prompt + warmup, steps
     e2e_ms = timed(lambda: [eng.forward(int(ids[i % ids.size]), i) for i in range(e2e_first, e2e_first + e2e_steps)])
-    e2e = e2e_steps * world / (e2e_ms / 1000)
+    e2e = e2e_steps / (e2e_ms / 1000)
 
     gemv, gemv_us, attention, achieved, w13_bytes = {}, {}, {}, None, None
     peak, peak_kind = peaks()
@@ -301,13 +304,14 @@ def main():
             L.pllm_graph_destroy(g)
             return ms
 
-        def w13_all():
+        def w13_all():  # this rank's rows (all of them on one GPU)
             for l in range(c.layers):
-                eng._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * c.hidden * c.dim, B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4,
-                          c.hidden, c.dim, B["x"].ptr, B["ffn_norm"].ptr + l * c.dim * 4, 1, 2, pair=c.hidden, pdl=False)
+                eng._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * sh.hidden * c.dim,
+                          B["s13"].ptr + l * 2 * sh.hidden * (c.dim // 32) * 4, sh.hidden, c.dim, B["x"].ptr,
+                          B["ffn_norm"].ptr + l * c.dim * 4, 1, 2, pair=sh.hidden, pdl=False)
 
         w13_ms = graph_ms(w13_all, c.layers)
-        w13_bytes = 2 * c.hidden * c.dim * 1.125 + c.dim * 4 * 2 + c.hidden * 4
+        w13_bytes = 2 * sh.hidden * c.dim * 1.125 + c.dim * 4 * 2 + sh.hidden * 4
         peak, peak_kind = peaks()
         achieved = w13_bytes / (w13_ms / 1000) / 1e9
         gemv = {"w13_swiglu": round(achieved, 1)}
@@ -323,29 +327,29 @@ def main():
             gemv_us[name] = round(ms * 1000, 2)
 
         each("wqkv", B["wqkv"].ptr, B["sqkv"].ptr, eng.rows_qkv, c.dim, B["x"].ptr, B["att_norm"].ptr, 1, 0)
-        each("wo", B["wo"].ptr, B["so"].ptr, c.dim, c.qdim, B["att"].ptr, 0, 2, 1)
-        each("w2", B["w2"].ptr, B["s2"].ptr, c.dim, c.hidden, B["hb"].ptr, 0, 2, 1)
+        each("wo", B["wo"].ptr, B["so"].ptr, c.dim, sh.qdim, B["att"].ptr, 0, 2, 1)
+        each("w2", B["w2"].ptr, B["s2"].ptr, c.dim, sh.hidden, B["hb"].ptr, 0, 2, 1)
         L.pllm_set_stream(eng.stream)
 
         def cls_run():
-            eng._gemv(B["logits"].ptr, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim, B["x"].ptr, B["final_norm"].ptr, 1, 0,
-                      pdl=False)
+            eng._gemv(B["logits"].ptr, B["cls"].ptr, B["cls_s"].ptr, sh.vocab, c.dim, B["x"].ptr, B["final_norm"].ptr, 1,
+                      0, pdl=False)
         cls_ms = graph_ms(cls_run, 1)
-        gemv["cls"] = round(c.vocab * c.dim * 1.125 / (cls_ms / 1000) / 1e9, 1)
+        gemv["cls"] = round(sh.vocab * c.dim * 1.125 / (cls_ms / 1000) / 1e9, 1)
         gemv_us["cls"] = round(cls_ms * 1000, 2)
 
         # the attention alone at the last decode position (36 layers' caches, 2 kernels a layer)
         def attention_all():
             for l in range(c.layers):
-                L.pllm_attention_step(B["att"].ptr, B["qkv"].ptr, B["kc"].ptr + l * c.seq_len * c.kvdim * E,
-                                      B["vc"].ptr + l * c.seq_len * c.kvdim * E, B["scratch"].ptr, B["tp"].ptr + 4,
-                                      c.seq_len, c.heads, c.kv_heads, c.head_size, int(c.half_kv), 0.0, eng.SPLIT,
+                L.pllm_attention_step(B["att"].ptr, B["qkv"].ptr, B["kc"].ptr + l * c.seq_len * sh.kvdim * E,
+                                      B["vc"].ptr + l * c.seq_len * sh.kvdim * E, B["scratch"].ptr, B["tp"].ptr + 4,
+                                      c.seq_len, sh.heads, sh.kv_heads, c.head_size, int(c.half_kv), 0.0, eng.SPLIT,
                                       B["q_norm"].ptr + l * c.head_size * 4, B["k_norm"].ptr + l * c.head_size * 4,
                                       B["cos_t"].ptr, B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, 0)
 
         att_ms = graph_ms(attention_all, c.layers)
         last_pos = int(B["tp"].download(np.int32)[1])
-        att_bytes = 2 * (last_pos + 1) * c.kvdim * E
+        att_bytes = 2 * (last_pos + 1) * sh.kvdim * E
         attention = {"us_per_layer": round(att_ms * 1000, 2), "position": last_pos,
                      "gbs": round(att_bytes / (att_ms / 1000) / 1e9, 1)}
 
@@ -362,14 +366,16 @@ def main():
 
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warmup,
-        "ms_per_step": decode_ms / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": decode_ms / steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int8", "data": "synthetic",
         "config": {"workload": "qwen3-8b-int8 batch-1 decode at positions 2048+ (BASELINE.json configs[3])",
                    "model": "Qwen3-8B-shaped int8 (36 layers, 4096 hidden, 32/8 heads x 128, QK-norm, 12288 FFN, "
-                            "151936 vocab), float16 KV cache", "global_batch": world, "seq_len": prompt,
-                   "parallelism": f"replicas x{world}" if world > 1 else "1 GPU", "layers": cfg.layers,
+                            "151936 vocab), float16 KV cache", "global_batch": 1, "seq_len": prompt,
+                   "parallelism": f"tp{world} (NVLink exchange in the products)" if world > 1 else "1 GPU",
+                   "layers": cfg.layers,
                    "l2": "no flush: every step streams 8.51 GB of weights (> 126 MB L2)"},
-        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": c.vocab * 4},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * world,  # every rank's copies
+                "d2h_bytes_per_step": sh.vocab * 4 * world},
         "prefill": {"value": prefill_tps, "unit": "tok/s", "method": "token by token through the decode graph"},
         "gemv_gbs": gemv,
         "gemv_us": gemv_us,
@@ -377,9 +383,10 @@ def main():
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if achieved else None,
                      "peak_kind": peak_kind, "kernel": "gemv_kernel<int8, 1 token, RMSNorm prologue, SwiGLU epilogue>",
-                     "bytes_per_launch": w13_bytes, "traffic": profile_traffic("gemv_q8_w13_qwen3-8b")},
-        "decode_roofline_frac": (c.weight_bytes() / (decode_ms / steps / 1000) / 1e9) / peak,
-        "gpu_launches": eng.launches_per_step * steps,
+                     "bytes_per_launch": w13_bytes,  # a rank's launch: its 1/N of the rows
+                     "traffic": (profile_traffic("gemv_q8_w13_qwen3-8b") or 0) / world or None},
+        "decode_roofline_frac": (c.weight_bytes() / (decode_ms / steps / 1000) / 1e9) / (peak * world),
+        "gpu_launches": eng.launches_per_step * steps * world,
         "clocks": clock,
     }
     if cpu:
@@ -387,6 +394,8 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     eng.close()
+    if xg:
+        xg.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

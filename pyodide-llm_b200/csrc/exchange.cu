@@ -4,14 +4,14 @@
 // and a layer has two reductions, after wo and after w2: dim floats from every rank, summed.
 //
 // A rank's exchange region (one cudaMalloc, mapped into every other rank by CUDA IPC):
-//   recv  [2 parities][world][dim] floats: rank s's partial of the reduction at [parity][s]
-//   count [2 parities][world] uint32: rank s's CTAs done there, monotonic (never reset)
+//   slots [2 parities][world][dim] x 8 bytes: rank s's partial of the reduction at [parity][s], each value with the
+//         reduction's mark in the upper 4 bytes (one 8-byte store: a reader sees the pair whole or the old one)
 //   step  uint32: this rank's steps (pllm_tp_step, the first kernel of a step)
-// The reductions of a step alternate parities (wo: 0, w2: 1), so a rank can only write a parity's slots again after
-// every rank has read them: its next write there follows its own reduction of the other parity, which needs this
-// rank's next partial, made after this rank's read. The k-th reduction of a parity in a step is complete when rank
-// s's count reaches ((step - 1) layers + k + 1) ncta (ncta: the CTAs of the producing product, the same on every
-// rank). The sends and the sums are in the bulk-copy product's epilogue and prologue (gemv_tma.cu: EPI_SEND,
+// The k-th reduction of a parity in a step has the mark (step - 1) layers + k + 1; a reader takes a slot once its mark
+// is that (no fence, no counter: the same scheme as a low-latency all-reduce). The reductions of a step alternate
+// parities (wo: 0, w2: 1), so a rank can only write a parity's slots again after every rank has read them: its next
+// write there follows its own reduction of the other parity, which needs this rank's next partial, made after this
+// rank's read. The sends and the sums are in the bulk-copy product's epilogue and prologue (gemv_tma.cu: EPI_SEND,
 // PRO_RMS_SUM); waits are bounded (2 s, then PLLM_ETIMEOUT in the device status word).
 #include <string.h>
 
@@ -24,12 +24,12 @@ namespace {
 
 struct Tp {
   int world, rank, dim, layers;
-  size_t cnt_off, step_off, bytes;
+  size_t step_off, bytes;
   uint8_t* local;
   uint8_t* peer[gemvk::TP_MAX];  // every rank's region as this process sees it (peer[rank] = local)
 };
 
-size_t recv_off(const Tp& t, int parity, int src) { return ((size_t)parity * t.world + src) * t.dim * sizeof(float); }
+size_t recv_off(const Tp& t, int parity, int src) { return ((size_t)parity * t.world + src) * t.dim * 8; }
 
 __global__ void tp_step_kernel(unsigned* step) { *step += 1u; }
 
@@ -51,8 +51,7 @@ PLLM_API uint64_t pllm_tp_open(int32_t world, int32_t rank, int32_t dim, int32_t
   t->rank = rank;
   t->dim = dim;
   t->layers = layers;
-  t->cnt_off = (recv_off(*t, 2, 0) + 255) & ~(size_t)255;
-  t->step_off = t->cnt_off + 256;
+  t->step_off = (recv_off(*t, 2, 0) + 255) & ~(size_t)255;
   t->bytes = t->step_off + 256;
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, t->bytes);
@@ -66,6 +65,10 @@ PLLM_API uint64_t pllm_tp_open(int32_t world, int32_t rank, int32_t dim, int32_t
   }
   t->local = static_cast<uint8_t*>(p);
   t->peer[rank] = t->local;
+  if (!gemvk::status_word()) {  // the products' waits report there; looked up here, outside any capture
+    pllm_tp_close((uint64_t)(uintptr_t)t);
+    return 0;
+  }
   return (uint64_t)(uintptr_t)t;
 }
 
@@ -156,23 +159,19 @@ PLLM_API void pllm_gemv_tp(uint64_t out, uint64_t x, uint64_t x_out, uint64_t no
       PLLM_REQUIRE(t->peer[r], "pllm_gemv_tp: rank %d is not connected", r);
     if (epi == EPI_SEND) {
       PLLM_REQUIRE(rows == t->dim, "pllm_gemv_tp: a sent product has dim (%d) rows, not %d", t->dim, rows);
-      for (int r = 0; r < t->world; r++) {
-        xg.dst[r] = reinterpret_cast<float*>(t->peer[r] + recv_off(*t, parity, t->rank));
-        xg.sig[r] = reinterpret_cast<unsigned*>(t->peer[r] + t->cnt_off) + parity * t->world + t->rank;
-      }
+      for (int r = 0; r < t->world; r++)
+        xg.dst[r] = reinterpret_cast<unsigned long long*>(t->peer[r] + recv_off(*t, parity, t->rank));
     }
     if (pro == PRO_RMS_SUM) {
       PLLM_REQUIRE(n == t->dim && x_out && x_out != x,
                    "pllm_gemv_tp: a summed input is dim (%d) floats, not %d, into another buffer", t->dim, n);
-      xg.src = reinterpret_cast<const float*>(t->local + recv_off(*t, parity, 0));
-      xg.cnt = reinterpret_cast<const unsigned*>(t->local + t->cnt_off) + parity * t->world;
+      xg.src = reinterpret_cast<const unsigned long long*>(t->local + recv_off(*t, parity, 0));
       xg.x_out = dptr<float>(x_out);
     }
     xg.step = reinterpret_cast<const unsigned*>(t->local + t->step_off);
     xg.world = t->world;
     xg.per_step = (unsigned)t->layers;
     xg.k = (unsigned)(use >> 1);
-    xg.ncta = (unsigned)gemv_tma_grid(t->dim, EPI_SEND);
   }
   if (!gemv_tma(a, F_Q8, pro, epi, pdl != 0, exchanged ? &xg : nullptr))
     pllm_fail(PLLM_EINVAL, "pllm_gemv_tp: the bulk-copy product does not take this call (pro %d epi %d n %d)", pro,

@@ -12,20 +12,62 @@ enum Pro { PRO_Q = 0, PRO_RMS = 1, PRO_QUANT = 2, PRO_RMS_SUM = 3 };
 enum Epi { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_SEND = 3 };
 
 // A tensor-parallel rank's side of one reduction over NVLink (exchange.cu): the row-parallel product (wo, w2: each
-// rank's share of K) sends its rows to every rank's receive region (EPI_SEND) and counts its CTAs done there; the
-// next product's prologue (PRO_RMS_SUM) waits for every rank's count, makes x + the ranks' partials (in rank order,
-// so every rank gets the same bits), writes that to x_out (CTA 0) and takes RMSNorm and quantize_x of it.
+// rank's share of K) sends its rows to every rank's receive region (EPI_SEND), each value in one 8-byte store with
+// the reduction's mark beside it; the next product's prologue (PRO_RMS_SUM) reads every rank's slots until their marks
+// are this reduction's, makes x + the ranks' partials (in rank order, so every rank gets the same bits), writes that
+// to x_out (CTA 0) and takes RMSNorm and quantize_x of it. No fence and no counter: a slot is whole or not there.
 constexpr int TP_MAX = 8;
 struct Xchg {
-  float* dst[TP_MAX];        // EPI_SEND: rank p's receive slot of this rank, this parity ([dim] floats)
-  unsigned* sig[TP_MAX];     // EPI_SEND: rank p's count of this rank's CTAs done, this parity
-  const float* src;          // PRO_RMS_SUM: this rank's receive region of this parity, [world][dim]
-  const unsigned* cnt;       // PRO_RMS_SUM: this rank's counts of this parity, [world]
-  const unsigned* step;      // this rank's step counter (pllm_tp_step: 1 in the first step)
-  float* x_out;              // PRO_RMS_SUM: x + the partials
+  unsigned long long* dst[TP_MAX];  // EPI_SEND: rank p's receive slots of this rank, this parity ([dim] x 8 bytes)
+  const unsigned long long* src;    // PRO_RMS_SUM: this rank's receive slots of this parity, [world][dim]
+  const unsigned* step;             // this rank's step counter (pllm_tp_step: 1 in the first step)
+  float* x_out;                     // PRO_RMS_SUM: x + the partials
+  int* status;                      // the device status word (a wait that gives up writes PLLM_ETIMEOUT there)
   int world;
-  unsigned per_step, k, ncta;  // a count is complete at ((step - 1) per_step + k + 1) ncta
+  unsigned per_step, k;             // the reduction's mark: (step - 1) per_step + k + 1
 };
+
+__device__ __forceinline__ unsigned xchg_mark(const Xchg& xg) { return (*xg.step - 1u) * xg.per_step + xg.k + 1u; }
+__device__ __forceinline__ unsigned long long ld_slot(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_slot(unsigned long long* p, float v, unsigned mark) {
+  const unsigned long long s = ((unsigned long long)mark << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(s) : "memory");
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+constexpr unsigned long long XCHG_WAIT_NS = 2000000000ull;  // the wait for the other ranks' partials: 2 s at most
+
+// rank p's four slots from float4 number i: read until all four carry the mark (past 2 s: PLLM_ETIMEOUT recorded,
+// and the values as they are)
+__device__ __forceinline__ float4 wait_slots(const unsigned long long* s, unsigned mark, int* status) {
+  unsigned long long a = ld_slot(s), b = ld_slot(s + 1), c = ld_slot(s + 2), d = ld_slot(s + 3);
+  if ((unsigned)(a >> 32) != mark || (unsigned)(b >> 32) != mark || (unsigned)(c >> 32) != mark ||
+      (unsigned)(d >> 32) != mark) {
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+      a = ld_slot(s);
+      b = ld_slot(s + 1);
+      c = ld_slot(s + 2);
+      d = ld_slot(s + 3);
+      if ((unsigned)(a >> 32) == mark && (unsigned)(b >> 32) == mark && (unsigned)(c >> 32) == mark &&
+          (unsigned)(d >> 32) == mark)
+        break;
+      if (global_ns() - t0 > XCHG_WAIT_NS) {
+        atomicExch(status, PLLM_ETIMEOUT);
+        break;
+      }
+    }
+  }
+  return make_float4(__uint_as_float((unsigned)a), __uint_as_float((unsigned)b), __uint_as_float((unsigned)c),
+                     __uint_as_float((unsigned)d));
+}
 
 struct GemvArgs {
   float* out;              // out + t * out_stride (floats) + row
@@ -118,14 +160,15 @@ __device__ __forceinline__ void quantize_pair(const GemvArgs& a, const float4* x
 struct CtaSync {
   __device__ __forceinline__ void operator()() const { __syncthreads(); }
 };
-// x's float4 number i of token t: PRO_RMS_SUM adds the ranks' partials in rank order (read from L2: other GPUs wrote
-// them) and CTA 0 stores the sum to x_out
+// x's float4 number i of token t: PRO_RMS_SUM adds the ranks' partials in rank order (waiting for their slots) and
+// CTA 0 stores the sum to x_out
 template <int PRO>
 __device__ __forceinline__ float4 x_vec(const GemvArgs& a, const Xchg* xg, int t, int i) {
   float4 v = reinterpret_cast<const float4*>(a.x + t * a.x_stride)[i];
   if constexpr (PRO == PRO_RMS_SUM) {
+    const unsigned mark = xchg_mark(*xg);
     for (int p = 0; p < xg->world; p++) {
-      const float4 r = __ldcg(reinterpret_cast<const float4*>(xg->src) + (size_t)p * (a.K / 4) + i);
+      const float4 r = wait_slots(xg->src + (size_t)p * a.K + 4 * (size_t)i, mark, xg->status);
       v.x += r.x;
       v.y += r.y;
       v.z += r.z;
@@ -239,6 +282,9 @@ __device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, 
 // gemv_tma.cu: the bulk-copy pipeline for int8 at 1 or 2 tokens; false where it does not apply (xg: the exchange of
 // PRO_RMS_SUM / EPI_SEND, which only this kernel takes)
 bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg* xg = nullptr);
+// the device status word's address on the current device (looked up on the first call a device: make that before any
+// stream capture; pllm_tp_open does)
+int* status_word();
 // the CTAs gemv_tma launches for rows r0..r1 (EPI_SEND's producers: their count is what a PRO_RMS_SUM waits for)
 int gemv_tma_grid(long long rows, int epi);
 extern int g_gemv_mode;

@@ -26,34 +26,6 @@ constexpr int NC = 8;                 // consumer warps
 constexpr int TR = NC;                // row slots a stage
 constexpr int TMA_THREADS = (NC + 1) * 32;
 constexpr long long WAIT_BOUND = 1ll << 26;  // polls of an mbarrier before giving up (seconds: never in a run that works)
-constexpr unsigned long long XCHG_WAIT_NS = 2000000000ull;  // the wait for the other ranks' partials: 2 s at most
-
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// PRO_RMS_SUM: thread s (< world) of the consumers waits until rank s's count of CTAs done reaches this reduction's
-// mark (system-scope acquire: the counts and the partials are written by other GPUs); past 2 s it records
-// PLLM_ETIMEOUT and goes on (the partials it then reads are wrong, and the host sees the status)
-__device__ __forceinline__ void wait_partials(const Xchg& xg) {
-  if (threadIdx.x < xg.world) {
-    const unsigned step = *xg.step;
-    const unsigned mark = ((step - 1u) * xg.per_step + xg.k + 1u) * xg.ncta;
-    const unsigned* c = xg.cnt + threadIdx.x;
-    const unsigned long long t0 = global_ns();
-    for (;;) {
-      unsigned v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
-      if ((int)(v - mark) >= 0) break;
-      if (global_ns() - t0 > XCHG_WAIT_NS) {
-        atomicExch(&g_pllm_status, PLLM_ETIMEOUT);
-        break;
-      }
-    }
-  }
-}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -183,10 +155,6 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   // ---- the consumers (a wait that gives up makes the warp skip its work from then on, but it still meets every
   // barrier of the consumers, so that none of them waits for it)
   pdl_wait();
-  if (PRO == PRO_RMS_SUM) {
-    wait_partials(xg);
-    consumer_sync();
-  }
   load_activations<F_Q8, MT, PRO, ConsumerSync>(a, sq, ss, nullptr, &xg);
   consumer_sync();
   pdl_launch_dependents();
@@ -259,19 +227,13 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
         if (lane == m) v = acc[m];
       float* o = a.out + lane * a.out_stride + t + warp;
       if (EPI == EPI_SEND) {
-        for (int r = 0; r < xg.world; r++) xg.dst[r][t + warp] = v;
+        const unsigned mark = xchg_mark(xg);
+        for (int r = 0; r < xg.world; r++) st_slot(xg.dst[r] + t + warp, v, mark);
       } else if (EPI == EPI_ADD) {
         *o += v;
       } else {
         *o = v;
       }
-    }
-  }
-  if (EPI == EPI_SEND) {  // this CTA's rows are at every rank: count it there (one fence orders the warps' stores)
-    consumer_sync();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
-      for (int r = 0; r < xg.world; r++) atomicAdd_system(xg.sig[r], 1u);
     }
   }
 }
@@ -309,6 +271,26 @@ int g_tma_budget = 200 * 1024;
 // 0: the bulk-copy kernel wherever it applies; 1: the register-streaming kernel only (for comparisons)
 int g_gemv_mode = 0;
 
+// the device address of the status word on the current device (looked up once a device)
+int* status_word() {
+  static int* addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    pllm_fail(PLLM_ECUDA, "gemv_tma: no current device");
+    return nullptr;
+  }
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_pllm_status);
+    if (e != cudaSuccess) {
+      pllm_fail(PLLM_ECUDA, "gemv_tma: the status word: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = static_cast<int*>(p);
+  }
+  return addr[dev];
+}
+
 int gemv_tma_grid(long long rows, int epi) {
   const long long per_tile = epi == EPI_SWIGLU ? TR / 2 : TR;
   const long long tiles = (rows + per_tile - 1) / per_tile;
@@ -338,8 +320,12 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
   p.stages = S;
   const size_t smem = (size_t)head + p.act_bytes + (size_t)S * p.stage_bytes;
   if (smem > 227 * 1024) return false;
-  const Xchg none = {};
-  const Xchg& x = xg ? *xg : none;
+  Xchg x = {};
+  if (xg) {
+    x = *xg;
+    x.status = status_word();
+    if (!x.status) return true;  // failed (recorded), not for want of a fit
+  }
 #define CASE(M, P, E) \
   if (MT == M && pro == P && epi == E) return launch<M, P, E>(a, p, smem, pdl, x);
   CASE(1, PRO_Q, EPI_STORE) CASE(1, PRO_Q, EPI_ADD) CASE(1, PRO_Q, EPI_SWIGLU)
