@@ -205,6 +205,20 @@ int32_t pllm_set_stage_budget(int32_t bytes);
  * of split_len positions whose partials the last slice combines through the scratch; returns the previous mode */
 int32_t pllm_set_attention_mode(int32_t mode);
 
+/* ---- prefill on the tensor cores (the reference's tile products, matmul_q8r_tile / q8rTile, relaxed/int8.ts:89-166,
+ * at a tile of 128 tokens): tcgen05 kind::i8 one group of 32 at a time, each group's exact int32 scaled in float32 */
+/* out (M x N, ldo floats a row) = the int8 product of xq (M x K signed int8), xs (M x K/32), wq (w_rows x K) with its
+ * scales transposed in ws_t (K/32 x w_rows); epi 0 store, 1 add into out, 2 silu(w1 row) x (w3 row) with w1's rows
+ * 0..N and w3's from pair; K % 128 == 0, N % 128 == 0 (epi 2: N % 64 == 0) */
+void pllm_gemm_q8(uint64_t out, int64_t ldo, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws_t, int32_t M, int32_t N,
+                  int32_t K, int64_t w_rows, int32_t epi, int64_t pair);
+/* rows of n floats (x_stride apart): RMSNorm with norm (0: none) then quantize_x with bias, as signed int8 (the bias
+ * taken off) and n / 32 scales a row */
+void pllm_norm_quantize_rows(uint64_t xq, uint64_t xs, uint64_t x, int64_t x_stride, uint64_t norm, float eps,
+                             int32_t n, int32_t rows, int32_t bias);
+/* dst[g][r] = src[r][g] for rows x groups scales */
+void pllm_transpose_scales(uint64_t dst, uint64_t src, int64_t rows, int32_t groups);
+
 /* ---- tensor-parallel decode over NVLink (no counterpart in the reference, whose engine splits rows across the
  * CPU threads of one memory, src/runtime/forward/threads.ts): one process a GPU, a layer's two reductions (after wo
  * and after w2) by peer stores into every rank's exchange region (mapped by CUDA IPC) and bounded waits */
