@@ -42,6 +42,27 @@ METRIC = "int8 decode tok/s (batch 1) + prefill tok/s; GEMV HBM GB/s vs 8 TB/s p
 PROMPT = 2048
 
 
+def gemm_tops(eng, cfg, M, timed):
+    """The prefill's dominant product alone: layer 0's w1/w3 (M x 2 hidden x dim, gated epilogue) on the prefill's own
+    buffers, 5 launches; int8 tera-ops a second against twice the measured bf16 dense rate (B200's int8 rate is twice
+    its bf16 rate; no int8 figure is measured)."""
+    from pllm.lib import L
+    c, sh, B, P = cfg, eng.shard, eng.B, eng.P
+    run = lambda: L.pllm_gemm_q8(P["HB"].ptr, sh.hidden, P["XQ"].ptr, P["XS"].ptr, B["w13"].ptr,  # noqa: E731
+                                 P["ts13"].ptr, M, sh.hidden, c.dim, 2 * sh.hidden, 2, sh.hidden)
+    run()
+    ms = timed(lambda: [run() for _ in range(5)]) / 5
+    tops = 2.0 * M * 2 * sh.hidden * c.dim / (ms / 1000) / 1e12
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, kind = 2 * float(json.load(f)["bf16_tflops"]), "2 x measured bf16 dense"
+    except Exception:
+        peak, kind = 2 * 1590.0, "2 x fallback bf16 dense"
+    return {"kernel": "gemm_q8_kernel<gated FFN> (w1/w3, layer 0)", "M": M, "N": 2 * sh.hidden, "K": c.dim,
+            "us": round(ms * 1000, 1), "tops": round(tops, 1), "bound": "tensor", "peak_tops": peak,
+            "peak_kind": kind, "frac": round(tops / peak, 4)}
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -262,10 +283,20 @@ def main():
 
     if not args.eager:
         eng.capture()
-    # the prompt: a decode step a token (the tensor-core prefill is not built yet), filling the cache
-    device_steps(0, 8)
-    prefill_ms = timed(lambda: device_steps(8, prompt - 8))
-    prefill_tps = (prompt - 8) / (prefill_ms / 1000)
+    # the prompt: the tensor-core prefill (every layer's products for all its tokens at once), filling the cache; with
+    # tensor parallelism (or shapes it does not take) a decode step a token
+    gemm = None
+    if eng.can_prefill():
+        eng.prefill(ids[:prompt], 0)  # warm: the scales' transposed copies, the buffers, the tensor maps' encoder
+        prefill_ms = timed(lambda: [eng.prefill(ids[:prompt], 0) for _ in range(3)]) / 3
+        prefill_tps = prompt / (prefill_ms / 1000)
+        prefill_method = "tensor-core prefill (pllm_gemm_q8 tcgen05 kind::i8 products, pllm_attention_prefill)"
+        gemm = gemm_tops(eng, cfg, prompt, timed)
+    else:
+        device_steps(0, 8)
+        prefill_ms = timed(lambda: device_steps(8, prompt - 8))
+        prefill_tps = (prompt - 8) / (prefill_ms / 1000)
+        prefill_method = "token by token through the decode graph"
     device_steps(prompt, warmup)
 
     try:
@@ -376,7 +407,8 @@ def main():
                    "l2": "no flush: every step streams 8.51 GB of weights (> 126 MB L2)"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * world,  # every rank's copies
                 "d2h_bytes_per_step": sh.vocab * 4 * world},
-        "prefill": {"value": prefill_tps, "unit": "tok/s", "method": "token by token through the decode graph"},
+        "prefill": {"value": prefill_tps, "unit": "tok/s", "tokens": prompt, "ms": prefill_ms, "method": prefill_method,
+                    "gemm": gemm},
         "gemv_gbs": gemv,
         "gemv_us": gemv_us,
         "attention": attention,

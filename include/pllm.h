@@ -218,6 +218,15 @@ void pllm_norm_quantize_rows(uint64_t xq, uint64_t xs, uint64_t x, int64_t x_str
                              int32_t n, int32_t rows, int32_t bias);
 /* dst[g][r] = src[r][g] for rows x groups scales */
 void pllm_transpose_scales(uint64_t dst, uint64_t src, int64_t rows, int32_t groups);
+/* count tokens' q / k head norms (null weights: none), RoPE at positions p0.., their keys and values into the cache;
+ * qkv rows stride floats apart (nh q heads, nkv k heads, nkv v heads) */
+void pllm_qk_rope_cache_rows(uint64_t qkv, int64_t stride, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t,
+                             uint64_t sin_t, int32_t p0, int32_t count, uint64_t kc, uint64_t vc, int32_t nh,
+                             int32_t nkv, int32_t hs, int32_t rot, float eps, int32_t half, uint64_t bad);
+/* count tokens at positions p0.. attend causally over a float16 cache holding positions 0 .. p0 + count - 1 (q from
+ * qkv rows qstride floats apart; out rows ostride floats apart); hs <= 128 */
+void pllm_attention_prefill(uint64_t out, int64_t ostride, uint64_t qkv, int64_t qstride, uint64_t kc, uint64_t vc,
+                            int32_t p0, int32_t count, int32_t nh, int32_t nkv, int32_t hs);
 
 /* ---- tensor-parallel decode over NVLink (no counterpart in the reference, whose engine splits rows across the
  * CPU threads of one memory, src/runtime/forward/threads.ts): one process a GPU, a layer's two reductions (after wo

@@ -80,6 +80,9 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 // x as the sum of two float16: hi = rn(x), lo = rn(x - hi) (the products of a float16 key or value with both are
 // exact in the float32 accumulation, so the sum keeps x to about 2^-22 of itself)
+__device__ __forceinline__ uint32_t pack_halves(__half lo16, __half hi16) {
+  return (uint32_t)__half_as_ushort(lo16) | ((uint32_t)__half_as_ushort(hi16) << 16);
+}
 __device__ __forceinline__ void split_half(float x, __half& hi, __half& lo) {
   hi = __float2half_rn(x);
   lo = __float2half_rn(x - __half2float(hi));
@@ -968,16 +971,205 @@ __global__ void rope_kernel(float* v, const float* fcr, const float* fci, int nh
   }
 }
 
+// ---- prefill: count tokens at positions p0.. attend causally over the float16 cache (attention.ts:87-211 for each
+// token, all of a prompt at once). grid (nkv, tiles): a CTA takes PF_ROWS query rows = PF_ROWS / KVM tokens x the KVM
+// query heads of kv head kvh (row r: token r / KVM, head r % KVM), a warp 16 rows; the keys of positions 0 .. the
+// CTA's last token come in chunks of PF_KEYS by cp.async (double-buffered). On the tensor cores (mma m16n8k16, float32
+// accumulation): S = Q K^T with q split into float16 hi + lo (exact products with the float16 keys), an online softmax
+// a row (keys past the row's own position are -inf), O += P V with P split the same way. The f16 cache rows are the
+// ones the decode step reads, so the prefill's numbers differ from token-by-token decoding only in summation order.
+constexpr int PF_ROWS = 64, PF_KEYS = 64, PF_THREADS = 128;
+
+template <int KVM>
+__global__ void __launch_bounds__(PF_THREADS) attention_prefill_kernel(float* out, long long ostride, const float* qkv,
+                                                                      long long qstride, const uint16_t* kc,
+                                                                      const uint16_t* vc, int p0, int count, int nkv,
+                                                                      int hs) {
+  constexpr int QT = PF_ROWS / KVM;  // tokens a CTA
+  extern __shared__ __align__(16) uint8_t pf_smem[];
+  const int rowb = hs * 2 + 16;      // a padded float16 row (conflict-free ldmatrix)
+  uint8_t* sQh = pf_smem;
+  uint8_t* sQl = sQh + PF_ROWS * rowb;
+  uint8_t* ring = sQl + PF_ROWS * rowb;  // [2 buffers][keys, values][PF_KEYS][rowb]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t4 = lane & 3;
+  const int kvh = blockIdx.x, t0 = blockIdx.y * QT;
+  const int ntok = min(QT, count - t0);
+  const int kvdim = nkv * hs, nmb = hs / 16, ndb = hs / 8;
+  const int nkeys = p0 + t0 + ntok;  // positions 0 .. the CTA's last token
+  const int nchunk = (nkeys + PF_KEYS - 1) / PF_KEYS;
+  const int pieces = hs / 8;         // 16-byte pieces a row
+  const float isq = 1.0f / sqrtf((float)hs);
+  auto load_chunk = [&](int c, int buf) {
+    uint8_t* sK = ring + (size_t)(2 * buf) * PF_KEYS * rowb;
+    uint8_t* sV = sK + PF_KEYS * rowb;
+    const int k0 = c * PF_KEYS;
+    for (int e = tid; e < PF_KEYS * pieces; e += PF_THREADS) {
+      const int t = e / pieces, pc = e % pieces;
+      if (k0 + t < nkeys) {
+        const long long off = ((long long)(k0 + t) * kvdim + (long long)kvh * hs) * 2 + pc * 16;
+        cp_async16(sK + t * rowb + pc * 16, reinterpret_cast<const uint8_t*>(kc) + off);
+        cp_async16(sV + t * rowb + pc * 16, reinterpret_cast<const uint8_t*>(vc) + off);
+      } else {  // a probability of 0 must meet a 0 (and no key past the cache is read)
+        *reinterpret_cast<int4*>(sK + t * rowb + pc * 16) = make_int4(0, 0, 0, 0);
+        *reinterpret_cast<int4*>(sV + t * rowb + pc * 16) = make_int4(0, 0, 0, 0);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  load_chunk(0, 0);
+  for (int e = tid; e < PF_ROWS * hs; e += PF_THREADS) {  // the query rows as float16 hi + lo (rows past ntok: 0)
+    const int r = e / hs, d = e % hs, t = r / KVM, j = r % KVM;
+    const float x = t < ntok ? qkv[(long long)(t0 + t) * qstride + (long long)(kvh * KVM + j) * hs + d] : 0.0f;
+    __half hi, lo;
+    split_half(x, hi, lo);
+    reinterpret_cast<__half*>(sQh + r * rowb)[d] = hi;
+    reinterpret_cast<__half*>(sQl + r * rowb)[d] = lo;
+  }
+  // this thread's rows (g and g + 8 of the warp's 16) and their positions
+  const int rA = 16 * warp + g, rB = rA + 8;
+  const int qpA = p0 + t0 + rA / KVM, qpB = p0 + t0 + rB / KVM;
+  float o[16][4];  // O rows g, g + 8 x dims (8 nd + 2 t4, +1), hs <= 128
+#pragma unroll
+  for (int nd = 0; nd < 16; nd++) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.0f;
+  float mA = -INFINITY, mB = -INFINITY, lA = 0.0f, lB = 0.0f;
+  const uint8_t* qa_h = sQh + (16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8) * rowb + (lane >> 4) * 16;
+  const uint8_t* qa_l = qa_h - sQh + sQl;
+  for (int c = 0; c < nchunk; c++) {
+    const int buf = c & 1;
+    if (c + 1 < nchunk) {
+      load_chunk(c + 1, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      cp_async_wait_all();
+    }
+    __syncthreads();
+    const uint8_t* sK = ring + (size_t)(2 * buf) * PF_KEYS * rowb;
+    const uint8_t* sV = sK + PF_KEYS * rowb;
+    const int k0 = c * PF_KEYS;
+    // S (16 rows x 64 keys): 8 key blocks of 8; keys as B (col-major k = dims x n = keys: the key rows as stored)
+    float sc[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; nb++) sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.0f;
+    for (int kk = 0; kk < nmb; kk++) {
+      uint32_t ah[4], al[4];
+      ldsm_x4(ah, qa_h + kk * 32);
+      ldsm_x4(al, qa_l + kk * 32);
+#pragma unroll
+      for (int nb = 0; nb < 8; nb += 2) {  // two key blocks a load: matrices (keys 8 nb.., dims +0 / +8), (8 nb + 8..)
+        uint32_t b[4];
+        ldsm_x4(b, sK + (8 * nb + (lane & 7) + ((lane >> 4) & 1) * 8) * rowb + kk * 32 + ((lane >> 3) & 1) * 16);
+        mma16816(sc[nb], ah, b[0], b[1]);
+        mma16816(sc[nb], al, b[0], b[1]);
+        mma16816(sc[nb + 1], ah, b[2], b[3]);
+        mma16816(sc[nb + 1], al, b[2], b[3]);
+      }
+    }
+    // scale, causal mask, the chunk's row maxima (a row's 64 keys are over the 4 threads of its quad)
+    float xA = -INFINITY, xB = -INFINITY;
+#pragma unroll
+    for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+        const int kp = k0 + 8 * nb + 2 * t4 + u;
+        sc[nb][u] = kp <= qpA ? sc[nb][u] * isq : -INFINITY;
+        sc[nb][2 + u] = kp <= qpB ? sc[nb][2 + u] * isq : -INFINITY;
+        xA = fmaxf(xA, sc[nb][u]);
+        xB = fmaxf(xB, sc[nb][2 + u]);
+      }
+    xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 1));
+    xA = fmaxf(xA, __shfl_xor_sync(0xffffffffu, xA, 2));
+    xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 1));
+    xB = fmaxf(xB, __shfl_xor_sync(0xffffffffu, xB, 2));
+    const float nA = fmaxf(mA, xA), nB = fmaxf(mB, xB);
+    const float bA = nA == -INFINITY ? 0.0f : nA, bB = nB == -INFINITY ? 0.0f : nB;
+    const float aA = expf(mA - bA), aB = expf(mB - bB);  // 0 at the first chunk
+    mA = nA;
+    mB = nB;
+    lA *= aA;
+    lB *= aB;
+#pragma unroll
+    for (int nd = 0; nd < 16; nd++) {
+      o[nd][0] *= aA;
+      o[nd][1] *= aA;
+      o[nd][2] *= aB;
+      o[nd][3] *= aB;
+    }
+    // P = exp(S - m) as float16 hi + lo A fragments, O += P V (V as B: ldmatrix.trans of the value rows)
+#pragma unroll
+    for (int k2 = 0; k2 < 4; k2++) {
+      float p[8];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        p[u] = expf(sc[2 * k2][u] - (u < 2 ? bA : bB));
+        p[4 + u] = expf(sc[2 * k2 + 1][u] - (u < 2 ? bA : bB));
+      }
+      lA += p[0] + p[1] + p[4] + p[5];
+      lB += p[2] + p[3] + p[6] + p[7];
+      __half h[8], l[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) split_half(p[u], h[u], l[u]);
+      uint32_t ph[4], pl[4];
+      // a0: row g keys 2 t4.. (block 2 k2: p0 p1), a1: row g + 8 (p2 p3), a2: row g keys +8 (block 2 k2 + 1: p4 p5),
+      // a3: row g + 8 keys +8 (p6 p7)
+      ph[0] = pack_halves(h[0], h[1]);
+      ph[1] = pack_halves(h[2], h[3]);
+      ph[2] = pack_halves(h[4], h[5]);
+      ph[3] = pack_halves(h[6], h[7]);
+      pl[0] = pack_halves(l[0], l[1]);
+      pl[1] = pack_halves(l[2], l[3]);
+      pl[2] = pack_halves(l[4], l[5]);
+      pl[3] = pack_halves(l[6], l[7]);
+#pragma unroll
+      for (int nd = 0; nd < 16; nd += 2) {
+        if (nd >= ndb) break;
+        uint32_t b[4];  // matrices: keys 16 k2 + 0..7 / 8..15 of dims 8 nd.., then of dims 8 nd + 8..
+        ldsm_x4_trans(b, sV + (16 * k2 + (lane & 7) + ((lane >> 3) & 1) * 8) * rowb + (8 * nd + (lane >> 4) * 8) * 2);
+        mma16816(o[nd], ph, b[0], b[1]);
+        mma16816(o[nd], pl, b[0], b[1]);
+        mma16816(o[nd + 1], ph, b[2], b[3]);
+        mma16816(o[nd + 1], pl, b[2], b[3]);
+      }
+    }
+    __syncthreads();  // the chunk's buffer is read: the next load may take it
+  }
+  lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+  lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+  lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+  lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+  const int tA = rA / KVM, tB = rB / KVM;
+  float* outA = out + (long long)(t0 + tA) * ostride + (long long)(kvh * KVM + rA % KVM) * hs;
+  float* outB = out + (long long)(t0 + tB) * ostride + (long long)(kvh * KVM + rB % KVM) * hs;
+#pragma unroll
+  for (int nd = 0; nd < 16; nd++) {
+    if (nd >= ndb) break;
+    const int d = 8 * nd + 2 * t4;
+    if (tA < ntok) {
+      outA[d] = o[nd][0] / lA;
+      outA[d + 1] = o[nd][1] / lA;
+    }
+    if (tB < ntok) {
+      outB[d] = o[nd][2] / lB;
+      outB[d + 1] = o[nd][3] / lB;
+    }
+  }
+}
+
 // The forward driver's step between the q/k/v product and the attention: per head the RMSNorm of q and k (Qwen3's
 // q_norm / k_norm, forward/attention.ts:140-143; skipped where the weight is null), RoPE at the position
 // (attention.ts:7-20 with the tables' row of pos), and the key and value into the cache at pos (float16 by
-// halves.ts's rounding, or float32). Blocks: nh query heads, then nkv key heads, then nkv value heads.
+// halves.ts's rounding, or float32). Blocks: nh query heads, then nkv key heads, then nkv value heads; blockIdx.y: a
+// token of a prefill (its q / k / v stride floats after the previous token's, its position pos + y).
 template <bool HALF>
 __global__ void qk_rope_cache_kernel(float* q, const float* k, const float* v, const float* qn, const float* kn,
                                      const float* cos_t, const float* sin_t, const int* pos_dev, int pos, void* kc,
-                                     void* vc, int nh, int nkv, int hs, int rot, float eps, int* bad) {
+                                     void* vc, int nh, int nkv, int hs, int rot, float eps, int* bad,
+                                     long long stride) {
   pdl_wait();
   if (pos_dev) pos = *pos_dev;
+  pos += blockIdx.y;
+  q += blockIdx.y * stride;
+  k += blockIdx.y * stride;
+  v += blockIdx.y * stride;
   __shared__ float buf[512];
   __shared__ float red[8];
   const int b = blockIdx.x;
@@ -1231,11 +1423,72 @@ PLLM_API void pllm_qk_rope_cache(uint64_t q, uint64_t k, uint64_t v, uint64_t q_
     e = cudaLaunchKernelEx(&cfg, qk_rope_cache_kernel<true>, dptr<float>(q), dptr<const float>(k), dptr<const float>(v),
                            dptr<const float>(q_norm), dptr<const float>(k_norm), dptr<const float>(cos_t),
                            dptr<const float>(sin_t), dptr<const int>(pos_dev), (int)pos, dptr<void>(kc), dptr<void>(vc),
-                           (int)nh, (int)nkv, (int)hs, (int)rot, eps, dptr<int>(bad));
+                           (int)nh, (int)nkv, (int)hs, (int)rot, eps, dptr<int>(bad), 0ll);
   else
     e = cudaLaunchKernelEx(&cfg, qk_rope_cache_kernel<false>, dptr<float>(q), dptr<const float>(k),
                            dptr<const float>(v), dptr<const float>(q_norm), dptr<const float>(k_norm),
                            dptr<const float>(cos_t), dptr<const float>(sin_t), dptr<const int>(pos_dev), (int)pos,
-                           dptr<void>(kc), dptr<void>(vc), (int)nh, (int)nkv, (int)hs, (int)rot, eps, dptr<int>(bad));
+                           dptr<void>(kc), dptr<void>(vc), (int)nh, (int)nkv, (int)hs, (int)rot, eps, dptr<int>(bad),
+                           0ll);
   if (e != cudaSuccess) pllm_fail(PLLM_ECUDA, "pllm_qk_rope_cache: %s", cudaGetErrorString(e));
+}
+
+// ---- prefill (many tokens at once)
+
+// count tokens' q / k head norms (null weights: none), RoPE at positions p0.., and their keys and values into the
+// cache: qkv rows stride floats apart (a token's nh q heads, nkv k heads, nkv v heads, as the q/k/v product writes)
+PLLM_API void pllm_qk_rope_cache_rows(uint64_t qkv, int64_t stride, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t,
+                                      uint64_t sin_t, int32_t p0, int32_t count, uint64_t kc, uint64_t vc, int32_t nh,
+                                      int32_t nkv, int32_t hs, int32_t rot, float eps, int32_t half, uint64_t bad) {
+  PLLM_REQUIRE(nh > 0 && nkv > 0 && hs > 0 && hs <= 512 && hs % 2 == 0 && p0 >= 0 && count >= 0 &&
+                   stride >= (int64_t)(nh + 2 * nkv) * hs,
+               "pllm_qk_rope_cache_rows: nh %d nkv %d hs %d p0 %d count %d", nh, nkv, hs, p0, count);
+  if (!count) return;
+  const dim3 grid(nh + 2 * nkv, count);
+  const int threads = hs >= 128 ? 128 : 64;
+  float* q = dptr<float>(qkv);
+  const float* k = q + (long long)nh * hs;
+  const float* v = k + (long long)nkv * hs;
+  if (half)
+    qk_rope_cache_kernel<true><<<grid, threads, 0, pllm_stream()>>>(
+        q, k, v, dptr<const float>(q_norm), dptr<const float>(k_norm), dptr<const float>(cos_t),
+        dptr<const float>(sin_t), nullptr, p0, dptr<void>(kc), dptr<void>(vc), nh, nkv, hs, rot, eps, dptr<int>(bad),
+        (long long)stride);
+  else
+    qk_rope_cache_kernel<false><<<grid, threads, 0, pllm_stream()>>>(
+        q, k, v, dptr<const float>(q_norm), dptr<const float>(k_norm), dptr<const float>(cos_t),
+        dptr<const float>(sin_t), nullptr, p0, dptr<void>(kc), dptr<void>(vc), nh, nkv, hs, rot, eps, dptr<int>(bad),
+        (long long)stride);
+  PLLM_LAUNCHED("pllm_qk_rope_cache_rows");
+}
+
+// count tokens (positions p0..) attend causally over a float16 cache that holds positions 0 .. p0 + count - 1: q
+// from qkv rows (qstride floats apart, the nh q heads first), out rows ostride floats apart (nh x hs)
+PLLM_API void pllm_attention_prefill(uint64_t out, int64_t ostride, uint64_t qkv, int64_t qstride, uint64_t kc,
+                                     uint64_t vc, int32_t p0, int32_t count, int32_t nh, int32_t nkv, int32_t hs) {
+  if (!check_heads("pllm_attention_prefill", nh, nkv, hs, 0, nh)) return;
+  PLLM_REQUIRE(hs <= 128 && p0 >= 0 && count >= 0 && !(kc & 15) && !(vc & 15),
+               "pllm_attention_prefill: hs %d (at most 128), p0 %d count %d, 16-byte aligned caches", hs, p0, count);
+  if (!count) return;
+  const int kvm = nh / nkv;
+  const size_t rowb = (size_t)hs * 2 + 16;
+  const size_t smem = 2 * PF_ROWS * rowb + 4 * PF_KEYS * rowb;
+  const int qt = PF_ROWS / kvm;
+  const dim3 grid(nkv, (count + qt - 1) / qt);
+  cudaError_t e = cudaSuccess;
+  auto run = [&](auto kernel) {
+    cudaError_t r = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (r != cudaSuccess) return r;
+    kernel<<<grid, PF_THREADS, smem, pllm_stream()>>>(dptr<float>(out), (long long)ostride, dptr<const float>(qkv),
+                                                     (long long)qstride, dptr<const uint16_t>(kc),
+                                                     dptr<const uint16_t>(vc), p0, count, nkv, hs);
+    return cudaGetLastError();
+  };
+  switch (kvm) {
+    case 1: e = run(attention_prefill_kernel<1>); break;
+    case 2: e = run(attention_prefill_kernel<2>); break;
+    case 4: e = run(attention_prefill_kernel<4>); break;
+    default: e = run(attention_prefill_kernel<8>); break;
+  }
+  if (e != cudaSuccess) pllm_fail(PLLM_ECUDA, "pllm_attention_prefill: %s", cudaGetErrorString(e));
 }

@@ -403,16 +403,104 @@ class Engine:
         return self.logits_host.array.copy() if need_logits else None
 
     def forward_many(self, tokens, pos):
-        """Tokens at pos, pos + 1, ...: each computed as it would be alone (engine.ts:590); the last one's logits."""
+        """Tokens at pos, pos + 1, ...: each computed as it would be alone (engine.ts:590); the last one's logits.
+        Where the shapes suit the tensor-core prefill (can_prefill) the tokens go through it at once, else one by
+        one through the decode step."""
+        if len(tokens) > 1 and self.can_prefill():
+            return self.prefill(tokens, pos)
         out = None
         for t, token in enumerate(tokens):
             out = self.forward(int(token), pos + t, need_logits=(t == len(tokens) - 1))
         return out
 
+    # ---- prefill: many tokens at once on the tensor cores
+    def can_prefill(self):
+        """The tensor-core prefill's shapes: products with K and rows in whole 128s, a float16 cache, one rank."""
+        c, sh = self.cfg, self.shard
+        return (not self.xg and c.half_kv and c.head_size <= 128 and all(
+            v % 128 == 0 for v in (c.dim, sh.qdim, sh.hidden, self.rows_qkv)))
+
+    def _prefill_buffers(self, M):
+        c, sh = self.cfg, self.shard
+        P = getattr(self, "P", None)
+        if P is None:  # the matrices' scales transposed once (the tensor-core product reads them by column)
+            P = {"M": 0}
+            B = self.B
+            for w, rows, cols in (("sqkv", self.rows_qkv, c.dim), ("so", c.dim, sh.qdim), ("s13", 2 * sh.hidden, c.dim),
+                                  ("s2", c.dim, sh.hidden)):
+                t = Buffer(B[w].nbytes)
+                per = rows * (cols // 32) * 4
+                for l in range(c.layers):
+                    L.pllm_transpose_scales(t.ptr + l * per, B[w].ptr + l * per, rows, cols // 32)
+                P["t" + w] = t
+            self.P = P
+        if P["M"] < M:
+            for k in ("X", "QKV", "ATT", "HB", "XQ", "XS", "TOK"):
+                if k in P:
+                    P[k].free()
+            wide = max(c.dim, sh.qdim, sh.hidden, self.rows_qkv)
+            P["X"], P["QKV"] = Buffer(M * c.dim * 4), Buffer(M * self.rows_qkv * 4)
+            P["ATT"], P["HB"] = Buffer(M * sh.qdim * 4), Buffer(M * sh.hidden * 4)
+            P["XQ"], P["XS"], P["TOK"] = Buffer(M * wide), Buffer(M * wide // 8), Buffer(M * 4)
+            P["M"] = M
+        return P
+
+    def prefill(self, tokens, pos=0, need_logits=True):
+        """tokens at positions pos.. through every layer at once (the products on the tensor cores, pllm_gemm_q8; the
+        attention of all of them at once, pllm_attention_prefill), the cache filled for them; the last token's logits
+        (the decode step's classifier)."""
+        c, sh, B = self.cfg, self.shard, self.B
+        M = len(tokens)
+        if not (M >= 1 and 0 <= pos and pos + M <= c.seq_len):
+            raise ValueError(f"{M} tokens at {pos}: out of range")
+        if not self.can_prefill():
+            raise ValueError("shapes the tensor-core prefill does not take")
+        L.pllm_set_stream(self.stream)
+        P = self._prefill_buffers(M)
+        P["TOK"].upload(np.asarray(tokens, np.int32))
+        E = 2
+        X, QKV, ATT, HB, XQ, XS = (P[k].ptr for k in ("X", "QKV", "ATT", "HB", "XQ", "XS"))
+        L.pllm_embed_q8(X, B["emb"].ptr, B["emb_s"].ptr, P["TOK"].ptr, 0, c.dim, M, c.dim)
+        bias = self.bias
+        for l in range(c.layers):
+            wqkv = B["wqkv"].ptr + l * self.rows_qkv * c.dim
+            tqkv = P["tsqkv"].ptr + l * self.rows_qkv * (c.dim // 32) * 4
+            L.pllm_norm_quantize_rows(XQ, XS, X, c.dim, B["att_norm"].ptr + l * c.dim * 4, c.eps, c.dim, M, bias)
+            L.pllm_gemm_q8(QKV, self.rows_qkv, XQ, XS, wqkv, tqkv, M, self.rows_qkv, c.dim, self.rows_qkv, 0, 0)
+            kc = B["kc"].ptr + l * c.seq_len * sh.kvdim * E
+            vc = B["vc"].ptr + l * c.seq_len * sh.kvdim * E
+            qn = B["q_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
+            kn = B["k_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
+            L.pllm_qk_rope_cache_rows(QKV, self.rows_qkv, qn, kn, B["cos_t"].ptr, B["sin_t"].ptr, pos, M, kc, vc,
+                                      sh.heads, sh.kv_heads, c.head_size, 0, c.eps, 1, B["bad"].ptr)
+            L.pllm_attention_prefill(ATT, sh.qdim, QKV, self.rows_qkv, kc, vc, pos, M, sh.heads, sh.kv_heads,
+                                     c.head_size)
+            L.pllm_norm_quantize_rows(XQ, XS, ATT, sh.qdim, 0, c.eps, sh.qdim, M, bias)
+            L.pllm_gemm_q8(X, c.dim, XQ, XS, B["wo"].ptr + l * c.dim * sh.qdim,
+                           P["tso"].ptr + l * c.dim * (sh.qdim // 32) * 4, M, c.dim, sh.qdim, c.dim, 1, 0)
+            L.pllm_norm_quantize_rows(XQ, XS, X, c.dim, B["ffn_norm"].ptr + l * c.dim * 4, c.eps, c.dim, M, bias)
+            L.pllm_gemm_q8(HB, sh.hidden, XQ, XS, B["w13"].ptr + l * 2 * sh.hidden * c.dim,
+                           P["ts13"].ptr + l * 2 * sh.hidden * (c.dim // 32) * 4, M, sh.hidden, c.dim,
+                           2 * sh.hidden, 2, sh.hidden)
+            L.pllm_norm_quantize_rows(XQ, XS, HB, sh.hidden, 0, c.eps, sh.hidden, M, bias)
+            L.pllm_gemm_q8(X, c.dim, XQ, XS, B["w2"].ptr + l * c.dim * sh.hidden,
+                           P["ts2"].ptr + l * c.dim * (sh.hidden // 32) * 4, M, c.dim, sh.hidden, c.dim, 1, 0)
+        if not need_logits:
+            L.pllm_sync()
+            check("prefill")
+            return None
+        L.pllm_d2d(B["x"].ptr, X + (M - 1) * c.dim * 4, c.dim * 4)
+        self._gemv(B["logits"].ptr, B["cls"].ptr, B["cls_s"].ptr, sh.vocab, c.dim, B["x"].ptr, B["final_norm"].ptr,
+                   PRO_RMS, EPI_STORE, pdl=False)
+        L.pllm_d2h(self.logits_host.ptr, B["logits"].ptr, sh.vocab * 4)
+        L.pllm_sync()
+        check("prefill")
+        return self.logits_host.array.copy()
+
     def close(self):
         if self.graph:
             L.pllm_graph_destroy(self.graph)
             self.graph = 0
-        for b in self.B.values():
+        for b in list(self.B.values()) + [v for k, v in getattr(self, "P", {}).items() if k != "M"]:
             if b is not None:
                 b.free()

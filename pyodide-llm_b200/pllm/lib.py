@@ -100,6 +100,9 @@ SIGNATURES = {
     "pllm_gemm_q8": ([U64, I64, U64, U64, U64, U64, I32, I32, I32, I64, I32, I64], None),
     "pllm_norm_quantize_rows": ([U64, U64, U64, I64, U64, F32, I32, I32, I32], None),
     "pllm_transpose_scales": ([U64, U64, I64, I32], None),
+    "pllm_qk_rope_cache_rows": ([U64, I64, U64, U64, U64, U64, I32, I32, U64, U64, I32, I32, I32, I32, F32, I32, U64],
+                                None),
+    "pllm_attention_prefill": ([U64, I64, U64, I64, U64, U64, I32, I32, I32, I32, I32], None),
     "pllm_tp_open": ([I32, I32, I32, I32], U64),
     "pllm_tp_handle": ([U64, P], I32),
     "pllm_tp_connect": ([U64, P], I32),
