@@ -42,6 +42,49 @@ METRIC = "int8 decode tok/s (batch 1) + prefill tok/s; GEMV HBM GB/s vs 8 TB/s p
 PROMPT = 2048
 
 
+def kernel_case(which):
+    """A kernel's small case for profiling, three launches: the prefill product at M 512, N 4096, K 4096 (a wo-sized
+    product; 21 MB of weights, > L2 after the first pass is not needed: one launch is captured), or the forward step's
+    attention at position 2559 of the Qwen3-8B shape (32 / 8 heads of 128, a float16 cache of 2560 positions)."""
+    from pllm.device import Buffer, init
+    from pllm.lib import L, check
+    init(0)
+    L.pllm_set_stream(0)
+    bufs = []
+    if which == "gemm":
+        M, N, K = 512, 4096, 4096
+        xq, xs, w, ws, wt, out = (Buffer(n) for n in (M * K, M * K // 8, N * K, N * K // 8, N * K // 8, M * N * 4))
+        bufs += [xq, xs, w, ws, wt, out]
+        L.pllm_synth_q8(w.ptr, ws.ptr, N, K, 1, 0.02)
+        L.pllm_synth_q8(xq.ptr, xs.ptr, M, K, 2, 1.0)
+        L.pllm_transpose_scales(wt.ptr, ws.ptr, N, K // 32)
+        for _ in range(3):
+            L.pllm_gemm_q8(out.ptr, N, xq.ptr, xs.ptr, w.ptr, wt.ptr, M, N, K, N, 0, 0)
+    else:
+        nh, nkv, hs, cap, split = 32, 8, 128, 2560, 128
+        rng = np.random.default_rng(0)
+        kc = Buffer.of(rng.normal(0, 1, cap * nkv * hs).astype(np.float16).view(np.uint16))
+        vc = Buffer.of(rng.normal(0, 1, cap * nkv * hs).astype(np.float16).view(np.uint16))
+        qkv = Buffer.of(rng.normal(0, 1, (nh + 2 * nkv) * hs).astype(np.float32))
+        ones = Buffer.of(np.ones(hs, np.float32))
+        ang = np.outer(np.arange(cap), 1.0 / 1e6 ** (np.arange(0, hs, 2) / hs))
+        cos, sin = Buffer.of(np.cos(ang).astype(np.float32)), Buffer.of(np.sin(ang).astype(np.float32))
+        out, bad = Buffer(nh * hs * 4), Buffer(4).zero()
+        sc = Buffer(L.pllm_attention_scratch_bytes(nh, hs, cap, split)).zero()
+        pos = Buffer.of(np.array([2559], np.int32))
+        bufs += [kc, vc, qkv, ones, cos, sin, out, bad, sc, pos]
+        for _ in range(3):
+            L.pllm_attention_step(out.ptr, qkv.ptr, kc.ptr, vc.ptr, sc.ptr, pos.ptr, cap, nh, nkv, hs, 1, 0.0, split,
+                                  ones.ptr, ones.ptr, cos.ptr, sin.ptr, 0, 1e-6, bad.ptr, 0)
+    L.pllm_sync()
+    check(which)
+    status = L.pllm_device_status()
+    for b in bufs:
+        b.free()
+    print(json.dumps({"kernel_case": which, "status": status}))
+    return 0 if status == 0 else 1
+
+
 def gemm_tops(eng, cfg, M, timed):
     """The prefill's dominant product alone: layer 0's w1/w3 (M x 2 hidden x dim, gated epilogue) on the prefill's own
     buffers, 5 launches; int8 tera-ops a second against twice the measured bf16 dense rate (B200's int8 rate is twice
@@ -223,8 +266,12 @@ def main():
     ap.add_argument("--no-micro", action="store_true", help="profiling only: skip the per-kernel timings")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: the same shapes with fewer layers (a small case for ncu captures)")
+    ap.add_argument("--kernel", choices=["gemm", "attention"],
+                    help="profiling only: three launches of one kernel's small case (for ncu), then exit")
     args = ap.parse_args()
 
+    if args.kernel:
+        return kernel_case(args.kernel)
     if args.impl == "reference":
         return run_reference(args, ReferenceShape())
     from dataclasses import replace
