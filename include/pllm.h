@@ -174,6 +174,22 @@ void pllm_gemv(uint64_t out, int64_t out_stride, uint64_t xq, uint64_t xs, int64
                uint64_t x, int64_t x_stride, uint64_t norm, float eps, int32_t bias, uint64_t wq, uint64_t ws,
                int32_t fmt, int32_t n, int32_t r0, int32_t r1, int32_t count, int32_t pro, int32_t epi, int64_t pair,
                int32_t pdl);
+/* a product of a chain (pllm_gemv_chain): pllm_gemv's arguments for one token, rows 0..rows */
+typedef struct {
+  uint64_t out, x, norm, wq, ws;
+  int64_t pair;   /* epi 2: the gate's partner row offset */
+  int32_t n;      /* K */
+  int32_t rows;
+  int32_t pro;    /* 1 RMSNorm + quantize_x, 2 quantize_x */
+  int32_t epi;    /* 0 store, 1 add into out, 2 silu(row) * row + pair */
+  float eps;
+  int32_t bias;   /* 0 or 64 */
+} pllm_chain_stage;
+/* up to 4 int8 products of one token in one persistent launch, each reading what the one before wrote (the forward
+ * step's wo, w1/w3, w2 and the next layer's q/k/v): the weights stream without a break while the CTAs wait for one
+ * another between products (bounded, pllm_device_status 3). counters: 4 uint32 of device memory, zero before the
+ * first call (every call leaves them at zero); a chain's calls must not overlap on the GPU. */
+void pllm_gemv_chain(const pllm_chain_stage* stages, int32_t count, uint64_t counters, int32_t pdl);
 /* q / k head norms (null weights: none), RoPE at the position, and k / v into the cache at it; the position is
  * read from device memory at pos_dev (or pos if pos_dev is 0), so one recorded graph serves every position */
 void pllm_qk_rope_cache(uint64_t q, uint64_t k, uint64_t v, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t,

@@ -30,7 +30,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from .device import Buffer, Pinned, init
-from .lib import L, check
+from .lib import ChainStage, L, check
 from .tp import Shard
 
 F_Q8 = 0
@@ -132,6 +132,11 @@ class Engine:
             L.pllm_set_stage_budget(int(os.environ["PLLM_STAGE_BUDGET"]))
         self.cfg, self.graphs = cfg, graphs
         self.pdl = pdl and not os.environ.get("PLLM_NO_PDL")  # (a switch for measuring what the early launches give)
+        # PLLM_CHAIN=1: a layer's wo, w1/w3, w2 and the next layer's q/k/v as one persistent launch (pllm_gemv_chain),
+        # where the shapes suit it (int8 products of K in whole 128s; one rank). Not the default: measured slower than
+        # the separate launches (the stages' barriers and prologues outrun what the ring of weights can bridge).
+        self.chained = (not exchange and bool(os.environ.get("PLLM_CHAIN")) and all(
+            k % 128 == 0 for k in (cfg.dim, cfg.qdim, cfg.hidden)))
         c = cfg
         self.rows_qkv = s.rows_qkv
         self.bias = 64 if c.relaxed else 0
@@ -168,6 +173,7 @@ class Engine:
         B["hb"] = Buffer(s.hidden * 4)
         B["logits"] = Buffer(s.vocab * 4)
         B["tp"] = Buffer(8).zero()      # the token and the position, read by the kernels
+        B["chain"] = Buffer((c.layers + 1) * 16).zero()  # a chain's 4 arrival counts (zero between calls)
         B["bad"] = Buffer(4).zero()     # non-finite keys / values written to a float16 cache (halves.ts:35)
         B["scratch"] = Buffer(L.pllm_attention_scratch_bytes(s.heads, c.head_size, c.seq_len, self.SPLIT)).zero()
         self.B = B
@@ -280,11 +286,60 @@ class Engine:
     def launches_per_step(self):
         """Kernels a step launches: the embedding, five a layer (the q/k/v product; the attention with the q / k
         norms, RoPE, the cache write and its slices' combine inside; the wo, w1/w3 and w2 products), the classifier."""
+        if self.chained:
+            return 2 + 2 * self.cfg.layers
         return 2 + 5 * self.cfg.layers + (1 if self.xg else 0)
+
+    def _stage(self, out, x, norm, wq, ws, n, rows, pro, epi, pair=0):
+        return ChainStage(out=out, x=x, norm=norm, wq=wq, ws=ws, pair=pair, n=n, rows=rows, pro=pro, epi=epi,
+                          eps=self.cfg.eps, bias=self.bias)
+
+    def _chain(self, index, stages):
+        arr = (ChainStage * len(stages))(*stages)
+        L.pllm_gemv_chain(arr, len(stages), self.B["chain"].ptr + 16 * index, int(self.pdl))
+
+    def _enqueue_chained_step(self, need_logits=True):
+        """A step as 2 + 2 x layers launches: the embedding; layer 0's q/k/v product; then per layer the attention
+        step and one chain [wo, w1/w3, w2, the next layer's q/k/v (or the classifier)]."""
+        c, B = self.cfg, self.B
+        tok, pos = B["tp"].ptr, B["tp"].ptr + 4
+        E = 2 if c.half_kv else 4
+        x, qkv, att, hb = B["x"].ptr, B["qkv"].ptr, B["att"].ptr, B["hb"].ptr
+        L.pllm_embed_q8(x, B["emb"].ptr, B["emb_s"].ptr, tok, 0, c.dim, 1, c.dim)
+
+        def wqkv(l):
+            return self._stage(qkv, x, B["att_norm"].ptr + l * c.dim * 4, B["wqkv"].ptr + l * self.rows_qkv * c.dim,
+                               B["sqkv"].ptr + l * self.rows_qkv * (c.dim // 32) * 4, c.dim, self.rows_qkv,
+                               PRO_RMS, EPI_STORE)
+        self._chain(0, [wqkv(0)])
+        for l in range(c.layers):
+            kc = B["kc"].ptr + l * c.seq_len * c.kvdim * E
+            vc = B["vc"].ptr + l * c.seq_len * c.kvdim * E
+            qn = B["q_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
+            kn = B["k_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
+            L.pllm_attention_step(att, qkv, kc, vc, B["scratch"].ptr, pos, c.seq_len, c.heads, c.kv_heads,
+                                  c.head_size, int(c.half_kv), 0.0, self.SPLIT, qn, kn, B["cos_t"].ptr,
+                                  B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, int(self.pdl))
+            stages = [
+                self._stage(x, att, 0, B["wo"].ptr + l * c.dim * c.qdim, B["so"].ptr + l * c.dim * (c.qdim // 32) * 4,
+                            c.qdim, c.dim, PRO_QUANT, EPI_ADD),
+                self._stage(hb, x, B["ffn_norm"].ptr + l * c.dim * 4, B["w13"].ptr + l * 2 * c.hidden * c.dim,
+                            B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.dim, c.hidden, PRO_RMS,
+                            EPI_SWIGLU, pair=c.hidden),
+                self._stage(x, hb, 0, B["w2"].ptr + l * c.dim * c.hidden,
+                            B["s2"].ptr + l * c.dim * (c.hidden // 32) * 4, c.hidden, c.dim, PRO_QUANT, EPI_ADD)]
+            if l + 1 < c.layers:
+                stages.append(wqkv(l + 1))
+            elif need_logits:
+                stages.append(self._stage(B["logits"].ptr, x, B["final_norm"].ptr, B["cls"].ptr, B["cls_s"].ptr,
+                                          c.dim, c.vocab, PRO_RMS, EPI_STORE))
+            self._chain(l + 1, stages)
 
     def _enqueue_step(self, need_logits=True):
         if self.xg:
             return self._enqueue_tp_step(need_logits)
+        if self.chained:
+            return self._enqueue_chained_step(need_logits)
         c, B = self.cfg, self.B
         tok, pos = B["tp"].ptr, B["tp"].ptr + 4
         E = 2 if c.half_kv else 4
