@@ -361,7 +361,12 @@ def main():
     e2e_first = prompt + warmup + steps
     if e2e_steps < 8:  # rewind into the decode range (the cache's later positions are rewritten, as a new request)
         e2e_first, e2e_steps = prompt + warmup, steps
-    e2e_ms = timed(lambda: [eng.forward(int(ids[i % ids.size]), i) for i in range(e2e_first, e2e_first + e2e_steps)])
+    if world == 1:  # the greedy step's public call: the token and position in, the next token out
+        e2e_ms = timed(lambda: [eng.next_token(int(ids[i % ids.size]), i) for i in range(e2e_first, e2e_first + e2e_steps)])
+        d2h_step = 4
+    else:  # a rank's vocab slice of the logits out
+        e2e_ms = timed(lambda: [eng.forward(int(ids[i % ids.size]), i) for i in range(e2e_first, e2e_first + e2e_steps)])
+        d2h_step = sh.vocab * 4 * world
     e2e = e2e_steps / (e2e_ms / 1000)
 
     gemv, gemv_us, attention, achieved, w13_bytes = {}, {}, {}, None, None
@@ -453,7 +458,8 @@ def main():
                    "layers": cfg.layers,
                    "l2": "no flush: every step streams 8.51 GB of weights (> 126 MB L2)"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * world,  # every rank's copies
-                "d2h_bytes_per_step": sh.vocab * 4 * world},
+                "d2h_bytes_per_step": d2h_step,
+                "call": "Engine.next_token (greedy: argmax on the device)" if world == 1 else "Engine.forward"},
         "prefill": {"value": prefill_tps, "unit": "tok/s", "tokens": prompt, "ms": prefill_ms, "method": prefill_method,
                     "gemm": gemm},
         "gemv_gbs": gemv,

@@ -105,6 +105,14 @@ void from_f16(uint64_t out, uint64_t x, int32_t n);
 /* replaces finite_f16, kernels/kernel/halves.ts:82 (jobs.ts:100): 1 if all finite, else 0 (waits) */
 int32_t finite_f16(uint64_t x, int32_t n);
 
+/* ===== the registry: from the logits to a token (kernels/kernel/sample.ts) */
+/* replaces argmax, sample.ts:6-10 (jobs.ts:116): the first index of the largest of n floats (a NaN never wins; one at
+ * index 0 is the answer, as the reference's walk); waits (the library's own small scratch: calls must not overlap) */
+int32_t argmax(uint64_t x, int32_t n);
+/* replaces penalize, sample.ts:16-30 (jobs.ts:117): each distinct token of tokens[0..count) once: a positive logit
+ * divided by penalty, another multiplied by it, then presence (if > 0) taken off */
+void penalize(uint64_t logits, uint64_t tokens, int32_t count, float penalty, float presence);
+
 /* ===== the registry: vector glue and stateful layers (kernels/kernel/activations.ts, kernels/kernel/stateful.ts) */
 /* replaces rmsnorm, kernels/kernel/activations.ts:8 (jobs.ts:83) */
 void rmsnorm(uint64_t out, uint64_t x, uint64_t w, int32_t n, float eps);
@@ -174,6 +182,9 @@ void pllm_gemv(uint64_t out, int64_t out_stride, uint64_t xq, uint64_t xs, int64
                uint64_t x, int64_t x_stride, uint64_t norm, float eps, int32_t bias, uint64_t wq, uint64_t ws,
                int32_t fmt, int32_t n, int32_t r0, int32_t r1, int32_t count, int32_t pro, int32_t epi, int64_t pair,
                int32_t pdl);
+/* argmax into device memory (out: one int32) without waiting: the forward driver's greedy step; scratch: 16 bytes of
+ * device memory, zero before the first call (every call leaves it at zero); a scratch's calls must not overlap */
+void pllm_argmax_dev(uint64_t out, uint64_t x, int32_t n, uint64_t scratch);
 /* a product of a chain (pllm_gemv_chain): pllm_gemv's arguments for one token, rows 0..rows */
 typedef struct {
   uint64_t out, x, norm, wq, ws;

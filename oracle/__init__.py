@@ -60,6 +60,7 @@ def _declare(L):
         "or_convolve": ([P, P, P, I32, I32], None), "or_short_conv": ([P, P, P, P, I32, I32], None),
         "or_delta_rule": ([P, P, P, P, P, I32, I32, I32, I32, I32, I32], None),
         "or_forward": ([P, P, I32, I32, P, I32], I32), "or_threads": ([], I32),
+        "or_argmax": ([P, I32], I32), "or_penalize": ([P, P, I32, F32, F32], None),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -261,6 +262,20 @@ def add_inplace(x, y):
     x = _c(x, np.float32).copy()
     lib().or_add_inplace(_p(x), _p(_c(y, np.float32)), x.size)
     return x
+
+
+def argmax(x):
+    """sample.ts:6-10"""
+    x = _c(x, np.float32)
+    return int(lib().or_argmax(_p(x), x.size))
+
+
+def penalize(logits, tokens, penalty, presence):
+    """sample.ts:16-30 (a copy of the logits, penalized)"""
+    out = _c(logits, np.float32).copy()
+    t = _c(tokens, np.int32)
+    lib().or_penalize(_p(out), _p(t), t.size, penalty, presence)
+    return out
 
 
 def gate(x, g):

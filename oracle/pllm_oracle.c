@@ -685,3 +685,32 @@ int32_t or_forward(const or_config *c, const or_weights *w, int32_t token, int32
   free(x); free(xb); free(xb2); free(q); free(k); free(v); free(hb); free(hb2); free(att); free(xq); free(xs);
   return 0;
 }
+
+/* sample.ts:6-10: the walk from the first element, a later one taking over only when strictly greater */
+int32_t or_argmax(const float *x, int32_t n) {
+  int32_t mi = 0;
+  float mv = x[0];
+  for (int32_t j = 1; j < n; j++)
+    if (x[j] > mv) {
+      mv = x[j];
+      mi = j;
+    }
+  return mi;
+}
+
+/* sample.ts:16-30: each token once (its first occurrence), divided or multiplied by penalty, less presence */
+void or_penalize(float *logits, const int32_t *tokens, int32_t count, float penalty, float presence) {
+  const float less = presence > 0 ? presence : 0;
+  for (int32_t i = 0; i < count; i++) {
+    const int32_t token = tokens[i];
+    int seen = 0;
+    for (int32_t j = 0; j < i; j++)
+      if (tokens[j] == token) {
+        seen = 1;
+        break;
+      }
+    if (seen) continue;
+    const float value = logits[token];
+    logits[token] = (value > 0 ? value / penalty : value * penalty) - less;
+  }
+}

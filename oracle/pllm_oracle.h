@@ -72,6 +72,8 @@ int32_t or_finite_f16(const uint16_t *x, int32_t n);            /* halves.ts:82-
 void or_rmsnorm(float *out, const float *x, const float *w, int32_t n, float eps);        /* activations.ts:8-20 */
 void or_swiglu(float *out, const float *h1, const float *h3, int32_t n);                  /* activations.ts:77-90 */
 void or_add_inplace(float *x, const float *y, int32_t n);                                 /* activations.ts:156-158 */
+int32_t or_argmax(const float *x, int32_t n);                                             /* sample.ts:6-10 */
+void or_penalize(float *logits, const int32_t *tokens, int32_t count, float penalty, float presence); /* sample.ts:16-30 */
 void or_gate(float *out, const float *x, const float *g, int32_t n);                      /* stateful.ts:12-23 */
 void or_convolve(float *out, const float *taps, const float *rows, int32_t n, int32_t count); /* stateful.ts:49-63 */
 void or_short_conv(float *out, const float *taps, float *rows, const float *b, int32_t n, int32_t count); /* stateful.ts:70-86 */

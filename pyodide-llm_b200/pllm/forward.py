@@ -175,6 +175,8 @@ class Engine:
         B["tp"] = Buffer(8).zero()      # the token and the position, read by the kernels
         B["chain"] = Buffer((c.layers + 1) * 16).zero()  # a chain's 4 arrival counts (zero between calls)
         B["bad"] = Buffer(4).zero()     # non-finite keys / values written to a float16 cache (halves.ts:35)
+        B["next"] = Buffer(4)           # the greedy step's token (pllm_argmax_dev) and its scratch
+        B["amx"] = Buffer(16).zero()
         B["scratch"] = Buffer(L.pllm_attention_scratch_bytes(s.heads, c.head_size, c.seq_len, self.SPLIT)).zero()
         self.B = B
         if host is not None:
@@ -184,6 +186,7 @@ class Engine:
         self.stream = L.pllm_stream_create()
         self.tp_host = Pinned(2, np.int32)
         self.logits_host = Pinned(s.vocab, np.float32)
+        self.next_host = Pinned(1, np.int32)
         self.graph = 0
         check("Engine")
 
@@ -456,6 +459,24 @@ class Engine:
         L.pllm_sync()
         check("forward")
         return self.logits_host.array.copy() if need_logits else None
+
+    def next_token(self, token, pos):
+        """One greedy decode step: the token at pos in, the most probable next token out (argmax of the logits on the
+        device, sample.ts:6-10): 8 bytes copied to the device, 4 back, where forward() copies the vocabulary's logits."""
+        c = self.cfg
+        if self.xg:
+            raise NotImplementedError("next_token takes one rank: with tensor parallelism gather the logits' slices")
+        if not (0 <= pos < c.seq_len and 0 <= token < c.vocab):
+            raise ValueError(f"token {token} at {pos}: out of range")
+        L.pllm_set_stream(self.stream)
+        self.tp_host.array[0], self.tp_host.array[1] = token, pos
+        L.pllm_h2d(self.B["tp"].ptr, self.tp_host.ptr, 8)
+        self.launch_step()
+        L.pllm_argmax_dev(self.B["next"].ptr, self.B["logits"].ptr, c.vocab, self.B["amx"].ptr)
+        L.pllm_d2h(self.next_host.ptr, self.B["next"].ptr, 4)
+        L.pllm_sync()
+        check("next_token")
+        return int(self.next_host.array[0])
 
     def forward_many(self, tokens, pos):
         """Tokens at pos, pos + 1, ...: each computed as it would be alone (engine.ts:590); the last one's logits.

@@ -109,6 +109,9 @@ SIGNATURES = {
     "pllm_tp_close": ([U64], None),
     "pllm_tp_step": ([U64], None),
     "pllm_gemv_chain": ([P, I32, U64, I32], None),
+    "argmax": ([U64, I32], I32),
+    "penalize": ([U64, U64, I32, F32, F32], None),
+    "pllm_argmax_dev": ([U64, U64, I32, U64], None),
     "pllm_gemv_tp": ([U64, U64, U64, U64, F32, I32, U64, U64, I32, I32, I32, I32, I64, I32, U64, I32], None),
     "pllm_synth_t2": ([U64, U64, I64, I32, U64, F32, F32], None),
 }

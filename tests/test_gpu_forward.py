@@ -149,3 +149,17 @@ def test_chained_step_is_the_separate_launches(layers, monkeypatch):
         assert np.array_equal(got, want), (pos, np.abs(got - want).max())
     plain.close()
     chained.close()
+
+
+def test_next_token_is_the_logits_argmax():
+    """The greedy step (argmax on the device, 4 bytes back) picks the argmax of the logits forward() returns."""
+    cfg = SMALL_QWEN3
+    a, b = Engine(cfg, seed=6), Engine(cfg, seed=6)
+    tok = 5
+    for pos in range(6):
+        logits = a.forward(tok, pos)
+        nxt = b.next_token(tok, pos)
+        assert nxt == int(O.argmax(logits))
+        tok = nxt
+    a.close()
+    b.close()

@@ -558,3 +558,34 @@ def test_attention_step(half, nh, nkv, hs, qk):
             np.testing.assert_allclose(get(out, np.float32), want, rtol=1e-4, atol=2e-5)
     counts = get(scratch, np.int32)[-(nh + 1):]
     assert np.all(counts == 0)
+
+
+@pytest.mark.parametrize("n", [1, 7, 1000, 151936])
+def test_argmax_and_penalize(n):
+    """sample.ts's argmax (device, both forms) and penalize against the oracle's walks: NaNs, ties, -inf."""
+    rng = np.random.default_rng(n)
+    cases = [rng.normal(0, 3, n).astype(np.float32)]
+    if n > 5:
+        t = rng.normal(0, 3, n).astype(np.float32)
+        t[[2, n - 1]] = t.max() + 1.0  # a tie: the first wins
+        t[1] = np.nan
+        cases.append(t)
+        z = rng.normal(0, 3, n).astype(np.float32)
+        z[0] = np.nan  # the walk starts from a NaN
+        cases.append(z)
+        cases.append(np.full(n, -np.inf, np.float32))
+    scratch = dev(np.zeros(4, np.int32))
+    out = dev(np.zeros(1, np.int32))
+    for x in cases:
+        X = dev(x)
+        want = O.argmax(x)
+        assert L.argmax(X.ptr, n) == want
+        L.pllm_argmax_dev(out.ptr, X.ptr, n, scratch.ptr)
+        check("pllm_argmax_dev")
+        assert int(get(out, np.int32)[0]) == want
+    tokens = rng.integers(0, n, 40).astype(np.int32)
+    logits = cases[0]
+    X, T = dev(logits), dev(tokens)
+    L.penalize(X.ptr, T.ptr, tokens.size, 1.3, 0.4)
+    check("penalize")
+    np.testing.assert_array_equal(get(X, np.float32)[:n], O.penalize(logits, tokens, 1.3, 0.4))

@@ -175,3 +175,19 @@ def test_exp_close_to_libm():
     got = np.array([O.lib().or_fexp(float(v)) for v in xs], np.float32)
     np.testing.assert_allclose(got, np.exp(xs.astype(np.float64)), rtol=3e-7)
     assert O.lib().or_fexp(-90.0) == 0.0 and O.lib().or_vexp(-90.0) > 0
+
+
+def test_argmax_and_penalize_walks():
+    """sample.ts's argmax (the first of equal largest; a NaN never greater, one at index 0 the answer) and penalize
+    (each distinct token once), against NumPy written the same way."""
+    x = np.array([1.0, 3.0, -2.0, 3.0, np.nan, 2.5], np.float32)
+    assert O.argmax(x) == 1
+    assert O.argmax(np.array([np.nan, 5.0, 7.0], np.float32)) == 0
+    assert O.argmax(np.array([-np.inf, -np.inf], np.float32)) == 0
+    logits = np.array([2.0, -1.0, 0.5, 4.0, -3.0], np.float32)
+    got = O.penalize(logits, np.array([3, 1, 3, 4, 1], np.int32), 1.3, 0.25)
+    want = logits.copy()
+    for t in (3, 1, 4):
+        v = want[t]
+        want[t] = (v / np.float32(1.3) if v > 0 else v * np.float32(1.3)) - np.float32(0.25)
+    np.testing.assert_array_equal(got, want)
