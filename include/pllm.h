@@ -112,6 +112,12 @@ int32_t argmax(uint64_t x, int32_t n);
 /* replaces penalize, sample.ts:16-30 (jobs.ts:117): each distinct token of tokens[0..count) once: a positive logit
  * divided by penalty, another multiplied by it, then presence (if > 0) taken off */
 void penalize(uint64_t logits, uint64_t tokens, int32_t count, float penalty, float presence);
+/* replaces sample, sample.ts:248-337 (kernels.py's restype i32): the token drawn from softmax(logits / temperature) by
+ * random in [0, 1), of the topk most probable (0: all), then of their nucleus (0 < topp < 1), then without those below
+ * minp times the most probable (0: none); -1 where the largest logit is not a finite number. probs, index: device
+ * scratch of n floats and n int32. Waits (the library's own scratch: calls must not overlap) */
+int32_t sample(uint64_t logits, int32_t n, float temperature, float topp, double random, uint64_t probs,
+               uint64_t index, int32_t topk, float minp);
 
 /* ===== the registry: vector glue and stateful layers (kernels/kernel/activations.ts, kernels/kernel/stateful.ts) */
 /* replaces rmsnorm, kernels/kernel/activations.ts:8 (jobs.ts:83) */
@@ -185,6 +191,10 @@ void pllm_gemv(uint64_t out, int64_t out_stride, uint64_t xq, uint64_t xs, int64
 /* argmax into device memory (out: one int32) without waiting: the forward driver's greedy step; scratch: 16 bytes of
  * device memory, zero before the first call (every call leaves it at zero); a scratch's calls must not overlap */
 void pllm_argmax_dev(uint64_t out, uint64_t x, int32_t n, uint64_t scratch);
+/* sample into device memory (out: one int32) without waiting, the random number a double at random_dev (written
+ * before the launch runs: a recorded step's) */
+void pllm_sample_dev(uint64_t out, uint64_t logits, int32_t n, float temperature, float topp, uint64_t random_dev,
+                     uint64_t probs, uint64_t index, int32_t topk, float minp);
 /* a product of a chain (pllm_gemv_chain): pllm_gemv's arguments for one token, rows 0..rows */
 typedef struct {
   uint64_t out, x, norm, wq, ws;
@@ -218,6 +228,26 @@ uint64_t pllm_attention_scratch_bytes(int32_t nh, int32_t hs, int32_t capacity, 
 void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t scratch, uint64_t pos_dev,
                         int32_t capacity, int32_t nh, int32_t nkv, int32_t hs, int32_t half, float cap,
                         int32_t split_len, int32_t pdl);
+
+/* ---- the next kernel's first bytes into L2 while this one runs (a decode step is a fixed sequence of kernels, each
+ * reading its own weights from HBM; between two of them the HBM would idle while the second one starts up).
+ * A range of rows cut into `parts` near-equal shares, as the next kernel's CTAs take them (parts 0: the SM count);
+ * of each share the bytes [skip, skip + first) from its first row are prefetched into L2
+ * (cp.async.bulk.prefetch.L2). rows_dev: a device int32 holding the row count (the step's position: the cache rows
+ * before it), or 0 for `rows`. base must be 16-byte aligned; a prefetch is a hint and changes no result. */
+typedef struct {
+  uint64_t base;
+  int64_t row_bytes;
+  int64_t rows;
+  uint64_t rows_dev;
+  int64_t skip;
+  int64_t first;
+  int32_t parts;
+  int32_t pad;
+} pllm_prefetch;
+/* up to 8 ranges for the next decode-product (bulk-copy pipeline) or attention-step launch on this host thread's
+ * library state to prefetch as it runs (that launch takes them; count 0 clears them) */
+void pllm_prefetch_next(const pllm_prefetch* ranges, int32_t count);
 
 /* a bounded device-side wait (an mbarrier of the bulk-copy product) gave up since the last call: PLLM_ETIMEOUT (3),
  * else 0; reading it clears it */

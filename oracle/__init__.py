@@ -61,6 +61,7 @@ def _declare(L):
         "or_delta_rule": ([P, P, P, P, P, I32, I32, I32, I32, I32, I32], None),
         "or_forward": ([P, P, I32, I32, P, I32], I32), "or_threads": ([], I32),
         "or_argmax": ([P, I32], I32), "or_penalize": ([P, P, I32, F32, F32], None),
+        "or_sample": ([P, I32, F32, F32, ctypes.c_double, I32, F32], I32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -276,6 +277,12 @@ def penalize(logits, tokens, penalty, presence):
     t = _c(tokens, np.int32)
     lib().or_penalize(_p(out), _p(t), t.size, penalty, presence)
     return out
+
+
+def sample(logits, temperature, topp, random, topk=0, minp=0.0):
+    """sample.ts:248-337: the token drawn with this random number in [0, 1) (-1: the largest logit is not finite)"""
+    x = _c(logits, np.float32)
+    return int(lib().or_sample(_p(x), x.size, temperature, topp, float(random), topk, minp))
 
 
 def gate(x, g):

@@ -714,3 +714,100 @@ void or_penalize(float *logits, const int32_t *tokens, int32_t count, float pena
     logits[token] = (value > 0 ? value / penalty : value * penalty) - less;
   }
 }
+
+/* sample.ts:248-337: a token drawn from softmax(logits / temperature), as the reference's kernel walks it.
+ *  - best = the largest logit (a NaN anywhere, or an infinity: -1);
+ *  - a nucleus (0 < topp < 1) leaves out what is below best - 16.118095 temperature (a ten millionth of the best's
+ *    probability); the others, in token order, become exp((v - best) / temperature): the first 4 (count / 4) by
+ *    vexp of the product with 1 / temperature, the rest by fexp of the quotient (sample.ts:274-282);
+ *  - total (double) and top; top-k (0 < topk < count) keeps the topk largest by (probability, the lower token) and
+ *    sums them again; least = min(minp, 1) top where minp > 0;
+ *  - with a nucleus or a top-k: the kept at or above the cutoff ((1 - topp) / (count - 1) total, at most top) and at
+ *    or above least, sorted by (probability, the lower token) descending, taken until their sum reaches topp total
+ *    (every one without a nucleus); else with minp: those at or above least in token order; else all in token order;
+ *  - the first whose cumulative sum (double) passes random x their sum, else the last.
+ * The reference sums top-k's survivors in its partition's order; this sums them in the sorted order (the double's
+ * last bits may differ). Scratch is allocated here. */
+typedef struct {
+  float p;
+  int32_t t;
+} or_place;
+static int or_ahead(const void *a, const void *b) {
+  const or_place *x = (const or_place *)a, *y = (const or_place *)b;
+  if (x->p != y->p) return x->p > y->p ? -1 : 1;
+  return x->t < y->t ? -1 : (x->t > y->t);
+}
+int32_t or_sample(const float *logits, int32_t n, float temperature, float topp, double random, int32_t topk,
+                  float minp) {
+  float best = logits[0];
+  for (int32_t i = 1; i < n; i++) best = wmax(best, logits[i]);
+  if (!isfinite(best)) return -1;
+  const int nucleus = topp > 0 && topp < 1;
+  const float floor_ = nucleus ? best - temperature * 16.118095f : -FLT_MAX;
+  or_place *c = (or_place *)malloc(sizeof(or_place) * (size_t)n);
+  int32_t count = 0;
+  for (int32_t i = 0; i < n; i++)
+    if (logits[i] >= floor_) {
+      c[count].p = logits[i] - best;
+      c[count].t = i;
+      count++;
+    }
+  const float inverse = 1.0f / temperature;
+  const int32_t fours = count / 4 * 4;
+  for (int32_t i = 0; i < count; i++) c[i].p = i < fours ? or_vexp(c[i].p * inverse) : or_fexp(c[i].p / temperature);
+  double total = 0;
+  float top = 0;
+  for (int32_t i = 0; i < count; i++) {
+    total += c[i].p;
+    top = top > c[i].p ? top : c[i].p;
+  }
+  const int narrowed = topk > 0 && topk < count;
+  if (narrowed) {
+    qsort(c, (size_t)count, sizeof(or_place), or_ahead);
+    count = topk;
+    total = 0;
+    for (int32_t i = 0; i < count; i++) total += c[i].p;
+  }
+  const float least = minp > 0 ? (minp < 1.0f ? minp : 1.0f) * top : 0.0f;
+  int32_t last = count - 1;
+  double mass = total;
+  if (nucleus || narrowed) {
+    const double cutoff0 = (1.0 - (double)topp) / (double)(count > 1 ? count - 1 : 1) * total;
+    const double cutoff = nucleus ? (cutoff0 < (double)top ? cutoff0 : (double)top) : 0;
+    int32_t likely = 0;
+    for (int32_t k = 0; k < count; k++)
+      if ((double)c[k].p >= cutoff && c[k].p >= least) c[likely++] = c[k];
+    qsort(c, (size_t)likely, sizeof(or_place), or_ahead);
+    const double limit = nucleus ? (double)topp * total : INFINITY;
+    mass = 0;
+    last = likely - 1;
+    for (int32_t k = 0; k < likely; k++) {
+      mass += c[k].p;
+      if (mass >= limit) {
+        last = k;
+        break;
+      }
+    }
+  } else if (minp > 0) {
+    int32_t likely = 0;
+    mass = 0;
+    for (int32_t k = 0; k < count; k++)
+      if (c[k].p >= least) {
+        mass += c[k].p;
+        c[likely++] = c[k];
+      }
+    last = likely - 1;
+  }
+  const double target = random * mass;
+  double cumulative = 0;
+  int32_t token = last >= 0 ? c[last].t : -1;
+  for (int32_t k = 0; k <= last; k++) {
+    cumulative += c[k].p;
+    if (cumulative > target) {
+      token = c[k].t;
+      break;
+    }
+  }
+  free(c);
+  return token;
+}

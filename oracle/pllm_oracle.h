@@ -74,6 +74,8 @@ void or_swiglu(float *out, const float *h1, const float *h3, int32_t n);        
 void or_add_inplace(float *x, const float *y, int32_t n);                                 /* activations.ts:156-158 */
 int32_t or_argmax(const float *x, int32_t n);                                             /* sample.ts:6-10 */
 void or_penalize(float *logits, const int32_t *tokens, int32_t count, float penalty, float presence); /* sample.ts:16-30 */
+int32_t or_sample(const float *logits, int32_t n, float temperature, float topp, double random, int32_t topk,
+                  float minp);                                                          /* sample.ts:248-337 */
 void or_gate(float *out, const float *x, const float *g, int32_t n);                      /* stateful.ts:12-23 */
 void or_convolve(float *out, const float *taps, const float *rows, int32_t n, int32_t count); /* stateful.ts:49-63 */
 void or_short_conv(float *out, const float *taps, float *rows, const float *b, int32_t n, int32_t count); /* stateful.ts:70-86 */

@@ -89,7 +89,8 @@ __device__ __forceinline__ int tile_rows(long long t, long long hi) {
 }
 
 template <int MT, int PRO, int EPI>
-__global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs a, const TmaPlan p, const Xchg xg) {
+__global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs a, const TmaPlan p, const Xchg xg,
+                                                                   const Prefetch pf) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages, KS = p.ks, chunks = p.chunks, K = a.K, ng = K / 32;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -148,6 +149,8 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
           }
         }
       }
+      // every copy of this CTA is issued: the next kernel's first bytes into L2 behind them
+      prefetch_next(pf, blockIdx.x, gridDim.x);
     }
     return;
   }
@@ -411,7 +414,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_chain_kernel(const ChainA
 }
 
 template <int MT, int PRO, int EPI>
-bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl, const Xchg& xg) {
+bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl, const Xchg& xg, const Prefetch& pf) {
   auto kernel = gemv_tma_kernel<MT, PRO, EPI>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return false;
   const long long grid = gemv_tma_grid(a.r1 - a.r0, EPI);
@@ -425,7 +428,7 @@ bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl, const Xc
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a, p, xg);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a, p, xg, pf);
   if (e != cudaSuccess) {
     pllm_fail(PLLM_ECUDA, "gemv_tma launch: %s", cudaGetErrorString(e));
     return true;  // failed, but not for want of a fit: do not fall back
@@ -473,6 +476,7 @@ int gemv_tma_grid(long long rows, int epi) {
 // The bulk-copy product for int8 weights at 1 or 2 tokens; false where it does not apply (the caller then takes the
 // register-streaming kernel).
 bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg* xg) {
+  const Prefetch pf = pllm_take_prefetch();  // this product's call takes the plan, whichever kernel runs it
   const bool tp = pro == PRO_RMS_SUM || epi == EPI_SEND;
   if (tp != (xg != nullptr)) return false;
   if (g_gemv_mode == 1 || fmt != F_Q8 || a.count < 1 || a.count > 2 || (tp && a.count != 1)) return false;
@@ -499,7 +503,7 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
     if (!x.status) return true;  // failed (recorded), not for want of a fit
   }
 #define CASE(M, P, E) \
-  if (MT == M && pro == P && epi == E) return launch<M, P, E>(a, p, smem, pdl, x);
+  if (MT == M && pro == P && epi == E) return launch<M, P, E>(a, p, smem, pdl, x, pf);
   CASE(1, PRO_Q, EPI_STORE) CASE(1, PRO_Q, EPI_ADD) CASE(1, PRO_Q, EPI_SWIGLU)
   CASE(1, PRO_RMS, EPI_STORE) CASE(1, PRO_RMS, EPI_ADD) CASE(1, PRO_RMS, EPI_SWIGLU)
   CASE(1, PRO_QUANT, EPI_STORE) CASE(1, PRO_QUANT, EPI_ADD) CASE(1, PRO_QUANT, EPI_SWIGLU)

@@ -8,6 +8,8 @@
 // The argmax is a grid of CTAs, each reducing its elements to one 64-bit key (the value's bits made to order as
 // unsigned integers, then the complement of the index, so that the largest key is the largest value at its lowest
 // index), combined by atomicMax; the last CTA turns the key into the index and sets the key and count back to zero.
+#include <cfloat>
+
 #include "pllm_common.cuh"
 
 namespace {
@@ -117,4 +119,457 @@ PLLM_API void penalize(uint64_t logits, uint64_t tokens, int32_t count, float pe
   penalize_kernel<<<(count + 255) / 256, 256, 0, pllm_stream()>>>(dptr<float>(logits), dptr<const int>(tokens), count,
                                                                  penalty, presence);
   PLLM_LAUNCHED("penalize");
+}
+
+// ---- sample (sample.ts:248-337): a token drawn from softmax(logits / temperature) by one random number, with the
+// reference's top-k, nucleus (top-p) and min-p, in the reference's order of the walk:
+//   1. the largest logit (a NaN anywhere or an infinity: -1), a grid of CTAs;
+//   2. the candidates (with a nucleus, those within 16.118095 temperature of it; else all), kept in token order:
+//      each CTA counts its share, then writes its candidates behind the counts of the CTAs before it;
+//   3. one CTA of 1024 threads does the rest: the probabilities (the first 4 (count / 4) as the reference's four-lane
+//      exp of x (1 / temperature) clamped to [-87, 88], the rest as its scalar one of x / temperature, 0 below -87:
+//      CUDA's expf inside the clamps, where the reference has its own table-free exp: probabilities within an ulp or
+//      two of its), their double sum and maximum; top-k by a radix select on (probability bits, complement of the
+//      token), 8 bits a pass; with a nucleus or a top-k, the survivors of the cutoff and min-p walked from the most
+//      probable (chunks of at most 1024 selected the same way and sorted by a bitonic sort in shared memory); else
+//      walked in token order (each thread a contiguous part, the parts' double sums scanned).
+// Double sums in another association than the reference's one-by-one walk may differ in their last bits: a draw
+// differs only where the random number falls within about 1e-15 of a boundary.
+namespace {
+
+constexpr int SP_THREADS = 256, SP_FINAL = 1024, SP_MAX_CTAS = 1024, SP_CHUNK = 1024;
+
+struct SampleScratch {
+  float part_max[SP_MAX_CTAS];
+  int counts[SP_MAX_CTAS];
+};
+__device__ SampleScratch g_sample;
+__device__ int g_sample_out;
+
+__device__ __forceinline__ unsigned long long sp_key(float p, int token) {
+  return ((unsigned long long)__float_as_uint(p) << 32) | (0xFFFFFFFFu - (unsigned)token);
+}
+__device__ __forceinline__ int sp_share(int n, int ctas, int c, int* hi) {
+  const int per = (n + ctas - 1) / ctas;
+  const int lo = min(n, c * per);
+  *hi = min(n, lo + per);
+  return lo;
+}
+
+__global__ void sample_max_kernel(const float* __restrict__ x, int n) {
+  int hi;
+  const int lo = sp_share(n, gridDim.x, blockIdx.x, &hi);
+  float best = -INFINITY;
+  bool nan = false;
+  for (int i = lo + threadIdx.x; i < hi; i += SP_THREADS) {
+    const float v = x[i];
+    nan |= v != v;
+    best = fmaxf(best, v);
+  }
+  best = warp_max(best);
+  nan = __any_sync(0xffffffffu, nan);
+  __shared__ float wm[SP_THREADS / 32];
+  __shared__ int wn[SP_THREADS / 32];
+  if ((threadIdx.x & 31) == 0) {
+    wm[threadIdx.x >> 5] = best;
+    wn[threadIdx.x >> 5] = nan;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < SP_THREADS / 32; w++) {
+      best = fmaxf(best, wm[w]);
+      nan |= wn[w] != 0;
+    }
+    g_sample.part_max[blockIdx.x] = nan ? __int_as_float(0x7fc00000) : best;
+  }
+}
+
+// the largest logit from the CTAs' maxima (NaN if any was)
+__device__ float sp_best(int ctas) {
+  __shared__ float b;
+  if (threadIdx.x == 0) {
+    float best = -INFINITY;
+    bool nan = false;
+    for (int c = 0; c < ctas; c++) {
+      const float v = g_sample.part_max[c];
+      nan |= v != v;
+      best = fmaxf(best, v);
+    }
+    b = nan ? __int_as_float(0x7fc00000) : best;
+  }
+  __syncthreads();
+  return b;
+}
+
+__device__ __forceinline__ float sp_floor(float best, float temperature, float topp) {
+  return (topp > 0.0f && topp < 1.0f) ? best - temperature * 16.118095f : -FLT_MAX;
+}
+
+__global__ void sample_count_kernel(const float* __restrict__ x, int n, float temperature, float topp) {
+  const float best = sp_best(gridDim.x);
+  if (!isfinite(best)) return;
+  const float fl = sp_floor(best, temperature, topp);
+  int hi;
+  const int lo = sp_share(n, gridDim.x, blockIdx.x, &hi);
+  int c = 0;
+  for (int i = lo + threadIdx.x; i < hi; i += SP_THREADS) c += x[i] >= fl;
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  __shared__ int wc[SP_THREADS / 32];
+  if ((threadIdx.x & 31) == 0) wc[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < SP_THREADS / 32; w++) c += wc[w];
+    g_sample.counts[blockIdx.x] = c;
+  }
+}
+
+// this CTA's candidates in token order behind the earlier CTAs' counts: probs = x - best, index = the token
+__global__ void sample_scatter_kernel(const float* __restrict__ x, int n, float temperature, float topp, float* probs,
+                                      int* index) {
+  const float best = sp_best(gridDim.x);
+  if (!isfinite(best)) return;
+  const float fl = sp_floor(best, temperature, topp);
+  __shared__ int base, wc[SP_THREADS / 32];
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int c = 0; c < (int)blockIdx.x; c++) s += g_sample.counts[c];
+    base = s;
+  }
+  __syncthreads();
+  int hi;
+  const int lo = sp_share(n, gridDim.x, blockIdx.x, &hi);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int t0 = lo; t0 < hi; t0 += SP_THREADS) {
+    const int i = t0 + threadIdx.x;
+    const float v = i < hi ? x[i] : 0.0f;
+    const bool keep = i < hi && v >= fl;
+    const unsigned m = __ballot_sync(0xffffffffu, keep);
+    if (lane == 0) wc[warp] = __popc(m);
+    __syncthreads();
+    int before = 0, all = 0;
+    for (int w = 0; w < SP_THREADS / 32; w++) {
+      before += w < warp ? wc[w] : 0;
+      all += wc[w];
+    }
+    if (keep) {
+      const int at = base + before + __popc(m & ((1u << lane) - 1));
+      probs[at] = v - best;
+      index[at] = i;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) base += all;
+    __syncthreads();
+  }
+}
+
+__device__ double sp_sum(double v, double* red) {  // a block's sum (every thread gets it)
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double s = threadIdx.x < SP_FINAL / 32 ? red[threadIdx.x] : 0.0;
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (threadIdx.x == 0) red[32] = s;
+  }
+  __syncthreads();
+  return red[32];
+}
+__device__ float sp_fmax(float v, float* red) {
+  v = warp_max(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float s = threadIdx.x < SP_FINAL / 32 ? red[threadIdx.x] : -INFINITY;
+    s = warp_max(s);
+    if (threadIdx.x == 0) red[32] = s;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// the rank-th largest (rank from 1) key among the elements where in(i) holds and key < upper: a radix select, 8 bits a
+// pass from the top (every thread returns it); none: 0
+template <typename In>
+__device__ unsigned long long sp_select(const float* probs, const int* index, int count, In in, unsigned long long upper,
+                                        int rank, unsigned* hist) {
+  unsigned long long prefix = 0, mask = 0;
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int b = threadIdx.x; b < 256; b += SP_FINAL) hist[b] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < count; i += SP_FINAL) {
+      if (!in(i)) continue;
+      const unsigned long long k = sp_key(probs[i], index[i]);
+      if (k >= upper || (k & mask) != prefix) continue;
+      atomicAdd(&hist[(k >> shift) & 255], 1u);
+    }
+    __syncthreads();
+    __shared__ int pick, left;
+    if (threadIdx.x == 0) {
+      int r = rank, b = 255;
+      for (; b >= 0; b--) {
+        if ((int)hist[b] >= r) break;
+        r -= hist[b];
+      }
+      pick = b;
+      left = r;
+    }
+    __syncthreads();
+    if (pick < 0) return 0;
+    prefix |= (unsigned long long)pick << shift;
+    mask |= 255ull << shift;
+    rank = left;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// the elements of the set with lo <= key < upper (at most SP_CHUNK of them) into shared memory, sorted descending;
+// returns how many
+template <typename In>
+__device__ int sp_chunk(const float* probs, const int* index, int count, In in, unsigned long long lo,
+                        unsigned long long upper, unsigned long long* keys, int* fill) {
+  if (threadIdx.x == 0) *fill = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < count; i += SP_FINAL) {
+    if (!in(i)) continue;
+    const unsigned long long k = sp_key(probs[i], index[i]);
+    if (k >= lo && k < upper) {
+      const int at = atomicAdd(fill, 1);
+      if (at < SP_CHUNK) keys[at] = k;
+    }
+  }
+  __syncthreads();
+  const int m = min(*fill, SP_CHUNK);
+  for (int i = m + threadIdx.x; i < SP_CHUNK; i += SP_FINAL) keys[i] = 0;  // padding sorts last
+  __syncthreads();
+  for (int size = 2; size <= SP_CHUNK; size <<= 1)  // bitonic sort, descending
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < SP_CHUNK; i += SP_FINAL) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool down = (i & size) == 0;
+          const unsigned long long a = keys[i], b = keys[j];
+          if (down ? a < b : a > b) {
+            keys[i] = b;
+            keys[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  return m;
+}
+
+__device__ __forceinline__ float sp_prob(unsigned long long k) { return __uint_as_float((unsigned)(k >> 32)); }
+__device__ __forceinline__ int sp_token(unsigned long long k) { return (int)(0xFFFFFFFFu - (unsigned)k); }
+
+__global__ void __launch_bounds__(SP_FINAL) sample_final_kernel(int ctas, float temperature, float topp,
+                                                                 const double* random_dev, double random_val, int topk,
+                                                                 float minp, float* probs, const int* index, int* out) {
+  __shared__ double red[33];
+  __shared__ float redf[33];
+  __shared__ unsigned hist[256];
+  __shared__ unsigned long long keys[SP_CHUNK];
+  __shared__ int fill, result;
+  const float best = sp_best(ctas);
+  if (!isfinite(best)) {
+    if (threadIdx.x == 0) *out = -1;
+    return;
+  }
+  const double random = random_dev ? *random_dev : random_val;
+  int count = 0;
+  for (int c = 0; c < ctas; c++) count += g_sample.counts[c];
+  const bool nucleus = topp > 0.0f && topp < 1.0f;
+  const int fours = count / 4 * 4;
+  const float inverse = 1.0f / temperature;
+  double s = 0.0;
+  float top = 0.0f;
+  for (int i = threadIdx.x; i < count; i += SP_FINAL) {
+    const float x = probs[i];
+    float p;
+    if (i < fours) {
+      p = expf(fminf(fmaxf(x * inverse, -87.0f), 88.0f));
+    } else {
+      const float y = x / temperature;
+      p = y < -87.0f ? 0.0f : expf(fminf(y, 88.0f));
+    }
+    probs[i] = p;
+    s += p;
+    top = fmaxf(top, p);
+  }
+  double total = sp_sum(s, red);
+  top = sp_fmax(top, redf);
+  const bool narrowed = topk > 0 && topk < count;
+  unsigned long long kth = 0;  // narrowed: the top-k's smallest key
+  if (narrowed) {
+    kth = sp_select(probs, index, count, [](int) { return true; }, ~0ull, topk, hist);
+    s = 0.0;
+    for (int i = threadIdx.x; i < count; i += SP_FINAL)
+      if (sp_key(probs[i], index[i]) >= kth) s += probs[i];
+    total = sp_sum(s, red);
+  }
+  const int live = narrowed ? topk : count;
+  const float least = minp > 0.0f ? fminf(minp, 1.0f) * top : 0.0f;
+  if (nucleus || narrowed) {
+    const double c0 = (1.0 - (double)topp) / (double)(live > 1 ? live - 1 : 1) * total;
+    const double cutoff = nucleus ? fmin(c0, (double)top) : 0.0;
+    auto in = [&](int i) {
+      const float p = probs[i];
+      return (!narrowed || sp_key(p, index[i]) >= kth) && (double)p >= cutoff && p >= least;
+    };
+    const double limit = nucleus ? (double)topp * total : INFINITY;
+    // pass 1: the nucleus's mass and its last key, chunk by chunk from the most probable
+    __shared__ double mass;
+    __shared__ unsigned long long last_key;
+    __shared__ bool done;
+    if (threadIdx.x == 0) {
+      mass = 0.0;
+      last_key = 0;
+      done = false;
+    }
+    __syncthreads();
+    unsigned long long upper = ~0ull;
+    while (!done) {
+      const unsigned long long lo = sp_select(probs, index, count, in, upper, SP_CHUNK, hist);
+      const int m = sp_chunk(probs, index, count, in, lo, upper, keys, &fill);
+      if (threadIdx.x == 0) {
+        for (int k = 0; k < m; k++) {
+          mass += sp_prob(keys[k]);
+          last_key = keys[k];
+          if (mass >= limit) {
+            done = true;
+            break;
+          }
+        }
+        if (lo == 0 || m == 0) done = true;  // the set is walked whole
+      }
+      __syncthreads();
+      upper = lo;
+    }
+    // pass 2: the first whose cumulative sum passes random x mass, from the most probable (else the last)
+    const double target = random * mass;
+    if (threadIdx.x == 0) {
+      result = sp_token(last_key);
+      done = false;
+    }
+    __syncthreads();
+    double cumulative = 0.0;
+    upper = ~0ull;
+    while (!done) {
+      const unsigned long long lo = sp_select(probs, index, count, in, upper, SP_CHUNK, hist);
+      const int m = sp_chunk(probs, index, count, in, lo, upper, keys, &fill);
+      if (threadIdx.x == 0) {
+        for (int k = 0; k < m && !done; k++) {
+          cumulative += sp_prob(keys[k]);
+          if (cumulative > target) {
+            result = sp_token(keys[k]);
+            done = true;
+          }
+          if (keys[k] == last_key) done = true;
+        }
+        if (lo == 0 || m == 0) done = true;
+      }
+      __syncthreads();
+      upper = lo;
+    }
+    if (threadIdx.x == 0) *out = result;
+    return;
+  }
+  // token order: every candidate, or those at or above least; a thread a contiguous part
+  const int per = (count + SP_FINAL - 1) / SP_FINAL;
+  const int a = min(count, (int)threadIdx.x * per), b = min(count, a + per);
+  double part = 0.0;
+  int mine_last = -1;
+  for (int i = a; i < b; i++)
+    if (probs[i] >= least) {
+      part += probs[i];
+      mine_last = i;
+    }
+  // the parts' exclusive scan (in thread order) and their total
+  __shared__ double scan[SP_FINAL];
+  __shared__ int lastv[SP_FINAL];
+  scan[threadIdx.x] = part;
+  lastv[threadIdx.x] = mine_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double run = 0.0;
+    int lastc = -1;
+    for (int t = 0; t < SP_FINAL; t++) {
+      const double v = scan[t];
+      scan[t] = run;
+      run += v;
+      lastc = lastv[t] >= 0 ? lastv[t] : lastc;
+    }
+    red[32] = run;
+    result = lastc >= 0 ? index[lastc] : -1;
+    fill = 0;
+  }
+  __syncthreads();
+  const double target = random * red[32];
+  double cumulative = scan[threadIdx.x];
+  if (cumulative <= target && cumulative + part > target) {
+    for (int i = a; i < b; i++) {
+      if (probs[i] < least) continue;
+      cumulative += probs[i];
+      if (cumulative > target) {
+        if (atomicAdd(&fill, 1) == 0) result = index[i];
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *out = result;
+}
+
+int sample_ctas(int n) {
+  int c = (n + 4095) / 4096;
+  return c < 1 ? 1 : (c > SP_MAX_CTAS ? SP_MAX_CTAS : c);
+}
+
+bool sample_enqueue(const float* x, int n, float temperature, float topp, const double* random_dev, double random,
+                    int topk, float minp, float* probs, int* index, int* out) {
+  const int ctas = sample_ctas(n);
+  cudaStream_t s = pllm_stream();
+  sample_max_kernel<<<ctas, SP_THREADS, 0, s>>>(x, n);
+  sample_count_kernel<<<ctas, SP_THREADS, 0, s>>>(x, n, temperature, topp);
+  sample_scatter_kernel<<<ctas, SP_THREADS, 0, s>>>(x, n, temperature, topp, probs, index);
+  sample_final_kernel<<<1, SP_FINAL, 0, s>>>(ctas, temperature, topp, random_dev, random, topk, minp, probs, index, out);
+  return cudaGetLastError() == cudaSuccess;
+}
+
+}  // namespace
+
+// sample (sample.ts:248): the token drawn by random in [0, 1) (-1: the largest logit is not a finite number); probs and
+// index: device scratch of n floats and n int32
+PLLM_API int32_t sample(uint64_t logits, int32_t n, float temperature, float topp, double random, uint64_t probs,
+                        uint64_t index, int32_t topk, float minp) {
+  PLLM_REQUIRE_RET(logits && probs && index && n > 0 && temperature > 0.0f, -1, "sample: n %d temperature %g", n,
+                   (double)temperature);
+  void* out = nullptr;
+  if (cudaGetSymbolAddress(&out, g_sample_out) != cudaSuccess ||
+      !sample_enqueue(dptr<const float>(logits), n, temperature, topp, nullptr, random, topk, minp, dptr<float>(probs),
+                      dptr<int>(index), (int*)out)) {
+    pllm_fail(PLLM_ECUDA, "sample: launch");
+    return -1;
+  }
+  int token = -1;
+  const cudaError_t e = cudaMemcpyAsync(&token, out, sizeof token, cudaMemcpyDeviceToHost, pllm_stream());
+  if (e != cudaSuccess || cudaStreamSynchronize(pllm_stream()) != cudaSuccess) {
+    pllm_fail(PLLM_ECUDA, "sample: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  return token;
+}
+
+// the same into device memory without waiting (a recorded step): out one int32, the random number a double in device
+// memory (written before the step runs)
+PLLM_API void pllm_sample_dev(uint64_t out, uint64_t logits, int32_t n, float temperature, float topp,
+                              uint64_t random_dev, uint64_t probs, uint64_t index, int32_t topk, float minp) {
+  PLLM_REQUIRE(out && logits && probs && index && random_dev && n > 0 && temperature > 0.0f,
+               "pllm_sample_dev: n %d temperature %g", n, (double)temperature);
+  if (!sample_enqueue(dptr<const float>(logits), n, temperature, topp, dptr<const double>(random_dev), 0.0, topk, minp,
+                      dptr<float>(probs), dptr<int>(index), dptr<int>(out)))
+    pllm_fail(PLLM_ECUDA, "pllm_sample_dev: launch");
 }

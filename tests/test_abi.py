@@ -33,7 +33,7 @@ def test_header_declares_the_registry():
                 "matmul_q6", "matmul_q6r", "matmul_t2", "matmul_t2r", "matmul_t2r_tile", "matmul_b1", "matmul_b1r",
                 "matmul_b1r_tile", "matmul_f32", "rope", "attention", "attention_f16", "attention_capped",
                 "attention_f16_capped", "to_f16", "from_f16", "finite_f16", "rmsnorm", "swiglu", "add_inplace", "gate",
-                "convolve", "short_conv", "delta_rule", "argmax", "penalize"}
+                "convolve", "short_conv", "delta_rule", "argmax", "penalize", "sample"}
     assert registry <= names, registry - names
 
 
@@ -62,6 +62,26 @@ def test_reference_signature_arity():
              "matmul_f32": 6, "six_sums": 3, "int8_sums": 3, "matmul_q8": 8, "interleave": 3, "matmul_t2": 9,
              "matmul_q6": 8, "quantize_x": 5, "gate": 4, "convolve": 5, "short_conv": 6, "delta_rule": 11,
              "matmul_q8r": 9, "matmul_q8r_tile": 12, "matmul_q6r": 9, "matmul_t2r": 9, "matmul_t2r_tile": 12,
-             "matmul_b1": 9, "matmul_b1r": 9, "matmul_b1r_tile": 12, "argmax": 2, "penalize": 5}
+             "matmul_b1": 9, "matmul_b1r": 9, "matmul_b1r_tile": 12, "argmax": 2, "penalize": 5, "sample": 9}
     for name, n in arity.items():
         assert len(pl.SIGNATURES[name][0]) == n, name
+
+
+def test_prefetch_plan_checks_its_ranges():
+    """pllm_prefetch_next keeps a plan for the next launch and refuses ranges it could not walk safely (a base off a
+    16-byte boundary, a negative size, more than 8 ranges); the checks are on the host, no GPU call is made."""
+    import pllm.lib as pl
+    R = pl.PrefetchRange
+    ok = (R * 2)(R(base=4096, row_bytes=64, rows=10, first=128, parts=4), R(base=8192, row_bytes=32, rows_dev=64,
+                                                                            first=1 << 40, parts=2))
+    pl.L.pllm_prefetch_next(ok, 2)
+    pl.check("a plan of two ranges")
+    for bad, count in (((R * 1)(R(base=4100, row_bytes=64, rows=10, first=128, parts=4)), 1),
+                       ((R * 1)(R(base=4096, row_bytes=0, rows=10, first=128, parts=4)), 1),
+                       ((R * 1)(R(base=4096, row_bytes=64, rows=10, first=-1, parts=4)), 1),
+                       (ok, 9)):
+        pl.L.pllm_prefetch_next(bad, count)
+        with pytest.raises(pl.PllmError):
+            pl.check("a bad plan")
+    pl.L.pllm_prefetch_next(None, 0)  # clears
+    pl.check("no plan")

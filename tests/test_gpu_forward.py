@@ -14,6 +14,7 @@ import pytest
 
 import oracle as O
 from pllm.forward import Config, Engine, synthetic_host_weights
+from pllm.lib import L
 
 pytestmark = pytest.mark.gpu
 
@@ -161,5 +162,50 @@ def test_next_token_is_the_logits_argmax():
         nxt = b.next_token(tok, pos)
         assert nxt == int(O.argmax(logits))
         tok = nxt
+    a.close()
+    b.close()
+
+
+def test_prefetch_changes_no_result(monkeypatch):
+    """The L2 prefetches of the next kernel's weights and of the layer's cache (pllm_prefetch_next, taken by the
+    products and the attention step) are hints: the step with them computes what the step without them does, to the
+    bit, and no wait gives up. Large budgets here, so that every range (whole shares, the cache to the position) is
+    walked, also past the ends of short shares."""
+    from dataclasses import replace
+    from pllm.forward import QWEN3_8B
+    cfg = replace(QWEN3_8B, layers=2, seq_len=64)
+    monkeypatch.setenv("PLLM_PREFETCH", "all=0")
+    plain = Engine(cfg, seed=5)
+    monkeypatch.setenv("PLLM_PREFETCH", "all=4096")
+    fetched = Engine(cfg, seed=5)
+    assert all(v == 0 for v in plain.prefetch.values()) and all(v > 0 for v in fetched.prefetch.values())
+    for pos, tok in enumerate(np.random.default_rng(8).integers(0, cfg.vocab, 5)):
+        want = plain.forward(int(tok), pos)
+        got = fetched.forward(int(tok), pos)
+        assert np.array_equal(got, want), (pos, np.abs(got - want).max())
+    assert L.pllm_device_status() == 0
+    plain.close()
+    fetched.close()
+
+
+def test_next_token_draws_what_the_oracle_samples():
+    """The drawn step (sample on the device, sample.ts:248-337: temperature, top-k, nucleus, min-p, a random number
+    from the caller) draws the token the oracle's sampler draws from the logits forward() returns, wherever the
+    oracle draws the same token at random x (1 -+ 1e-5) (the device's probabilities come of CUDA's expf)."""
+    cfg = SMALL_QWEN3
+    a, b = Engine(cfg, seed=6), Engine(cfg, seed=6)
+    rng = np.random.default_rng(9)
+    tok, steady_draws = 5, 0
+    for pos in range(8):
+        logits = a.forward(tok, pos)
+        r = float(rng.random())
+        want = O.sample(logits, 0.8, 0.9, r, 40, 0.02)
+        steady = all(O.sample(logits, 0.8, 0.9, r * f, 40, 0.02) == want for f in (1 - 1e-5, 1 + 1e-5))
+        got = b.next_token(tok, pos, temperature=0.8, topp=0.9, topk=40, minp=0.02, random=r)
+        if steady:
+            assert got == want, (pos, got, want)
+            steady_draws += 1
+        tok = got
+    assert steady_draws >= 6
     a.close()
     b.close()

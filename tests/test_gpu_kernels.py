@@ -589,3 +589,39 @@ def test_argmax_and_penalize(n):
     L.penalize(X.ptr, T.ptr, tokens.size, 1.3, 0.4)
     check("penalize")
     np.testing.assert_array_equal(get(X, np.float32)[:n], O.penalize(logits, tokens, 1.3, 0.4))
+
+
+@pytest.mark.parametrize("n", [50, 1000, 4096, 151936])
+def test_sample_draws_the_oracles_tokens(n):
+    """sample (sample.ts:248-337) on the device against the oracle's walk (pinned to the reference's NumPy sampler):
+    temperature, top-p, top-k and min-p settings, seeded random numbers. The device's probabilities come of CUDA's
+    expf (within an ulp or two of the reference's exp) and its double sums of another association, so a draw may
+    differ only where the random number falls at a boundary of the walk: wherever the oracle draws the same token
+    at random x (1 - 1e-5) and x (1 + 1e-5), the device's token is that token. Both entry points (the waiting one,
+    and the one that reads its random number from device memory)."""
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal(n) * 4.0).astype(np.float32)
+    x[n // 3] = x[n // 5]  # a tie
+    X, P, I = dev(x), dev(np.zeros(n, np.float32)), dev(np.zeros(n, np.int32))
+    R, out = dev(np.zeros(1, np.float64)), dev(np.zeros(1, np.int32))
+    checked = 0
+    for temperature, topp, topk, minp in [(1.0, 0.9, 0, 0.0), (0.7, 1.0, 0, 0.0), (1.3, 0.0, 40, 0.0),
+                                          (1.0, 0.5, 40, 0.05), (1.0, 0.0, 0, 0.05), (0.8, 0.95, 1, 0.0),
+                                          (2.0, 0.999, 2000, 0.0)]:
+        for r in rng.random(6):
+            want = O.sample(x, temperature, topp, r, topk, minp)
+            steady = all(O.sample(x, temperature, topp, r * f, topk, minp) == want for f in (1 - 1e-5, 1 + 1e-5))
+            got = L.sample(X.ptr, n, temperature, topp, float(r), P.ptr, I.ptr, topk, minp)
+            check("sample")
+            R.upload(np.array([r], np.float64))
+            L.pllm_sample_dev(out.ptr, X.ptr, n, temperature, topp, R.ptr, P.ptr, I.ptr, topk, minp)
+            check("pllm_sample_dev")
+            got_dev = int(get(out, np.int32)[0])
+            if steady:
+                assert got == want and got_dev == want, (temperature, topp, topk, minp, r, got, got_dev, want)
+                checked += 1
+    assert checked >= 30
+    bad = x.copy()
+    bad[7] = np.nan
+    B = dev(bad)
+    assert L.sample(B.ptr, n, 1.0, 0.9, 0.5, P.ptr, I.ptr, 0, 0.0) == -1

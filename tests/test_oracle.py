@@ -1,5 +1,7 @@
 """The CPU oracle pinned to the reference's known answers (tests/golden/golden.npz) before it is trusted as the
 checker of the CUDA kernels. CPU only."""
+import os
+
 import numpy as np
 import pytest
 
@@ -191,3 +193,18 @@ def test_argmax_and_penalize_walks():
         v = want[t]
         want[t] = (v / np.float32(1.3) if v > 0 else v * np.float32(1.3)) - np.float32(0.25)
     np.testing.assert_array_equal(got, want)
+
+
+def test_sample_draws_the_reference_samplers_tokens():
+    """or_sample (sample.ts:248-337) against the reference's NumPy sampler (engine/sampler.py NumpySampler.drawing,
+    which the kernel restates) on the draws of tests/golden/sampling.npz: three vocabularies, temperature, top-p,
+    top-k and min-p settings, random numbers handed in; every token the same."""
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "sampling.npz"))
+    logits = [g["logits0"], g["logits1"], g["logits2"]]
+    for v, t, p, k, m, r, tok in g["draws"]:
+        assert O.sample(logits[int(v)], float(t), float(p), r, int(k), float(m)) == int(tok), (v, t, p, k, m, r)
+    bad = logits[1].copy()
+    bad[7] = np.nan
+    assert O.sample(bad, 1.0, 0.9, 0.5) == -1
+    bad[7] = np.inf
+    assert O.sample(bad, 1.0, 0.9, 0.5) == -1
