@@ -119,6 +119,33 @@ void penalize(uint64_t logits, uint64_t tokens, int32_t count, float penalty, fl
 int32_t sample(uint64_t logits, int32_t n, float temperature, float topp, double random, uint64_t probs,
                uint64_t index, int32_t topk, float minp);
 
+/* ===== the registry: llama.cpp's blocks of 256 weights (kernels/blocks.ts:11-13, kernels/blocks_relaxed.ts:5-6;
+ * kernels/blocks/types.ts): Q2_K 10, Q4_K 12, IQ2_XXS 16, IQ2_XS 17, IQ3_XXS 18, IQ1_S 19, IQ3_S 21, IQ2_S 22,
+ * IQ4_XS 23, IQ1_M 29 (type: the type's number in a GGUF); rows of whole blocks (n a multiple of 256); tab: sb_tables'
+ * area. Every group's integers are the reference's; the float32 row within rounding of its order. */
+/* replaces sb_tables, blocks/types.ts:294: the tables (34,992 bytes at area) from the checkpoint's codebooks row;
+ * returns the bytes */
+int32_t sb_tables(uint64_t area, uint64_t codebooks);
+/* replaces sums_x, blocks/token.ts:160: after the n / 32 scales at xs, the int16 sums of each 16 activations of xq,
+ * then of each 8 */
+void sums_x(uint64_t xs, uint64_t xq, int32_t n);
+/* replaces matmul_sb, blocks/token.ts:133, and matmul_sbr, :138 (the same numbers): one token, rows r0..r1 */
+void matmul_sb(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t w, uint64_t tab, int32_t n, int32_t r0, int32_t r1,
+               int32_t type);
+void matmul_sbr(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t w, uint64_t tab, int32_t n, int32_t r0, int32_t r1,
+                int32_t type);
+/* replaces matmul_sbr_tile, blocks/tile.ts:149, and matmul_sbw_tile (the same numbers; its scratch is not needed):
+ * count tokens, activations and xs frame bytes apart, outputs os bytes apart */
+void matmul_sbr_tile(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t w, uint64_t tab, int32_t n, int32_t r0,
+                     int32_t r1, int32_t count, int32_t os, int32_t frame, int32_t type);
+void matmul_sbw_tile(uint64_t xout, uint64_t xq, uint64_t xs, uint64_t w, uint64_t tab, int32_t n, int32_t r0,
+                     int32_t r1, int32_t count, int32_t os, int32_t frame, int32_t type, uint64_t scratch);
+/* replaces signed_dots, blocks/tile.ts: out[l] = sum over i < 4 of a[4 l + i] b[4 l + i], signed bytes by signed
+ * bytes (exact here for every a and b) */
+void signed_dots(uint64_t out, uint64_t a, uint64_t b);
+/* replaces sb_row, blocks/row.ts:60: a row of n weights as float32 (each as the reference's reader makes it) */
+void sb_row(uint64_t out, uint64_t w, uint64_t tab, int32_t n, int32_t type);
+
 /* ===== the registry: vector glue and stateful layers (kernels/kernel/activations.ts, kernels/kernel/stateful.ts) */
 /* replaces rmsnorm, kernels/kernel/activations.ts:8 (jobs.ts:83) */
 void rmsnorm(uint64_t out, uint64_t x, uint64_t w, int32_t n, float eps);

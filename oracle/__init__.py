@@ -62,6 +62,8 @@ def _declare(L):
         "or_forward": ([P, P, I32, I32, P, I32], I32), "or_threads": ([], I32),
         "or_argmax": ([P, I32], I32), "or_penalize": ([P, P, I32, F32, F32], None),
         "or_sample": ([P, I32, F32, F32, ctypes.c_double, I32, F32], I32),
+        "or_sb_size": ([I32], I32), "or_sb_tables": ([P, P], I32), "or_sums_x": ([P, P, I32], None),
+        "or_matmul_sb": ([P, P, P, P, P, I32, I32, I32, I32], None), "or_sb_row": ([P, P, P, I32, I32], None),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -283,6 +285,40 @@ def sample(logits, temperature, topp, random, topk=0, minp=0.0):
     """sample.ts:248-337: the token drawn with this random number in [0, 1) (-1: the largest logit is not finite)"""
     x = _c(logits, np.float32)
     return int(lib().or_sample(_p(x), x.size, temperature, topp, float(random), topk, minp))
+
+
+SB_TABLES = 34992  # sb_tables' bytes (blocks/types.ts:94)
+
+
+def sb_tables(codebooks):
+    """blocks/types.ts:294-322: the kernels' tables from the checkpoint's codebooks row (uint8)"""
+    area = np.zeros(SB_TABLES, np.uint8)
+    lib().or_sb_tables(_p(area), _p(_c(codebooks, np.uint8)))
+    return area
+
+
+def sums_x(xs, xq):
+    """blocks/token.ts:158-172: the scales followed by the int16 sums of each 16 and each 8 activations"""
+    n = xq.size
+    out = np.zeros(n // 32 + n // 16 // 2 + n // 8 // 2, np.float32)
+    out[:n // 32] = xs
+    lib().or_sums_x(_p(out), _p(_c(xq, np.int8)), n)
+    return out
+
+
+def matmul_sb(xq, xs, w, tab, n, rows, btype):
+    """blocks/token.ts:130-141: one token against rows of n weights in llama.cpp's blocks of btype"""
+    out = np.zeros(rows, np.float32)
+    lib().or_matmul_sb(_p(out), _p(_c(xq, np.int8)), _p(_c(xs, np.float32)), _p(_c(w, np.uint8)),
+                       _p(_c(tab, np.uint8)), n, 0, rows, btype)
+    return out
+
+
+def sb_row(w, tab, n, btype):
+    """blocks/row.ts: a row of n weights in blocks of btype as float32"""
+    out = np.zeros(n, np.float32)
+    lib().or_sb_row(_p(out), _p(_c(w, np.uint8)), _p(_c(tab, np.uint8)), n, btype)
+    return out
 
 
 def gate(x, g):

@@ -811,3 +811,276 @@ int32_t or_sample(const float *logits, int32_t n, float temperature, float topp,
   free(c);
   return token;
 }
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * llama.cpp's blocks of 256 weights (kernels/blocks/types.ts): the ten types' reading, a unit of 16 weights at a time,
+ * as signed integers W with the integer S of their unit and, for the K types, the integer minimum m; F and Fm of the
+ * block; then the token's arithmetic of types.ts:66-83 (G[k] = sum over group k's 32 of S W a, exact;
+ * lane k & 3 += ((G[k] xs[k] + G[k + 4] xs[k + 4]) F) - ((M[k] xs[k] + M[k + 4] xs[k + 4]) Fm); the lanes added in
+ * order at the row's end). The tables are sb_tables' (types.ts:294-322): the grids, then the 7-bit signs' table, then
+ * IQ4_XS's values, from the checkpoint's codebooks row. */
+#define SB_T_IQ2XS 2048
+#define SB_T_IQ2S 6144
+#define SB_T_IQ3XXS 14336
+#define SB_T_IQ3S 15360
+#define SB_T_IQ1S 17408
+#define SB_T_SIGNS 33792
+#define SB_T_IQ4 34816
+#define SB_T_VECTORS 34864
+#define SB_GRIDS 33792
+#define SB_TABLES 34992
+
+static inline uint32_t rd16(const uint8_t *p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
+static inline uint32_t rd32(const uint8_t *p) { return rd16(p) | (rd16(p + 2) << 16); }
+
+int32_t or_sb_size(int32_t type) {
+  switch (type) {
+    case 10: return 84;  case 12: return 144; case 16: return 66;  case 17: return 74;  case 18: return 98;
+    case 19: return 50;  case 21: return 110; case 22: return 82;  case 23: return 136; case 29: return 56;
+    default: return 0;
+  }
+}
+
+/* sb_tables (types.ts:294-322): the grids as the codebooks hold them (IQ1_S's grid plus 1: codes 0, 1, 2), the signs
+ * of 8 weights by a 7-bit index (the eighth makes the number of minuses even), IQ4_XS's values / magnitudes / minus
+ * masks, and the small vectors */
+int32_t or_sb_tables(uint8_t *area, const uint8_t *codebooks) {
+  for (int i = 0; i < SB_GRIDS; i++) area[i] = (uint8_t)(codebooks[i] + (i >= SB_T_IQ1S ? 1 : 0));
+  for (uint32_t i = 0; i < 128; i++) {
+    uint32_t ones = 0;
+    for (int j = 0; j < 7; j++) ones += (i >> j) & 1;
+    const uint32_t held = i | ((ones & 1) << 7);
+    for (int j = 0; j < 8; j++) area[SB_T_SIGNS + i * 8 + j] = ((held >> j) & 1) ? 255 : 0;
+  }
+  for (int i = 0; i < 16; i++) {
+    const int8_t v = (int8_t)codebooks[SB_GRIDS + i];
+    area[SB_T_IQ4 + i] = (uint8_t)v;
+    area[SB_T_IQ4 + 16 + i] = (uint8_t)(v < 0 ? -v : v);
+    area[SB_T_IQ4 + 32 + i] = v < 0 ? 255 : 0;
+  }
+  uint8_t *vec = area + SB_T_VECTORS;
+  for (int j = 0; j < 16; j++) {
+    vec[0 + j] = (uint8_t)(1u << (j & 7));
+    vec[16 + j] = (uint8_t)(j >> 3);
+    vec[32 + j] = 3;
+    vec[48 + j] = 15;
+    vec[80 + j] = 7;
+    vec[96 + j] = 1;
+  }
+  for (int j = 0; j < 4; j++) {
+    const int32_t p3 = 512 >> (j * 3), p4 = 4096 >> (j * 4);
+    memcpy(vec + 64 + 4 * j, &p3, 4);
+    memcpy(vec + 112 + 4 * j, &p4, 4);
+  }
+  return SB_TABLES;
+}
+
+static inline int sb_minus(const uint8_t *tab, uint32_t idx7, int j) { return tab[SB_T_SIGNS + (idx7 & 127) * 8 + j] != 0; }
+
+/* unit u (16 weights) of the block at p: W[16] (IQ1: 8 g + 1, or 8 g - 1 where the shift is down), S, m */
+static void sb_unit(int type, const uint8_t *p, int u, const uint8_t *tab, int32_t *W, int32_t *S, int32_t *m) {
+  const int g = u >> 1;
+  *m = 0;
+  switch (type) {
+    case 10: {  /* Q2_K: bits 2 s, 2 s + 1 of byte b of a half's 32 are weight 32 s + b of the half */
+      const int half = u >> 3, s = (u & 7) >> 1;
+      const uint8_t *q = p + 16 + 32 * half + 16 * (u & 1);
+      for (int j = 0; j < 16; j++) W[j] = (q[j] >> (2 * s)) & 3;
+      *S = p[u] & 15;
+      *m = p[u] >> 4;
+      return;
+    }
+    case 12: {  /* Q4_K: of every 32 bytes the low halves are 32 weights, the high halves the next 32 */
+      const uint8_t *q = p + 16 + 32 * (g >> 1) + 16 * (u & 1), *sc = p + 4;
+      for (int j = 0; j < 16; j++) W[j] = (g & 1) ? q[j] >> 4 : q[j] & 15;
+      *S = g < 4 ? sc[g] & 63 : (sc[g + 4] & 15) | ((sc[g - 4] >> 6) << 4);
+      *m = g < 4 ? sc[g + 4] & 63 : (sc[g + 4] >> 4) | ((sc[g] >> 6) << 4);
+      return;
+    }
+    case 23: {  /* IQ4_XS: of a group's 16 bytes the low halves are its first 16 weights */
+      const uint8_t *q = p + 8 + 16 * g;
+      for (int j = 0; j < 16; j++) W[j] = (int8_t)tab[SB_T_IQ4 + ((u & 1) ? q[j] >> 4 : q[j] & 15)];
+      *S = (int32_t)(((p[4 + (g >> 1)] >> (4 * (g & 1))) & 15) | (((rd16(p + 2) >> (2 * g)) & 3) << 4)) - 32;
+      return;
+    }
+    case 16: {  /* IQ2_XXS: 8 bytes a group: four grid indices, then a word of four 7-bit sign indices and s */
+      const uint8_t *q = p + 2 + 8 * g;
+      const uint32_t aux = rd32(q + 4), sh = 14 * (u & 1);
+      for (int e = 0; e < 2; e++) {
+        const uint8_t *entry = tab + q[2 * (u & 1) + e] * 8;
+        const uint32_t sg = aux >> (sh + 7 * e);
+        for (int j = 0; j < 8; j++) W[8 * e + j] = sb_minus(tab, sg, j) ? -(int32_t)entry[j] : entry[j];
+      }
+      *S = (int32_t)(2 * (aux >> 28) + 1);
+      return;
+    }
+    case 17: {  /* IQ2_XS: a 16-bit word for 8 weights: 9 bits of index, 7 of signs */
+      for (int e = 0; e < 2; e++) {
+        const uint32_t q = rd16(p + 2 + 4 * u + 2 * e);
+        const uint8_t *entry = tab + SB_T_IQ2XS + (q & 511) * 8;
+        for (int j = 0; j < 8; j++) W[8 * e + j] = sb_minus(tab, q >> 9, j) ? -(int32_t)entry[j] : entry[j];
+      }
+      *S = (int32_t)(2 * ((p[66 + g] >> (4 * (u & 1))) & 15) + 1);
+      return;
+    }
+    case 22: {  /* IQ2_S: 10-bit indices (qs, and 2 bits of qh), a byte of signs for each 8 */
+      const uint32_t hi = p[66 + g] >> (4 * (u & 1)), signs = rd16(p + 34 + 2 * u);
+      const uint32_t idx[2] = {p[2 + 2 * u] | ((hi & 3) << 8), p[3 + 2 * u] | ((hi & 12) << 6)};
+      for (int e = 0; e < 2; e++)
+        for (int j = 0; j < 8; j++) {
+          const int32_t v = tab[SB_T_IQ2S + idx[e] * 8 + j];
+          W[8 * e + j] = ((signs >> (8 * e + j)) & 1) ? -v : v;
+        }
+      *S = (int32_t)(2 * ((p[74 + g] >> (4 * (u & 1))) & 15) + 1);
+      return;
+    }
+    case 18: {  /* IQ3_XXS: a byte an index of 4 weights; a word a group: its signs and s */
+      const uint32_t aux = rd32(p + 66 + 4 * g), sh = 14 * (u & 1);
+      for (int i = 0; i < 4; i++) {
+        const uint8_t *entry = tab + SB_T_IQ3XXS + p[2 + 4 * u + i] * 4;
+        for (int j = 0; j < 4; j++) {
+          const int w = 4 * i + j;
+          W[w] = sb_minus(tab, aux >> (sh + 7 * (w >> 3)), w & 7) ? -(int32_t)entry[j] : entry[j];
+        }
+      }
+      *S = (int32_t)(2 * (aux >> 28) + 1);
+      return;
+    }
+    case 21: {  /* IQ3_S: 9-bit indices (qs and a bit of qh each), 16 bits of signs, 4-bit scales a 32 */
+      const uint32_t hi = p[66 + g] >> (4 * (u & 1)), signs = rd16(p + 74 + 2 * u);
+      for (int i = 0; i < 4; i++) {
+        const uint32_t idx = p[2 + 4 * u + i] | (((hi >> i) & 1) << 8);
+        for (int j = 0; j < 4; j++) {
+          const int w = 4 * i + j;
+          const int32_t v = tab[SB_T_IQ3S + idx * 4 + j];
+          W[w] = ((signs >> w) & 1) ? -v : v;
+        }
+      }
+      *S = (int32_t)(2 * ((p[106 + (u >> 2)] >> (4 * ((u >> 1) & 1))) & 15) + 1);
+      return;
+    }
+    case 19: {  /* IQ1_S: 11-bit indices (qs and 3 bits of the group's word), the word's top bit the shift's sign */
+      const uint32_t qh = rd16(p + 34 + 2 * g), hi = qh >> (6 * (u & 1)), down = qh >> 15;
+      const uint32_t idx[2] = {p[2 + 2 * u] | ((hi & 7) << 8), p[3 + 2 * u] | ((hi & 56) << 5)};
+      for (int e = 0; e < 2; e++)
+        for (int j = 0; j < 8; j++) {
+          const int32_t code = tab[SB_T_IQ1S + idx[e] * 8 + j];  /* 0, 1, 2 */
+          W[8 * e + j] = 8 * (code - 1) + (down ? -1 : 1);
+        }
+      *S = (int32_t)(2 * ((qh >> 12) & 7) + 1);
+      return;
+    }
+    case 29: {  /* IQ1_M: a byte of qh a unit: 3 bits of each index and the shifts' signs (bits 3 and 7) */
+      const uint32_t hq = p[32 + u];
+      const uint32_t idx[2] = {p[2 * u] | ((hq & 7) << 8), p[2 * u + 1] | ((hq & 0x70) << 4)};
+      const uint32_t down[2] = {(hq >> 3) & 1, hq >> 7};
+      for (int e = 0; e < 2; e++)
+        for (int j = 0; j < 8; j++) {
+          const int32_t code = tab[SB_T_IQ1S + idx[e] * 8 + j];
+          W[8 * e + j] = 8 * (code - 1) + (down[e] ? -1 : 1);
+        }
+      *S = (int32_t)(2 * ((rd16(p + 48 + 2 * (u >> 2)) >> (3 * (u & 3))) & 7) + 1);
+      return;
+    }
+  }
+}
+
+/* IQ1_M's d: the top four bits of its four scale words, the first word's the lowest (types.ts:283-287) */
+static float sb_whole(const uint8_t *p) {
+  const uint32_t w0 = rd16(p + 48), w1 = rd16(p + 50), w2 = rd16(p + 52), w3 = rd16(p + 54);
+  return or_half((uint16_t)((w0 >> 12) | ((w1 >> 8) & 0xf0) | ((w2 >> 4) & 0xf00) | (w3 & 0xf000)));
+}
+static float sb_F(int type, const uint8_t *p) {
+  switch (type) {
+    case 16: case 17: case 22: case 19: return or_half((uint16_t)rd16(p)) * 0.125f;
+    case 18: return or_half((uint16_t)rd16(p)) * 0.25f;
+    case 29: return sb_whole(p) * 0.125f;
+    case 10: return or_half((uint16_t)rd16(p + 80));
+    default: return or_half((uint16_t)rd16(p));
+  }
+}
+static float sb_Fm(int type, const uint8_t *p) {
+  return type == 10 ? or_half((uint16_t)rd16(p + 82)) : or_half((uint16_t)rd16(p + 2));
+}
+
+/* sums_x (token.ts:158-172): after the n / 32 scales at xs, the int16 sums of each 16 of xq, then of each 8 */
+void or_sums_x(float *xs, const int8_t *xq, int32_t n) {
+  int16_t *s16 = (int16_t *)(xs + n / 32), *s8 = s16 + n / 16;
+  for (int32_t i = 0; i < n / 16; i++) {
+    int32_t s = 0;
+    for (int j = 0; j < 16; j++) s += xq[16 * i + j];
+    s16[i] = (int16_t)s;
+  }
+  for (int32_t i = 0; i < n / 8; i++) {
+    int32_t s = 0;
+    for (int j = 0; j < 8; j++) s += xq[8 * i + j];
+    s8[i] = (int16_t)s;
+  }
+}
+
+/* matmul_sb (token.ts:130-141) on one token: out[i] for rows r0..r1 of n weights in blocks of type */
+void or_matmul_sb(float *out, const int8_t *xq, const float *xs, const uint8_t *w, const uint8_t *tab, int32_t n,
+                  int32_t r0, int32_t r1, int32_t type) {
+  const int size = or_sb_size(type), blocks = n / 256, kq = type == 10 || type == 12;
+  for (int32_t i = r0; i < r1; i++) {
+    const uint8_t *row = w + (size_t)i * blocks * size;
+    float facc[4] = {0, 0, 0, 0};
+    for (int b = 0; b < blocks; b++) {
+      const uint8_t *p = row + (size_t)b * size;
+      const int8_t *x = xq + 256 * b;
+      int32_t G[8] = {0}, M[8] = {0};
+      for (int u = 0; u < 16; u++) {
+        int32_t W[16], S, m;
+        sb_unit(type, p, u, tab, W, &S, &m);
+        int32_t d = 0, s16 = 0;
+        for (int j = 0; j < 16; j++) {
+          d += W[j] * x[16 * u + j];
+          s16 += x[16 * u + j];
+        }
+        G[u >> 1] += S * d;
+        M[u >> 1] += m * s16;
+      }
+      const float *s = xs + 8 * b, F = sb_F(type, p);
+      for (int j = 0; j < 4; j++) {
+        float part = ((float)G[j] * s[j] + (float)G[j + 4] * s[j + 4]) * F;
+        if (kq) part = part - ((float)M[j] * s[j] + (float)M[j + 4] * s[j + 4]) * sb_Fm(type, p);
+        facc[j] += part;
+      }
+    }
+    out[i] = ((facc[0] + facc[1]) + facc[2]) + facc[3];
+  }
+}
+
+/* sb_row (row.ts): a row of n weights as float32, each as the reference's reader makes it: the unit's float scale
+ * (row.ts:11-19) times W (IQ1: the grid's value plus or minus 1/8), less the block's Fm m for the K types */
+void or_sb_row(float *out, const uint8_t *w, const uint8_t *tab, int32_t n, int32_t type) {
+  const int size = or_sb_size(type);
+  for (int b = 0; b < n / 256; b++) {
+    const uint8_t *p = w + (size_t)b * size;
+    for (int u = 0; u < 16; u++) {
+      int32_t W[16], S, m;
+      sb_unit(type, p, u, tab, W, &S, &m);
+      const float s = (float)(S >> 1);
+      float scale;
+      switch (type) {
+        case 16: case 17: case 22: scale = or_half((uint16_t)rd16(p)) * (0.5f + s) * 0.25f; break;
+        case 18: scale = or_half((uint16_t)rd16(p)) * (0.5f + s) * 0.5f; break;
+        case 29: scale = sb_whole(p) * (float)S; break;
+        case 10: scale = or_half((uint16_t)rd16(p + 80)) * (float)S; break;
+        default: scale = or_half((uint16_t)rd16(p)) * (float)S;
+      }
+      for (int j = 0; j < 16; j++) {
+        float v;
+        if (type == 19 || type == 29) {  /* (8 g +- 1) / 8 = g +- 1/8, as the reader adds them */
+          const int32_t shift = ((W[j] % 8) + 8) % 8 == 1 ? 1 : -1;  /* 8 g + 1 is 1 mod 8, 8 g - 1 is 7 */
+          v = (float)((W[j] - shift) / 8) + (shift < 0 ? -0.125f : 0.125f);
+        } else {
+          v = (float)W[j];
+        }
+        float o = scale * v;
+        if (type == 10 || type == 12) o = o - sb_Fm(type, p) * (float)m;
+        out[256 * b + 16 * u + j] = o;
+      }
+    }
+  }
+}

@@ -74,6 +74,12 @@ void or_swiglu(float *out, const float *h1, const float *h3, int32_t n);        
 void or_add_inplace(float *x, const float *y, int32_t n);                                 /* activations.ts:156-158 */
 int32_t or_argmax(const float *x, int32_t n);                                             /* sample.ts:6-10 */
 void or_penalize(float *logits, const int32_t *tokens, int32_t count, float penalty, float presence); /* sample.ts:16-30 */
+int32_t or_sb_size(int32_t type);
+int32_t or_sb_tables(uint8_t *area, const uint8_t *codebooks);                          /* blocks/types.ts:294-322 */
+void or_sums_x(float *xs, const int8_t *xq, int32_t n);                                /* blocks/token.ts:158-172 */
+void or_matmul_sb(float *out, const int8_t *xq, const float *xs, const uint8_t *w, const uint8_t *tab, int32_t n,
+                  int32_t r0, int32_t r1, int32_t type);                                /* blocks/token.ts:130-141 */
+void or_sb_row(float *out, const uint8_t *w, const uint8_t *tab, int32_t n, int32_t type); /* blocks/row.ts:21-72 */
 int32_t or_sample(const float *logits, int32_t n, float temperature, float topp, double random, int32_t topk,
                   float minp);                                                          /* sample.ts:248-337 */
 void or_gate(float *out, const float *x, const float *g, int32_t n);                      /* stateful.ts:12-23 */

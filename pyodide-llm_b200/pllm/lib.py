@@ -113,6 +113,14 @@ SIGNATURES = {
     "argmax": ([U64, I32], I32),
     "penalize": ([U64, U64, I32, F32, F32], None),
     "pllm_argmax_dev": ([U64, U64, I32, U64], None),
+    "sb_tables": ([U64, U64], I32),
+    "sums_x": ([U64, U64, I32], None),
+    "matmul_sb": ([U64, U64, U64, U64, U64, I32, I32, I32, I32], None),
+    "matmul_sbr": ([U64, U64, U64, U64, U64, I32, I32, I32, I32], None),
+    "matmul_sbr_tile": ([U64, U64, U64, U64, U64, I32, I32, I32, I32, I32, I32, I32], None),
+    "matmul_sbw_tile": ([U64, U64, U64, U64, U64, I32, I32, I32, I32, I32, I32, I32, U64], None),
+    "signed_dots": ([U64, U64, U64], None),
+    "sb_row": ([U64, U64, U64, I32, I32], None),
     "sample": ([U64, I32, F32, F32, ctypes.c_double, U64, U64, I32, F32], I32),
     "pllm_sample_dev": ([U64, U64, I32, F32, F32, U64, U64, U64, I32, F32], None),
     "pllm_gemv_tp": ([U64, U64, U64, U64, F32, I32, U64, U64, I32, I32, I32, I32, I64, I32, U64, I32], None),

@@ -33,7 +33,9 @@ def test_header_declares_the_registry():
                 "matmul_q6", "matmul_q6r", "matmul_t2", "matmul_t2r", "matmul_t2r_tile", "matmul_b1", "matmul_b1r",
                 "matmul_b1r_tile", "matmul_f32", "rope", "attention", "attention_f16", "attention_capped",
                 "attention_f16_capped", "to_f16", "from_f16", "finite_f16", "rmsnorm", "swiglu", "add_inplace", "gate",
-                "convolve", "short_conv", "delta_rule", "argmax", "penalize", "sample"}
+                "convolve", "short_conv", "delta_rule", "argmax", "penalize", "sample",
+                "sb_tables", "sums_x", "matmul_sb", "matmul_sbr", "matmul_sbr_tile", "matmul_sbw_tile", "signed_dots",
+                "sb_row"}
     assert registry <= names, registry - names
 
 
@@ -62,7 +64,9 @@ def test_reference_signature_arity():
              "matmul_f32": 6, "six_sums": 3, "int8_sums": 3, "matmul_q8": 8, "interleave": 3, "matmul_t2": 9,
              "matmul_q6": 8, "quantize_x": 5, "gate": 4, "convolve": 5, "short_conv": 6, "delta_rule": 11,
              "matmul_q8r": 9, "matmul_q8r_tile": 12, "matmul_q6r": 9, "matmul_t2r": 9, "matmul_t2r_tile": 12,
-             "matmul_b1": 9, "matmul_b1r": 9, "matmul_b1r_tile": 12, "argmax": 2, "penalize": 5, "sample": 9}
+             "matmul_b1": 9, "matmul_b1r": 9, "matmul_b1r_tile": 12, "argmax": 2, "penalize": 5, "sample": 9,
+             "sb_tables": 2, "sums_x": 3, "matmul_sb": 9, "matmul_sbr": 9, "matmul_sbr_tile": 12, "matmul_sbw_tile": 13,
+             "signed_dots": 3, "sb_row": 5}
     for name, n in arity.items():
         assert len(pl.SIGNATURES[name][0]) == n, name
 

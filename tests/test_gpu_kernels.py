@@ -625,3 +625,96 @@ def test_sample_draws_the_oracles_tokens(n):
     bad[7] = np.nan
     B = dev(bad)
     assert L.sample(B.ptr, n, 1.0, 0.9, 0.5, P.ptr, I.ptr, 0, 0.0) == -1
+
+
+SB_TYPES = {"Q2_K": (10, 84, (80, 82)), "Q4_K": (12, 144, (0, 2)), "IQ2_XXS": (16, 66, (0,)), "IQ2_XS": (17, 74, (0,)),
+            "IQ3_XXS": (18, 98, (0,)), "IQ1_S": (19, 50, (0,)), "IQ3_S": (21, 110, (0,)), "IQ2_S": (22, 82, (0,)),
+            "IQ4_XS": (23, 136, (0,)), "IQ1_M": (29, 56, ())}
+
+
+def sb_blocks(rng, size, halves, count):
+    """random blocks (any bytes are blocks) with finite float16 scales of a model's size"""
+    raw = rng.integers(0, 256, (count, size), dtype=np.uint8)
+    for at in halves:
+        d = rng.uniform(0.002, 0.05, count) * np.where(rng.random(count) < 0.2, -1, 1)
+        raw[:, at:at + 2] = d.astype("<f2").view(np.uint8).reshape(count, 2)
+    if size == 56:  # IQ1_M: d in the top four bits of its four scale words
+        d = rng.uniform(0.002, 0.05, count).astype("<f2").view("<u2")
+        for k in range(4):
+            word = raw[:, 48 + 2 * k:50 + 2 * k].copy().view("<u2").reshape(-1)
+            word = (word & 0x0fff) | (((d >> (4 * k)) & 15) << 12)
+            raw[:, 48 + 2 * k:50 + 2 * k] = word.astype("<u2").view(np.uint8).reshape(count, 2)
+    return raw
+
+
+@pytest.mark.parametrize("name", list(SB_TYPES))
+def test_superblock_products(name):
+    """llama.cpp's blocks (blocks/*.ts) on the device against the oracle (pinned to the reference's reader):
+    sb_tables' bytes and sb_row's floats to the bit; sums_x to the bit; matmul_sb, matmul_sbr and the tiles (five
+    tokens, frame and os strides) within 1e-5 of the sum of |weight x activation| of each row (the blocks' float32
+    partial sums in another order; every group's integer is exact); rows r0..r1 only."""
+    import os
+    t, size, halves = SB_TYPES[name]
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "superblocks.npz"))
+    books = g["codebooks"]
+    tab_want = O.sb_tables(books)
+    tab = dev(np.zeros(O.SB_TABLES, np.uint8))
+    assert L.sb_tables(tab.ptr, dev(books).ptr) == O.SB_TABLES
+    check("sb_tables")
+    assert np.array_equal(get(tab, np.uint8), tab_want)
+    rng = np.random.default_rng(t)
+    rows, n = 37, 1536
+    w = sb_blocks(rng, size, halves, rows * n // 256).reshape(rows, -1)
+    W = dev(w)
+    out = dev(np.zeros(n, np.float32))
+    L.sb_row(out.ptr, W.ptr + 5 * w.shape[1], tab.ptr, n, t)
+    check("sb_row")
+    assert np.array_equal(get(out, np.float32).view(np.uint32), O.sb_row(w[5], tab_want, n, t).view(np.uint32))
+    widened = np.stack([O.sb_row(w[r], tab_want, n, t) for r in range(rows)]).astype(np.float64)
+    count, frame = 5, n + n // 2 + 64  # a token's activations then its xs (scales and sums), frame bytes apart
+    X = np.zeros((count, frame), np.uint8)
+    want = np.zeros((count, rows), np.float64)
+    bound = np.zeros((count, rows))
+    for k in range(count):
+        x = rng.normal(0, 1, n).astype(np.float32)
+        xq, xs = O.quantize_x(x, 0)
+        X[k, :n] = xq
+        X[k, n:n + n // 2] = O.sums_x(xs, xq.view(np.int8)).view(np.uint8)
+        a = (xq.view(np.int8).astype(np.float64).reshape(-1, 32) * xs[:, None]).reshape(-1)
+        want[k] = O.matmul_sb(xq.view(np.int8), xs, w, tab_want, n, rows, t)
+        bound[k] = 1e-5 * (np.abs(widened) * np.abs(a)).sum(axis=1)
+    XB = dev(X.reshape(-1))
+    for fn in ("matmul_sb", "matmul_sbr"):
+        o = dev(np.full(rows, -9.0, np.float32))
+        getattr(L, fn)(o.ptr, XB.ptr, XB.ptr + n, W.ptr, tab.ptr, n, 3, rows - 2, t)
+        check(fn)
+        got = get(o, np.float32)
+        assert np.all(got[:3] == -9.0) and np.all(got[rows - 2:] == -9.0)
+        assert np.all(np.abs(got[3:rows - 2] - want[0, 3:rows - 2]) <= bound[0, 3:rows - 2]), fn
+    os_ = 4 * (rows + 3)
+    for fn in ("matmul_sbr_tile", "matmul_sbw_tile"):
+        o = dev(np.zeros(count * (rows + 3), np.float32))
+        args = [o.ptr, XB.ptr, XB.ptr + n, W.ptr, tab.ptr, n, 0, rows, count, os_, frame, t]
+        getattr(L, fn)(*(args + ([0] if fn == "matmul_sbw_tile" else [])))
+        check(fn)
+        got = get(o, np.float32).reshape(count, rows + 3)[:, :rows]
+        assert np.all(np.abs(got - want) <= bound), fn
+
+
+def test_sums_x_and_signed_dots():
+    rng = np.random.default_rng(3)
+    n = 4096
+    xq = rng.integers(-127, 128, n).astype(np.int8)
+    xs = rng.random(n // 32).astype(np.float32)
+    buf = np.zeros(n // 2 // 4, np.float32)
+    buf[:n // 32] = xs
+    B, Q = dev(buf), dev(xq)
+    L.sums_x(B.ptr, Q.ptr, n)
+    check("sums_x")
+    assert np.array_equal(get(B, np.float32).view(np.uint32), O.sums_x(xs, xq).view(np.uint32))
+    a = rng.integers(-128, 128, 16).astype(np.int8)
+    b = rng.integers(-128, 128, 16).astype(np.int8)
+    out = dev(np.zeros(4, np.int32))
+    L.signed_dots(out.ptr, dev(a).ptr, dev(b).ptr)
+    check("signed_dots")
+    assert np.array_equal(get(out, np.int32), (a.astype(np.int32) * b).reshape(4, 4).sum(axis=1))

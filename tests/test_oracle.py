@@ -208,3 +208,40 @@ def test_sample_draws_the_reference_samplers_tokens():
     assert O.sample(bad, 1.0, 0.9, 0.5) == -1
     bad[7] = np.inf
     assert O.sample(bad, 1.0, 0.9, 0.5) == -1
+
+
+SB_TYPES = ["Q2_K", "Q4_K", "IQ2_XXS", "IQ2_XS", "IQ3_XXS", "IQ1_S", "IQ3_S", "IQ2_S", "IQ4_XS", "IQ1_M"]
+
+
+def test_superblock_rows_are_the_reference_readers():
+    """or_sb_row (blocks/row.ts: each weight as the reference's reader makes it) on the ten block types of
+    tests/golden/superblocks.npz equals the reference's NumPy reader (convert/superblocks.py) to the bit: the bytes'
+    layouts, the scales' order of float32 products, IQ1's shifts, the K types' minima. And or_matmul_sb (the token's
+    arithmetic, blocks/types.ts:66-83) agrees with the widened rows times the dequantized activations."""
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "superblocks.npz"))
+    tab = O.sb_tables(g["codebooks"])
+    rng = np.random.default_rng(0)
+    for name in SB_TYPES:
+        t, blocks = int(g[f"{name}/ggml"]), g[f"{name}/blocks"]
+        got = np.stack([O.sb_row(b, tab, 256, t) for b in blocks])
+        assert np.array_equal(got.view(np.uint32), g[f"{name}/weights"].view(np.uint32)), name
+        w = blocks.reshape(3, -1)  # 3 rows of 4 blocks
+        x = rng.normal(0, 1, 1024).astype(np.float32)
+        xq, xs = O.quantize_x(x, 0)
+        out = O.matmul_sb(xq.view(np.int8), xs, w, tab, 1024, 3, t)
+        a = (xq.view(np.int8).astype(np.float64).reshape(-1, 32) * xs[:, None]).reshape(-1)
+        rows = np.stack([O.sb_row(w[r], tab, 1024, t) for r in range(3)]).astype(np.float64)
+        bound = 1e-5 * (np.abs(rows) * np.abs(a)).sum(axis=1)
+        assert np.all(np.abs(out - rows @ a) <= bound), name
+
+
+def test_sums_x_is_the_sums():
+    rng = np.random.default_rng(1)
+    xq = rng.integers(-127, 128, 512).astype(np.int8)
+    xs = rng.random(16).astype(np.float32)
+    out = O.sums_x(xs, xq)
+    assert np.array_equal(out[:16], xs)
+    s16 = out[16:16 + 16].view(np.int16)
+    s8 = out[32:32 + 32].view(np.int16)
+    assert np.array_equal(s16, xq.reshape(-1, 16).astype(np.int32).sum(axis=1))
+    assert np.array_equal(s8, xq.reshape(-1, 8).astype(np.int32).sum(axis=1))
