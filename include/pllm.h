@@ -282,6 +282,11 @@ int32_t pllm_device_status(void);
 /* which decode-product kernel: 0 the bulk-copy pipeline where it applies (int8 weights, 1 or 2 tokens), 1 the
  * register-streaming kernel always; returns the previous mode */
 int32_t pllm_set_gemv_mode(int32_t mode);
+/* dynamic tiles for the bulk-copy product: each CTA takes its next tile of rows from a grid-wide count as it goes
+ * (the rows are the same, the order the CTAs take them changes nothing of a row's sum). buf: count pairs of uint32 of
+ * device memory, zero (each launch leaves its pair at zero); every launch takes the next pair, so a recorded step
+ * needs at least as many pairs as it has products. count 0: each CTA its own rows (the default). */
+void pllm_set_tile_counters(uint64_t buf, int32_t count);
 /* the shared-memory bytes the bulk-copy product's ring of stages may take (32 KB..227 KB; default 200 KB) */
 int32_t pllm_set_stage_budget(int32_t bytes);
 /* how the forward driver's float16 attention (pllm_attention_dev, pllm_attention_step) combines its parts: 1 (the

@@ -188,6 +188,13 @@ class Engine:
         B["logits"] = Buffer(s.vocab * 4)
         B["tp"] = Buffer(8).zero()      # the token and the position, read by the kernels
         B["chain"] = Buffer((c.layers + 1) * 16).zero()  # a chain's 4 arrival counts (zero between calls)
+        # PLLM_DYNAMIC=1: the decode products take their row tiles from grid-wide counts (pllm_set_tile_counters), a
+        # pair of counts for each product of a recorded step
+        self.dynamic = bool(os.environ.get("PLLM_DYNAMIC"))
+        if self.dynamic:
+            pairs = 8 * (c.layers + 2)
+            B["tiles"] = Buffer(8 * pairs).zero()
+            L.pllm_set_tile_counters(B["tiles"].ptr, pairs)
         B["bad"] = Buffer(4).zero()     # non-finite keys / values written to a float16 cache (halves.ts:35)
         B["next"] = Buffer(4)           # the greedy step's token (pllm_argmax_dev) and its scratch
         B["amx"] = Buffer(16).zero()
@@ -644,6 +651,9 @@ class Engine:
         if self.graph:
             L.pllm_graph_destroy(self.graph)
             self.graph = 0
+        if getattr(self, "dynamic", False):
+            L.pllm_sync()
+            L.pllm_set_tile_counters(0, 0)
         for b in list(self.B.values()) + [v for k, v in getattr(self, "P", {}).items() if k != "M"]:
             if b is not None:
                 b.free()

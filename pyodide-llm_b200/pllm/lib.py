@@ -93,6 +93,7 @@ SIGNATURES = {
     "pllm_device_status": ([], I32),
     "pllm_set_gemv_mode": ([I32], I32),
     "pllm_set_stage_budget": ([I32], I32),
+    "pllm_set_tile_counters": ([U64, I32], None),
     "pllm_set_attention_mode": ([I32], I32),
     "pllm_synth_f32": ([U64, I64, U64, F32, F32], None),
     "pllm_synth_q8": ([U64, U64, I64, I32, U64, F32], None),

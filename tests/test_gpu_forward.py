@@ -209,3 +209,25 @@ def test_next_token_draws_what_the_oracle_samples():
     assert steady_draws >= 6
     a.close()
     b.close()
+
+
+def test_dynamic_tiles_change_no_result(monkeypatch):
+    """The decode products with dynamic tiles (each CTA takes its next tile of rows from a grid-wide count,
+    pllm_set_tile_counters) compute what the static rows compute, to the bit (a row's sum is one warp's in the same
+    order whichever CTA takes it), graphs and eager launches both; every count is back at zero after a step."""
+    from dataclasses import replace
+    from pllm.forward import QWEN3_8B
+    cfg = replace(QWEN3_8B, layers=2, seq_len=64)
+    plain = Engine(cfg, seed=4)
+    want = [plain.forward(int(t), p) for p, t in enumerate([3, 77, 1000, 5])]
+    plain.close()
+    monkeypatch.setenv("PLLM_DYNAMIC", "1")
+    for graphs in (True, False):
+        dyn = Engine(cfg, seed=4, graphs=graphs)
+        assert dyn.dynamic
+        for p, t in enumerate([3, 77, 1000, 5]):
+            got = dyn.forward(int(t), p)
+            assert np.array_equal(got, want[p]), (graphs, p, np.abs(got - want[p]).max())
+        assert L.pllm_device_status() == 0
+        assert not dyn.B["tiles"].download(np.uint32).any()
+        dyn.close()
