@@ -256,37 +256,12 @@ void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint
                         int32_t capacity, int32_t nh, int32_t nkv, int32_t hs, int32_t half, float cap,
                         int32_t split_len, int32_t pdl);
 
-/* ---- the next kernel's first bytes into L2 while this one runs (a decode step is a fixed sequence of kernels, each
- * reading its own weights from HBM; between two of them the HBM would idle while the second one starts up).
- * A range of rows cut into `parts` near-equal shares, as the next kernel's CTAs take them (parts 0: the SM count);
- * of each share the bytes [skip, skip + first) from its first row are prefetched into L2
- * (cp.async.bulk.prefetch.L2). rows_dev: a device int32 holding the row count (the step's position: the cache rows
- * before it), or 0 for `rows`. base must be 16-byte aligned; a prefetch is a hint and changes no result. */
-typedef struct {
-  uint64_t base;
-  int64_t row_bytes;
-  int64_t rows;
-  uint64_t rows_dev;
-  int64_t skip;
-  int64_t first;
-  int32_t parts;
-  int32_t pad;
-} pllm_prefetch;
-/* up to 8 ranges for the next decode-product (bulk-copy pipeline) or attention-step launch on this host thread's
- * library state to prefetch as it runs (that launch takes them; count 0 clears them) */
-void pllm_prefetch_next(const pllm_prefetch* ranges, int32_t count);
-
 /* a bounded device-side wait (an mbarrier of the bulk-copy product) gave up since the last call: PLLM_ETIMEOUT (3),
  * else 0; reading it clears it */
 int32_t pllm_device_status(void);
 /* which decode-product kernel: 0 the bulk-copy pipeline where it applies (int8 weights, 1 or 2 tokens), 1 the
  * register-streaming kernel always; returns the previous mode */
 int32_t pllm_set_gemv_mode(int32_t mode);
-/* dynamic tiles for the bulk-copy product: each CTA takes its next tile of rows from a grid-wide count as it goes
- * (the rows are the same, the order the CTAs take them changes nothing of a row's sum). buf: count pairs of uint32 of
- * device memory, zero (each launch leaves its pair at zero); every launch takes the next pair, so a recorded step
- * needs at least as many pairs as it has products. count 0: each CTA its own rows (the default). */
-void pllm_set_tile_counters(uint64_t buf, int32_t count);
 /* the shared-memory bytes the bulk-copy product's ring of stages may take (32 KB..227 KB; default 200 KB) */
 int32_t pllm_set_stage_budget(int32_t bytes);
 /* how the forward driver's float16 attention (pllm_attention_dev, pllm_attention_step) combines its parts: 1 (the

@@ -54,7 +54,6 @@ struct Fuse {
   float eps;
   int rot;
   int* bad;             // non-finite keys or values written to a float16 cache are counted here (may be null)
-  Prefetch pf;          // the next kernel's first bytes, into L2 while this one runs (pllm_prefetch_next)
 };
 
 // tensor-core helpers (float16 caches): ldmatrix fragments and the m16n8k16 product with float32 accumulation
@@ -218,8 +217,6 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_f32_kernel(const AttArg
   const int count = pos + 1;
   const int kvh = blockIdx.x, split = blockIdx.y;
   const int nsplit = a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
-  // the next kernel's weights into L2 while this one runs (this kernel leaves most of the HBM's time idle)
-  if (FUSE && threadIdx.x == 0) prefetch_next(f.pf, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
   if (split >= nsplit) return;
   const int p0 = split * a.split_len;
   const int p1 = min(count, p0 + a.split_len);
@@ -424,10 +421,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
   const int kvh = CS ? blockIdx.y : blockIdx.x, split = CS ? 0 : blockIdx.y;
   const int rank = CS ? blockIdx.x : 0;  // the CTA's rank in its cluster
   const int nsplit = CS ? 1 : a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
-  if (split >= nsplit) {  // a slice past the position: only its share of the next kernel's prefetch
-    if (FUSE && tid == 0) prefetch_next(f.pf, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
-    return;
-  }
+  if (split >= nsplit) return;
   const int p0 = CS ? 0 : split * a.split_len, p1 = CS ? count : min(count, p0 + a.split_len);
   constexpr int TW = (CS ? CS : 1) * CH_WARPS;  // the warps the chunks are dealt to
   const int gw = rank * CH_WARPS + warp;       // this warp's turn
@@ -456,8 +450,6 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   for (int i = 0; i < ring && i < mine; i++) load_chunk(i);
-  // the next kernel's weights into L2 behind this CTA's cache reads (this kernel leaves most of the HBM's time idle)
-  if (FUSE && tid == 0) prefetch_next(f.pf, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
   for (int e = tid; e < (HP - KVM) * qst; e += CH_THREADS) {  // the padded heads' q: zero
     sqh[KVM * qst + e] = __float2half_rn(0.0f);
     sql[KVM * qst + e] = __float2half_rn(0.0f);
@@ -1400,7 +1392,6 @@ PLLM_API void pllm_attention_step(uint64_t out, uint64_t qkv, uint64_t kc, uint6
   f.eps = eps;
   f.rot = rot;
   f.bad = dptr<int>(bad);
-  f.pf = pllm_take_prefetch();
   run_attention("pllm_attention_step", a, half != 0, pdl != 0, &f);
 }
 

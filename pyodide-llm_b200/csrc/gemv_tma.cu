@@ -71,7 +71,6 @@ struct TmaPlan {
   int chunks;       // K / ks
   int stage_bytes;  // TR * ks * 1.125, 128-aligned
   int act_bytes;    // activations and their scales, 128-aligned
-  unsigned* ctr;    // dynamic tiles: [next tile, CTAs done], zero between launches; null: each CTA its own rows
 };
 
 // this CTA's rows: [lo, hi) of [r0, r1), near-equal shares
@@ -90,15 +89,13 @@ __device__ __forceinline__ int tile_rows(long long t, long long hi) {
 }
 
 template <int MT, int PRO, int EPI>
-__global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs a, const TmaPlan p, const Xchg xg,
-                                                                   const Prefetch pf) {
+__global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs a, const TmaPlan p, const Xchg xg) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages, KS = p.ks, chunks = p.chunks, K = a.K, ng = K / 32;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
   float* res = reinterpret_cast<float*>(smem + 16 * S);  // [2][TR][MT] row results (EPI_SWIGLU)
-  int* meta = reinterpret_cast<int*>(res + 2 * TR * MT);  // [S] dynamic tiles: a stage's tile (-1: none left)
-  uint8_t* act = smem + ((16 * S + 2 * TR * MT * 4 + 4 * S + 127) & ~127);
+  uint8_t* act = smem + ((16 * S + 2 * TR * MT * 4 + 127) & ~127);
   int8_t* sq = reinterpret_cast<int8_t*>(act);
   float* ss = reinterpret_cast<float*>(act + (size_t)MT * K);
   uint8_t* stage0 = act + p.act_bytes;
@@ -106,14 +103,6 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   long long lo, hi;
   cta_rows(a, lo, hi);
   const long long per_tile = EPI == EPI_SWIGLU ? TR / 2 : TR;
-  // dynamic tiles (p.ctr): every CTA takes the next tile of [r0, r1) from a grid-wide count as its producer reaches it
-  const bool dyn = p.ctr != nullptr;
-  const long long ntiles = (a.r1 - a.r0 + per_tile - 1) / per_tile;
-  if (dyn) {
-    lo = a.r0;
-    hi = a.r1;
-  }
-  __shared__ long long s_tile;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
@@ -129,27 +118,13 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
       uint64_t policy;
       asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
       long long it = 0;
-      for (long long t = lo;; t += per_tile) {
-        if (dyn) {  // the next tile of the grid's count; none left: a stage that says so
-          const long long i = (long long)atomicAdd(p.ctr, 1u);
-          if (i >= ntiles) {
-            const int slot = (int)(it % S);
-            if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
-            meta[slot] = -1;
-            mbar_arrive(&full[slot]);
-            break;
-          }
-          t = a.r0 + i * per_tile;
-        } else if (t >= hi) {
-          break;
-        }
+      for (long long t = lo; t < hi; t += per_tile) {
         const int n = tile_rows<EPI>(t, hi);
         for (int c = 0; c < chunks; c++, it++) {
           const int slot = (int)(it % S);
           const unsigned round = (unsigned)(it / S);
           if (!mbar_wait(&empty[slot], (round & 1) ^ 1)) return;
           uint8_t* w = stage0 + (size_t)slot * p.stage_bytes;
-          if (dyn) meta[slot] = (int)((t - a.r0) / per_tile);
           float* sc = reinterpret_cast<float*>(w + (size_t)TR * KS);
           const int nrows = EPI == EPI_SWIGLU ? 2 * n : n;
           mbar_expect_tx(&full[slot], (unsigned)(nrows * (KS + KS / 8)));
@@ -173,8 +148,6 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
           }
         }
       }
-      // every copy of this CTA is issued: the next kernel's first bytes into L2 behind them
-      prefetch_next(pf, blockIdx.x, gridDim.x);
     }
     return;
   }
@@ -189,19 +162,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   const int swz = (lane >> 2) & 1;  // which half of its 32 bytes a lane reads first: no bank conflicts
   long long it = 0;
   int tiles = 0;
-  for (long long t = lo;; t += per_tile, tiles++) {
-    if (dyn) {  // the tile of the next stage, read by one thread and agreed on by all (a wait that gives up: stop)
-      if (warp == 0 && lane == 0) {
-        const int slot = (int)(it % S);
-        s_tile = ok && mbar_wait(&full[slot], (unsigned)(it / S) & 1) ? (long long)meta[slot] : -2;
-      }
-      consumer_sync();
-      if (s_tile < 0) break;
-      t = a.r0 + s_tile * per_tile;
-      consumer_sync();  // every warp has read s_tile before it is written again
-    } else if (t >= hi) {
-      break;
-    }
+  for (long long t = lo; t < hi; t += per_tile, tiles++) {
     const int n = tile_rows<EPI>(t, hi);
     const bool mine = EPI == EPI_SWIGLU ? ((warp % (TR / 2)) < n) : (warp < n);
     float acc[MT];
@@ -273,13 +234,6 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
       } else {
         *o = v;
       }
-    }
-  }
-  if (dyn && threadIdx.x == 0) {  // the last CTA out sets the count back to zero for the count's next launch
-    __threadfence();
-    if (atomicAdd(p.ctr + 1, 1u) == gridDim.x - 1) {
-      atomicExch(p.ctr, 0u);
-      atomicExch(p.ctr + 1, 0u);
     }
   }
 }
@@ -457,7 +411,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_chain_kernel(const ChainA
 }
 
 template <int MT, int PRO, int EPI>
-bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl, const Xchg& xg, const Prefetch& pf) {
+bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl, const Xchg& xg) {
   auto kernel = gemv_tma_kernel<MT, PRO, EPI>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return false;
   const long long grid = gemv_tma_grid(a.r1 - a.r0, EPI);
@@ -471,7 +425,7 @@ bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl, const Xc
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a, p, xg, pf);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a, p, xg);
   if (e != cudaSuccess) {
     pllm_fail(PLLM_ECUDA, "gemv_tma launch: %s", cudaGetErrorString(e));
     return true;  // failed, but not for want of a fit: do not fall back
@@ -488,9 +442,6 @@ namespace gemvk {
 int g_tma_budget = 200 * 1024;
 // 0: the bulk-copy kernel wherever it applies; 1: the register-streaming kernel only (for comparisons)
 int g_gemv_mode = 0;
-// dynamic tiles: a pool of counts (pllm_set_tile_counters), each launch the next one of it; none: static rows
-unsigned* g_ctr_pool = nullptr;
-int g_ctr_count = 0, g_ctr_next = 0;
 
 // the device address of the status word on the current device (looked up once a device)
 int* status_word() {
@@ -522,7 +473,6 @@ int gemv_tma_grid(long long rows, int epi) {
 // The bulk-copy product for int8 weights at 1 or 2 tokens; false where it does not apply (the caller then takes the
 // register-streaming kernel).
 bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg* xg) {
-  const Prefetch pf = pllm_take_prefetch();  // this product's call takes the plan, whichever kernel runs it
   const bool tp = pro == PRO_RMS_SUM || epi == EPI_SEND;
   if (tp != (xg != nullptr)) return false;
   if (g_gemv_mode == 1 || fmt != F_Q8 || a.count < 1 || a.count > 2 || (tp && a.count != 1)) return false;
@@ -535,7 +485,7 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
   const int MT = a.count;
   p.stage_bytes = (TR * p.ks + TR * (p.ks / 32) * 4 + 127) & ~127;
   p.act_bytes = (int)((MT * (size_t)K + MT * (size_t)(K / 32) * 4 + 127) & ~127);
-  const int head = (16 * 8 + 2 * TR * MT * 4 + 4 * 8 + 127) & ~127;
+  const int head = (16 * 8 + 2 * TR * MT * 4 + 127) & ~127;
   int S = (g_tma_budget - p.act_bytes - head) / p.stage_bytes;
   if (S > 8) S = 8;
   if (S < 2) return false;
@@ -548,12 +498,8 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
     x.status = status_word();
     if (!x.status) return true;  // failed (recorded), not for want of a fit
   }
-  if (g_ctr_count > 0) {
-    p.ctr = g_ctr_pool + 2 * g_ctr_next;
-    g_ctr_next = (g_ctr_next + 1) % g_ctr_count;
-  }
 #define CASE(M, P, E) \
-  if (MT == M && pro == P && epi == E) return launch<M, P, E>(a, p, smem, pdl, x, pf);
+  if (MT == M && pro == P && epi == E) return launch<M, P, E>(a, p, smem, pdl, x);
   CASE(1, PRO_Q, EPI_STORE) CASE(1, PRO_Q, EPI_ADD) CASE(1, PRO_Q, EPI_SWIGLU)
   CASE(1, PRO_RMS, EPI_STORE) CASE(1, PRO_RMS, EPI_ADD) CASE(1, PRO_RMS, EPI_SWIGLU)
   CASE(1, PRO_QUANT, EPI_STORE) CASE(1, PRO_QUANT, EPI_ADD) CASE(1, PRO_QUANT, EPI_SWIGLU)
@@ -628,15 +574,6 @@ PLLM_API int32_t pllm_set_gemv_mode(int32_t mode) {
 
 // the bytes of shared memory the bulk-copy product's stage ring may take (default 200 KB); a smaller ring leaves
 // room on each SM for the next kernel's CTA to start streaming early. Returns the previous value.
-// dynamic tiles for the bulk-copy product: counts at buf (count pairs of uint32, zero; every launch leaves its pair at
-// zero), each launch taking the next pair (a recorded step needs a pair for each of its products); count 0: off
-PLLM_API void pllm_set_tile_counters(uint64_t buf, int32_t count) {
-  PLLM_REQUIRE(count >= 0 && (count == 0 || (buf && !(buf & 7))), "pllm_set_tile_counters: count %d", count);
-  gemvk::g_ctr_pool = count ? dptr<unsigned>(buf) : nullptr;
-  gemvk::g_ctr_count = count;
-  gemvk::g_ctr_next = 0;
-}
-
 PLLM_API int32_t pllm_set_stage_budget(int32_t bytes) {
   const int old = gemvk::g_tma_budget;
   if (bytes >= 32 * 1024 && bytes <= 227 * 1024) gemvk::g_tma_budget = bytes;

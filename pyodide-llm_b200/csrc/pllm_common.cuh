@@ -58,42 +58,6 @@ static inline unsigned cdiv(unsigned a, unsigned b) { return (a + b - 1) / b; }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
-// ---- the next kernel's first bytes into L2 (pllm_prefetch_next): ranges of rows cut into shares as the next
-// kernel's CTAs take them; of each share, bytes [skip, skip + first) from its first row
-constexpr int PF_MAX = 8;
-struct Prefetch {
-  const uint8_t* base[PF_MAX];
-  long long rowb[PF_MAX], rows[PF_MAX], skip[PF_MAX], first[PF_MAX];
-  const int* rows_dev[PF_MAX];
-  int parts[PF_MAX];
-  int n;
-};
-// the plan set by pllm_prefetch_next, handed to the launch that takes it (and cleared)
-Prefetch pllm_take_prefetch();
-
-__device__ __forceinline__ void l2_prefetch(const void* p, unsigned bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-// the shares worker, worker + workers, ... of every range (one thread calls it); each piece 16-byte aligned inside
-// its range (its start rounded down, its end rounded down), at most 64 KB a prefetch
-__device__ inline void prefetch_next(const Prefetch& p, int worker, int workers) {
-  for (int e = 0; e < p.n; e++) {
-    const long long rows = p.rows_dev[e] ? (long long)*p.rows_dev[e] : p.rows[e];
-    const int parts = p.parts[e];
-    if (rows <= 0 || parts <= 0) continue;
-    const long long per = rows / parts, rem = rows % parts;
-    for (int c = worker; c < parts; c += workers) {
-      const long long lo = c * per + (c < rem ? c : rem), hi = lo + per + (c < rem ? 1 : 0);
-      const long long end = hi * p.rowb[e];
-      long long b0 = lo * p.rowb[e] + p.skip[e], b1 = b0 + p.first[e];
-      b1 = (b1 < end ? b1 : end) & ~15ll;
-      b0 &= ~15ll;
-      for (long long b = b0; b < b1; b += 65536)
-        l2_prefetch(p.base[e] + b, (unsigned)(b1 - b < 65536 ? b1 - b : 65536));
-    }
-  }
-}
-
 // ---- float16 as the reference reads and writes it (kernels/kernel/halves.ts)
 // halves.ts:12-23: the half's 16 bits sign-extended, shifted up by 13, the copies of the sign cleared, times 2^112.
 // Exact for every finite half; an infinity reads as 65536 and a NaN is not kept.

@@ -121,37 +121,6 @@ PLLM_API void pllm_stream_destroy(uint64_t s) {
 }
 // every kernel and copy after this goes on stream s (0: the legacy default stream)
 PLLM_API void pllm_set_stream(uint64_t s) { g_stream = (cudaStream_t)(uintptr_t)s; }
-
-// ---- the prefetch plan for the next launch that takes one (a host thread's own)
-static thread_local Prefetch g_prefetch = {};
-
-PLLM_API void pllm_prefetch_next(const pllm_prefetch* ranges, int32_t count) {
-  g_prefetch = Prefetch{};
-  PLLM_REQUIRE(count >= 0 && count <= PF_MAX && (count == 0 || ranges), "pllm_prefetch_next: count %d", count);
-  for (int i = 0; i < count; i++) {
-    const pllm_prefetch& r = ranges[i];
-    PLLM_REQUIRE(r.base && !(r.base & 15) && r.row_bytes > 0 && r.rows >= 0 && r.skip >= 0 && r.first >= 0 &&
-                     r.parts >= 0,
-                 "pllm_prefetch_next: range %d", i);
-  }
-  for (int i = 0; i < count; i++) {
-    const pllm_prefetch& r = ranges[i];
-    g_prefetch.base[i] = dptr<const uint8_t>(r.base);
-    g_prefetch.rowb[i] = r.row_bytes;
-    g_prefetch.rows[i] = r.rows;
-    g_prefetch.rows_dev[i] = dptr<const int>(r.rows_dev);
-    g_prefetch.skip[i] = r.skip;
-    g_prefetch.first[i] = r.first;
-    g_prefetch.parts[i] = r.parts ? r.parts : pllm_num_sms();
-  }
-  g_prefetch.n = count;
-}
-
-Prefetch pllm_take_prefetch() {
-  const Prefetch p = g_prefetch;
-  g_prefetch = Prefetch{};
-  return p;
-}
 PLLM_API uint64_t pllm_get_stream() { return (uint64_t)(uintptr_t)g_stream; }
 PLLM_API int32_t pllm_sync() { return check(cudaStreamSynchronize(g_stream), "pllm_sync"); }
 PLLM_API int32_t pllm_device_sync() { return check(cudaDeviceSynchronize(), "pllm_device_sync"); }

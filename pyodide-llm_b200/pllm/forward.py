@@ -30,7 +30,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from .device import Buffer, Pinned, init
-from .lib import ChainStage, L, PrefetchRange, check
+from .lib import ChainStage, L, check
 from .tp import Shard
 
 F_Q8 = 0
@@ -123,11 +123,6 @@ class Engine:
     """One model's forward pass on the current device."""
 
     SPLIT = 128  # positions a slice of the split-KV attention (two tiles of 64 a CTA, double-buffered)
-    # the L2 prefetches of a decode step, megabytes of the next product's weights (kv: the layer's cache before the
-    # position, all of it or none): taken by the q/k/v product (the cache, wo), the attention (wo, then w1/w3), wo
-    # (more of w1/w3), w1/w3 (w2), w2 (the next layer's q/k/v or the classifier), the classifier (layer 0's q/k/v)
-    PREFETCH_MB = {"kv": 1, "qkv_wo": 0, "att_wo": 64, "att_w13": 32, "wo_w13": 16, "w13_w2": 16, "w2_next": 32,
-                   "cls_qkv": 32}
 
     def __init__(self, cfg, host=None, seed=0, device=0, graphs=True, pdl=True, exchange=None):
         init(device)
@@ -142,15 +137,6 @@ class Engine:
         # the separate launches (the stages' barriers and prologues outrun what the ring of weights can bridge).
         self.chained = (not exchange and bool(os.environ.get("PLLM_CHAIN")) and all(
             k % 128 == 0 for k in (cfg.dim, cfg.qdim, cfg.hidden)))
-        # the L2 prefetch of the next kernel's first bytes (pllm_prefetch_next), megabytes a boundary; PLLM_PREFETCH
-        # "name=MB,..." overrides (0 everywhere: none)
-        self.prefetch, self._sms = dict(self.PREFETCH_MB), None
-        for item in filter(None, os.environ.get("PLLM_PREFETCH", "").split(",")):
-            k, v = item.split("=")
-            if k == "all":
-                self.prefetch = {n: float(v) for n in self.prefetch}
-            else:
-                self.prefetch[k] = float(v)
         c = cfg
         self.rows_qkv = s.rows_qkv
         self.bias = 64 if c.relaxed else 0
@@ -188,13 +174,6 @@ class Engine:
         B["logits"] = Buffer(s.vocab * 4)
         B["tp"] = Buffer(8).zero()      # the token and the position, read by the kernels
         B["chain"] = Buffer((c.layers + 1) * 16).zero()  # a chain's 4 arrival counts (zero between calls)
-        # PLLM_DYNAMIC=1: the decode products take their row tiles from grid-wide counts (pllm_set_tile_counters), a
-        # pair of counts for each product of a recorded step
-        self.dynamic = bool(os.environ.get("PLLM_DYNAMIC"))
-        if self.dynamic:
-            pairs = 8 * (c.layers + 2)
-            B["tiles"] = Buffer(8 * pairs).zero()
-            L.pllm_set_tile_counters(B["tiles"].ptr, pairs)
         B["bad"] = Buffer(4).zero()     # non-finite keys / values written to a float16 cache (halves.ts:35)
         B["next"] = Buffer(4)           # the greedy step's token (pllm_argmax_dev) and its scratch
         B["amx"] = Buffer(16).zero()
@@ -301,29 +280,6 @@ class Engine:
         return {k: (np.ascontiguousarray(v) if v is not None else None) for k, v in W.items()}
 
     # ---- one step
-    def _ranges(self, wq, ws, rows, n, pair, mb, skip_mb=0.0):
-        """The prefetch ranges of a product's first `mb` megabytes of weights (and their scales), as the product's
-        CTAs take its rows (pairs of rows for the gated FFN: both halves)"""
-        if mb <= 0:
-            return []
-        if self._sms is None:
-            self._sms = L.pllm_num_sms_of_device()
-        sms = self._sms
-        halves = 2 if pair else 1
-        first = int(mb * 2**20 / (sms * halves * 1.125))
-        skip = int(skip_mb * 2**20 / (sms * halves * 1.125))
-        out = []
-        for h in range(halves):
-            out.append(PrefetchRange(base=wq + h * pair * n, row_bytes=n, rows=rows, skip=skip, first=first))
-            out.append(PrefetchRange(base=ws + h * pair * n // 8, row_bytes=n // 8, rows=rows, skip=skip // 8,
-                                     first=first // 8))
-        return [r for r in out if r.base % 16 == 0]
-
-    def _prefetch(self, *groups):
-        ranges = [r for g in groups for r in g][:8]
-        arr = (PrefetchRange * max(len(ranges), 1))(*ranges)
-        L.pllm_prefetch_next(arr, len(ranges))
-
     def _gemv(self, out, wq, ws, rows, n, x, norm, pro, epi, pair=0, pdl=True):
         c = self.cfg
         L.pllm_gemv(out, 0, 0, 0, 0, 0, x, 0, norm, c.eps, self.bias, wq, ws, F_Q8, n, 0, rows, 1, pro, epi, pair,
@@ -391,41 +347,26 @@ class Engine:
         tok, pos = B["tp"].ptr, B["tp"].ptr + 4
         E = 2 if c.half_kv else 4
         L.pllm_embed_q8(B["x"].ptr, B["emb"].ptr, B["emb_s"].ptr, tok, 0, c.dim, 1, c.dim)
-        mb = self.prefetch
-        # the products of layer l: (wq, ws, rows, K, pair)
-        qkv_of = lambda l: (B["wqkv"].ptr + l * self.rows_qkv * c.dim,  # noqa: E731
-                            B["sqkv"].ptr + l * self.rows_qkv * (c.dim // 32) * 4, self.rows_qkv, c.dim, 0)
-        wo_of = lambda l: (B["wo"].ptr + l * c.dim * c.qdim, B["so"].ptr + l * c.dim * (c.qdim // 32) * 4,  # noqa: E731
-                           c.dim, c.qdim, 0)
-        w13_of = lambda l: (B["w13"].ptr + l * 2 * c.hidden * c.dim,  # noqa: E731
-                            B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.hidden, c.dim, c.hidden)
-        w2_of = lambda l: (B["w2"].ptr + l * c.dim * c.hidden,  # noqa: E731
-                           B["s2"].ptr + l * c.dim * (c.hidden // 32) * 4, c.dim, c.hidden, 0)
-        cls = (B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim, 0)
         for l in range(c.layers):
-            wqkv, sqkv = qkv_of(l)[:2]
-            kc = B["kc"].ptr + l * c.seq_len * c.kvdim * E
-            vc = B["vc"].ptr + l * c.seq_len * c.kvdim * E
-            kv = [PrefetchRange(base=b, row_bytes=c.kvdim * E, rows_dev=pos, first=1 << 40) for b in (kc, vc)]
-            self._prefetch(kv if mb["kv"] > 0 else [], self._ranges(*wo_of(l), mb["qkv_wo"]))
+            wqkv = B["wqkv"].ptr + l * self.rows_qkv * c.dim
+            sqkv = B["sqkv"].ptr + l * self.rows_qkv * (c.dim // 32) * 4
             self._gemv(B["qkv"].ptr, wqkv, sqkv, self.rows_qkv, c.dim, B["x"].ptr, B["att_norm"].ptr + l * c.dim * 4,
                        PRO_RMS, EPI_STORE)
+            kc = B["kc"].ptr + l * c.seq_len * c.kvdim * E
+            vc = B["vc"].ptr + l * c.seq_len * c.kvdim * E
             qn = B["q_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
             kn = B["k_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
-            self._prefetch(self._ranges(*wo_of(l), mb["att_wo"]), self._ranges(*w13_of(l), mb["att_w13"]))
             L.pllm_attention_step(B["att"].ptr, B["qkv"].ptr, kc, vc, B["scratch"].ptr, pos, c.seq_len, c.heads,
                                   c.kv_heads, c.head_size, int(c.half_kv), 0.0, self.SPLIT, qn, kn, B["cos_t"].ptr,
                                   B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, int(self.pdl))
-            self._prefetch(self._ranges(*w13_of(l), mb["wo_w13"], mb["att_w13"]))
-            self._gemv(B["x"].ptr, *wo_of(l)[:2], c.dim, c.qdim, B["att"].ptr, 0, PRO_QUANT, EPI_ADD)
-            self._prefetch(self._ranges(*w2_of(l), mb["w13_w2"]))
-            self._gemv(B["hb"].ptr, *w13_of(l)[:2], c.hidden, c.dim, B["x"].ptr, B["ffn_norm"].ptr + l * c.dim * 4,
-                       PRO_RMS, EPI_SWIGLU, pair=c.hidden)
-            nxt = qkv_of(l + 1) if l + 1 < c.layers else cls if need_logits else None
-            self._prefetch(self._ranges(*nxt, mb["w2_next"]) if nxt else [])
-            self._gemv(B["x"].ptr, *w2_of(l)[:2], c.dim, c.hidden, B["hb"].ptr, 0, PRO_QUANT, EPI_ADD)
+            self._gemv(B["x"].ptr, B["wo"].ptr + l * c.dim * c.qdim, B["so"].ptr + l * c.dim * (c.qdim // 32) * 4,
+                       c.dim, c.qdim, B["att"].ptr, 0, PRO_QUANT, EPI_ADD)
+            self._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * c.hidden * c.dim,
+                       B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.hidden, c.dim, B["x"].ptr,
+                       B["ffn_norm"].ptr + l * c.dim * 4, PRO_RMS, EPI_SWIGLU, pair=c.hidden)
+            self._gemv(B["x"].ptr, B["w2"].ptr + l * c.dim * c.hidden, B["s2"].ptr + l * c.dim * (c.hidden // 32) * 4,
+                       c.dim, c.hidden, B["hb"].ptr, 0, PRO_QUANT, EPI_ADD)
         if need_logits:
-            self._prefetch(self._ranges(*qkv_of(0), mb["cls_qkv"]))
             self._gemv(B["logits"].ptr, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim, B["x"].ptr, B["final_norm"].ptr,
                        PRO_RMS, EPI_STORE)
 
@@ -651,9 +592,6 @@ class Engine:
         if self.graph:
             L.pllm_graph_destroy(self.graph)
             self.graph = 0
-        if getattr(self, "dynamic", False):
-            L.pllm_sync()
-            L.pllm_set_tile_counters(0, 0)
         for b in list(self.B.values()) + [v for k, v in getattr(self, "P", {}).items() if k != "M"]:
             if b is not None:
                 b.free()

@@ -93,7 +93,6 @@ SIGNATURES = {
     "pllm_device_status": ([], I32),
     "pllm_set_gemv_mode": ([I32], I32),
     "pllm_set_stage_budget": ([I32], I32),
-    "pllm_set_tile_counters": ([U64, I32], None),
     "pllm_set_attention_mode": ([I32], I32),
     "pllm_synth_f32": ([U64, I64, U64, F32, F32], None),
     "pllm_synth_q8": ([U64, U64, I64, I32, U64, F32], None),
@@ -110,7 +109,6 @@ SIGNATURES = {
     "pllm_tp_close": ([U64], None),
     "pllm_tp_step": ([U64], None),
     "pllm_gemv_chain": ([P, I32, U64, I32], None),
-    "pllm_prefetch_next": ([P, I32], None),
     "argmax": ([U64, I32], I32),
     "penalize": ([U64, U64, I32, F32, F32], None),
     "pllm_argmax_dev": ([U64, U64, I32, U64], None),
@@ -136,13 +134,6 @@ class ChainStage(ctypes.Structure):
     """include/pllm.h's pllm_chain_stage: one product of a pllm_gemv_chain."""
     _fields_ = [("out", U64), ("x", U64), ("norm", U64), ("wq", U64), ("ws", U64), ("pair", I64), ("n", I32),
                 ("rows", I32), ("pro", I32), ("epi", I32), ("eps", F32), ("bias", I32)]
-
-
-class PrefetchRange(ctypes.Structure):
-    """include/pllm.h's pllm_prefetch: rows cut into `parts` shares (0: the SM count) as the next kernel's CTAs take
-    them; of each share, bytes [skip, skip + first) from its first row go into L2 while the current kernel runs."""
-    _fields_ = [("base", U64), ("row_bytes", I64), ("rows", I64), ("rows_dev", U64), ("skip", I64), ("first", I64),
-                ("parts", I32), ("pad", I32)]
 
 
 class PllmError(RuntimeError):

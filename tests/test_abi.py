@@ -70,22 +70,3 @@ def test_reference_signature_arity():
     for name, n in arity.items():
         assert len(pl.SIGNATURES[name][0]) == n, name
 
-
-def test_prefetch_plan_checks_its_ranges():
-    """pllm_prefetch_next keeps a plan for the next launch and refuses ranges it could not walk safely (a base off a
-    16-byte boundary, a negative size, more than 8 ranges); the checks are on the host, no GPU call is made."""
-    import pllm.lib as pl
-    R = pl.PrefetchRange
-    ok = (R * 2)(R(base=4096, row_bytes=64, rows=10, first=128, parts=4), R(base=8192, row_bytes=32, rows_dev=64,
-                                                                            first=1 << 40, parts=2))
-    pl.L.pllm_prefetch_next(ok, 2)
-    pl.check("a plan of two ranges")
-    for bad, count in (((R * 1)(R(base=4100, row_bytes=64, rows=10, first=128, parts=4)), 1),
-                       ((R * 1)(R(base=4096, row_bytes=0, rows=10, first=128, parts=4)), 1),
-                       ((R * 1)(R(base=4096, row_bytes=64, rows=10, first=-1, parts=4)), 1),
-                       (ok, 9)):
-        pl.L.pllm_prefetch_next(bad, count)
-        with pytest.raises(pl.PllmError):
-            pl.check("a bad plan")
-    pl.L.pllm_prefetch_next(None, 0)  # clears
-    pl.check("no plan")

@@ -166,28 +166,6 @@ def test_next_token_is_the_logits_argmax():
     b.close()
 
 
-def test_prefetch_changes_no_result(monkeypatch):
-    """The L2 prefetches of the next kernel's weights and of the layer's cache (pllm_prefetch_next, taken by the
-    products and the attention step) are hints: the step with them computes what the step without them does, to the
-    bit, and no wait gives up. Large budgets here, so that every range (whole shares, the cache to the position) is
-    walked, also past the ends of short shares."""
-    from dataclasses import replace
-    from pllm.forward import QWEN3_8B
-    cfg = replace(QWEN3_8B, layers=2, seq_len=64)
-    monkeypatch.setenv("PLLM_PREFETCH", "all=0")
-    plain = Engine(cfg, seed=5)
-    monkeypatch.setenv("PLLM_PREFETCH", "all=4096")
-    fetched = Engine(cfg, seed=5)
-    assert all(v == 0 for v in plain.prefetch.values()) and all(v > 0 for v in fetched.prefetch.values())
-    for pos, tok in enumerate(np.random.default_rng(8).integers(0, cfg.vocab, 5)):
-        want = plain.forward(int(tok), pos)
-        got = fetched.forward(int(tok), pos)
-        assert np.array_equal(got, want), (pos, np.abs(got - want).max())
-    assert L.pllm_device_status() == 0
-    plain.close()
-    fetched.close()
-
-
 def test_next_token_draws_what_the_oracle_samples():
     """The drawn step (sample on the device, sample.ts:248-337: temperature, top-k, nucleus, min-p, a random number
     from the caller) draws the token the oracle's sampler draws from the logits forward() returns, wherever the
@@ -210,24 +188,3 @@ def test_next_token_draws_what_the_oracle_samples():
     a.close()
     b.close()
 
-
-def test_dynamic_tiles_change_no_result(monkeypatch):
-    """The decode products with dynamic tiles (each CTA takes its next tile of rows from a grid-wide count,
-    pllm_set_tile_counters) compute what the static rows compute, to the bit (a row's sum is one warp's in the same
-    order whichever CTA takes it), graphs and eager launches both; every count is back at zero after a step."""
-    from dataclasses import replace
-    from pllm.forward import QWEN3_8B
-    cfg = replace(QWEN3_8B, layers=2, seq_len=64)
-    plain = Engine(cfg, seed=4)
-    want = [plain.forward(int(t), p) for p, t in enumerate([3, 77, 1000, 5])]
-    plain.close()
-    monkeypatch.setenv("PLLM_DYNAMIC", "1")
-    for graphs in (True, False):
-        dyn = Engine(cfg, seed=4, graphs=graphs)
-        assert dyn.dynamic
-        for p, t in enumerate([3, 77, 1000, 5]):
-            got = dyn.forward(int(t), p)
-            assert np.array_equal(got, want[p]), (graphs, p, np.abs(got - want[p]).max())
-        assert L.pllm_device_status() == 0
-        assert not dyn.B["tiles"].download(np.uint32).any()
-        dyn.close()
