@@ -36,6 +36,7 @@ struct AttArgs {
   int nsplit;           // slices (the grid's y); with pos_dev, those past the position return
   float cap;
   int* counters;        // [nkv] slices done, zero between calls; null: a second kernel combines the slices
+  int cs;               // the chunk kernel's cluster size (its CL form), 2..CS_MAX
 };
 
 
@@ -386,15 +387,17 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_f32_kernel(const AttArg
 // halves (hi + lo: their products with a float16 key or value are exact in the accumulation, so the sum keeps them to
 // about 2^-22 of themselves). The score fragment's columns (heads 2 t4, 2 t4 + 1) are the output fragment's columns,
 // so a thread rescales its own output with its own running maxima. The warps' parts are merged at the slice's end.
-// CS > 0 (the forward driver's calls): a thread-block cluster of CS CTAs a kv head takes all of its positions, the
-// chunks dealt to the cluster's CS x CH_WARPS warps in turn (grid (CS, nkv), cluster (CS, 1, 1)); each CTA merges its
-// warps, and the CTAs' parts are combined through distributed shared memory, each CTA making 1/CS of the output (the
+// CL (the forward driver's calls): a thread-block cluster of cs CTAs a kv head takes all of its positions, the
+// chunks dealt to the cluster's cs x CH_WARPS warps in turn (grid (cs, nkv), cluster (cs, 1, 1)); each CTA merges its
+// warps, and the CTAs' parts are combined through distributed shared memory, each CTA making 1/cs of the output (the
 // cluster's CTAs run together, so they can wait for one another; no partials leave the SMs).
 constexpr int CH_WARPS = 8, CH_THREADS = 32 * CH_WARPS, CHUNK = 16;
 constexpr int HP = 8;    // heads padded to the products' n = 8
 constexpr int PST = 24;  // halves a head's row of a warp's probabilities (conflict-free fragment reads)
 
-template <int KVM, bool FUSE, int MBM, int CS>
+constexpr int CS_MAX = 16;  // the largest cluster (a non-portable size)
+
+template <int KVM, bool FUSE, int MBM, bool CL>
 __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const AttArgs a, const Fuse f, const int ring) {
   extern __shared__ __align__(16) uint8_t att_smem[];
   constexpr int DL = MBM / 2;                          // a lane's values of a head: d = lane + 32 i (hs <= 32 DL)
@@ -418,12 +421,13 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
   // the position: written by the host before the step's first kernel, so readable before the dependency wait
   const int pos = a.pos_dev ? *a.pos_dev : a.pos;
   const int count = pos + 1;
-  const int kvh = CS ? blockIdx.y : blockIdx.x, split = CS ? 0 : blockIdx.y;
-  const int rank = CS ? blockIdx.x : 0;  // the CTA's rank in its cluster
-  const int nsplit = CS ? 1 : a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
+  const int kvh = CL ? blockIdx.y : blockIdx.x, split = CL ? 0 : blockIdx.y;
+  const int rank = CL ? blockIdx.x : 0;  // the CTA's rank in its cluster
+  const int ncta = CL ? a.cs : 1;  // the cluster's CTAs
+  const int nsplit = CL ? 1 : a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
   if (split >= nsplit) return;
-  const int p0 = CS ? 0 : split * a.split_len, p1 = CS ? count : min(count, p0 + a.split_len);
-  constexpr int TW = (CS ? CS : 1) * CH_WARPS;  // the warps the chunks are dealt to
+  const int p0 = CL ? 0 : split * a.split_len, p1 = CL ? count : min(count, p0 + a.split_len);
+  const int TW = ncta * CH_WARPS;  // the warps the chunks are dealt to
   const int gw = rank * CH_WARPS + warp;       // this warp's turn
   const int nchunk = (p1 - p0 + CHUNK - 1) / CHUNK;
   const int mine = gw < nchunk ? (nchunk - 1 - gw) / TW + 1 : 0;  // chunks of this warp
@@ -454,7 +458,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
     sqh[KVM * qst + e] = __float2half_rn(0.0f);
     sql[KVM * qst + e] = __float2half_rn(0.0f);
   }
-  const bool holds_pos = FUSE && (CS ? (pos / CHUNK) % TW / CH_WARPS == rank : p1 == count);
+  const bool holds_pos = FUSE && (CL ? (pos / CHUNK) % TW / CH_WARPS == rank : p1 == count);
   // the head norms' weights and the RoPE tables' row of pos (not the previous kernel's output): read before the wait
   const int turned = f.rot > 0 && f.rot < hs ? f.rot : hs;
   float wq[DL], wk[DL], cs[DL], sn[DL];
@@ -644,7 +648,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
   }
   __syncthreads();
   // the warps' parts merged, a thread a (head, dimension) pair: the slice's output (one slice: the head's output);
-  // CS: the CTA's part, [KVM][hs] then KVM maxima and KVM sums, where q's halves were (no warp reads them now)
+  // CL: the CTA's part, [KVM][hs] then KVM maxima and KVM sums, where q's halves were (no warp reads them now)
   float* cpart = reinterpret_cast<float*>(sqh);
   for (int e = tid; e < KVM * hs; e += CH_THREADS) {
     const int j = e / hs, d = e % hs, h = hbase + j;
@@ -659,7 +663,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
       o = fmaf(reinterpret_cast<const float*>(att_smem + (size_t)w * ring * chunkb)[j * (hs + 4) + d], wt, o);
       l = fmaf(sml[(w * KVM + j) * 2 + 1], wt, l);
     }
-    if (CS) {
+    if (CL) {
       cpart[e] = o;
       if (d == 0) {
         cpart[KVM * hs + j] = mx;
@@ -679,17 +683,18 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
       }
     }
   }
-  if constexpr (CS > 0) {  // the cluster's parts combined: this CTA makes pairs [rank per, (rank + 1) per) from every CTA's part
+  if constexpr (CL) {  // the cluster's parts combined: this CTA makes pairs [rank per, (rank + 1) per) from every CTA's part
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
-    const int per = (KVM * hs + CS - 1) / CS;
+    const int per = (KVM * hs + ncta - 1) / ncta;
     const int e = rank * per + tid;
     if (tid < per && e < KVM * hs) {
       const int j = e / hs, d = e % hs;
-      float m[CS], l[CS], o[CS];
+      float m[CS_MAX], l[CS_MAX], o[CS_MAX];
 #pragma unroll
-      for (int c = 0; c < CS; c++) {  // every load in flight together
+      for (int c = 0; c < CS_MAX; c++) {  // every load in flight together
+        if (c >= ncta) break;
         const float* remote = cluster.map_shared_rank(cpart, c);
         m[c] = remote[KVM * hs + j];
         l[c] = remote[KVM * hs + KVM + j];
@@ -697,11 +702,13 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
       }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < CS; c++) mx = fmaxf(mx, m[c]);
+      for (int c = 0; c < CS_MAX; c++)
+        if (c < ncta) mx = fmaxf(mx, m[c]);
       const float base = mx == -INFINITY ? 0.0f : mx;
       float os = 0.0f, ls = 0.0f;
 #pragma unroll
-      for (int c = 0; c < CS; c++) {
+      for (int c = 0; c < CS_MAX; c++) {
+        if (c >= ncta) break;
         const float wt = expf(m[c] - base);  // 0 for a CTA without chunks
         os = fmaf(o[c], wt, os);
         ls = fmaf(l[c], wt, ls);
@@ -770,41 +777,43 @@ template <int KVM>
 cudaError_t launch_chunks(const AttArgs& a, const Fuse* f, const cudaLaunchConfig_t& cfg, int ring) {
   const Fuse none = {};
   if (a.hs <= 128) {
-    if (f) return launch_with(attention_chunk_kernel<KVM, true, 8, 0>, cfg, a, *f, ring);
-    return launch_with(attention_chunk_kernel<KVM, false, 8, 0>, cfg, a, none, ring);
+    if (f) return launch_with(attention_chunk_kernel<KVM, true, 8, false>, cfg, a, *f, ring);
+    return launch_with(attention_chunk_kernel<KVM, false, 8, false>, cfg, a, none, ring);
   }
-  if (f) return launch_with(attention_chunk_kernel<KVM, true, 16, 0>, cfg, a, *f, ring);
-  return launch_with(attention_chunk_kernel<KVM, false, 16, 0>, cfg, a, none, ring);
+  if (f) return launch_with(attention_chunk_kernel<KVM, true, 16, false>, cfg, a, *f, ring);
+  return launch_with(attention_chunk_kernel<KVM, false, 16, false>, cfg, a, none, ring);
 }
 
-// One cluster size's launch (grid (CS, nkv), cluster (CS, 1, 1)), or (fits non-null) the number of such clusters
+// One cluster size's launch (grid (cs, nkv), cluster (cs, 1, 1)), or (fits non-null) the number of such clusters
 // the device can hold at once.
-template <int CS, int KVM, bool FUSE, int MBM>
-cudaError_t launch_cluster_cs(const AttArgs& a, const Fuse& f, const cudaLaunchConfig_t& base, int ring, int* fits) {
-  auto k = attention_chunk_kernel<KVM, FUSE, MBM, CS>;
+template <int KVM, bool FUSE, int MBM>
+cudaError_t launch_cluster_cs(AttArgs a, const Fuse& f, const cudaLaunchConfig_t& base, int ring, int cs, int* fits) {
+  auto k = attention_chunk_kernel<KVM, FUSE, MBM, true>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)base.dynamicSmemBytes);
-  if (e == cudaSuccess && CS > 8) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess && cs > 8) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = base;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CS;
+  attr[0].val.clusterDim.x = (unsigned)cs;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1] = base.numAttrs ? base.attrs[0] : attr[0];  // the dependent-launch attribute, where asked for
-  cfg.gridDim = dim3(CS, a.nkv);
+  cfg.gridDim = dim3((unsigned)cs, a.nkv);
   cfg.attrs = attr;
   cfg.numAttrs = 1 + (base.numAttrs ? 1 : 0);
   if (fits) {
     cfg.numAttrs = 1;
     return cudaOccupancyMaxActiveClusters(fits, k, &cfg);
   }
+  a.cs = cs;
   return cudaLaunchKernelEx(&cfg, k, a, f, ring);
 }
 
-// The cluster size for a configuration: 16 (a non-portable size) where the device holds all nkv such clusters at
-// once, else 8 where it holds one, else 0 (the slices' kernel). Found once a configuration (kernel, shared memory,
-// nkv) and device, before its first launch.
+// The cluster size for a configuration: the largest of 16 (a non-portable size) down to 8 CTAs of which the device
+// holds all nkv clusters at once (the most warps to deal the chunks to, with no cluster waiting for another's SMs:
+// on the B200s measured 10, where 16 and 12 held only 7 clusters), else 8 where it holds one, else 0 (the slices'
+// kernel). Found once a configuration (kernel, shared memory, nkv) and device, before its first launch.
 template <int KVM, bool FUSE, int MBM>
 cudaError_t launch_cluster(const AttArgs& a, const Fuse& f, const cudaLaunchConfig_t& cfg, int ring, bool* launched) {
   struct Choice {
@@ -822,16 +831,17 @@ cudaError_t launch_cluster(const AttArgs& a, const Fuse& f, const cudaLaunchConf
     if (cache[i].dev == dev && cache[i].nkv == a.nkv && cache[i].hs == a.hs && cache[i].smem == cfg.dynamicSmemBytes)
       cs = cache[i].cs;
   if (cs < 0) {
-    int n16 = 0, n8 = 0;
-    if (launch_cluster_cs<16, KVM, FUSE, MBM>(a, f, cfg, ring, &n16) != cudaSuccess) n16 = 0;
-    if (launch_cluster_cs<8, KVM, FUSE, MBM>(a, f, cfg, ring, &n8) != cudaSuccess) n8 = 0;
+    cs = 0;
+    for (int c = CS_MAX; c >= 8 && !cs; c--) {
+      int n = 0;
+      if (launch_cluster_cs<KVM, FUSE, MBM>(a, f, cfg, ring, c, &n) != cudaSuccess) n = 0;
+      if (n >= a.nkv || (c == 8 && n >= 1)) cs = c;
+    }
     cudaGetLastError();  // a refused query leaves no error behind: the choice falls back
-    cs = n16 >= a.nkv ? 16 : n8 >= 1 ? 8 : 0;
     if (used < 64) cache[used++] = Choice{dev, a.nkv, a.hs, cfg.dynamicSmemBytes, cs};
   }
   *launched = cs != 0;
-  if (cs == 16) return launch_cluster_cs<16, KVM, FUSE, MBM>(a, f, cfg, ring, nullptr);
-  if (cs == 8) return launch_cluster_cs<8, KVM, FUSE, MBM>(a, f, cfg, ring, nullptr);
+  if (cs) return launch_cluster_cs<KVM, FUSE, MBM>(a, f, cfg, ring, cs, nullptr);
   return cudaSuccess;
 }
 
