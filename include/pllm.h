@@ -262,7 +262,7 @@ int32_t pllm_device_status(void);
 /* which decode-product kernel: 0 the bulk-copy pipeline where it applies (int8 weights, 1 or 2 tokens), 1 the
  * register-streaming kernel always; returns the previous mode */
 int32_t pllm_set_gemv_mode(int32_t mode);
-/* the shared-memory bytes the bulk-copy product's ring of stages may take (32 KB..227 KB; default 200 KB) */
+/* the shared-memory bytes the bulk-copy product's ring of stages may take (32 KB..227 KB; default 180 KB) */
 int32_t pllm_set_stage_budget(int32_t bytes);
 /* how the forward driver's float16 attention (pllm_attention_dev, pllm_attention_step) combines its parts: 1 (the
  * default) one thread-block cluster a kv head over the whole cache, combined in distributed shared memory; 0 slices

@@ -12,8 +12,9 @@
 // activations. Every wait on an mbarrier is bounded: past the bound the kernel records PLLM_ETIMEOUT in the device
 // status word and returns (the host reads it with pllm_device_status).
 //
-// A stage holds TR rows x KS columns (KS = K, or K cut into equal chunks of at most 8192): rows whole are one
-// contiguous copy of TR x K bytes (and one of TR x K/32 scales); rows cut into chunks are a copy a row.
+// A stage holds TR = 8 rows x KS columns (KS = K, or K cut into equal chunks of at most 8192): rows whole are one
+// contiguous copy of 8 x K bytes (and one of 8 x K/32 scales); rows cut into chunks are a copy a row. Consumer warp w
+// takes row w of every stage (for one token of rows of at most 4096, a lane's activation groups held in registers).
 #include "gemv_common.cuh"
 
 __device__ int g_pllm_status = 0;  // a bounded wait gave up (PLLM_ETIMEOUT), read by pllm_device_status
@@ -23,7 +24,8 @@ namespace {
 using namespace gemvk;
 
 constexpr int NC = 8;                 // consumer warps
-constexpr int TR = NC;                // row slots a stage
+constexpr int TR = NC;                // row slots a stage (a row a consumer warp)
+constexpr int TRP = TR;               // the product kernel's stage rows (the chain's are TR too)
 constexpr int TMA_THREADS = (NC + 1) * 32;
 constexpr long long WAIT_BOUND = 1ll << 26;  // polls of an mbarrier before giving up (seconds: never in a run that works)
 
@@ -71,6 +73,7 @@ struct TmaPlan {
   int chunks;       // K / ks
   int stage_bytes;  // TR * ks * 1.125, 128-aligned
   int act_bytes;    // activations and their scales, 128-aligned
+  int gate_bytes;   // EPI_SWIGLU: a CTA's w1 results (its pairs x MT floats)
 };
 
 // this CTA's rows: [lo, hi) of [r0, r1), near-equal shares
@@ -81,11 +84,19 @@ __device__ __forceinline__ void cta_rows(const GemvArgs& a, long long& lo, long 
   hi = lo + base + (c < rem ? 1 : 0);
 }
 
-// the rows of a tile: slots [0, n) (EPI_SWIGLU: pairs [0, n) in slots [0, n) and [TR/2, TR/2 + n))
-template <int EPI>
-__device__ __forceinline__ int tile_rows(long long t, long long hi) {
-  const long long per = EPI == EPI_SWIGLU ? TR / 2 : TR;
-  return (int)min(per, hi - t);
+// a group of 32 of one row (its two 16-byte halves at w, read in the lane's order: no bank conflicts) against the
+// activations' halves read in the same order: the group's integer (the same sum in any order)
+__device__ __forceinline__ int group_dot(const uint8_t* w, int swz, const int4 xa, const int4 xb) {
+  const int4 wa = *reinterpret_cast<const int4*>(w + 16 * swz);
+  const int4 wb = *reinterpret_cast<const int4*>(w + 16 * (swz ^ 1));
+  int g0 = __dp4a(wa.x, xa.x, 0), g1 = __dp4a(wb.x, xb.x, 0);
+  g0 = __dp4a(wa.y, xa.y, g0);
+  g1 = __dp4a(wb.y, xb.y, g1);
+  g0 = __dp4a(wa.z, xa.z, g0);
+  g1 = __dp4a(wb.z, xb.z, g1);
+  g0 = __dp4a(wa.w, xa.w, g0);
+  g1 = __dp4a(wb.w, xb.w, g1);
+  return g0 + g1;
 }
 
 template <int MT, int PRO, int EPI>
@@ -94,15 +105,17 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   const int S = p.stages, KS = p.ks, chunks = p.chunks, K = a.K, ng = K / 32;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
-  float* res = reinterpret_cast<float*>(smem + 16 * S);  // [2][TR][MT] row results (EPI_SWIGLU)
-  uint8_t* act = smem + ((16 * S + 2 * TR * MT * 4 + 127) & ~127);
+  float* gate = reinterpret_cast<float*>(smem + 16 * S);  // EPI_SWIGLU: [pairs of this CTA][MT] the w1 rows' results
+  uint8_t* act = smem + ((16 * S + p.gate_bytes + 127) & ~127);
   int8_t* sq = reinterpret_cast<int8_t*>(act);
   float* ss = reinterpret_cast<float*>(act + (size_t)MT * K);
   uint8_t* stage0 = act + p.act_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   long long lo, hi;
   cta_rows(a, lo, hi);
-  const long long per_tile = EPI == EPI_SWIGLU ? TR / 2 : TR;
+  // EPI_SWIGLU: the CTA's rows of w1 (pairs [lo, hi)) a tile after another, then the same rows of w3 (at + pair): each
+  // tile TRP rows in a row, and warp w of w3's tile k finishes the pair whose w1 row it made in tile k
+  constexpr int PHASES = EPI == EPI_SWIGLU ? 2 : 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
@@ -118,36 +131,32 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
       uint64_t policy;
       asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
       long long it = 0;
-      for (long long t = lo; t < hi; t += per_tile) {
-        const int n = tile_rows<EPI>(t, hi);
-        for (int c = 0; c < chunks; c++, it++) {
-          const int slot = (int)(it % S);
-          const unsigned round = (unsigned)(it / S);
-          if (!mbar_wait(&empty[slot], (round & 1) ^ 1)) return;
-          uint8_t* w = stage0 + (size_t)slot * p.stage_bytes;
-          float* sc = reinterpret_cast<float*>(w + (size_t)TR * KS);
-          const int nrows = EPI == EPI_SWIGLU ? 2 * n : n;
-          mbar_expect_tx(&full[slot], (unsigned)(nrows * (KS + KS / 8)));
-          const int halves = EPI == EPI_SWIGLU ? 2 : 1;
-          for (int h = 0; h < halves; h++) {
-            const long long row0 = t + (h ? a.pair : 0);
-            const int slot0 = h ? TR / 2 : 0;
+      for (int ph = 0; ph < PHASES; ph++)
+        for (long long t = lo; t < hi; t += TRP) {
+          const int n = (int)min((long long)TRP, hi - t);
+          const long long row0 = t + (ph ? a.pair : 0);
+          for (int c = 0; c < chunks; c++, it++) {
+            const int slot = (int)(it % S);
+            const unsigned round = (unsigned)(it / S);
+            if (!mbar_wait(&empty[slot], (round & 1) ^ 1)) return;
+            uint8_t* w = stage0 + (size_t)slot * p.stage_bytes;
+            float* sc = reinterpret_cast<float*>(w + (size_t)TRP * KS);
+            mbar_expect_tx(&full[slot], (unsigned)(n * (KS + KS / 8)));
             if (chunks == 1) {
-              bulk_copy(w + (size_t)slot0 * KS, a.wq + row0 * K, (unsigned)(n * K), &full[slot], policy);
-              bulk_copy(sc + (size_t)slot0 * (KS / 32), reinterpret_cast<const float*>(a.ws) + row0 * ng,
-                        (unsigned)(n * ng * 4), &full[slot], policy);
+              bulk_copy(w, a.wq + row0 * K, (unsigned)(n * K), &full[slot], policy);
+              bulk_copy(sc, reinterpret_cast<const float*>(a.ws) + row0 * ng, (unsigned)(n * ng * 4), &full[slot],
+                        policy);
             } else {
               for (int r = 0; r < n; r++) {
-                bulk_copy(w + (size_t)(slot0 + r) * KS, a.wq + (row0 + r) * K + (long long)c * KS, (unsigned)KS,
-                          &full[slot], policy);
-                bulk_copy(sc + (size_t)(slot0 + r) * (KS / 32),
+                bulk_copy(w + (size_t)r * KS, a.wq + (row0 + r) * K + (long long)c * KS, (unsigned)KS, &full[slot],
+                          policy);
+                bulk_copy(sc + (size_t)r * (KS / 32),
                           reinterpret_cast<const float*>(a.ws) + (row0 + r) * ng + (long long)c * (KS / 32),
                           (unsigned)(KS / 8), &full[slot], policy);
               }
             }
           }
         }
-      }
     }
     return;
   }
@@ -160,82 +169,95 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   pdl_launch_dependents();
   bool ok = true;
   const int swz = (lane >> 2) & 1;  // which half of its 32 bytes a lane reads first: no bank conflicts
+  // one token and rows of at most 32 x RG groups in one chunk: a lane's activation groups (the same for every row) and
+  // their scales held in registers, so that a row's shared-memory reads are its weights only
+  constexpr int RG = 4;
+  const bool reg = MT == 1 && chunks == 1 && KS / 32 <= 32 * RG;
+  int4 ra[RG], rb[RG];
+  float rx[RG];
+#pragma unroll
+  for (int k = 0; k < RG; k++) {
+    const int u = lane + 32 * k;
+    ra[k] = rb[k] = make_int4(0, 0, 0, 0);
+    rx[k] = 0.0f;
+    if (reg && u < KS / 32) {
+      ra[k] = *reinterpret_cast<const int4*>(sq + (size_t)u * 32 + 16 * swz);
+      rb[k] = *reinterpret_cast<const int4*>(sq + (size_t)u * 32 + 16 * (swz ^ 1));
+      rx[k] = ss[u];
+    }
+  }
   long long it = 0;
-  int tiles = 0;
-  for (long long t = lo; t < hi; t += per_tile, tiles++) {
-    const int n = tile_rows<EPI>(t, hi);
-    const bool mine = EPI == EPI_SWIGLU ? ((warp % (TR / 2)) < n) : (warp < n);
-    float acc[MT];
+  for (int ph = 0; ph < PHASES; ph++)
+    for (long long t = lo; t < hi; t += TRP) {
+      const int n = (int)min((long long)TRP, hi - t);
+      const bool mine = warp < n;
+      float acc[MT];
 #pragma unroll
-    for (int m = 0; m < MT; m++) acc[m] = 0.0f;
-    for (int c = 0; c < chunks; c++, it++) {
-      const int slot = (int)(it % S);
-      const unsigned round = (unsigned)(it / S);
-      if (ok) ok = mbar_wait(&full[slot], round & 1);
-      if (mine && ok) {
-        const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * KS;
-        const float* sc = reinterpret_cast<const float*>(stage0 + (size_t)slot * p.stage_bytes + (size_t)TR * KS) +
-                          (size_t)warp * (KS / 32);
-        const int u0 = c * (KS / 32);
-        for (int u = lane; u < KS / 32; u += 32) {
-          const int4 wa = *reinterpret_cast<const int4*>(w + u * 32 + 16 * swz);
-          const int4 wb = *reinterpret_cast<const int4*>(w + u * 32 + 16 * (swz ^ 1));
-          const uint32_t wv[8] = {(uint32_t)(swz ? wb.x : wa.x), (uint32_t)(swz ? wb.y : wa.y),
-                                  (uint32_t)(swz ? wb.z : wa.z), (uint32_t)(swz ? wb.w : wa.w),
-                                  (uint32_t)(swz ? wa.x : wb.x), (uint32_t)(swz ? wa.y : wb.y),
-                                  (uint32_t)(swz ? wa.z : wb.z), (uint32_t)(swz ? wa.w : wb.w)};
-          const float s = sc[u];
+      for (int m = 0; m < MT; m++) acc[m] = 0.0f;
+      for (int c = 0; c < chunks; c++, it++) {
+        const int slot = (int)(it % S);
+        const unsigned round = (unsigned)(it / S);
+        if (ok) ok = mbar_wait(&full[slot], round & 1);
+        if (mine && ok) {
+          const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * KS;
+          const float* sc = reinterpret_cast<const float*>(stage0 + (size_t)slot * p.stage_bytes + (size_t)TRP * KS) +
+                            (size_t)warp * (KS / 32);
+          const int u0 = c * (KS / 32);
+          // the groups in the order u = lane, lane + 32, ...
+          if (MT == 1 && reg) {
 #pragma unroll
-          for (int m = 0; m < MT; m++) {
-            const int8_t* x = sq + (size_t)m * K + (size_t)(u0 + u) * 32;
-            const int4 xa = *reinterpret_cast<const int4*>(x + 16 * swz);
-            const int4 xb = *reinterpret_cast<const int4*>(x + 16 * (swz ^ 1));
-            const int G = dot32_words(wv, swz ? xb : xa, swz ? xa : xb);
-            acc[m] = fmaf((float)G, __fmul_rn(s, ss[m * ng + u0 + u]), acc[m]);
+            for (int k = 0; k < RG; k++) {
+              const int u = lane + 32 * k;
+              if (u >= KS / 32) break;
+              const int G = group_dot(w + u * 32, swz, ra[k], rb[k]);
+              acc[0] = fmaf((float)G, __fmul_rn(sc[u], rx[k]), acc[0]);
+            }
+          } else {
+            for (int u = lane; u < KS / 32; u += 32) {
+              const float s = sc[u];
+#pragma unroll
+              for (int m = 0; m < MT; m++) {
+                const int8_t* x = sq + (size_t)m * K + (size_t)(u0 + u) * 32;
+                const int4 xa = *reinterpret_cast<const int4*>(x + 16 * swz);
+                const int4 xb = *reinterpret_cast<const int4*>(x + 16 * (swz ^ 1));
+                const int G = group_dot(w + u * 32, swz, xa, xb);
+                acc[m] = fmaf((float)G, __fmul_rn(s, ss[m * ng + u0 + u]), acc[m]);
+              }
+            }
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
-    }
-    if (!mine) {
-      if (EPI == EPI_SWIGLU) consumer_sync();
-      continue;
-    }
+      if (!mine) continue;
 #pragma unroll
-    for (int m = 0; m < MT; m++) acc[m] = warp_sum(acc[m]);
-    if (EPI == EPI_SWIGLU) {
-      float* r = res + (tiles & 1) * TR * MT;
-      if (lane == 0)
-#pragma unroll
-        for (int m = 0; m < MT; m++) r[warp * MT + m] = acc[m];
-      consumer_sync();
-      if (warp < TR / 2 && lane < MT && lane < a.count) {
-        float h1 = r[warp * MT], h3 = r[(warp + TR / 2) * MT];
-#pragma unroll
-        for (int m = 1; m < MT; m++)
-          if (lane == m) {
-            h1 = r[warp * MT + m];
-            h3 = r[(warp + TR / 2) * MT + m];
-          }
-        a.out[lane * a.out_stride + t + warp] = (h1 / (1.0f + expf(-h1))) * h3;
-      }
-    } else if (lane < MT && lane < a.count) {
+      for (int m = 0; m < MT; m++) acc[m] = warp_sum(acc[m]);
+      if (lane >= MT || lane >= a.count) continue;
       float v = acc[0];
 #pragma unroll
       for (int m = 1; m < MT; m++)
         if (lane == m) v = acc[m];
-      float* o = a.out + lane * a.out_stride + t + warp;
-      if (EPI == EPI_SEND) {
-        const unsigned mark = xchg_mark(xg);
-        for (int r = 0; r < xg.world; r++) st_slot(xg.dst[r] + t + warp, v, mark);
-      } else if (EPI == EPI_ADD) {
-        *o += v;
+      const long long row = t + warp;
+      if (EPI == EPI_SWIGLU) {
+        float* g = gate + (size_t)(row - lo) * MT + lane;
+        if (ph == 0) {
+          *g = v;  // this warp's own slot: the same warp (and lane) reads it in the w3 phase
+        } else {
+          const float h1 = *g;
+          a.out[lane * a.out_stride + row] = (h1 / (1.0f + expf(-h1))) * v;
+        }
       } else {
-        *o = v;
+        float* o = a.out + lane * a.out_stride + row;
+        if (EPI == EPI_SEND) {
+          const unsigned mark = xchg_mark(xg);
+          for (int r = 0; r < xg.world; r++) st_slot(xg.dst[r] + row, v, mark);
+        } else if (EPI == EPI_ADD) {
+          *o += v;
+        } else {
+          *o = v;
+        }
       }
     }
-  }
 }
 
 // ---- a chain of products in one persistent launch (one CTA an SM, every SM): the producer warp streams the
@@ -364,15 +386,17 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_chain_kernel(const ChainA
           for (int u = lane; u < KS / 32; u += 32) {
             const int4 wa = *reinterpret_cast<const int4*>(w + u * 32 + 16 * swz);
             const int4 wb = *reinterpret_cast<const int4*>(w + u * 32 + 16 * (swz ^ 1));
-            const uint32_t wv[8] = {(uint32_t)(swz ? wb.x : wa.x), (uint32_t)(swz ? wb.y : wa.y),
-                                    (uint32_t)(swz ? wb.z : wa.z), (uint32_t)(swz ? wb.w : wa.w),
-                                    (uint32_t)(swz ? wa.x : wb.x), (uint32_t)(swz ? wa.y : wb.y),
-                                    (uint32_t)(swz ? wa.z : wb.z), (uint32_t)(swz ? wa.w : wb.w)};
             const int8_t* x = sq + (size_t)(u0 + u) * 32;
             const int4 xa = *reinterpret_cast<const int4*>(x + 16 * swz);
             const int4 xb = *reinterpret_cast<const int4*>(x + 16 * (swz ^ 1));
-            const int G = dot32_words(wv, swz ? xb : xa, swz ? xa : xb);
-            acc = fmaf((float)G, __fmul_rn(sc[u], ss[u0 + u]), acc);
+            int g0 = __dp4a(wa.x, xa.x, 0), g1 = __dp4a(wb.x, xb.x, 0);  // paired as read: the same integer
+            g0 = __dp4a(wa.y, xa.y, g0);
+            g1 = __dp4a(wb.y, xb.y, g1);
+            g0 = __dp4a(wa.z, xa.z, g0);
+            g1 = __dp4a(wb.z, xb.z, g1);
+            g0 = __dp4a(wa.w, xa.w, g0);
+            g1 = __dp4a(wb.w, xb.w, g1);
+            acc = fmaf((float)(g0 + g1), __fmul_rn(sc[u], ss[u0 + u]), acc);
           }
         }
         __syncwarp();
@@ -438,8 +462,8 @@ bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl, const Xc
 namespace gemvk {
 
 // the stage budget: a stage ring of about this many bytes (a smaller one leaves room on the SM for the next
-// kernel's CTA)
-int g_tma_budget = 200 * 1024;
+// kernel's CTA); the default takes what one CTA may have
+int g_tma_budget = 180 * 1024;  // (measured best of 160..226 KB on the Qwen3-8B step)
 // 0: the bulk-copy kernel wherever it applies; 1: the register-streaming kernel only (for comparisons)
 int g_gemv_mode = 0;
 
@@ -464,8 +488,8 @@ int* status_word() {
 }
 
 int gemv_tma_grid(long long rows, int epi) {
-  const long long per_tile = epi == EPI_SWIGLU ? TR / 2 : TR;
-  const long long tiles = (rows + per_tile - 1) / per_tile;
+  (void)epi;  // a tile is TRP rows of one matrix in every form (EPI_SWIGLU: of w1, then of w3)
+  const long long tiles = (rows + TRP - 1) / TRP;
   const long long sms = pllm_num_sms();
   return (int)(tiles < sms ? tiles : sms);
 }
@@ -483,9 +507,15 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
   while (K % (p.chunks * 128)) p.chunks++;
   p.ks = K / p.chunks;
   const int MT = a.count;
-  p.stage_bytes = (TR * p.ks + TR * (p.ks / 32) * 4 + 127) & ~127;
+  p.stage_bytes = (TRP * p.ks + TRP * (p.ks / 32) * 4 + 127) & ~127;
   p.act_bytes = (int)((MT * (size_t)K + MT * (size_t)(K / 32) * 4 + 127) & ~127);
-  const int head = (16 * 8 + 2 * TR * MT * 4 + 127) & ~127;
+  if (epi == EPI_SWIGLU) {  // the w1 results of a CTA's pairs, held until its w3 rows come
+    const long long grid = gemv_tma_grid(a.r1 - a.r0, epi);
+    const long long pairs = (a.r1 - a.r0 + grid - 1) / grid;
+    if (pairs * MT * 4 > 32 * 1024) return false;
+    p.gate_bytes = (int)(pairs * MT * 4);
+  }
+  const int head = (16 * 8 + p.gate_bytes + 127) & ~127;
   int S = (g_tma_budget - p.act_bytes - head) / p.stage_bytes;
   if (S > 8) S = 8;
   if (S < 2) return false;
