@@ -51,7 +51,19 @@ def kernel_case(which):
     init(0)
     L.pllm_set_stream(0)
     bufs = []
-    if which == "gemm":
+    if which == "gemv":  # the decode step's w1/w3 product (rows 2 x 12288, K 4096: 113 MB > L2), RMSNorm and SwiGLU
+        from pllm.forward import F_Q8
+        hidden, K = 12288, 4096
+        w, ws = Buffer(2 * hidden * K), Buffer(2 * hidden * K // 8)
+        x, norm, out = Buffer(K * 4), Buffer(K * 4), Buffer(hidden * 4)
+        bufs += [w, ws, x, norm, out]
+        L.pllm_synth_q8(w.ptr, ws.ptr, 2 * hidden, K, 1, 0.02)
+        L.pllm_synth_f32(x.ptr, K, 2, 0.0, 1.0)
+        L.pllm_synth_f32(norm.ptr, K, 3, 1.0, 0.1)
+        for _ in range(3):
+            L.pllm_gemv(out.ptr, 0, 0, 0, 0, 0, x.ptr, 0, norm.ptr, 1e-6, 0, w.ptr, ws.ptr, F_Q8, K, 0, hidden, 1, 1, 2,
+                        hidden, 0)
+    elif which == "gemm":
         M, N, K = 512, 4096, 4096
         xq, xs, w, ws, wt, out = (Buffer(n) for n in (M * K, M * K // 8, N * K, N * K // 8, N * K // 8, M * N * 4))
         bufs += [xq, xs, w, ws, wt, out]
@@ -266,7 +278,7 @@ def main():
     ap.add_argument("--no-micro", action="store_true", help="profiling only: skip the per-kernel timings")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: the same shapes with fewer layers (a small case for ncu captures)")
-    ap.add_argument("--kernel", choices=["gemm", "attention"],
+    ap.add_argument("--kernel", choices=["gemm", "attention", "gemv"],
                     help="profiling only: three launches of one kernel's small case (for ncu), then exit")
     args = ap.parse_args()
 
