@@ -257,7 +257,7 @@ void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint
                         int32_t split_len, int32_t pdl);
 
 /* a bounded device-side wait (an mbarrier of the bulk-copy product) gave up since the last call: PLLM_ETIMEOUT (3),
- * else 0; reading it clears it */
+ * else 0; reading it clears it (and, after a wait that gave up, puts the products' tile counters back to zero) */
 int32_t pllm_device_status(void);
 /* which decode-product kernel: 0 the bulk-copy pipeline where it applies (int8 weights, 1 or 2 tokens), 1 the
  * register-streaming kernel always; returns the previous mode */

@@ -296,7 +296,7 @@ struct ChainStage {
   int ks, chunks;
 };
 bool gemv_chain(const ChainStage* st, int n, unsigned* counters, bool pdl);
-// the CTAs gemv_tma launches for rows r0..r1 (EPI_SEND's producers: their count is what a PRO_RMS_SUM waits for)
+// the CTAs gemv_tma launches for rows r0..r1 (one an SM at most: the tiles of 8 rows are dealt among them)
 int gemv_tma_grid(long long rows, int epi);
 extern int g_gemv_mode;
 extern int g_tma_budget;

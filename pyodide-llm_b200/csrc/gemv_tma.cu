@@ -15,9 +15,22 @@
 // A stage holds TR = 8 rows x KS columns (KS = K, or K cut into equal chunks of at most 8192): rows whole are one
 // contiguous copy of 8 x K bytes (and one of 8 x K/32 scales); rows cut into chunks are a copy a row. Consumer warp w
 // takes row w of every stage (for one token of rows of at most 4096, a lane's activation groups held in registers).
+//
+// The rows are dealt as tiles of 8 from a ticket counter, not as fixed shares: each CTA's producer takes the next
+// tile's ticket while the current tile streams, so the CTAs that start early (on SMs the kernel ahead leaves first)
+// stream more of the matrix and none waits at the end for a late one's fixed share. A tile is all its stages in a row
+// (EPI_SWIGLU: its w1 rows, then the same rows of w3; K cut into chunks: a stage a chunk), and the producer writes the
+// tile's number into the stage's header before the copies' barrier completes, so a consumer warp reads it after its
+// wait, with no barrier among the consumers. Every CTA's producer takes exactly one ticket past the tiles; the one
+// that takes the last of those (tiles + grid - 1) sets the counter back to zero for the launch that next uses it.
 #include "gemv_common.cuh"
 
 __device__ int g_pllm_status = 0;  // a bounded wait gave up (PLLM_ETIMEOUT), read by pllm_device_status
+
+// the launches' ticket counters: a launch takes the next of them in turn (host side), so two launches share one only
+// TICKET_SLOTS launches apart on a device, long after the first has finished
+constexpr int TICKET_SLOTS = 1024;
+__device__ unsigned g_tickets[TICKET_SLOTS];
 
 namespace {
 
@@ -25,7 +38,7 @@ using namespace gemvk;
 
 constexpr int NC = 8;                 // consumer warps
 constexpr int TR = NC;                // row slots a stage (a row a consumer warp)
-constexpr int TRP = TR;               // the product kernel's stage rows (the chain's are TR too)
+constexpr int TRP = TR;               // the product kernel's tile rows (the chain's are TR too)
 constexpr int TMA_THREADS = (NC + 1) * 32;
 constexpr long long WAIT_BOUND = 1ll << 26;  // polls of an mbarrier before giving up (seconds: never in a run that works)
 
@@ -73,7 +86,7 @@ struct TmaPlan {
   int chunks;       // K / ks
   int stage_bytes;  // TR * ks * 1.125, 128-aligned
   int act_bytes;    // activations and their scales, 128-aligned
-  int gate_bytes;   // EPI_SWIGLU: a CTA's w1 results (its pairs x MT floats)
+  int slot;         // this launch's ticket counter (g_tickets)
 };
 
 // this CTA's rows: [lo, hi) of [r0, r1), near-equal shares
@@ -105,17 +118,16 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   const int S = p.stages, KS = p.ks, chunks = p.chunks, K = a.K, ng = K / 32;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
-  float* gate = reinterpret_cast<float*>(smem + 16 * S);  // EPI_SWIGLU: [pairs of this CTA][MT] the w1 rows' results
-  uint8_t* act = smem + ((16 * S + p.gate_bytes + 127) & ~127);
+  int* hdr = reinterpret_cast<int*>(smem + 16 * S);  // [S] the tile a stage holds, -1: no more tiles
+  uint8_t* act = smem + ((20 * S + 127) & ~127);
   int8_t* sq = reinterpret_cast<int8_t*>(act);
   float* ss = reinterpret_cast<float*>(act + (size_t)MT * K);
   uint8_t* stage0 = act + p.act_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  long long lo, hi;
-  cta_rows(a, lo, hi);
-  // EPI_SWIGLU: the CTA's rows of w1 (pairs [lo, hi)) a tile after another, then the same rows of w3 (at + pair): each
-  // tile TRP rows in a row, and warp w of w3's tile k finishes the pair whose w1 row it made in tile k
+  // EPI_SWIGLU: a tile's w1 rows, then the same rows of w3 (at + pair); warp w makes row w of both, so the w1 result
+  // waits in a register
   constexpr int PHASES = EPI == EPI_SWIGLU ? 2 : 1;
+  const int per_tile = PHASES * chunks;  // stages a tile
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
@@ -130,17 +142,24 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
     if (lane == 0) {
       uint64_t policy;
       asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+      const unsigned tiles = (unsigned)((a.r1 - a.r0 + TRP - 1) / TRP);
+      unsigned* ticket = g_tickets + p.slot;
+      unsigned next = atomicAdd(ticket, 1u);
       long long it = 0;
-      for (int ph = 0; ph < PHASES; ph++)
-        for (long long t = lo; t < hi; t += TRP) {
-          const int n = (int)min((long long)TRP, hi - t);
+      for (;;) {
+        const unsigned tile = next;
+        if (tile >= tiles) break;
+        next = atomicAdd(ticket, 1u);  // the following tile's ticket, on its way while this tile streams
+        const long long t = a.r0 + (long long)tile * TRP;
+        const int n = (int)min((long long)TRP, a.r1 - t);
+        for (int ph = 0; ph < PHASES; ph++) {
           const long long row0 = t + (ph ? a.pair : 0);
           for (int c = 0; c < chunks; c++, it++) {
             const int slot = (int)(it % S);
-            const unsigned round = (unsigned)(it / S);
-            if (!mbar_wait(&empty[slot], (round & 1) ^ 1)) return;
+            if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
             uint8_t* w = stage0 + (size_t)slot * p.stage_bytes;
             float* sc = reinterpret_cast<float*>(w + (size_t)TRP * KS);
+            hdr[slot] = (int)tile;  // seen by the consumers once the stage's barrier completes (its arrive releases)
             mbar_expect_tx(&full[slot], (unsigned)(n * (KS + KS / 8)));
             if (chunks == 1) {
               bulk_copy(w, a.wq + row0 * K, (unsigned)(n * K), &full[slot], policy);
@@ -157,17 +176,22 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
             }
           }
         }
+      }
+      // the end: a stage without rows
+      const int slot = (int)(it % S);
+      if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
+      hdr[slot] = -1;
+      mbar_arrive(&full[slot]);
+      if (next == tiles + gridDim.x - 1) atomicExch(ticket, 0u);  // the last ticket of the launch
     }
     return;
   }
 
-  // ---- the consumers (a wait that gives up makes the warp skip its work from then on, but it still meets every
-  // barrier of the consumers, so that none of them waits for it)
+  // ---- the consumers (a wait that gives up ends the warp: there is no barrier among the consumers past the prologue)
   pdl_wait();
   load_activations<F_Q8, MT, PRO, ConsumerSync>(a, sq, ss, nullptr, &xg);
   consumer_sync();
   pdl_launch_dependents();
-  bool ok = true;
   const int swz = (lane >> 2) & 1;  // which half of its 32 bytes a lane reads first: no bank conflicts
   // one token and rows of at most 32 x RG groups in one chunk: a lane's activation groups (the same for every row) and
   // their scales held in registers, so that a row's shared-memory reads are its weights only
@@ -186,66 +210,64 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
       rx[k] = ss[u];
     }
   }
+  float h1 = 0.0f;  // EPI_SWIGLU: this lane's w1 result of the tile's row
   long long it = 0;
-  for (int ph = 0; ph < PHASES; ph++)
-    for (long long t = lo; t < hi; t += TRP) {
-      const int n = (int)min((long long)TRP, hi - t);
-      const bool mine = warp < n;
-      float acc[MT];
+  for (;;) {
+    float acc[MT];
 #pragma unroll
-      for (int m = 0; m < MT; m++) acc[m] = 0.0f;
-      for (int c = 0; c < chunks; c++, it++) {
-        const int slot = (int)(it % S);
-        const unsigned round = (unsigned)(it / S);
-        if (ok) ok = mbar_wait(&full[slot], round & 1);
-        if (mine && ok) {
-          const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * KS;
-          const float* sc = reinterpret_cast<const float*>(stage0 + (size_t)slot * p.stage_bytes + (size_t)TRP * KS) +
-                            (size_t)warp * (KS / 32);
-          const int u0 = c * (KS / 32);
-          // the groups in the order u = lane, lane + 32, ...
-          if (MT == 1 && reg) {
+    for (int m = 0; m < MT; m++) acc[m] = 0.0f;
+    for (int k = 0; k < per_tile; k++, it++) {
+      const int slot = (int)(it % S);
+      if (!mbar_wait(&full[slot], (unsigned)(it / S) & 1)) return;
+      const int tile = hdr[slot];
+      if (tile < 0) return;  // no more tiles (only ever the first stage of a tile)
+      const int c = k % chunks, ph = k / chunks;
+      const long long row = a.r0 + (long long)tile * TRP + warp;
+      const bool mine = row < a.r1;
+      if (mine) {
+        const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * KS;
+        const float* sc = reinterpret_cast<const float*>(stage0 + (size_t)slot * p.stage_bytes + (size_t)TRP * KS) +
+                          (size_t)warp * (KS / 32);
+        const int u0 = c * (KS / 32);
+        // the groups in the order u = lane, lane + 32, ...
+        if (MT == 1 && reg) {
 #pragma unroll
-            for (int k = 0; k < RG; k++) {
-              const int u = lane + 32 * k;
-              if (u >= KS / 32) break;
-              const int G = group_dot(w + u * 32, swz, ra[k], rb[k]);
-              acc[0] = fmaf((float)G, __fmul_rn(sc[u], rx[k]), acc[0]);
-            }
-          } else {
-            for (int u = lane; u < KS / 32; u += 32) {
-              const float s = sc[u];
+          for (int k2 = 0; k2 < RG; k2++) {
+            const int u = lane + 32 * k2;
+            if (u >= KS / 32) break;
+            const int G = group_dot(w + u * 32, swz, ra[k2], rb[k2]);
+            acc[0] = fmaf((float)G, __fmul_rn(sc[u], rx[k2]), acc[0]);
+          }
+        } else {
+          for (int u = lane; u < KS / 32; u += 32) {
+            const float s = sc[u];
 #pragma unroll
-              for (int m = 0; m < MT; m++) {
-                const int8_t* x = sq + (size_t)m * K + (size_t)(u0 + u) * 32;
-                const int4 xa = *reinterpret_cast<const int4*>(x + 16 * swz);
-                const int4 xb = *reinterpret_cast<const int4*>(x + 16 * (swz ^ 1));
-                const int G = group_dot(w + u * 32, swz, xa, xb);
-                acc[m] = fmaf((float)G, __fmul_rn(s, ss[m * ng + u0 + u]), acc[m]);
-              }
+            for (int m = 0; m < MT; m++) {
+              const int8_t* x = sq + (size_t)m * K + (size_t)(u0 + u) * 32;
+              const int4 xa = *reinterpret_cast<const int4*>(x + 16 * swz);
+              const int4 xb = *reinterpret_cast<const int4*>(x + 16 * (swz ^ 1));
+              const int G = group_dot(w + u * 32, swz, xa, xb);
+              acc[m] = fmaf((float)G, __fmul_rn(s, ss[m * ng + u0 + u]), acc[m]);
             }
           }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
       }
-      if (!mine) continue;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (c != chunks - 1 || !mine) continue;
+      // the row of this phase is done
 #pragma unroll
       for (int m = 0; m < MT; m++) acc[m] = warp_sum(acc[m]);
-      if (lane >= MT || lane >= a.count) continue;
       float v = acc[0];
 #pragma unroll
       for (int m = 1; m < MT; m++)
         if (lane == m) v = acc[m];
-      const long long row = t + warp;
+#pragma unroll
+      for (int m = 0; m < MT; m++) acc[m] = 0.0f;
+      if (lane >= MT || lane >= a.count) continue;
       if (EPI == EPI_SWIGLU) {
-        float* g = gate + (size_t)(row - lo) * MT + lane;
-        if (ph == 0) {
-          *g = v;  // this warp's own slot: the same warp (and lane) reads it in the w3 phase
-        } else {
-          const float h1 = *g;
-          a.out[lane * a.out_stride + row] = (h1 / (1.0f + expf(-h1))) * v;
-        }
+        if (ph == 0) h1 = v;
+        else a.out[lane * a.out_stride + row] = (h1 / (1.0f + expf(-h1))) * v;
       } else {
         float* o = a.out + lane * a.out_stride + row;
         if (EPI == EPI_SEND) {
@@ -258,6 +280,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
         }
       }
     }
+  }
 }
 
 // ---- a chain of products in one persistent launch (one CTA an SM, every SM): the producer warp streams the
@@ -509,13 +532,7 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
   const int MT = a.count;
   p.stage_bytes = (TRP * p.ks + TRP * (p.ks / 32) * 4 + 127) & ~127;
   p.act_bytes = (int)((MT * (size_t)K + MT * (size_t)(K / 32) * 4 + 127) & ~127);
-  if (epi == EPI_SWIGLU) {  // the w1 results of a CTA's pairs, held until its w3 rows come
-    const long long grid = gemv_tma_grid(a.r1 - a.r0, epi);
-    const long long pairs = (a.r1 - a.r0 + grid - 1) / grid;
-    if (pairs * MT * 4 > 32 * 1024) return false;
-    p.gate_bytes = (int)(pairs * MT * 4);
-  }
-  const int head = (16 * 8 + p.gate_bytes + 127) & ~127;
+  const int head = (20 * 8 + 127) & ~127;  // the barriers and headers of up to 8 stages
   int S = (g_tma_budget - p.act_bytes - head) / p.stage_bytes;
   if (S > 8) S = 8;
   if (S < 2) return false;
@@ -528,6 +545,10 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
     x.status = status_word();
     if (!x.status) return true;  // failed (recorded), not for want of a fit
   }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  static unsigned next_slot[64] = {0};  // a device's launches take its ticket counters in turn
+  p.slot = (int)(next_slot[dev]++ % TICKET_SLOTS);
 #define CASE(M, P, E) \
   if (MT == M && pro == P && epi == E) return launch<M, P, E>(a, p, smem, pdl, x);
   CASE(1, PRO_Q, EPI_STORE) CASE(1, PRO_Q, EPI_ADD) CASE(1, PRO_Q, EPI_SWIGLU)
@@ -590,7 +611,12 @@ bool gemv_chain(const ChainStage* st, int n, unsigned* counters, bool pdl) {
 PLLM_API int32_t pllm_device_status() {
   int v = 0, zero = 0;
   cudaMemcpyFromSymbol(&v, g_pllm_status, sizeof v);
-  if (v) cudaMemcpyToSymbol(g_pllm_status, &zero, sizeof zero);
+  if (v) {
+    cudaMemcpyToSymbol(g_pllm_status, &zero, sizeof zero);
+    // a product that gave up may not have put its ticket counter back to zero: every counter starts over
+    static const unsigned zeros[TICKET_SLOTS] = {0};
+    cudaMemcpyToSymbol(g_tickets, zeros, sizeof zeros);
+  }
   return v;
 }
 
@@ -602,7 +628,7 @@ PLLM_API int32_t pllm_set_gemv_mode(int32_t mode) {
   return old;
 }
 
-// the bytes of shared memory the bulk-copy product's stage ring may take (default 200 KB); a smaller ring leaves
+// the bytes of shared memory the bulk-copy product's stage ring may take (default 180 KB); a smaller ring leaves
 // room on each SM for the next kernel's CTA to start streaming early. Returns the previous value.
 PLLM_API int32_t pllm_set_stage_budget(int32_t bytes) {
   const int old = gemvk::g_tma_budget;
