@@ -20,9 +20,11 @@
 // tile's ticket while the current tile streams, so the CTAs that start early (on SMs the kernel ahead leaves first)
 // stream more of the matrix and none waits at the end for a late one's fixed share. A tile is all its stages in a row
 // (EPI_SWIGLU: its w1 rows, then the same rows of w3; K cut into chunks: a stage a chunk), and the producer writes the
-// tile's number into the stage's header before the copies' barrier completes, so a consumer warp reads it after its
-// wait, with no barrier among the consumers. Every CTA's producer takes exactly one ticket past the tiles; the one
-// that takes the last of those (tiles + grid - 1) sets the counter back to zero for the launch that next uses it.
+// tile's first row and row count into the stage's header before the copies' barrier completes, so a consumer warp
+// reads it after its wait, with no barrier among the consumers. Every CTA's producer takes exactly one ticket past the
+// tiles; the one that takes the last of those (tiles + grid - 1) sets the counter back to zero for the launch that
+// next uses it. Rows cut into chunks (K > 8192) keep fixed shares: their tiles are two stages or more, and the last
+// tile dealt ends the launch later than even shares do (measured at K = 12288).
 #include "gemv_common.cuh"
 
 __device__ int g_pllm_status = 0;  // a bounded wait gave up (PLLM_ETIMEOUT), read by pllm_device_status
@@ -87,6 +89,7 @@ struct TmaPlan {
   int stage_bytes;  // TR * ks * 1.125, 128-aligned
   int act_bytes;    // activations and their scales, 128-aligned
   int slot;         // this launch's ticket counter (g_tickets)
+  int tickets;      // 1: tiles dealt by tickets; 0: each CTA its own share of the rows (rows cut into chunks)
 };
 
 // this CTA's rows: [lo, hi) of [r0, r1), near-equal shares
@@ -118,7 +121,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   const int S = p.stages, KS = p.ks, chunks = p.chunks, K = a.K, ng = K / 32;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
-  int* hdr = reinterpret_cast<int*>(smem + 16 * S);  // [S] the tile a stage holds, -1: no more tiles
+  int* hdr = reinterpret_cast<int*>(smem + 16 * S);  // [S] a stage's tile: its first row from r0 x 16 + its rows; -1: the end
   uint8_t* act = smem + ((20 * S + 127) & ~127);
   int8_t* sq = reinterpret_cast<int8_t*>(act);
   float* ss = reinterpret_cast<float*>(act + (size_t)MT * K);
@@ -144,14 +147,22 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
       asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
       const unsigned tiles = (unsigned)((a.r1 - a.r0 + TRP - 1) / TRP);
       unsigned* ticket = g_tickets + p.slot;
-      unsigned next = atomicAdd(ticket, 1u);
+      long long lo = a.r0, hi = a.r1;  // the rows this CTA streams: all of them by tickets, or its own share
+      if (!p.tickets) cta_rows(a, lo, hi);
+      unsigned next = p.tickets ? atomicAdd(ticket, 1u) : 0u;
       long long it = 0;
-      for (;;) {
-        const unsigned tile = next;
-        if (tile >= tiles) break;
-        next = atomicAdd(ticket, 1u);  // the following tile's ticket, on its way while this tile streams
-        const long long t = a.r0 + (long long)tile * TRP;
-        const int n = (int)min((long long)TRP, a.r1 - t);
+      for (long long ts = lo;;) {
+        long long t;
+        if (p.tickets) {
+          if (next >= tiles) break;
+          t = a.r0 + (long long)next * TRP;
+          next = atomicAdd(ticket, 1u);  // the following tile's ticket, on its way while this tile streams
+        } else {
+          if (ts >= hi) break;
+          t = ts;
+          ts += TRP;
+        }
+        const int n = (int)min((long long)TRP, hi - t);
         for (int ph = 0; ph < PHASES; ph++) {
           const long long row0 = t + (ph ? a.pair : 0);
           for (int c = 0; c < chunks; c++, it++) {
@@ -159,7 +170,9 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
             if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
             uint8_t* w = stage0 + (size_t)slot * p.stage_bytes;
             float* sc = reinterpret_cast<float*>(w + (size_t)TRP * KS);
-            hdr[slot] = (int)tile;  // seen by the consumers once the stage's barrier completes (its arrive releases)
+            // the tile's first row (from r0) and its rows, seen by the consumers once the stage's barrier completes
+            // (the expect_tx arrive releases it)
+            hdr[slot] = (int)(((t - a.r0) << 4) | n);
             mbar_expect_tx(&full[slot], (unsigned)(n * (KS + KS / 8)));
             if (chunks == 1) {
               bulk_copy(w, a.wq + row0 * K, (unsigned)(n * K), &full[slot], policy);
@@ -182,7 +195,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
       if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
       hdr[slot] = -1;
       mbar_arrive(&full[slot]);
-      if (next == tiles + gridDim.x - 1) atomicExch(ticket, 0u);  // the last ticket of the launch
+      if (p.tickets && next == tiles + gridDim.x - 1) atomicExch(ticket, 0u);  // the last ticket of the launch
     }
     return;
   }
@@ -222,8 +235,8 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
       const int tile = hdr[slot];
       if (tile < 0) return;  // no more tiles (only ever the first stage of a tile)
       const int c = k % chunks, ph = k / chunks;
-      const long long row = a.r0 + (long long)tile * TRP + warp;
-      const bool mine = row < a.r1;
+      const long long row = a.r0 + (tile >> 4) + warp;
+      const bool mine = warp < (tile & 15);
       if (mine) {
         const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * KS;
         const float* sc = reinterpret_cast<const float*>(stage0 + (size_t)slot * p.stage_bytes + (size_t)TRP * KS) +
@@ -549,6 +562,8 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
   static unsigned next_slot[64] = {0};  // a device's launches take its ticket counters in turn
   p.slot = (int)(next_slot[dev]++ % TICKET_SLOTS);
+  // rows cut into chunks make tiles of two stages or more, the last of which ends the launch late: fixed shares there
+  p.tickets = p.chunks == 1;
 #define CASE(M, P, E) \
   if (MT == M && pro == P && epi == E) return launch<M, P, E>(a, p, smem, pdl, x);
   CASE(1, PRO_Q, EPI_STORE) CASE(1, PRO_Q, EPI_ADD) CASE(1, PRO_Q, EPI_SWIGLU)
