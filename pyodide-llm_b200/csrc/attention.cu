@@ -416,7 +416,12 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
   uint16_t* sx = reinterpret_cast<uint16_t*>(sql + HP * qst + CH_WARPS * 2 * HP * PST);  // [2][hs] new key, value
   float* sml = reinterpret_cast<float*>(sx + 2 * hs);  // [CH_WARPS][KVM][2] the warps' maxima and sums
   float* sw = sml + CH_WARPS * KVM * 2;                // [KVM][nsplit] the combine's weights
+  // CL: [ncta][per + 2 KVM] the cluster's parts of the (head, dimension) pairs this CTA makes (outputs, then maxima
+  // and sums), stored by the other CTAs
+  float* rcv = sw;
   __shared__ float sL[KVM];
+  // CL: this CTA has started (other CTAs store into its shared memory only once every CTA of the cluster has)
+  if constexpr (CL) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   pdl_launch_dependents();  // the next kernel waits for this one's completion; its CTAs may take the SMs this one leaves
   // the position: written by the host before the step's first kernel, so readable before the dependency wait
   const int pos = a.pos_dev ? *a.pos_dev : a.pos;
@@ -648,8 +653,11 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
   }
   __syncthreads();
   // the warps' parts merged, a thread a (head, dimension) pair: the slice's output (one slice: the head's output);
-  // CL: the CTA's part, [KVM][hs] then KVM maxima and KVM sums, where q's halves were (no warp reads them now)
-  float* cpart = reinterpret_cast<float*>(sqh);
+  // CL: the CTA's part of pair e stored into the receive buffer of the CTA that makes e (slot: this CTA's rank), the
+  // part's maxima and sums into every CTA's
+  namespace cg = cooperative_groups;
+  const int per = CL ? (KVM * hs + ncta - 1) / ncta : 1, RS = per + 2 * KVM;  // CL: the pairs a CTA makes; a slot
+  if constexpr (CL) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA has started
   for (int e = tid; e < KVM * hs; e += CH_THREADS) {
     const int j = e / hs, d = e % hs, h = hbase + j;
     float mx = -INFINITY;
@@ -664,11 +672,15 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
       l = fmaf(sml[(w * KVM + j) * 2 + 1], wt, l);
     }
     if (CL) {
-      cpart[e] = o;
-      if (d == 0) {
-        cpart[KVM * hs + j] = mx;
-        cpart[KVM * hs + KVM + j] = l;
-      }
+      cg::cluster_group cluster = cg::this_cluster();
+      const int c = e / per;
+      cluster.map_shared_rank(rcv, c)[rank * RS + e - c * per] = o;
+      if (d == 0)
+        for (int c2 = 0; c2 < ncta; c2++) {
+          float* dst = cluster.map_shared_rank(rcv, c2) + rank * RS + per;
+          dst[j] = mx;
+          dst[KVM + j] = l;
+        }
       continue;
     }
     if (h < a.h0 || h >= a.h1) continue;
@@ -683,22 +695,21 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
       }
     }
   }
-  if constexpr (CL) {  // the cluster's parts combined: this CTA makes pairs [rank per, (rank + 1) per) from every CTA's part
-    namespace cg = cooperative_groups;
+  if constexpr (CL) {  // the cluster's parts combined: this CTA makes pairs [rank per, (rank + 1) per), each CTA's part
+    // in its receive buffer (no CTA reads another's shared memory after the barrier, so none waits to leave)
     cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    const int per = (KVM * hs + ncta - 1) / ncta;
+    cluster.sync();  // every part stored (release / acquire)
     const int e = rank * per + tid;
     if (tid < per && e < KVM * hs) {
       const int j = e / hs, d = e % hs;
       float m[CS_MAX], l[CS_MAX], o[CS_MAX];
 #pragma unroll
-      for (int c = 0; c < CS_MAX; c++) {  // every load in flight together
+      for (int c = 0; c < CS_MAX; c++) {
         if (c >= ncta) break;
-        const float* remote = cluster.map_shared_rank(cpart, c);
-        m[c] = remote[KVM * hs + j];
-        l[c] = remote[KVM * hs + KVM + j];
-        o[c] = remote[e];
+        const float* src = rcv + c * RS;
+        m[c] = src[per + j];
+        l[c] = src[per + KVM + j];
+        o[c] = src[tid];
       }
       float mx = -INFINITY;
 #pragma unroll
@@ -715,7 +726,6 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
       }
       a.out[(long long)(hbase + j) * hs + d] = os / ls;
     }
-    cluster.sync();  // no CTA leaves while another reads its shared memory
     return;
   }
   if (nsplit == 1 || !a.counters) return;
@@ -875,7 +885,9 @@ void run_attention(const char* name, AttArgs a, bool half, bool pdl, const Fuse*
     if (a.pos_dev && a.h0 == 0 && a.h1 == a.nh && g_cluster_attention) {
       // the whole cache a cluster: two ring slots a warp (hs <= 128), no partials
       const int ring = a.hs <= 128 ? 2 : 1;
-      const cudaLaunchConfig_t cfg = launch_config(grid, CH_THREADS, smem_of(ring, 0), pdl, attr);
+      // the receive buffer: at most kvm hs outputs + CS_MAX x (1 + 2 kvm) floats over the cluster's slots
+      const size_t rcv = ((size_t)kvm * a.hs + (size_t)CS_MAX * (1 + 2 * kvm)) * 4;
+      const cudaLaunchConfig_t cfg = launch_config(grid, CH_THREADS, smem_of(ring, 0) + rcv, pdl, attr);
       bool launched = false;
       switch (kvm) {
         case 1: e = launch_clusters<1>(a, f, cfg, ring, &launched); break;
