@@ -113,7 +113,7 @@ __device__ __forceinline__ void combine_slices(const AttArgs& a, int kvh, int ns
   const int row = hs + 4;  // floats a slice's partial (16-byte rows)
   const int room = (int)(stage_bytes / ((size_t)KVM * row * 4));
   float* stage = reinterpret_cast<float*>(stage_mem);
-  constexpr int PMAX = KVM * 256 / THREADS;  // (head, dimension) pairs a thread (hs <= 256)
+  constexpr int PMAX = (KVM * 256 + THREADS - 1) / THREADS;  // (head, dimension) pairs a thread (hs <= 256)
   float o[PMAX];
 #pragma unroll
   for (int k = 0; k < PMAX; k++) o[k] = 0.0f;
@@ -377,8 +377,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_f32_kernel(const AttArg
 }
 
 // ---- float16 caches
-// grid (nkv, nsplit), CH_WARPS warps. A CTA takes one kv head's slice of positions for its KVM query heads; the slice
-// is cut into chunks of 16 positions dealt to the warps in turn (warp w: chunks w, w + CH_WARPS, ...). Each warp copies
+// grid (nkv, nsplit), W warps (CH_WARPS; the clusters' form CL_WARPS where hs <= 128). A CTA takes one kv head's slice
+// of positions for its KVM query heads; the slice is cut into chunks of 16 positions dealt to the warps in turn (warp
+// w: chunks w, w + W, ...). Each warp copies
 // its chunks' keys and values into its own ring in shared memory (asynchronous 16-byte copies, the first ones issued
 // before the dependency wait: the cache rows before this token's are not the previous kernel's output) and keeps its
 // own online softmax (a running max and sum a head) and output over them, with no barrier shared with other warps:
@@ -388,17 +389,18 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_f32_kernel(const AttArg
 // about 2^-22 of themselves). The score fragment's columns (heads 2 t4, 2 t4 + 1) are the output fragment's columns,
 // so a thread rescales its own output with its own running maxima. The warps' parts are merged at the slice's end.
 // CL (the forward driver's calls): a thread-block cluster of cs CTAs a kv head takes all of its positions, the
-// chunks dealt to the cluster's cs x CH_WARPS warps in turn (grid (cs, nkv), cluster (cs, 1, 1)); each CTA merges its
+// chunks dealt to the cluster's cs x W warps in turn (grid (cs, nkv), cluster (cs, 1, 1)); each CTA merges its
 // warps, and the CTAs' parts are combined through distributed shared memory, each CTA making 1/cs of the output (the
 // cluster's CTAs run together, so they can wait for one another; no partials leave the SMs).
 constexpr int CH_WARPS = 8, CH_THREADS = 32 * CH_WARPS, CHUNK = 16;
+constexpr int CL_WARPS = 16;  // the clusters' warps a CTA (hs <= 128)
 constexpr int HP = 8;    // heads padded to the products' n = 8
 constexpr int PST = 24;  // halves a head's row of a warp's probabilities (conflict-free fragment reads)
 
 constexpr int CS_MAX = 16;  // the largest cluster (a non-portable size)
 
-template <int KVM, bool FUSE, int MBM, bool CL>
-__global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const AttArgs a, const Fuse f, const int ring) {
+template <int KVM, bool FUSE, int MBM, bool CL, int W>
+__global__ void __launch_bounds__(32 * W, 1) attention_chunk_kernel(const AttArgs a, const Fuse f, const int ring) {
   extern __shared__ __align__(16) uint8_t att_smem[];
   constexpr int DL = MBM / 2;                          // a lane's values of a head: d = lane + 32 i (hs <= 32 DL)
   const int hs = a.hs, nmb = hs / 16;
@@ -409,13 +411,13 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
   const int g = lane >> 2, t4 = lane & 3;              // an mma fragment's row group and column pair
   const int j0 = 2 * t4, j1 = 2 * t4 + 1;              // this thread's two head columns
   uint8_t* myring = att_smem + (size_t)warp * ring * chunkb;
-  __half* sqh = reinterpret_cast<__half*>(att_smem + (size_t)CH_WARPS * ring * chunkb);  // [HP][qst] high halves
+  __half* sqh = reinterpret_cast<__half*>(att_smem + (size_t)W * ring * chunkb);  // [HP][qst] high halves
   __half* sql = sqh + HP * qst;                                                          // and low halves
   __half* sph = sql + HP * qst + warp * 2 * HP * PST;  // this warp's probabilities [HP][PST]: high, then low halves
   __half* spl = sph + HP * PST;
-  uint16_t* sx = reinterpret_cast<uint16_t*>(sql + HP * qst + CH_WARPS * 2 * HP * PST);  // [2][hs] new key, value
-  float* sml = reinterpret_cast<float*>(sx + 2 * hs);  // [CH_WARPS][KVM][2] the warps' maxima and sums
-  float* sw = sml + CH_WARPS * KVM * 2;                // [KVM][nsplit] the combine's weights
+  uint16_t* sx = reinterpret_cast<uint16_t*>(sql + HP * qst + W * 2 * HP * PST);  // [2][hs] new key, value
+  float* sml = reinterpret_cast<float*>(sx + 2 * hs);  // [W][KVM][2] the warps' maxima and sums
+  float* sw = sml + W * KVM * 2;                // [KVM][nsplit] the combine's weights
   // CL: [ncta][per + 2 KVM] the cluster's parts of the (head, dimension) pairs this CTA makes (outputs, then maxima
   // and sums), stored by the other CTAs
   float* rcv = sw;
@@ -432,8 +434,8 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
   const int nsplit = CL ? 1 : a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
   if (split >= nsplit) return;
   const int p0 = CL ? 0 : split * a.split_len, p1 = CL ? count : min(count, p0 + a.split_len);
-  const int TW = ncta * CH_WARPS;  // the warps the chunks are dealt to
-  const int gw = rank * CH_WARPS + warp;       // this warp's turn
+  const int TW = ncta * W;  // the warps the chunks are dealt to
+  const int gw = rank * W + warp;       // this warp's turn
   const int nchunk = (p1 - p0 + CHUNK - 1) / CHUNK;
   const int mine = gw < nchunk ? (nchunk - 1 - gw) / TW + 1 : 0;  // chunks of this warp
   const int kvdim = a.nkv * hs, hbase = kvh * KVM, pieces = hs / 8;       // 16-byte pieces a row
@@ -459,11 +461,11 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   for (int i = 0; i < ring && i < mine; i++) load_chunk(i);
-  for (int e = tid; e < (HP - KVM) * qst; e += CH_THREADS) {  // the padded heads' q: zero
+  for (int e = tid; e < (HP - KVM) * qst; e += (32 * W)) {  // the padded heads' q: zero
     sqh[KVM * qst + e] = __float2half_rn(0.0f);
     sql[KVM * qst + e] = __float2half_rn(0.0f);
   }
-  const bool holds_pos = FUSE && (CL ? (pos / CHUNK) % TW / CH_WARPS == rank : p1 == count);
+  const bool holds_pos = FUSE && (CL ? (pos / CHUNK) % TW / W == rank : p1 == count);
   // the head norms' weights and the RoPE tables' row of pos (not the previous kernel's output): read before the wait
   const int turned = f.rot > 0 && f.rot < hs ? f.rot : hs;
   float wq[DL], wk[DL], cs[DL], sn[DL];
@@ -482,7 +484,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
   pdl_wait();
   // the query heads a warp each; where this slice holds the position, its key and value too (FUSE: the heads' RMSNorm
   // over the lanes' strided sums, then RoPE on lane pairs)
-  for (int j = warp; j < KVM + (holds_pos ? 2 : 0); j += CH_WARPS) {
+  for (int j = warp; j < KVM + (holds_pos ? 2 : 0); j += W) {
     const float* src = j < KVM ? a.q + (long long)(hbase + j) * hs : (j == KVM ? f.k : f.v) + (long long)kvh * hs;
     float x[DL];
 #pragma unroll
@@ -658,15 +660,15 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
   namespace cg = cooperative_groups;
   const int per = CL ? (KVM * hs + ncta - 1) / ncta : 1, RS = per + 2 * KVM;  // CL: the pairs a CTA makes; a slot
   if constexpr (CL) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA has started
-  for (int e = tid; e < KVM * hs; e += CH_THREADS) {
+  for (int e = tid; e < KVM * hs; e += (32 * W)) {
     const int j = e / hs, d = e % hs, h = hbase + j;
     float mx = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < CH_WARPS; w++) mx = fmaxf(mx, sml[(w * KVM + j) * 2]);
+    for (int w = 0; w < W; w++) mx = fmaxf(mx, sml[(w * KVM + j) * 2]);
     const float base = mx == -INFINITY ? 0.0f : mx;
     float o = 0.0f, l = 0.0f;
 #pragma unroll
-    for (int w = 0; w < CH_WARPS; w++) {
+    for (int w = 0; w < W; w++) {
       const float wt = expf(sml[(w * KVM + j) * 2] - base);  // 0 for a warp without chunks
       o = fmaf(reinterpret_cast<const float*>(att_smem + (size_t)w * ring * chunkb)[j * (hs + 4) + d], wt, o);
       l = fmaf(sml[(w * KVM + j) * 2 + 1], wt, l);
@@ -729,7 +731,7 @@ __global__ void __launch_bounds__(CH_THREADS, 1) attention_chunk_kernel(const At
     return;
   }
   if (nsplit == 1 || !a.counters) return;
-  combine_slices<KVM, CH_THREADS>(a, kvh, nsplit, att_smem, (size_t)CH_WARPS * ring * chunkb, sw, sL);
+  combine_slices<KVM, (32 * W)>(a, kvh, nsplit, att_smem, (size_t)W * ring * chunkb, sw, sL);
 }
 
 // a block a head: the slices' partials combined
@@ -787,18 +789,18 @@ template <int KVM>
 cudaError_t launch_chunks(const AttArgs& a, const Fuse* f, const cudaLaunchConfig_t& cfg, int ring) {
   const Fuse none = {};
   if (a.hs <= 128) {
-    if (f) return launch_with(attention_chunk_kernel<KVM, true, 8, false>, cfg, a, *f, ring);
-    return launch_with(attention_chunk_kernel<KVM, false, 8, false>, cfg, a, none, ring);
+    if (f) return launch_with(attention_chunk_kernel<KVM, true, 8, false, CH_WARPS>, cfg, a, *f, ring);
+    return launch_with(attention_chunk_kernel<KVM, false, 8, false, CH_WARPS>, cfg, a, none, ring);
   }
-  if (f) return launch_with(attention_chunk_kernel<KVM, true, 16, false>, cfg, a, *f, ring);
-  return launch_with(attention_chunk_kernel<KVM, false, 16, false>, cfg, a, none, ring);
+  if (f) return launch_with(attention_chunk_kernel<KVM, true, 16, false, CH_WARPS>, cfg, a, *f, ring);
+  return launch_with(attention_chunk_kernel<KVM, false, 16, false, CH_WARPS>, cfg, a, none, ring);
 }
 
 // One cluster size's launch (grid (cs, nkv), cluster (cs, 1, 1)), or (fits non-null) the number of such clusters
 // the device can hold at once.
-template <int KVM, bool FUSE, int MBM>
+template <int KVM, bool FUSE, int MBM, int W>
 cudaError_t launch_cluster_cs(AttArgs a, const Fuse& f, const cudaLaunchConfig_t& base, int ring, int cs, int* fits) {
-  auto k = attention_chunk_kernel<KVM, FUSE, MBM, true>;
+  auto k = attention_chunk_kernel<KVM, FUSE, MBM, true, W>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)base.dynamicSmemBytes);
   if (e == cudaSuccess && cs > 8) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return e;
@@ -824,7 +826,7 @@ cudaError_t launch_cluster_cs(AttArgs a, const Fuse& f, const cudaLaunchConfig_t
 // holds all nkv clusters at once (the most warps to deal the chunks to, with no cluster waiting for another's SMs:
 // on the B200s measured 10, where 16 and 12 held only 7 clusters), else 8 where it holds one, else 0 (the slices'
 // kernel). Found once a configuration (kernel, shared memory, nkv) and device, before its first launch.
-template <int KVM, bool FUSE, int MBM>
+template <int KVM, bool FUSE, int MBM, int W>
 cudaError_t launch_cluster(const AttArgs& a, const Fuse& f, const cudaLaunchConfig_t& cfg, int ring, bool* launched) {
   struct Choice {
     int dev, nkv, hs;
@@ -844,26 +846,26 @@ cudaError_t launch_cluster(const AttArgs& a, const Fuse& f, const cudaLaunchConf
     cs = 0;
     for (int c = CS_MAX; c >= 8 && !cs; c--) {
       int n = 0;
-      if (launch_cluster_cs<KVM, FUSE, MBM>(a, f, cfg, ring, c, &n) != cudaSuccess) n = 0;
+      if (launch_cluster_cs<KVM, FUSE, MBM, W>(a, f, cfg, ring, c, &n) != cudaSuccess) n = 0;
       if (n >= a.nkv || (c == 8 && n >= 1)) cs = c;
     }
     cudaGetLastError();  // a refused query leaves no error behind: the choice falls back
     if (used < 64) cache[used++] = Choice{dev, a.nkv, a.hs, cfg.dynamicSmemBytes, cs};
   }
   *launched = cs != 0;
-  if (cs) return launch_cluster_cs<KVM, FUSE, MBM>(a, f, cfg, ring, cs, nullptr);
+  if (cs) return launch_cluster_cs<KVM, FUSE, MBM, W>(a, f, cfg, ring, cs, nullptr);
   return cudaSuccess;
 }
 
 template <int KVM>
 cudaError_t launch_clusters(const AttArgs& a, const Fuse* f, const cudaLaunchConfig_t& cfg, int ring, bool* launched) {
   const Fuse none = {};
-  if (a.hs <= 128) {
-    if (f) return launch_cluster<KVM, true, 8>(a, *f, cfg, ring, launched);
-    return launch_cluster<KVM, false, 8>(a, none, cfg, ring, launched);
+  if (a.hs <= 128) {  // CL_WARPS warps, a ring slot each
+    if (f) return launch_cluster<KVM, true, 8, CL_WARPS>(a, *f, cfg, ring, launched);
+    return launch_cluster<KVM, false, 8, CL_WARPS>(a, none, cfg, ring, launched);
   }
-  if (f) return launch_cluster<KVM, true, 16>(a, *f, cfg, ring, launched);
-  return launch_cluster<KVM, false, 16>(a, none, cfg, ring, launched);
+  if (f) return launch_cluster<KVM, true, 16, CH_WARPS>(a, *f, cfg, ring, launched);
+  return launch_cluster<KVM, false, 16, CH_WARPS>(a, none, cfg, ring, launched);
 }
 
 // the forward driver's float16 attention by clusters (1) or by slices and a combine (0); pllm_set_attention_mode
@@ -877,17 +879,18 @@ void run_attention(const char* name, AttArgs a, bool half, bool pdl, const Fuse*
   cudaError_t e;
   if (half) {
     const size_t rowb = (size_t)a.hs * 2 + 16;
-    auto smem_of = [&](int ring, size_t comb_floats) {
-      return (size_t)CH_WARPS * ring * 2 * CHUNK * rowb + 2 * (size_t)HP * (a.hs + 8) * 2 +
-             (size_t)CH_WARPS * 2 * HP * PST * 2 + 2 * (size_t)a.hs * 2 + (size_t)CH_WARPS * kvm * 2 * 4 +
+    auto smem_of = [&](int ring, size_t comb_floats, int warps = CH_WARPS) {
+      return (size_t)warps * ring * 2 * CHUNK * rowb + 2 * (size_t)HP * (a.hs + 8) * 2 +
+             (size_t)warps * 2 * HP * PST * 2 + 2 * (size_t)a.hs * 2 + (size_t)warps * kvm * 2 * 4 +
              (size_t)kvm * comb_floats * 4;
     };
     if (a.pos_dev && a.h0 == 0 && a.h1 == a.nh && g_cluster_attention) {
-      // the whole cache a cluster: two ring slots a warp (hs <= 128), no partials
-      const int ring = a.hs <= 128 ? 2 : 1;
+      // the whole cache a cluster: one ring slot a warp (hs <= 128: CL_WARPS warps, so that a cluster of 10 holds a
+      // chunk a warp up to 2,560 positions), no partials
+      const int ring = 1, warps = a.hs <= 128 ? CL_WARPS : CH_WARPS;
       // the receive buffer: at most kvm hs outputs + CS_MAX x (1 + 2 kvm) floats over the cluster's slots
       const size_t rcv = ((size_t)kvm * a.hs + (size_t)CS_MAX * (1 + 2 * kvm)) * 4;
-      const cudaLaunchConfig_t cfg = launch_config(grid, CH_THREADS, smem_of(ring, 0) + rcv, pdl, attr);
+      const cudaLaunchConfig_t cfg = launch_config(grid, 32 * warps, smem_of(ring, 0, warps) + rcv, pdl, attr);
       bool launched = false;
       switch (kvm) {
         case 1: e = launch_clusters<1>(a, f, cfg, ring, &launched); break;
