@@ -8,8 +8,10 @@ A step is one decode token of the 36-layer model (8.51 GB of int8 weights and sc
 reference's group-of-32 format); the prompt is seeded random ids. Prints one JSON line (rank 0):
   value       decode tok/s of the whole job, device-timed (CUDA events on the engine's stream), each step's token and
               position already in device memory; the 8.5 GB of weights (> the 126 MB L2) stream from HBM every step
-  e2e         the same through the engine's public call forward(token, pos): the token and position copied from
-              pinned host memory and the logits (151936 floats) copied back every step
+  e2e         the same through the engine's public call: at N = 1 Engine.next_token(token, pos), the greedy step (the
+              token and position copied from pinned host memory, 8 bytes, and the next token back, 4 bytes, every
+              step: the argmax runs on the device); at N > 1 Engine.forward (each rank's vocab slice of the logits
+              back every step)
   roofline    the dominant kernel (the fused w1/w3 product: 2 x 12288 x 4096 int8 + scales, SwiGLU epilogue), its
               algorithmic bytes a launch over its CUDA-event duration, against MEASURED_PEAKS.json's HBM copy GB/s
   cpu_baseline  the CPU oracle (the reference kernels' arithmetic in C, OpenMP over rows) decoding the same model
@@ -370,7 +372,8 @@ def main():
     clock = clocks.stop()
     value = steps / (decode_ms / 1000)
 
-    # end to end through the public call: token and position in from pinned memory, logits out, every step
+    # end to end through the public call: token and position in from pinned memory, the next token (N = 1) or the
+    # rank's logits (N > 1) out, every step
     e2e_steps = min(steps, cfg.seq_len - prompt - warmup - steps) or 0
     e2e_first = prompt + warmup + steps
     if e2e_steps < 8:  # rewind into the decode range (the cache's later positions are rewritten, as a new request)

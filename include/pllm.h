@@ -9,10 +9,18 @@
  *
  * Differences from the reference's contract, all at the boundary:
  *  - Memory: every address is device memory of the current device (pllm_alloc or any CUDA allocation). The
- *    kernels allocate nothing and keep no state between calls (as kernels/README.md:365-370 requires of the
- *    reference's), except the one status word of to_f16 / finite_f16.
- *  - Ordering: a call enqueues its kernel on the current stream (pllm_set_stream; default: the legacy stream 0) and
- *    returns; calls on one stream run in order. Only to_f16 and finite_f16 (which return a count) wait for the stream.
+ *    kernels allocate nothing in a call (as kernels/README.md:365-370 requires of the reference's). The library
+ *    keeps this state of its own, each per device: the status word of to_f16 / finite_f16 (one int32, made on the
+ *    first call), the scratch of argmax and sample (a few words), the bounded waits' status word and the bulk-copy
+ *    product's 1,024 tile-ticket counters (pllm_device_status), and the 4 MiB partials array of
+ *    pllm_attention_f16_noalloc.
+ *  - Threads: as the reference's threads.ts:90-133 shares a kernel's rows among threads, many host threads may call
+ *    the kernels at once (on disjoint outputs, each on its own stream: the current stream is a thread's own). The
+ *    calls that wait for a result in the library's scratch (argmax, sample, to_f16, finite_f16) take turns; each
+ *    bulk-copy product launch takes its own ticket counter.
+ *  - Ordering: a call enqueues its kernel on the calling thread's current stream (pllm_set_stream; default: the
+ *    legacy stream 0) and returns; calls on one stream run in order. Only to_f16, finite_f16, argmax and sample
+ *    (which return a number) wait for the stream.
  *  - Errors: the reference does not check its arguments (built --noAssert, kernels/build.py:13). Here a call whose
  *    arguments the reference's kernel could not take (n not whole groups, r0 > r1, a null or misaligned address)
  *    launches nothing and sets the sticky error that pllm_last_error returns; a failed launch sets it too.
@@ -107,7 +115,8 @@ int32_t finite_f16(uint64_t x, int32_t n);
 
 /* ===== the registry: from the logits to a token (kernels/kernel/sample.ts) */
 /* replaces argmax, sample.ts:6-10 (jobs.ts:116): the first index of the largest of n floats (a NaN never wins; one at
- * index 0 is the answer, as the reference's walk); waits (the library's own small scratch: calls must not overlap) */
+ * index 0 is the answer, as the reference's walk); waits (the library's own small scratch: concurrent host calls take
+ * turns) */
 int32_t argmax(uint64_t x, int32_t n);
 /* replaces penalize, sample.ts:16-30 (jobs.ts:117): each distinct token of tokens[0..count) once: a positive logit
  * divided by penalty, another multiplied by it, then presence (if > 0) taken off */
@@ -115,7 +124,7 @@ void penalize(uint64_t logits, uint64_t tokens, int32_t count, float penalty, fl
 /* replaces sample, sample.ts:248-337 (kernels.py's restype i32): the token drawn from softmax(logits / temperature) by
  * random in [0, 1), of the topk most probable (0: all), then of their nucleus (0 < topp < 1), then without those below
  * minp times the most probable (0: none); -1 where the largest logit is not a finite number. probs, index: device
- * scratch of n floats and n int32. Waits (the library's own scratch: calls must not overlap) */
+ * scratch of n floats and n int32. Waits (the library's own scratch: concurrent host calls take turns) */
 int32_t sample(uint64_t logits, int32_t n, float temperature, float topp, double random, uint64_t probs,
                uint64_t index, int32_t topk, float minp);
 
@@ -179,7 +188,7 @@ void pllm_d2d(uint64_t dst, uint64_t src, uint64_t bytes);
 void pllm_memset(uint64_t dst, int32_t value, uint64_t bytes);
 uint64_t pllm_stream_create(void);
 void pllm_stream_destroy(uint64_t s);
-void pllm_set_stream(uint64_t s);                      /* 0: the legacy default stream */
+void pllm_set_stream(uint64_t s);                      /* the calling thread's; 0: the legacy default stream */
 uint64_t pllm_get_stream(void);
 int32_t pllm_sync(void);                               /* wait for the current stream */
 int32_t pllm_device_sync(void);
@@ -222,22 +231,6 @@ void pllm_argmax_dev(uint64_t out, uint64_t x, int32_t n, uint64_t scratch);
  * before the launch runs: a recorded step's) */
 void pllm_sample_dev(uint64_t out, uint64_t logits, int32_t n, float temperature, float topp, uint64_t random_dev,
                      uint64_t probs, uint64_t index, int32_t topk, float minp);
-/* a product of a chain (pllm_gemv_chain): pllm_gemv's arguments for one token, rows 0..rows */
-typedef struct {
-  uint64_t out, x, norm, wq, ws;
-  int64_t pair;   /* epi 2: the gate's partner row offset */
-  int32_t n;      /* K */
-  int32_t rows;
-  int32_t pro;    /* 1 RMSNorm + quantize_x, 2 quantize_x */
-  int32_t epi;    /* 0 store, 1 add into out, 2 silu(row) * row + pair */
-  float eps;
-  int32_t bias;   /* 0 or 64 */
-} pllm_chain_stage;
-/* up to 4 int8 products of one token in one persistent launch, each reading what the one before wrote (the forward
- * step's wo, w1/w3, w2 and the next layer's q/k/v): the weights stream without a break while the CTAs wait for one
- * another between products (bounded, pllm_device_status 3). counters: 4 uint32 of device memory, zero before the
- * first call (every call leaves them at zero); a chain's calls must not overlap on the GPU. */
-void pllm_gemv_chain(const pllm_chain_stage* stages, int32_t count, uint64_t counters, int32_t pdl);
 /* q / k head norms (null weights: none), RoPE at the position, and k / v into the cache at it; the position is
  * read from device memory at pos_dev (or pos if pos_dev is 0), so one recorded graph serves every position */
 void pllm_qk_rope_cache(uint64_t q, uint64_t k, uint64_t v, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t,
@@ -312,6 +305,32 @@ void pllm_tp_step(uint64_t tp);
 void pllm_gemv_tp(uint64_t out, uint64_t x, uint64_t x_out, uint64_t norm, float eps, int32_t bias, uint64_t wq,
                   uint64_t ws, int32_t n, int32_t rows, int32_t pro, int32_t epi, int64_t pair, int32_t pdl,
                   uint64_t tp, int32_t use);
+
+/* ---- a decode step in the reference's own order of float32 operations (no counterpart in the reference's registry:
+ * its kernels have one order each, which these restate on the device so that a forward's logits are the reference
+ * kernels' to the bit; the default kernels above agree with them within rounding). Exponentials: the Cephes expf
+ * that kernels/kernel/math.ts:28-58 follows. */
+/* x (n floats; mode 2: h1 then h3, 2 n floats) as it is (mode 0), through rmsnorm with norm (mode 1,
+ * activations.ts:8-20) or swiglu (mode 2, activations.ts:77-90), then quantize_x with bias into xq / xs (n <= 49152);
+ * out (0: none) gets the float32 vector that was quantized */
+void pllm_exact_prepare(uint64_t xq, uint64_t xs, uint64_t out, uint64_t x, uint64_t norm, int32_t n, float eps,
+                        int32_t bias, int32_t mode);
+/* rows 0..rows of an int8 product of one token in matmul_q8's order (relaxed 0, matmul.ts:77-104: xq signed) or
+ * matmul_q8r's (relaxed 1, relaxed/int8.ts:17-50: xq the bias-64 bytes); add (0: none) makes out[r] = add[r] + row
+ * (add may be out) */
+void pllm_exact_product(uint64_t out, uint64_t add, uint64_t xq, uint64_t xs, uint64_t wq, uint64_t ws, int32_t n,
+                        int32_t rows, int32_t relaxed);
+/* qkv (nh q, nkv k, nkv v heads of hs floats): the q / k head norms (null weights: none), rope (attention.ts:7-20)
+ * at the position (pos_dev: device int32, or pos where pos_dev is 0), the key and value into the cache (to_f16 where
+ * half, counting non-finite values into the device int32 at bad) */
+void pllm_exact_qk_rope_cache(uint64_t qkv, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t, uint64_t sin_t,
+                              uint64_t pos_dev, int32_t pos, uint64_t kc, uint64_t vc, int32_t nh, int32_t nkv,
+                              int32_t hs, float eps, int32_t half, uint64_t bad);
+/* attentionOf (attention.ts:87-211) of nh heads over positions 0..pos (pos_dev or pos) of a cache of capacity
+ * positions; att: nh x capacity floats of scratch (the scaled scores afterwards); cap > 0: attention_capped's
+ * scores; hs % 16 == 0, nh / nkv <= 8, the kv head's probabilities in shared memory (refused beyond it) */
+void pllm_exact_attention(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t att, uint64_t pos_dev,
+                          int32_t pos, int32_t capacity, int32_t nh, int32_t nkv, int32_t hs, int32_t half, float cap);
 
 /* attention_f16 for callers that cannot allocate device memory (no counterpart in the reference): the same
  * arguments without att; the slices' partials live in a 4 MiB device array of the library's own, held by every GPU

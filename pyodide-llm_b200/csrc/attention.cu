@@ -835,6 +835,7 @@ cudaError_t launch_cluster(const AttArgs& a, const Fuse& f, const cudaLaunchConf
   };
   static Choice cache[64];
   static int used = 0;
+  std::lock_guard<std::mutex> hold(pllm_lookup_lock());
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -1294,6 +1295,7 @@ static __device__ __align__(256) float g_noalloc_partials[NOALLOC_FLOATS];
 namespace {
 float* noalloc_partials() {
   static float* ptrs[64] = {nullptr};
+  std::lock_guard<std::mutex> hold(pllm_lookup_lock());
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     pllm_fail(PLLM_ECUDA, "pllm_attention_f16_noalloc: no current device");

@@ -290,6 +290,7 @@ typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, v
 
 EncodeTiled encoder() {
   static EncodeTiled fn = nullptr;
+  std::lock_guard<std::mutex> hold(pllm_lookup_lock());
   if (!fn) {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;

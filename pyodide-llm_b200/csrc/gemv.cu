@@ -467,39 +467,6 @@ PLLM_API void pllm_gemv(uint64_t out, int64_t out_stride, uint64_t xq, uint64_t 
 #undef EPI_CASES
 }
 
-// The forward driver's chain of products (gemv_tma.cu's persistent kernel).
-PLLM_API void pllm_gemv_chain(const pllm_chain_stage* stages, int32_t count, uint64_t counters, int32_t pdl) {
-  PLLM_REQUIRE(stages && count >= 1 && count <= CHAIN_MAX && counters && !(counters & 3),
-               "pllm_gemv_chain: %d stages, counters %llu", count, (unsigned long long)counters);
-  ChainStage st[CHAIN_MAX] = {};
-  for (int i = 0; i < count; i++) {
-    const pllm_chain_stage& c = stages[i];
-    PLLM_REQUIRE((c.pro == PRO_RMS || c.pro == PRO_QUANT) && c.epi >= EPI_STORE && c.epi <= EPI_SWIGLU &&
-                     c.n > 0 && c.n % 128 == 0 && c.rows > 0 && (c.bias == 0 || c.bias == 64) && c.out && c.x &&
-                     c.wq && c.ws && (c.pro != PRO_RMS || c.norm),
-                 "pllm_gemv_chain: stage %d: pro %d epi %d n %d rows %d bias %d", i, c.pro, c.epi, c.n, c.rows,
-                 c.bias);
-    GemvArgs& a = st[i].a;
-    a.out = dptr<float>(c.out);
-    a.x = dptr<const float>(c.x);
-    a.norm = dptr<const float>(c.norm);
-    a.eps = c.eps;
-    a.bias = c.bias;
-    a.wq = dptr<const uint8_t>(c.wq);
-    a.ws = dptr<const void>(c.ws);
-    a.K = c.n;
-    a.r0 = 0;
-    a.r1 = c.rows;
-    a.count = 1;
-    a.pair = c.pair;
-    st[i].pro = c.pro;
-    st[i].epi = c.epi;
-  }
-  if (!gemv_chain(st, count, dptr<unsigned>(counters), pdl != 0))
-    pllm_fail(PLLM_EINVAL, "pllm_gemv_chain: the chained product does not take these stages (the bulk-copy form "
-                           "only: int8, K a multiple of 128, 16-byte aligned weights; gemv mode 0)");
-}
-
 // ---- matmul_f32 (matmul.ts:13): float32 weights, a warp a row
 namespace {
 __global__ void matmul_f32_kernel(float* __restrict__ out, const float* __restrict__ x, const float* __restrict__ w,

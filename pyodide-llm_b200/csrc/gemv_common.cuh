@@ -164,8 +164,7 @@ struct CtaSync {
 // CTA 0 stores the sum to x_out
 template <int PRO>
 __device__ __forceinline__ float4 x_vec(const GemvArgs& a, const Xchg* xg, int t, int i) {
-  // from L2 (.cg): in a chain of products in one launch (gemv_tma.cu) the previous product's CTAs on other SMs wrote
-  // x, and this SM's L1 may hold an older copy
+  // from L2 (.cg): x was written by the kernel ahead of this one (its CTAs on other SMs)
   float4 v = __ldcg(reinterpret_cast<const float4*>(a.x + t * a.x_stride) + i);
   if constexpr (PRO == PRO_RMS_SUM) {
     const unsigned mark = xchg_mark(*xg);
@@ -287,15 +286,6 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
 // the device status word's address on the current device (looked up on the first call a device: make that before any
 // stream capture; pllm_tp_open does)
 int* status_word();
-// A chain of products in one persistent launch (gemv_tma.cu): stage s + 1 reads what stage s wrote, its weights
-// streamed while the CTAs wait for one another
-constexpr int CHAIN_MAX = 4;
-struct ChainStage {
-  GemvArgs a;
-  int pro, epi;  // PRO_RMS / PRO_QUANT; EPI_STORE / EPI_ADD / EPI_SWIGLU
-  int ks, chunks;
-};
-bool gemv_chain(const ChainStage* st, int n, unsigned* counters, bool pdl);
 // the CTAs gemv_tma launches for rows r0..r1 (one an SM at most: the tiles of 8 rows are dealt among them)
 int gemv_tma_grid(long long rows, int epi);
 extern int g_gemv_mode;

@@ -26,6 +26,7 @@
 // next uses it. Rows cut into chunks (K > 8192) keep fixed shares: their tiles are two stages or more, and the last
 // tile dealt ends the launch later than even shares do (measured at K = 12288).
 #include "gemv_common.cuh"
+#include <atomic>
 
 __device__ int g_pllm_status = 0;  // a bounded wait gave up (PLLM_ETIMEOUT), read by pllm_device_status
 
@@ -40,7 +41,7 @@ using namespace gemvk;
 
 constexpr int NC = 8;                 // consumer warps
 constexpr int TR = NC;                // row slots a stage (a row a consumer warp)
-constexpr int TRP = TR;               // the product kernel's tile rows (the chain's are TR too)
+constexpr int TRP = TR;               // the product kernel's tile rows
 constexpr int TMA_THREADS = (NC + 1) * 32;
 constexpr long long WAIT_BOUND = 1ll << 26;  // polls of an mbarrier before giving up (seconds: never in a run that works)
 
@@ -296,180 +297,6 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   }
 }
 
-// ---- a chain of products in one persistent launch (one CTA an SM, every SM): the producer warp streams the
-// weights of stage after stage into the ring without a break, while the consumers of a stage wait (a grid-wide count,
-// bounded) until every CTA has finished the stage before it, whose outputs its prologue reads. The launch's ramp and
-// tail, and the stream's pause at a kernel boundary, are paid once a chain instead of once a product.
-struct ChainArgs {
-  ChainStage st[CHAIN_MAX];
-  int n;
-  unsigned* bar;      // [CHAIN_MAX] arrivals after each stage; the last stage's is the exit count
-  int S, slot_bytes, act_bytes;
-  int* status;
-};
-
-// thread 0 of the consumers: every CTA has arrived at *bar (acquire), bounded at 2 s
-__device__ __forceinline__ void wait_grid(const unsigned* bar, unsigned want, int* status) {
-  if (threadIdx.x != 0) return;
-  const unsigned long long t0 = global_ns();
-  for (;;) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
-    if (v >= want) return;
-    if (global_ns() - t0 > XCHG_WAIT_NS) {
-      atomicExch(status, PLLM_ETIMEOUT);
-      return;
-    }
-  }
-}
-
-__global__ void __launch_bounds__(TMA_THREADS, 1) gemv_chain_kernel(const ChainArgs c) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int S = c.S;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + S;
-  float* res = reinterpret_cast<float*>(smem + 16 * S);  // [2][TR] row results (EPI_SWIGLU)
-  uint8_t* act = smem + ((16 * S + 2 * TR * 4 + 127) & ~127);
-  uint8_t* stage0 = act + c.act_bytes;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; s++) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NC);
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-
-  if (warp == NC) {  // ---- the producer: every stage's rows, one ring
-    if (lane == 0) {
-      uint64_t policy;
-      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-      long long it = 0;
-      for (int s = 0; s < c.n; s++) {
-        const GemvArgs& a = c.st[s].a;
-        const int epi = c.st[s].epi, KS = c.st[s].ks, chunks = c.st[s].chunks, K = a.K, ng = K / 32;
-        const long long per_tile = epi == EPI_SWIGLU ? TR / 2 : TR;
-        long long lo, hi;
-        cta_rows(a, lo, hi);
-        for (long long t = lo; t < hi; t += per_tile) {
-          const int n = (int)min(per_tile, hi - t);
-          for (int ch = 0; ch < chunks; ch++, it++) {
-            const int slot = (int)(it % S);
-            if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
-            uint8_t* w = stage0 + (size_t)slot * c.slot_bytes;
-            float* sc = reinterpret_cast<float*>(w + (size_t)TR * KS);
-            const int halves = epi == EPI_SWIGLU ? 2 : 1;
-            mbar_expect_tx(&full[slot], (unsigned)(halves * n * (KS + KS / 8)));
-            for (int h = 0; h < halves; h++) {
-              const long long row0 = t + (h ? a.pair : 0);
-              const int slot0 = h ? TR / 2 : 0;
-              if (chunks == 1) {
-                bulk_copy(w + (size_t)slot0 * KS, a.wq + row0 * K, (unsigned)(n * K), &full[slot], policy);
-                bulk_copy(sc + (size_t)slot0 * (KS / 32), reinterpret_cast<const float*>(a.ws) + row0 * ng,
-                          (unsigned)(n * ng * 4), &full[slot], policy);
-              } else {
-                for (int r = 0; r < n; r++) {
-                  bulk_copy(w + (size_t)(slot0 + r) * KS, a.wq + (row0 + r) * K + (long long)ch * KS, (unsigned)KS,
-                            &full[slot], policy);
-                  bulk_copy(sc + (size_t)(slot0 + r) * (KS / 32),
-                            reinterpret_cast<const float*>(a.ws) + (row0 + r) * ng + (long long)ch * (KS / 32),
-                            (unsigned)(KS / 8), &full[slot], policy);
-                }
-              }
-            }
-          }
-        }
-      }
-    }
-    return;
-  }
-
-  // ---- the consumers
-  const int swz = (lane >> 2) & 1;
-  long long it = 0;
-  int tiles = 0;
-  bool ok = true;
-  pdl_wait();
-  for (int s = 0; s < c.n; s++) {
-    const GemvArgs& a = c.st[s].a;
-    const int epi = c.st[s].epi, KS = c.st[s].ks, chunks = c.st[s].chunks, K = a.K;
-    if (s > 0) {  // every CTA is done with the stage before (its outputs are this stage's input)
-      wait_grid(c.bar + s - 1, gridDim.x, c.status);
-      consumer_sync();
-    }
-    int8_t* sq = reinterpret_cast<int8_t*>(act);
-    float* ss = reinterpret_cast<float*>(act + (size_t)K);
-    if (c.st[s].pro == PRO_RMS) load_activations<F_Q8, 1, PRO_RMS, ConsumerSync>(a, sq, ss, nullptr, nullptr);
-    else load_activations<F_Q8, 1, PRO_QUANT, ConsumerSync>(a, sq, ss, nullptr, nullptr);
-    consumer_sync();
-    if (s == 0) pdl_launch_dependents();
-    const long long per_tile = epi == EPI_SWIGLU ? TR / 2 : TR;
-    long long lo, hi;
-    cta_rows(a, lo, hi);
-    for (long long t = lo; t < hi; t += per_tile, tiles++) {
-      const int n = (int)min(per_tile, hi - t);
-      const bool mine = epi == EPI_SWIGLU ? ((warp % (TR / 2)) < n) : (warp < n);
-      float acc = 0.0f;
-      for (int ch = 0; ch < chunks; ch++, it++) {
-        const int slot = (int)(it % S);
-        if (ok) ok = mbar_wait(&full[slot], (unsigned)(it / S) & 1);
-        if (mine && ok) {
-          const uint8_t* w = stage0 + (size_t)slot * c.slot_bytes + (size_t)warp * KS;
-          const float* sc = reinterpret_cast<const float*>(stage0 + (size_t)slot * c.slot_bytes + (size_t)TR * KS) +
-                            (size_t)warp * (KS / 32);
-          const int u0 = ch * (KS / 32);
-          for (int u = lane; u < KS / 32; u += 32) {
-            const int4 wa = *reinterpret_cast<const int4*>(w + u * 32 + 16 * swz);
-            const int4 wb = *reinterpret_cast<const int4*>(w + u * 32 + 16 * (swz ^ 1));
-            const int8_t* x = sq + (size_t)(u0 + u) * 32;
-            const int4 xa = *reinterpret_cast<const int4*>(x + 16 * swz);
-            const int4 xb = *reinterpret_cast<const int4*>(x + 16 * (swz ^ 1));
-            int g0 = __dp4a(wa.x, xa.x, 0), g1 = __dp4a(wb.x, xb.x, 0);  // paired as read: the same integer
-            g0 = __dp4a(wa.y, xa.y, g0);
-            g1 = __dp4a(wb.y, xb.y, g1);
-            g0 = __dp4a(wa.z, xa.z, g0);
-            g1 = __dp4a(wb.z, xb.z, g1);
-            g0 = __dp4a(wa.w, xa.w, g0);
-            g1 = __dp4a(wb.w, xb.w, g1);
-            acc = fmaf((float)(g0 + g1), __fmul_rn(sc[u], ss[u0 + u]), acc);
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-      }
-      if (!mine) {
-        if (epi == EPI_SWIGLU) consumer_sync();
-        continue;
-      }
-      acc = warp_sum(acc);
-      if (epi == EPI_SWIGLU) {
-        float* r = res + (tiles & 1) * TR;
-        if (lane == 0) r[warp] = acc;
-        consumer_sync();
-        if (warp < TR / 2 && lane == 0) {
-          const float h1 = r[warp], h3 = r[warp + TR / 2];
-          a.out[t + warp] = (h1 / (1.0f + expf(-h1))) * h3;
-        }
-      } else if (lane == 0) {
-        float* o = a.out + t + warp;
-        if (epi == EPI_ADD) *o = __ldcg(o) + acc;
-        else *o = acc;
-      }
-    }
-    // this CTA's rows of stage s are written: count it (one fence orders the warps' stores)
-    consumer_sync();
-    if (threadIdx.x == 0) {
-      __threadfence();
-      const unsigned before = atomicAdd(c.bar + s, 1u);
-      if (s == c.n - 1 && before == gridDim.x - 1) {  // the last CTA out: every count back to zero for the next launch
-        for (int k = 0; k < c.n; k++) atomicExch(c.bar + k, 0u);
-        __threadfence();
-      }
-    }
-  }
-}
-
 template <int MT, int PRO, int EPI>
 bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl, const Xchg& xg) {
   auto kernel = gemv_tma_kernel<MT, PRO, EPI>;
@@ -506,6 +333,7 @@ int g_gemv_mode = 0;
 // the device address of the status word on the current device (looked up once a device)
 int* status_word() {
   static int* addr[64] = {nullptr};
+  std::lock_guard<std::mutex> hold(pllm_lookup_lock());
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     pllm_fail(PLLM_ECUDA, "gemv_tma: no current device");
@@ -560,8 +388,8 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
   }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  static unsigned next_slot[64] = {0};  // a device's launches take its ticket counters in turn
-  p.slot = (int)(next_slot[dev]++ % TICKET_SLOTS);
+  static std::atomic<unsigned> next_slot[64];  // a device's launches take its ticket counters in turn (any thread)
+  p.slot = (int)(next_slot[dev].fetch_add(1u, std::memory_order_relaxed) % TICKET_SLOTS);
   // rows cut into chunks make tiles of two stages or more, the last of which ends the launch late: fixed shares there
   p.tickets = p.chunks == 1;
 #define CASE(M, P, E) \
@@ -573,51 +401,6 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
   CASE(1, PRO_RMS_SUM, EPI_STORE) CASE(1, PRO_RMS_SUM, EPI_SWIGLU) CASE(1, PRO_QUANT, EPI_SEND)
 #undef CASE
   return false;
-}
-
-// The chain's launch: every SM a CTA, the ring's slots sized for the largest stage's chunk.
-bool gemv_chain(const ChainStage* st, int n, unsigned* counters, bool pdl) {
-  if (n < 1 || n > CHAIN_MAX || g_gemv_mode == 1) return false;
-  ChainArgs c = {};
-  int ks_max = 0, k_max = 0;
-  for (int i = 0; i < n; i++) {
-    c.st[i] = st[i];
-    const int K = st[i].a.K;
-    if (K % 128 || st[i].a.count != 1 || ((uintptr_t)st[i].a.wq & 15) || ((uintptr_t)st[i].a.ws & 15)) return false;
-    int chunks = (K + 4095) / 4096;
-    while (K % (chunks * 128)) chunks++;
-    c.st[i].chunks = chunks;
-    c.st[i].ks = K / chunks;
-    ks_max = c.st[i].ks > ks_max ? c.st[i].ks : ks_max;
-    k_max = K > k_max ? K : k_max;
-  }
-  c.n = n;
-  c.bar = counters;
-  c.status = status_word();
-  if (!c.status) return false;
-  c.slot_bytes = (TR * ks_max + TR * (ks_max / 32) * 4 + 127) & ~127;
-  c.act_bytes = (int)((k_max + (k_max / 32) * 4 + 127) & ~127);
-  const int head = (16 * 8 + 2 * TR * 4 + 127) & ~127;
-  int S = (g_tma_budget - c.act_bytes - head) / c.slot_bytes;
-  if (S > 8) S = 8;
-  if (S < 2) return false;
-  c.S = S;
-  const size_t smem = (size_t)head + c.act_bytes + (size_t)S * c.slot_bytes;
-  if (cudaFuncSetAttribute(gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return false;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)pllm_num_sms());
-  cfg.blockDim = dim3(TMA_THREADS);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = pllm_stream();
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_chain_kernel, c);
-  if (e != cudaSuccess) pllm_fail(PLLM_ECUDA, "gemv_chain launch: %s", cudaGetErrorString(e));
-  return true;
 }
 
 }  // namespace gemvk

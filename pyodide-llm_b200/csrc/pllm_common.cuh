@@ -6,6 +6,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <mutex>
 #include "pllm.h"  // the declarations every definition must match
 
 #define PLLM_API extern "C" __attribute__((visibility("default")))
@@ -13,8 +14,13 @@
 // ---- the sticky error (pllm_last_error): the first failure since the last pllm_clear_error is kept
 void pllm_fail(int code, const char* fmt, ...);
 int pllm_failed();
-cudaStream_t pllm_stream();
+cudaStream_t pllm_stream();  // the calling host thread's current stream (pllm_set_stream)
 int pllm_num_sms();
+// the library's host-side state is shared by every host thread: lookups that fill a per-device cache hold
+// pllm_lookup_lock; the calls that wait for a result in the library's own device scratch (argmax, sample, to_f16,
+// finite_f16) hold pllm_scratch_lock from their launch to their result
+std::mutex& pllm_lookup_lock();
+std::mutex& pllm_scratch_lock();
 
 enum PllmError {
   PLLM_OK = 0,

@@ -93,6 +93,7 @@ __global__ void finite_f16_kernel(const uint16_t* __restrict__ x, int n, int* __
 // one int32 of device memory for the calls that return a count (to_f16, finite_f16), made once per device
 int* status_word() {
   static int* words[64] = {nullptr};
+  std::lock_guard<std::mutex> hold(pllm_lookup_lock());
   int dev = 0;
   cudaGetDevice(&dev);
   if (!words[dev & 63]) {
@@ -160,6 +161,7 @@ PLLM_API void six_sums(uint64_t out, uint64_t w, int32_t groups) {
 PLLM_API int32_t to_f16(uint64_t out, uint64_t x, int32_t n) {
   PLLM_REQUIRE_RET(n >= 0, -1, "to_f16: n %d", n);
   if (!n) return 0;
+  std::lock_guard<std::mutex> hold(pllm_scratch_lock());  // one status word a device: one call at a time
   int* bad = status_word();
   if (!bad) return -1;
   cudaMemsetAsync(bad, 0, sizeof(int), pllm_stream());
@@ -194,6 +196,7 @@ PLLM_API void from_f16(uint64_t out, uint64_t x, int32_t n) {
 PLLM_API int32_t finite_f16(uint64_t x, int32_t n) {
   PLLM_REQUIRE_RET(n >= 0, -1, "finite_f16: n %d", n);
   if (!n) return 1;
+  std::lock_guard<std::mutex> hold(pllm_scratch_lock());
   int* found = status_word();
   if (!found) return -1;
   cudaMemsetAsync(found, 0, sizeof(int), pllm_stream());

@@ -10,7 +10,9 @@ namespace {
 std::mutex g_lock;
 int g_code = 0;
 char g_msg[512] = {0};
-cudaStream_t g_stream = nullptr;  // nullptr: the legacy default stream, as torch's default stream is
+// each host thread's current stream (nullptr: the legacy default stream, as torch's default stream is), so that
+// threads that call the kernels concurrently on disjoint row ranges each enqueue on their own
+thread_local cudaStream_t g_stream = nullptr;
 int g_sms = 0;
 int g_device = -1;
 }  // namespace
@@ -26,6 +28,14 @@ void pllm_fail(int code, const char* fmt, ...) {
 }
 
 int pllm_failed() { return g_code; }
+std::mutex& pllm_lookup_lock() {
+  static std::mutex m;
+  return m;
+}
+std::mutex& pllm_scratch_lock() {
+  static std::mutex m;
+  return m;
+}
 cudaStream_t pllm_stream() { return g_stream; }
 
 int pllm_num_sms() {
@@ -131,7 +141,10 @@ PLLM_API int32_t pllm_graph_begin() {
 }
 PLLM_API uint64_t pllm_graph_end() {
   cudaGraph_t graph = nullptr;
-  if (check(cudaStreamEndCapture(g_stream, &graph), "pllm_graph_end")) return 0;
+  if (check(cudaStreamEndCapture(g_stream, &graph), "pllm_graph_end")) {
+    cudaGetLastError();  // an invalidated capture also leaves the thread's last error set: the next launch is not at fault
+    return 0;
+  }
   cudaGraphExec_t exec = nullptr;
   cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
   cudaGraphDestroy(graph);

@@ -77,7 +77,8 @@ int grid_for(int n) {
 }  // namespace
 
 // The library's own scratch for the registry's argmax (it returns the index, so it waits for it): a key and a count,
-// zero between calls; calls that overlap on the GPU race on it.
+// zero between calls. The call holds the library's scratch lock from its launch until it has the index, so host
+// threads that call it at once take turns.
 static __device__ unsigned long long g_argmax_key = 0;
 static __device__ unsigned g_argmax_count = 0;
 static __device__ int g_argmax_out = 0;
@@ -85,6 +86,7 @@ static __device__ int g_argmax_out = 0;
 // argmax (sample.ts:6): the first index of the largest of n floats at x
 PLLM_API int32_t argmax(uint64_t x, int32_t n) {
   PLLM_REQUIRE_RET(x && n > 0, 0, "argmax: n %d", n);
+  std::lock_guard<std::mutex> hold(pllm_scratch_lock());  // the scratch is the library's: one call at a time
   void *key = nullptr, *count = nullptr, *out = nullptr;
   if (cudaGetSymbolAddress(&key, g_argmax_key) != cudaSuccess ||
       cudaGetSymbolAddress(&count, g_argmax_count) != cudaSuccess ||
@@ -547,6 +549,7 @@ PLLM_API int32_t sample(uint64_t logits, int32_t n, float temperature, float top
                         uint64_t index, int32_t topk, float minp) {
   PLLM_REQUIRE_RET(logits && probs && index && n > 0 && temperature > 0.0f, -1, "sample: n %d temperature %g", n,
                    (double)temperature);
+  std::lock_guard<std::mutex> hold(pllm_scratch_lock());
   void* out = nullptr;
   if (cudaGetSymbolAddress(&out, g_sample_out) != cudaSuccess ||
       !sample_enqueue(dptr<const float>(logits), n, temperature, topp, nullptr, random, topk, minp, dptr<float>(probs),

@@ -22,7 +22,9 @@ adding them to x, and the next product sums them into x in its prologue (pro 3),
 (the prologue's CTAs all read one while the first writes the other). The logits are the rank's vocab rows.
 
 Every product's group sums are the reference kernels' exact integers; the float32 around them agrees with the
-reference's within rounding (the tests hold the logits to the oracle's within 1e-3 relative).
+reference's within rounding of other summation orders, which a deep random net carries through quantize_x's rounding
+boundaries (the tests: 2e-2 of the largest logit at two layers of the Qwen3-8B widths). Engine(exact=True) runs every
+step in the reference kernels' own order of float32 operations instead (pllm_exact_*): the oracle's logits to the bit.
 """
 import os
 from dataclasses import dataclass
@@ -30,7 +32,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from .device import Buffer, Pinned, init
-from .lib import ChainStage, L, check
+from .lib import L, check
 from .tp import Shard
 
 F_Q8 = 0
@@ -124,19 +126,20 @@ class Engine:
 
     SPLIT = 128  # positions a slice of the split-KV attention (two tiles of 64 a CTA, double-buffered)
 
-    def __init__(self, cfg, host=None, seed=0, device=0, graphs=True, pdl=True, exchange=None):
+    def __init__(self, cfg, host=None, seed=0, device=0, graphs=True, pdl=True, exchange=None, exact=False):
+        """exact: every step in the reference kernels' own order of float32 operations (pllm_exact_*: the oracle's
+        logits to the bit, several times slower); else the fused kernels (the same integers, float32 within
+        rounding). One rank only."""
         init(device)
+        if exact and exchange:
+            raise ValueError("the reference-order step runs on one rank")
+        self.exact = exact
         self.xg = exchange
         self.shard = s = Shard(cfg, exchange.rank, exchange.world) if exchange else Shard(cfg)
         if os.environ.get("PLLM_STAGE_BUDGET"):  # the bulk-copy product's stage ring, bytes (a tuning knob)
             L.pllm_set_stage_budget(int(os.environ["PLLM_STAGE_BUDGET"]))
         self.cfg, self.graphs = cfg, graphs
         self.pdl = pdl and not os.environ.get("PLLM_NO_PDL")  # (a switch for measuring what the early launches give)
-        # PLLM_CHAIN=1: a layer's wo, w1/w3, w2 and the next layer's q/k/v as one persistent launch (pllm_gemv_chain),
-        # where the shapes suit it (int8 products of K in whole 128s; one rank). Not the default: measured slower than
-        # the separate launches (the stages' barriers and prologues outrun what the ring of weights can bridge).
-        self.chained = (not exchange and bool(os.environ.get("PLLM_CHAIN")) and all(
-            k % 128 == 0 for k in (cfg.dim, cfg.qdim, cfg.hidden)))
         c = cfg
         self.rows_qkv = s.rows_qkv
         self.bias = 64 if c.relaxed else 0
@@ -173,11 +176,14 @@ class Engine:
         B["hb"] = Buffer(s.hidden * 4)
         B["logits"] = Buffer(s.vocab * 4)
         B["tp"] = Buffer(8).zero()      # the token and the position, read by the kernels
-        B["chain"] = Buffer((c.layers + 1) * 16).zero()  # a chain's 4 arrival counts (zero between calls)
         B["bad"] = Buffer(4).zero()     # non-finite keys / values written to a float16 cache (halves.ts:35)
         B["next"] = Buffer(4)           # the greedy step's token (pllm_argmax_dev) and its scratch
         B["amx"] = Buffer(16).zero()
         B["scratch"] = Buffer(L.pllm_attention_scratch_bytes(s.heads, c.head_size, c.seq_len, self.SPLIT)).zero()
+        if exact:  # the reference-order step's quantized activations, w1 / w3 rows and attention scores
+            wide = max(c.dim, c.qdim, c.hidden)
+            B["xq"], B["xs"] = Buffer(wide), Buffer(wide // 8)
+            B["h13"], B["scores"] = Buffer(2 * c.hidden * 4), Buffer(c.heads * c.seq_len * 4)
         self.B = B
         if host is not None:
             self.load(host)
@@ -289,60 +295,50 @@ class Engine:
     def launches_per_step(self):
         """Kernels a step launches: the embedding, five a layer (the q/k/v product; the attention with the q / k
         norms, RoPE, the cache write and its slices' combine inside; the wo, w1/w3 and w2 products), the classifier."""
-        if self.chained:
-            return 2 + 2 * self.cfg.layers
+        if self.exact:
+            return 3 + 11 * self.cfg.layers
         return 2 + 5 * self.cfg.layers + (1 if self.xg else 0)
 
-    def _stage(self, out, x, norm, wq, ws, n, rows, pro, epi, pair=0):
-        return ChainStage(out=out, x=x, norm=norm, wq=wq, ws=ws, pair=pair, n=n, rows=rows, pro=pro, epi=epi,
-                          eps=self.cfg.eps, bias=self.bias)
-
-    def _chain(self, index, stages):
-        arr = (ChainStage * len(stages))(*stages)
-        L.pllm_gemv_chain(arr, len(stages), self.B["chain"].ptr + 16 * index, int(self.pdl))
-
-    def _enqueue_chained_step(self, need_logits=True):
-        """A step as 2 + 2 x layers launches: the embedding; layer 0's q/k/v product; then per layer the attention
-        step and one chain [wo, w1/w3, w2, the next layer's q/k/v (or the classifier)]."""
+    def _enqueue_exact_step(self, need_logits=True):
+        """A step in the reference kernels' order of float32 operations (pllm_exact_*), as the oracle's forward
+        (oracle/pllm_oracle.c or_forward) and the reference's engine.ts:421-475 run it: rmsnorm + quantize_x, the
+        q/k/v products, the head norms, rope and the cache, attentionOf, quantize_x + wo (x +=), rmsnorm + quantize_x,
+        w1 and w3, swiglu + quantize_x, w2 (x +=); the final norm and the classifier."""
         c, B = self.cfg, self.B
         tok, pos = B["tp"].ptr, B["tp"].ptr + 4
-        E = 2 if c.half_kv else 4
-        x, qkv, att, hb = B["x"].ptr, B["qkv"].ptr, B["att"].ptr, B["hb"].ptr
+        E, half, rel = (2 if c.half_kv else 4), int(c.half_kv), int(c.relaxed)
+        xq, xs, x = B["xq"].ptr, B["xs"].ptr, B["x"].ptr
         L.pllm_embed_q8(x, B["emb"].ptr, B["emb_s"].ptr, tok, 0, c.dim, 1, c.dim)
-
-        def wqkv(l):
-            return self._stage(qkv, x, B["att_norm"].ptr + l * c.dim * 4, B["wqkv"].ptr + l * self.rows_qkv * c.dim,
-                               B["sqkv"].ptr + l * self.rows_qkv * (c.dim // 32) * 4, c.dim, self.rows_qkv,
-                               PRO_RMS, EPI_STORE)
-        self._chain(0, [wqkv(0)])
         for l in range(c.layers):
+            L.pllm_exact_prepare(xq, xs, 0, x, B["att_norm"].ptr + l * c.dim * 4, c.dim, c.eps, self.bias, 1)
+            L.pllm_exact_product(B["qkv"].ptr, 0, xq, xs, B["wqkv"].ptr + l * self.rows_qkv * c.dim,
+                                 B["sqkv"].ptr + l * self.rows_qkv * (c.dim // 32) * 4, c.dim, self.rows_qkv, rel)
             kc = B["kc"].ptr + l * c.seq_len * c.kvdim * E
             vc = B["vc"].ptr + l * c.seq_len * c.kvdim * E
             qn = B["q_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
             kn = B["k_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
-            L.pllm_attention_step(att, qkv, kc, vc, B["scratch"].ptr, pos, c.seq_len, c.heads, c.kv_heads,
-                                  c.head_size, int(c.half_kv), 0.0, self.SPLIT, qn, kn, B["cos_t"].ptr,
-                                  B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, int(self.pdl))
-            stages = [
-                self._stage(x, att, 0, B["wo"].ptr + l * c.dim * c.qdim, B["so"].ptr + l * c.dim * (c.qdim // 32) * 4,
-                            c.qdim, c.dim, PRO_QUANT, EPI_ADD),
-                self._stage(hb, x, B["ffn_norm"].ptr + l * c.dim * 4, B["w13"].ptr + l * 2 * c.hidden * c.dim,
-                            B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.dim, c.hidden, PRO_RMS,
-                            EPI_SWIGLU, pair=c.hidden),
-                self._stage(x, hb, 0, B["w2"].ptr + l * c.dim * c.hidden,
-                            B["s2"].ptr + l * c.dim * (c.hidden // 32) * 4, c.hidden, c.dim, PRO_QUANT, EPI_ADD)]
-            if l + 1 < c.layers:
-                stages.append(wqkv(l + 1))
-            elif need_logits:
-                stages.append(self._stage(B["logits"].ptr, x, B["final_norm"].ptr, B["cls"].ptr, B["cls_s"].ptr,
-                                          c.dim, c.vocab, PRO_RMS, EPI_STORE))
-            self._chain(l + 1, stages)
+            L.pllm_exact_qk_rope_cache(B["qkv"].ptr, qn, kn, B["cos_t"].ptr, B["sin_t"].ptr, pos, 0, kc, vc, c.heads,
+                                       c.kv_heads, c.head_size, c.eps, half, B["bad"].ptr)
+            L.pllm_exact_attention(B["att"].ptr, B["qkv"].ptr, kc, vc, B["scores"].ptr, pos, 0, c.seq_len, c.heads,
+                                   c.kv_heads, c.head_size, half, 0.0)
+            L.pllm_exact_prepare(xq, xs, 0, B["att"].ptr, 0, c.qdim, c.eps, self.bias, 0)
+            L.pllm_exact_product(x, x, xq, xs, B["wo"].ptr + l * c.dim * c.qdim,
+                                 B["so"].ptr + l * c.dim * (c.qdim // 32) * 4, c.qdim, c.dim, rel)
+            L.pllm_exact_prepare(xq, xs, 0, x, B["ffn_norm"].ptr + l * c.dim * 4, c.dim, c.eps, self.bias, 1)
+            L.pllm_exact_product(B["h13"].ptr, 0, xq, xs, B["w13"].ptr + l * 2 * c.hidden * c.dim,
+                                 B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.dim, 2 * c.hidden, rel)
+            L.pllm_exact_prepare(xq, xs, 0, B["h13"].ptr, 0, c.hidden, c.eps, self.bias, 2)
+            L.pllm_exact_product(x, x, xq, xs, B["w2"].ptr + l * c.dim * c.hidden,
+                                 B["s2"].ptr + l * c.dim * (c.hidden // 32) * 4, c.hidden, c.dim, rel)
+        if need_logits:
+            L.pllm_exact_prepare(xq, xs, 0, x, B["final_norm"].ptr, c.dim, c.eps, self.bias, 1)
+            L.pllm_exact_product(B["logits"].ptr, 0, xq, xs, B["cls"].ptr, B["cls_s"].ptr, c.dim, c.vocab, rel)
 
     def _enqueue_step(self, need_logits=True):
+        if self.exact:
+            return self._enqueue_exact_step(need_logits)
         if self.xg:
             return self._enqueue_tp_step(need_logits)
-        if self.chained:
-            return self._enqueue_chained_step(need_logits)
         c, B = self.cfg, self.B
         tok, pos = B["tp"].ptr, B["tp"].ptr + 4
         E = 2 if c.half_kv else 4
@@ -508,7 +504,7 @@ class Engine:
     def can_prefill(self):
         """The tensor-core prefill's shapes: products with K and rows in whole 128s, a float16 cache, one rank."""
         c, sh = self.cfg, self.shard
-        return (not self.xg and c.half_kv and c.head_size <= 128 and all(
+        return (not self.xg and not self.exact and c.half_kv and c.head_size <= 128 and all(
             v % 128 == 0 for v in (c.dim, sh.qdim, sh.hidden, self.rows_qkv)))
 
     def _prefill_buffers(self, M):

@@ -108,7 +108,6 @@ SIGNATURES = {
     "pllm_tp_connect": ([U64, P], I32),
     "pllm_tp_close": ([U64], None),
     "pllm_tp_step": ([U64], None),
-    "pllm_gemv_chain": ([P, I32, U64, I32], None),
     "argmax": ([U64, I32], I32),
     "penalize": ([U64, U64, I32, F32, F32], None),
     "pllm_argmax_dev": ([U64, U64, I32, U64], None),
@@ -124,16 +123,14 @@ SIGNATURES = {
     "pllm_sample_dev": ([U64, U64, I32, F32, F32, U64, U64, U64, I32, F32], None),
     "pllm_gemv_tp": ([U64, U64, U64, U64, F32, I32, U64, U64, I32, I32, I32, I32, I64, I32, U64, I32], None),
     "pllm_synth_t2": ([U64, U64, I64, I32, U64, F32, F32], None),
+    "pllm_exact_prepare": ([U64, U64, U64, U64, U64, I32, F32, I32, I32], None),
+    "pllm_exact_product": ([U64, U64, U64, U64, U64, U64, I32, I32, I32], None),
+    "pllm_exact_qk_rope_cache": ([U64, U64, U64, U64, U64, U64, I32, U64, U64, I32, I32, I32, F32, I32, U64], None),
+    "pllm_exact_attention": ([U64, U64, U64, U64, U64, U64, I32, I32, I32, I32, I32, I32, F32], None),
 }
 
 # the registry's names: what a drop-in for the reference's kernel modules exports (tests check each is there)
 REGISTRY = [name for name in SIGNATURES if not name.startswith("pllm_")]
-
-
-class ChainStage(ctypes.Structure):
-    """include/pllm.h's pllm_chain_stage: one product of a pllm_gemv_chain."""
-    _fields_ = [("out", U64), ("x", U64), ("norm", U64), ("wq", U64), ("ws", U64), ("pair", I64), ("n", I32),
-                ("rows", I32), ("pro", I32), ("epi", I32), ("eps", F32), ("bias", I32)]
 
 
 class PllmError(RuntimeError):

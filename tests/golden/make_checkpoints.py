@@ -1,7 +1,7 @@
 """Generates tests/golden/checkpoints.npz: checkpoint files written by the reference's own code, and what the reference
 reads from them, to pin the checkpoint reader (pyodide-llm_b200/pllm/checkpoint.py) and the forward driver on them.
 
-Run in a container that holds the reference read-only (its path in PLLM_REFERENCE, default /root/reference):
+Run in a container that holds the reference read-only (its path in the environment variable PLLM_REFERENCE, which must be set):
     python tests/golden/make_checkpoints.py
 The output is committed; no test reads the reference at run time.
 
@@ -20,7 +20,9 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("PLLM_REFERENCE", "/root/reference")
+REF = os.environ.get("PLLM_REFERENCE")
+if not REF:
+    sys.exit("set PLLM_REFERENCE to the reference's source tree (read-only)")
 sys.path.insert(0, os.path.join(REF, "src", "python"))
 sys.path.insert(0, os.path.join(REF, "tests"))
 import made_up  # noqa: E402  (the reference's own made-up models)

@@ -1,6 +1,6 @@
 """Generates tests/golden/golden.npz: the known answers the CPU oracle is pinned to before it is trusted.
 
-Run in a container that holds the reference read-only (its path in PLLM_REFERENCE, default /root/reference):
+Run in a container that holds the reference read-only (its path in the environment variable PLLM_REFERENCE, which must be set):
     python tests/golden/make_golden.py
 The output is committed; no test reads the reference at run time.
 
@@ -23,7 +23,9 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("PLLM_REFERENCE", "/root/reference")
+REF = os.environ.get("PLLM_REFERENCE")
+if not REF:
+    sys.exit("set PLLM_REFERENCE to the reference's source tree (read-only)")
 sys.path.insert(0, os.path.join(REF, "src", "python"))
 from engine import layers, packing  # noqa: E402  (the reference's own NumPy)
 

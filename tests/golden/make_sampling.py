@@ -2,7 +2,7 @@
 NumpySampler.drawing, the sampler the reference's sample kernel restates: kernels/kernel/sample.ts:1-2), to pin the
 oracle's sample (or_sample) and through it the device's.
 
-Run in a container that holds the reference read-only (its path in PLLM_REFERENCE, default /root/reference):
+Run in a container that holds the reference read-only (its path in the environment variable PLLM_REFERENCE, which must be set):
     python tests/golden/make_sampling.py
 The output is committed; no test reads the reference at run time.
 
@@ -15,7 +15,9 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("PLLM_REFERENCE", "/root/reference")
+REF = os.environ.get("PLLM_REFERENCE")
+if not REF:
+    sys.exit("set PLLM_REFERENCE to the reference's source tree (read-only)")
 sys.path.insert(0, os.path.join(REF, "src", "python"))
 from engine.sampler import NumpySampler, Sampling  # noqa: E402
 

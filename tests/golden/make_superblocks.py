@@ -2,7 +2,7 @@
 (src/python/convert/superblocks.py SUPERBLOCKS), to pin the oracle's reading of the ten types the reference's block
 kernels multiply (kernels/blocks/types.ts) and, through it, the device's.
 
-Run in a container that holds the reference read-only (its path in PLLM_REFERENCE, default /root/reference):
+Run in a container that holds the reference read-only (its path in the environment variable PLLM_REFERENCE, which must be set):
     python tests/golden/make_superblocks.py
 The output is committed; no test reads the reference at run time.
 
@@ -16,7 +16,9 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("PLLM_REFERENCE", "/root/reference")
+REF = os.environ.get("PLLM_REFERENCE")
+if not REF:
+    sys.exit("set PLLM_REFERENCE to the reference's source tree (read-only)")
 sys.path.insert(0, os.path.join(REF, "src", "python"))
 from convert.grids import codebooks  # noqa: E402
 from convert.superblocks import SUPERBLOCKS  # noqa: E402

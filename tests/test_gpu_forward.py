@@ -133,25 +133,6 @@ def test_qwen3_8b_shape_matches_oracle(layers):
     eng.close()
 
 
-@pytest.mark.parametrize("layers", [2])
-def test_chained_step_is_the_separate_launches(layers, monkeypatch):
-    """The step as chains of products in persistent launches (pllm_gemv_chain: wo, w1/w3, w2 and the next layer's
-    q/k/v in one) computes what the separate launches compute, to the bit: the same products, the same orders."""
-    from dataclasses import replace
-    from pllm.forward import QWEN3_8B
-    cfg = replace(QWEN3_8B, layers=layers, seq_len=64)
-    plain = Engine(cfg, seed=3)
-    monkeypatch.setenv("PLLM_CHAIN", "1")
-    chained = Engine(cfg, seed=3)
-    assert chained.chained and not plain.chained
-    for pos, tok in enumerate(np.random.default_rng(4).integers(0, cfg.vocab, 4)):
-        want = plain.forward(int(tok), pos)
-        got = chained.forward(int(tok), pos)
-        assert np.array_equal(got, want), (pos, np.abs(got - want).max())
-    plain.close()
-    chained.close()
-
-
 def test_next_token_is_the_logits_argmax():
     """The greedy step (argmax on the device, 4 bytes back) picks the argmax of the logits forward() returns."""
     cfg = SMALL_QWEN3

@@ -1,8 +1,9 @@
 """The attention variant for callers that cannot allocate device memory (pllm_attention_f16_noalloc): a caller that
 owns a fixed device arena, or runs where an allocation is not allowed, gets the same attention as attention_f16
 without handing it a scratch buffer; the partials live in the library's own 4 MiB device array. Checked through the
-C ABI against attention_f16 (the existing entry point, with its att scratch), within the attention's tolerance
-(1e-4 relative, 2e-5 absolute), on two calls in a row; and a shape whose partials exceed the array is refused.
+C ABI against attention_f16 (the existing entry point, with its att scratch) and against the oracle's attention
+(the reference's attentionOf restated on the CPU), within the attention's tolerance (1e-4 relative, 2e-5 absolute),
+on two calls in a row; and a shape whose partials exceed the array is refused.
 This file is collected last, so that a failure here comes after every other test has run."""
 import numpy as np
 import pytest
@@ -41,6 +42,8 @@ def test_noalloc_attention_matches_attention_f16():
         check("pllm_attention_f16_noalloc")
         a, b = want.download(np.float32), got.download(np.float32)
         np.testing.assert_allclose(b, a, rtol=1e-4, atol=2e-5, err_msg=f"call {call}")
+        ref, _ = O.attention(q, kc, vc, pos, nh, nkv, hs, half=True)
+        np.testing.assert_allclose(b, ref, rtol=1e-4, atol=2e-5, err_msg=f"call {call} against the oracle")
 
 
 def test_noalloc_attention_refuses_what_does_not_fit():
