@@ -243,11 +243,28 @@ void pllm_attention_step(uint64_t out, uint64_t qkv, uint64_t kc, uint64_t vc, u
                          int32_t capacity, int32_t nh, int32_t nkv, int32_t hs, int32_t half, float cap,
                          int32_t split_len, uint64_t q_norm, uint64_t k_norm, uint64_t cos_t, uint64_t sin_t, int32_t rot,
                          float eps, uint64_t bad, int32_t pdl);
+/* the same step for a batch of sequences in one launch: sequence z's q/k/v at qkv + z qkv_stride floats, its output at
+ * out + z out_stride floats, its float16 caches at kc / vc + z cache_stride bytes, its position pos_dev[z], its
+ * scratch the z-th of batch regions of pllm_attention_scratch_bytes rounded up to 256 (zero before their first use) */
+void pllm_attention_step_batch(uint64_t out, int64_t out_stride, uint64_t qkv, int64_t qkv_stride, uint64_t kc,
+                               uint64_t vc, int64_t cache_stride, uint64_t scratch, uint64_t pos_dev, int32_t batch,
+                               int32_t capacity, int32_t nh, int32_t nkv, int32_t hs, float cap, int32_t split_len,
+                               uint64_t q_norm, uint64_t k_norm, uint64_t cos_t, uint64_t sin_t, int32_t rot,
+                               float eps, uint64_t bad, int32_t pdl);
 /* attention at the device position over a cache of capacity positions; scratch: pllm_attention_scratch_bytes */
 uint64_t pllm_attention_scratch_bytes(int32_t nh, int32_t hs, int32_t capacity, int32_t split_len);
 void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t vc, uint64_t scratch, uint64_t pos_dev,
                         int32_t capacity, int32_t nh, int32_t nkv, int32_t hs, int32_t half, float cap,
                         int32_t split_len, int32_t pdl);
+
+/* count tokens of delta_rule's recurrence in one launch (a prompt's block, no counterpart in the reference, whose
+ * engine calls delta_rule a token at a time, forward/linear.ts:99-183): token t's inputs at c + t c_stride floats,
+ * its gates / delta at work + t work_stride, its outputs at out + t out_stride; state read once, the state after the
+ * last token written to next once; every token's numbers delta_rule's to the bit. vd % 16 == 0, 16-byte aligned
+ * states */
+void pllm_delta_rule_block(uint64_t out, int64_t out_stride, uint64_t state, uint64_t next, uint64_t c,
+                           int64_t c_stride, uint64_t work, int64_t work_stride, int32_t count, int32_t kh, int32_t kd,
+                           int32_t vd, int32_t vh, int32_t h0, int32_t h1);
 
 /* a bounded device-side wait (an mbarrier of the bulk-copy product) gave up since the last call: PLLM_ETIMEOUT (3),
  * else 0; reading it clears it (and, after a wait that gave up, puts the products' tile counters back to zero) */

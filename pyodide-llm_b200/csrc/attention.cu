@@ -37,7 +37,26 @@ struct AttArgs {
   float cap;
   int* counters;        // [nkv] slices done, zero between calls; null: a second kernel combines the slices
   int cs;               // the chunk kernel's cluster size (its CL form), 2..CS_MAX
+  // a batch of sequences (grid z; 1 for one): sequence z's out, q (and the Fuse's k, v), cache, partials and counts
+  // are these strides after sequence 0's (floats; the cache in bytes; the counts with the partials, in 4-byte
+  // words), and its position is pos_dev[z]
+  int batch;
+  long long z_out, z_q, z_kv, z_part;
 };
+
+// sequence z's arguments (grid z) from sequence 0's, each array assigned from the launch's own argument
+__device__ __forceinline__ AttArgs sequence_of(const AttArgs& a0, int z) {
+  AttArgs a = a0;
+  const long long zz = z;
+  a.out = a0.out + zz * a0.z_out;
+  a.q = a0.q + zz * a0.z_q;
+  a.kc = reinterpret_cast<const uint8_t*>(a0.kc) + zz * a0.z_kv;
+  a.vc = reinterpret_cast<const uint8_t*>(a0.vc) + zz * a0.z_kv;
+  a.pos_dev = a0.pos_dev ? a0.pos_dev + zz : nullptr;
+  a.part = a0.part ? a0.part + zz * a0.z_part : nullptr;
+  a.counters = a0.counters ? a0.counters + zz * a0.z_part : nullptr;
+  return a;
+}
 
 
 // What the forward driver's attention does before it reads the cache (FUSE): the per-head RMSNorm of q and k
@@ -56,6 +75,13 @@ struct Fuse {
   int rot;
   int* bad;             // non-finite keys or values written to a float16 cache are counted here (may be null)
 };
+
+__device__ __forceinline__ Fuse sequence_of(const Fuse& f0, const AttArgs& a0, int z) {
+  Fuse f = f0;
+  f.k = f0.k ? f0.k + (long long)z * a0.z_q : nullptr;
+  f.v = f0.v ? f0.v + (long long)z * a0.z_q : nullptr;
+  return f;
+}
 
 // tensor-core helpers (float16 caches): ldmatrix fragments and the m16n8k16 product with float32 accumulation
 __device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void* p) {
@@ -400,8 +426,10 @@ constexpr int PST = 24;  // halves a head's row of a warp's probabilities (confl
 constexpr int CS_MAX = 16;  // the largest cluster (a non-portable size)
 
 template <int KVM, bool FUSE, int MBM, bool CL, int W>
-__global__ void __launch_bounds__(32 * W, 1) attention_chunk_kernel(const AttArgs a, const Fuse f, const int ring) {
+__global__ void __launch_bounds__(32 * W, 1) attention_chunk_kernel(const AttArgs a0, const Fuse f0, const int ring) {
   extern __shared__ __align__(16) uint8_t att_smem[];
+  const AttArgs a = sequence_of(a0, blockIdx.z);
+  const Fuse f = sequence_of(f0, a0, blockIdx.z);
   constexpr int DL = MBM / 2;                          // a lane's values of a head: d = lane + 32 i (hs <= 32 DL)
   const int hs = a.hs, nmb = hs / 16;
   const int rowb = hs * 2 + 16;                        // a padded row of a chunk, bytes (conflict-free ldmatrix)
@@ -735,7 +763,8 @@ __global__ void __launch_bounds__(32 * W, 1) attention_chunk_kernel(const AttArg
 }
 
 // a block a head: the slices' partials combined
-__global__ void attention_combine_kernel(const AttArgs a) {
+__global__ void attention_combine_kernel(const AttArgs a0) {
+  const AttArgs a = sequence_of(a0, blockIdx.z);
   pdl_wait();
   const int pos = a.pos_dev ? *a.pos_dev : a.pos;
   const int count = pos + 1;
@@ -811,7 +840,7 @@ cudaError_t launch_cluster_cs(AttArgs a, const Fuse& f, const cudaLaunchConfig_t
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1] = base.numAttrs ? base.attrs[0] : attr[0];  // the dependent-launch attribute, where asked for
-  cfg.gridDim = dim3((unsigned)cs, a.nkv);
+  cfg.gridDim = dim3((unsigned)cs, a.nkv, a.batch > 1 ? a.batch : 1);
   cfg.attrs = attr;
   cfg.numAttrs = 1 + (base.numAttrs ? 1 : 0);
   if (fits) {
@@ -874,7 +903,7 @@ int g_cluster_attention = 1;
 
 void run_attention(const char* name, AttArgs a, bool half, bool pdl, const Fuse* f = nullptr) {
   const int kvm = a.nh / a.nkv;
-  const dim3 grid(a.nkv, a.nsplit);
+  const dim3 grid(a.nkv, a.nsplit, a.batch > 1 ? a.batch : 1);
   const size_t comb = a.counters ? (size_t)a.nsplit : 0;  // the combine's weights: kvm x nsplit floats
   cudaLaunchAttribute attr[1];
   cudaError_t e;
@@ -935,7 +964,8 @@ void run_attention(const char* name, AttArgs a, bool half, bool pdl, const Fuse*
     return;
   }
   if ((a.nsplit > 1 || a.pos_dev) && !a.counters) {
-    const cudaLaunchConfig_t cfg = launch_config(dim3(a.h1 - a.h0), a.hs >= 128 ? 128 : 64, 0, pdl, attr);
+    const cudaLaunchConfig_t cfg =
+        launch_config(dim3(a.h1 - a.h0, 1, a.batch > 1 ? a.batch : 1), a.hs >= 128 ? 128 : 64, 0, pdl, attr);
     e = cudaLaunchKernelEx(&cfg, attention_combine_kernel, a);
     if (e != cudaSuccess) pllm_fail(PLLM_ECUDA, "%s: combine launch failed: %s", name, cudaGetErrorString(e));
   }
@@ -1420,6 +1450,57 @@ PLLM_API void pllm_attention_step(uint64_t out, uint64_t qkv, uint64_t kc, uint6
   f.rot = rot;
   f.bad = dptr<int>(bad);
   run_attention("pllm_attention_step", a, half != 0, pdl != 0, &f);
+}
+
+// The same step for a batch of sequences in one launch (grid z a sequence): sequence z's q/k/v at qkv + z
+// qkv_stride floats, its output at out + z out_stride floats, its caches at kc / vc + z cache_stride bytes, its
+// position pos_dev[z], its scratch the z-th of batch regions of pllm_attention_scratch_bytes rounded up to 256 bytes;
+// a float16 cache (each sequence its own positions: no cache row is shared)
+PLLM_API void pllm_attention_step_batch(uint64_t out, int64_t out_stride, uint64_t qkv, int64_t qkv_stride,
+                                        uint64_t kc, uint64_t vc, int64_t cache_stride, uint64_t scratch,
+                                        uint64_t pos_dev, int32_t batch, int32_t capacity, int32_t nh, int32_t nkv,
+                                        int32_t hs, float cap, int32_t split_len, uint64_t q_norm, uint64_t k_norm,
+                                        uint64_t cos_t, uint64_t sin_t, int32_t rot, float eps, uint64_t bad,
+                                        int32_t pdl) {
+  if (!check_heads("pllm_attention_step_batch", nh, nkv, hs, 0, nh)) return;
+  const uint64_t per = (pllm_attention_scratch_bytes(nh, hs, capacity, split_len) + 255) & ~255ull;
+  PLLM_REQUIRE(capacity > 0 && split_len > 0 && split_len <= 2048 && hs % 2 == 0 && pos_dev && batch >= 1 &&
+                   batch <= 65535 && out_stride >= (int64_t)nh * hs && qkv_stride >= (int64_t)(nh + 2 * nkv) * hs &&
+                   cache_stride % 16 == 0 && cache_stride >= (int64_t)capacity * nkv * hs * 2 && per % 4 == 0,
+               "pllm_attention_step_batch: batch %d capacity %d strides %lld %lld %lld", batch, capacity,
+               (long long)out_stride, (long long)qkv_stride, (long long)cache_stride);
+  AttArgs a = {};
+  a.out = dptr<float>(out);
+  a.q = dptr<const float>(qkv);
+  a.kc = dptr<const void>(kc);
+  a.vc = dptr<const void>(vc);
+  a.part = dptr<float>(scratch);
+  a.pos_dev = dptr<const int>(pos_dev);
+  a.nh = nh;
+  a.nkv = nkv;
+  a.hs = hs;
+  a.h0 = 0;
+  a.h1 = nh;
+  a.split_len = split_len;
+  a.nsplit = (capacity + split_len - 1) / split_len;
+  a.cap = cap;
+  a.counters = dptr<int>(scratch + partial_bytes(nh, hs, capacity, split_len));
+  a.batch = batch;
+  a.z_out = out_stride;
+  a.z_q = qkv_stride;
+  a.z_kv = cache_stride;
+  a.z_part = (long long)(per / 4);
+  Fuse f = {};
+  f.k = dptr<const float>(qkv) + (long long)nh * hs;
+  f.v = f.k + (long long)nkv * hs;
+  f.qn = dptr<const float>(q_norm);
+  f.kn = dptr<const float>(k_norm);
+  f.cos_t = dptr<const float>(cos_t);
+  f.sin_t = dptr<const float>(sin_t);
+  f.eps = eps;
+  f.rot = rot;
+  f.bad = dptr<int>(bad);
+  run_attention("pllm_attention_step_batch", a, true, pdl != 0, &f);
 }
 
 // 1: the forward driver's float16 attention by clusters (the default); 0: by slices and the last slice's combine.

@@ -110,7 +110,7 @@ __host__ __device__ constexpr size_t smem_bytes(int K, int MT) {
 // takes the shuffle).
 template <int PRO>
 __device__ __forceinline__ void quantize_pair(const GemvArgs& a, const float4* xv, const float4* wv, float rs, int g,
-                                              int h, int t, int8_t* sq, float* ss) {
+                                              int h, int t, int8_t* sq, float* ss, size_t sq_stride) {
   const int K = a.K, ng = K / 32;
   float u[16];
 #pragma unroll
@@ -150,7 +150,7 @@ __device__ __forceinline__ void quantize_pair(const GemvArgs& a, const float4* x
     }
     packed[k] = word;
   }
-  *reinterpret_cast<int4*>(sq + (size_t)t * K + 32 * g + 16 * h) =
+  *reinterpret_cast<int4*>(sq + (size_t)t * sq_stride + 32 * g + 16 * h) =
       make_int4((int)packed[0], (int)packed[1], (int)packed[2], (int)packed[3]);
   if (h == 0) ss[t * ng + g] = scale;
 }
@@ -180,17 +180,19 @@ __device__ __forceinline__ float4 x_vec(const GemvArgs& a, const Xchg* xg, int t
   return v;
 }
 
+// sq_stride: bytes from a token's activations to the next's (0: K; the batched tensor-core product pads its rows)
 template <int FMT, int MT, int PRO, class SYNC = CtaSync>
 __device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, float* ss, int32_t* sm,
-                                                 const Xchg* xg = nullptr) {
+                                                 const Xchg* xg = nullptr, size_t sq_stride = 0) {
   const SYNC sync;
   const int K = a.K, ng = K / 32;
+  const size_t SQ = sq_stride ? sq_stride : (size_t)K;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (PRO == PRO_Q) {
     for (int t = 0; t < MT; t++) {
       if (t >= a.count) break;
       const int4* src = reinterpret_cast<const int4*>(a.xq + t * a.xq_stride);
-      int4* dst = reinterpret_cast<int4*>(sq + (size_t)t * K);
+      int4* dst = reinterpret_cast<int4*>(sq + (size_t)t * SQ);
       const int bias4 = a.bias ? 0x40404040 : 0;
       for (int i = threadIdx.x; i < K / 16; i += THREADS) {
         int4 v = src[i];
@@ -260,7 +262,7 @@ __device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, 
       constexpr int QP = NORM ? PRO_RMS : PRO;
 #pragma unroll
       for (int r = 0; r < RMAX; r++) {
-        if (r < rounds) quantize_pair<QP>(a, v[r], w[r], rs, pair + 128 * r, h, t, sq, ss);
+        if (r < rounds) quantize_pair<QP>(a, v[r], w[r], rs, pair + 128 * r, h, t, sq, ss, SQ);
       }
       for (int r = RMAX; r < rounds; r++) {
         const int g = pair + 128 * r;
@@ -269,12 +271,12 @@ __device__ __forceinline__ void load_activations(const GemvArgs& a, int8_t* sq, 
           xv[k] = g < ng ? x_vec<PRO>(a, xg, t, (32 * g + 16 * h) / 4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
           wv[k] = (NORM && g < ng) ? __ldg(n4 + (32 * g + 16 * h) / 4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        quantize_pair<QP>(a, xv, wv, rs, g, h, t, sq, ss);
+        quantize_pair<QP>(a, xv, wv, rs, g, h, t, sq, ss, SQ);
       }
     }
   }
   for (int t = a.count; t < MT; t++) {  // tokens past count: zeros (their outputs are not written)
-    for (int i = threadIdx.x; i < K; i += THREADS) sq[(size_t)t * K + i] = 0;
+    for (int i = threadIdx.x; i < K; i += THREADS) sq[(size_t)t * SQ + i] = 0;
     for (int i = threadIdx.x; i < ng; i += THREADS) ss[t * ng + i] = 0.0f;
   }
 }

@@ -116,6 +116,72 @@ __device__ __forceinline__ int group_dot(const uint8_t* w, int swz, const int4 x
   return g0 + g1;
 }
 
+// The producer (one thread): the tiles' stages into the ring, dealt by tickets or as this CTA's share (see the file's
+// head). PAD: each row at KS + 16 bytes from the one before in the stage (one copy a row: the batched tensor-core
+// consumer's fragment reads are then free of bank conflicts), the scales after TRP such rows.
+template <int PHASES, bool PAD>
+__device__ __forceinline__ void produce(const GemvArgs& a, const TmaPlan& p, uint64_t* full, uint64_t* empty, int* hdr,
+                                        uint8_t* stage0) {
+  const int S = p.stages, KS = p.ks, chunks = p.chunks, K = a.K, ng = K / 32;
+  const int RS = PAD ? KS + 16 : KS;
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  const unsigned tiles = (unsigned)((a.r1 - a.r0 + TRP - 1) / TRP);
+  unsigned* ticket = g_tickets + p.slot;
+  long long lo = a.r0, hi = a.r1;  // the rows this CTA streams: all of them by tickets, or its own share
+  if (!p.tickets) cta_rows(a, lo, hi);
+  unsigned next = p.tickets ? atomicAdd(ticket, 1u) : 0u;
+  long long it = 0;
+  for (long long ts = lo;;) {
+    long long t;
+    if (p.tickets) {
+      if (next >= tiles) break;
+      t = a.r0 + (long long)next * TRP;
+      next = atomicAdd(ticket, 1u);  // the following tile's ticket, on its way while this tile streams
+    } else {
+      if (ts >= hi) break;
+      t = ts;
+      ts += TRP;
+    }
+    const int n = (int)min((long long)TRP, hi - t);
+    for (int ph = 0; ph < PHASES; ph++) {
+      const long long row0 = t + (ph ? a.pair : 0);
+      for (int c = 0; c < chunks; c++, it++) {
+        const int slot = (int)(it % S);
+        if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
+        uint8_t* w = stage0 + (size_t)slot * p.stage_bytes;
+        float* sc = reinterpret_cast<float*>(w + (size_t)TRP * RS);
+        // the tile's first row (from r0) and its rows, seen by the consumers once the stage's barrier completes
+        // (the expect_tx arrive releases it)
+        hdr[slot] = (int)(((t - a.r0) << 4) | n);
+        mbar_expect_tx(&full[slot], (unsigned)(n * (KS + KS / 8)));
+        if (chunks == 1 && !PAD) {
+          bulk_copy(w, a.wq + row0 * K, (unsigned)(n * K), &full[slot], policy);
+          bulk_copy(sc, reinterpret_cast<const float*>(a.ws) + row0 * ng, (unsigned)(n * ng * 4), &full[slot], policy);
+        } else {
+          for (int r = 0; r < n; r++)
+            bulk_copy(w + (size_t)r * RS, a.wq + (row0 + r) * K + (long long)c * KS, (unsigned)KS, &full[slot], policy);
+          if (chunks == 1) {
+            bulk_copy(sc, reinterpret_cast<const float*>(a.ws) + row0 * ng, (unsigned)(n * ng * 4), &full[slot],
+                      policy);
+          } else {
+            for (int r = 0; r < n; r++)
+              bulk_copy(sc + (size_t)r * (KS / 32),
+                        reinterpret_cast<const float*>(a.ws) + (row0 + r) * ng + (long long)c * (KS / 32),
+                        (unsigned)(KS / 8), &full[slot], policy);
+          }
+        }
+      }
+    }
+  }
+  // the end: a stage without rows
+  const int slot = (int)(it % S);
+  if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
+  hdr[slot] = -1;
+  mbar_arrive(&full[slot]);
+  if (p.tickets && next == tiles + gridDim.x - 1) atomicExch(ticket, 0u);  // the last ticket of the launch
+}
+
 template <int MT, int PRO, int EPI>
 __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs a, const TmaPlan p, const Xchg xg) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -143,61 +209,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   __syncthreads();
 
   if (warp == NC) {  // ---- the producer
-    if (lane == 0) {
-      uint64_t policy;
-      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-      const unsigned tiles = (unsigned)((a.r1 - a.r0 + TRP - 1) / TRP);
-      unsigned* ticket = g_tickets + p.slot;
-      long long lo = a.r0, hi = a.r1;  // the rows this CTA streams: all of them by tickets, or its own share
-      if (!p.tickets) cta_rows(a, lo, hi);
-      unsigned next = p.tickets ? atomicAdd(ticket, 1u) : 0u;
-      long long it = 0;
-      for (long long ts = lo;;) {
-        long long t;
-        if (p.tickets) {
-          if (next >= tiles) break;
-          t = a.r0 + (long long)next * TRP;
-          next = atomicAdd(ticket, 1u);  // the following tile's ticket, on its way while this tile streams
-        } else {
-          if (ts >= hi) break;
-          t = ts;
-          ts += TRP;
-        }
-        const int n = (int)min((long long)TRP, hi - t);
-        for (int ph = 0; ph < PHASES; ph++) {
-          const long long row0 = t + (ph ? a.pair : 0);
-          for (int c = 0; c < chunks; c++, it++) {
-            const int slot = (int)(it % S);
-            if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
-            uint8_t* w = stage0 + (size_t)slot * p.stage_bytes;
-            float* sc = reinterpret_cast<float*>(w + (size_t)TRP * KS);
-            // the tile's first row (from r0) and its rows, seen by the consumers once the stage's barrier completes
-            // (the expect_tx arrive releases it)
-            hdr[slot] = (int)(((t - a.r0) << 4) | n);
-            mbar_expect_tx(&full[slot], (unsigned)(n * (KS + KS / 8)));
-            if (chunks == 1) {
-              bulk_copy(w, a.wq + row0 * K, (unsigned)(n * K), &full[slot], policy);
-              bulk_copy(sc, reinterpret_cast<const float*>(a.ws) + row0 * ng, (unsigned)(n * ng * 4), &full[slot],
-                        policy);
-            } else {
-              for (int r = 0; r < n; r++) {
-                bulk_copy(w + (size_t)r * KS, a.wq + (row0 + r) * K + (long long)c * KS, (unsigned)KS, &full[slot],
-                          policy);
-                bulk_copy(sc + (size_t)r * (KS / 32),
-                          reinterpret_cast<const float*>(a.ws) + (row0 + r) * ng + (long long)c * (KS / 32),
-                          (unsigned)(KS / 8), &full[slot], policy);
-              }
-            }
-          }
-        }
-      }
-      // the end: a stage without rows
-      const int slot = (int)(it % S);
-      if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
-      hdr[slot] = -1;
-      mbar_arrive(&full[slot]);
-      if (p.tickets && next == tiles + gridDim.x - 1) atomicExch(ticket, 0u);  // the last ticket of the launch
-    }
+    if (lane == 0) produce<PHASES, false>(a, p, full, empty, hdr, stage0);
     return;
   }
 
@@ -297,6 +309,208 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   }
 }
 
+// ---- the batched form (3..16 tokens, the registry's tiles and a batch of sequences): each group of 32 of a stage's
+// rows is one tensor-core product (mma.sync m16n8k32, int8 x int8 -> int32, 16 tokens x 8 rows), whose int32 are the
+// exact group sums (the same integers as every other form; tokens past count are zeros), each scaled by ws x xs and
+// summed in float32. The consumer warps split a stage's groups (warp w: groups w, w + 8, ...), so each holds a part of
+// the tile's 16 x 8 sums; at the end of a tile's phase they add their parts in shared memory, in warp order, behind a
+// bounded barrier, and 128 threads write the outputs. Activations: ASMEM, all tokens in shared memory (rows padded by
+// 16 bytes: conflict-free fragment reads), made by the prologue; else (K too long for shared memory) the caller's
+// quantized activations read from global memory (L2) fragment by fragment.
+constexpr int MB = 16;                      // tokens of the batched form
+constexpr int RED_BYTES = 2 * NC * 128 * 4;  // two buffers of the warps' parts
+
+__device__ __forceinline__ void mma_s8(int c[4], const uint32_t a[4], const uint32_t b[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t r[2], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
+}
+// an exact int32 of magnitude below 2^22 as float32: its bits added to those of 1.5 x 2^23, that float less 1.5 x 2^23
+__device__ __forceinline__ float exact_float(int v) {
+  return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
+}
+
+// the consumer warps' barrier, bounded: false (and the status word set) past the bound. bar: [0] arrivals, [1] the
+// generation.
+__device__ __forceinline__ bool consumers_meet(unsigned* bar) {
+  __syncwarp();
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) {
+    volatile unsigned* gen = bar + 1;
+    const unsigned g0 = *gen;
+    __threadfence_block();
+    if (atomicAdd(bar, 1u) == NC - 1) {
+      bar[0] = 0;
+      __threadfence_block();
+      atomicAdd(bar + 1, 1u);
+    } else {
+      long long i = 0;
+      while (*gen == g0)
+        if (++i > WAIT_BOUND) {
+          atomicExch(&g_pllm_status, PLLM_ETIMEOUT);
+          ok = 0;
+          break;
+        }
+    }
+    __threadfence_block();
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
+template <int PRO, int EPI, bool ASMEM>
+__global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_mma_kernel(const GemvArgs a, const TmaPlan p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int S = p.stages, KS = p.ks, chunks = p.chunks, K = a.K, ng = K / 32, RS = KS + 16, AS = K + 16;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + S;
+  int* hdr = reinterpret_cast<int*>(smem + 16 * S);
+  unsigned* bar = reinterpret_cast<unsigned*>(smem + 20 * S);  // [2]
+  float* red = reinterpret_cast<float*>(smem + ((20 * S + 8 + 127) & ~127));
+  uint8_t* act = reinterpret_cast<uint8_t*>(red) + RED_BYTES;
+  int8_t* sq = reinterpret_cast<int8_t*>(act);                         // ASMEM: [MB][AS]
+  float* ss = reinterpret_cast<float*>(act + (size_t)MB * AS);         //        [MB][ng]
+  float* sst = ss + MB * ng;                                           //        [ng][MB]: by group
+  uint8_t* stage0 = act + p.act_bytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  constexpr int PHASES = EPI == EPI_SWIGLU ? 2 : 1;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NC);
+    }
+    bar[0] = bar[1] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == NC) {
+    if (lane == 0) produce<PHASES, true>(a, p, full, empty, hdr, stage0);
+    return;
+  }
+  pdl_wait();
+  if (ASMEM) {
+    load_activations<F_Q8, MB, PRO, ConsumerSync>(a, sq, ss, nullptr, nullptr, (size_t)AS);
+    consumer_sync();
+    for (int i = tid; i < MB * ng; i += NC * 32) sst[(i % ng) * MB + i / ng] = ss[i];
+    consumer_sync();
+  }
+  pdl_launch_dependents();
+  const int g = lane >> 2, t4 = lane & 3;
+  // ldmatrix rows: A (tokens (lane & 7) + 8 ((lane >> 3) & 1), bytes 16 (lane >> 4) of a group), B (weight rows lane & 7,
+  // bytes 16 ((lane >> 3) & 1))
+  const int a_tok = (lane & 7) + 8 * ((lane >> 3) & 1), a_off = 16 * (lane >> 4);
+  const int b_row = lane & 7, b_off = 16 * ((lane >> 3) & 1);
+  // ASMEM off: this lane's tokens g and g + 8 in the caller's activations (q - 64 where they are biased)
+  const uint8_t* xg0 = a.xq + (long long)g * a.xq_stride;
+  const uint8_t* xg1 = a.xq + (long long)(g + 8) * a.xq_stride;
+  const float* xs0 = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(a.xs) + (long long)g * a.xs_stride);
+  const float* xs1 =
+      reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(a.xs) + (long long)(g + 8) * a.xs_stride);
+  const bool tok0 = g < a.count, tok1 = g + 8 < a.count;
+  const unsigned bias4 = a.bias ? 0x40404040u : 0u;
+  float h1 = 0.0f;  // EPI_SWIGLU: thread tid < 128's w1 result
+  int buf = 0;
+  long long it = 0;
+  for (;;) {
+    int tile = 0;
+    for (int ph = 0; ph < PHASES; ph++) {
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int c = 0; c < chunks; c++, it++) {
+        const int slot = (int)(it % S);
+        if (!mbar_wait(&full[slot], (unsigned)(it / S) & 1)) return;  // every consumer warp gives up at this stage
+        tile = hdr[slot];
+        if (tile < 0) return;  // no more tiles (only ever the first stage of a tile)
+        const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes;
+        const float* sc = reinterpret_cast<const float*>(w + (size_t)TRP * RS);
+        const int gs = KS / 32, u0 = c * gs;
+        const float* ws0 = sc + (2 * t4) * gs;
+        const float* ws1 = ws0 + gs;
+        for (int u = warp; u < gs; u += NC) {
+          uint32_t af[4], bf[2];
+          float x0, x1;
+          if (ASMEM) {
+            ldsm_x4(af, sq + (size_t)a_tok * AS + (size_t)(u0 + u) * 32 + a_off);
+            x0 = sst[(u0 + u) * MB + g];
+            x1 = sst[(u0 + u) * MB + g + 8];
+          } else {
+            const long long o = (long long)(u0 + u) * 32 + 4 * t4;
+            af[0] = tok0 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg0 + o)), bias4) : 0u;
+            af[1] = tok1 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg1 + o)), bias4) : 0u;
+            af[2] = tok0 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg0 + o + 16)), bias4) : 0u;
+            af[3] = tok1 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg1 + o + 16)), bias4) : 0u;
+            x0 = tok0 ? __ldg(xs0 + u0 + u) : 0.0f;
+            x1 = tok1 ? __ldg(xs1 + u0 + u) : 0.0f;
+          }
+          ldsm_x2(bf, w + (size_t)b_row * RS + (size_t)u * 32 + b_off);
+          int cf[4] = {0, 0, 0, 0};
+          mma_s8(cf, af, bf);
+          const float w0 = ws0[u], w1 = ws1[u];
+          acc[0] = fmaf(exact_float(cf[0]), __fmul_rn(w0, x0), acc[0]);
+          acc[1] = fmaf(exact_float(cf[1]), __fmul_rn(w1, x0), acc[1]);
+          acc[2] = fmaf(exact_float(cf[2]), __fmul_rn(w0, x1), acc[2]);
+          acc[3] = fmaf(exact_float(cf[3]), __fmul_rn(w1, x1), acc[3]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+      // the tile's phase is done: the warps' parts added in warp order, a thread an output
+      float* rb = red + buf * (NC * 128);
+      *reinterpret_cast<float4*>(rb + warp * 128 + 4 * lane) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      if (!consumers_meet(bar)) return;
+      if (tid < 128) {
+        float v = 0.0f;
+#pragma unroll
+        for (int w2 = 0; w2 < NC; w2++) v += rb[w2 * 128 + tid];
+        const int el = tid >> 2, i = tid & 3;
+        const int token = (el >> 2) + (i >= 2 ? 8 : 0), r = 2 * (el & 3) + (i & 1);
+        if (r < (tile & 15) && token < a.count) {
+          const long long row = a.r0 + (tile >> 4) + r;
+          float* o = a.out + token * a.out_stride + row;
+          if (EPI == EPI_SWIGLU) {
+            if (ph == 0) h1 = v;
+            else *o = (h1 / (1.0f + expf(-h1))) * v;
+          } else if (EPI == EPI_ADD) {
+            *o += v;
+          } else {
+            *o = v;
+          }
+        }
+      }
+      buf ^= 1;
+    }
+  }
+}
+
+template <int PRO, int EPI, bool ASMEM>
+bool launch_mma(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl) {
+  auto kernel = gemv_tma_mma_kernel<PRO, EPI, ASMEM>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return false;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)gemv_tma_grid(a.r1 - a.r0, EPI));
+  cfg.blockDim = dim3(TMA_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = pllm_stream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a, p);
+  if (e != cudaSuccess) pllm_fail(PLLM_ECUDA, "gemv_tma (batched) launch: %s", cudaGetErrorString(e));
+  return true;
+}
+
 template <int MT, int PRO, int EPI>
 bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl, const Xchg& xg) {
   auto kernel = gemv_tma_kernel<MT, PRO, EPI>;
@@ -351,6 +565,12 @@ int* status_word() {
   return addr[dev];
 }
 
+// a device's launches take its ticket counters in turn (from any host thread)
+unsigned next_ticket_slot(int dev) {
+  static std::atomic<unsigned> next_slot[64];
+  return next_slot[dev & 63].fetch_add(1u, std::memory_order_relaxed);
+}
+
 int gemv_tma_grid(long long rows, int epi) {
   (void)epi;  // a tile is TRP rows of one matrix in every form (EPI_SWIGLU: of w1, then of w3)
   const long long tiles = (rows + TRP - 1) / TRP;
@@ -358,14 +578,70 @@ int gemv_tma_grid(long long rows, int epi) {
   return (int)(tiles < sms ? tiles : sms);
 }
 
-// The bulk-copy product for int8 weights at 1 or 2 tokens; false where it does not apply (the caller then takes the
+// The batched form (3..16 tokens): stages of at most 4096 columns (rows padded), the activations in shared memory
+// where they fit beside two stages, else (the caller's quantized activations only) read from global memory.
+bool gemv_tma_batched(const GemvArgs& a, int pro, int epi, bool pdl) {
+  const int K = a.K;
+  if (epi > EPI_SWIGLU || ((uintptr_t)a.xq & 3)) return false;
+  TmaPlan p = {};
+  p.chunks = (K + 4095) / 4096;
+  while (K % (p.chunks * 128)) p.chunks++;
+  p.ks = K / p.chunks;
+  p.stage_bytes = (TRP * (p.ks + 16) + TRP * (p.ks / 32) * 4 + 127) & ~127;
+  const int head = (20 * 8 + 8 + 127) & ~127;  // the barriers, headers and meeting counts of up to 8 stages
+  const int most = 227 * 1024;
+  int act = (int)(((size_t)MB * (K + 16) + 2 * (size_t)MB * (K / 32) * 4 + 127) & ~127);
+  const bool asmem = head + RED_BYTES + act + 2 * p.stage_bytes <= most;
+  if (!asmem) {
+    if (pro != PRO_Q || (a.xq_stride & 3) || (a.xs_stride & 3)) return false;
+    act = 0;
+  }
+  p.act_bytes = act;
+  int S = (most - head - RED_BYTES - act) / p.stage_bytes;
+  if (S > 8) S = 8;
+  if (S < 2) return false;
+  p.stages = S;
+  const size_t smem = (size_t)head + RED_BYTES + act + (size_t)S * p.stage_bytes;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  p.slot = (int)(next_ticket_slot(dev) % TICKET_SLOTS);
+  p.tickets = p.chunks == 1;
+#define CASE(P, E) \
+  if (pro == P && epi == E) return asmem ? launch_mma<P, E, true>(a, p, smem, pdl) : launch_mma<P, E, false>(a, p, smem, pdl);
+  CASE(PRO_Q, EPI_STORE) CASE(PRO_Q, EPI_ADD) CASE(PRO_Q, EPI_SWIGLU)
+#undef CASE
+#define CASE(P, E) \
+  if (pro == P && epi == E) return asmem ? launch_mma<P, E, true>(a, p, smem, pdl) : false;
+  CASE(PRO_RMS, EPI_STORE) CASE(PRO_RMS, EPI_ADD) CASE(PRO_RMS, EPI_SWIGLU)
+  CASE(PRO_QUANT, EPI_STORE) CASE(PRO_QUANT, EPI_ADD) CASE(PRO_QUANT, EPI_SWIGLU)
+#undef CASE
+  return false;
+}
+
+// The bulk-copy product for int8 weights at 1 to 16 tokens; false where it does not apply (the caller then takes the
 // register-streaming kernel).
 bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg* xg) {
   const bool tp = pro == PRO_RMS_SUM || epi == EPI_SEND;
   if (tp != (xg != nullptr)) return false;
-  if (g_gemv_mode == 1 || fmt != F_Q8 || a.count < 1 || a.count > 2 || (tp && a.count != 1)) return false;
+  if (g_gemv_mode == 1 || fmt != F_Q8 || a.count < 1 || (tp && a.count != 1)) return false;
   const int K = a.K;
   if (K % 128 || ((uintptr_t)a.wq & 15) || ((uintptr_t)a.ws & 15)) return false;
+  if (a.count > 2) {  // the batched form, in passes of 16 tokens (each pass streams the rows again)
+    for (int t0 = 0; t0 < a.count; t0 += MB) {
+      GemvArgs b = a;
+      b.count = a.count - t0 < MB ? a.count - t0 : MB;
+      b.out = a.out + t0 * a.out_stride;
+      b.xq = a.xq + t0 * a.xq_stride;
+      b.xs = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(a.xs) + t0 * a.xs_stride);
+      b.x = a.x + t0 * a.x_stride;
+      if (!gemv_tma_batched(b, pro, epi, pdl)) {
+        if (t0 == 0) return false;  // the register kernel instead
+        pllm_fail(PLLM_ECUDA, "gemv_tma: a pass of the batched form did not launch");
+        return true;
+      }
+    }
+    return true;
+  }
   TmaPlan p = {};
   p.chunks = (K + 8191) / 8192;
   while (K % (p.chunks * 128)) p.chunks++;
@@ -388,8 +664,7 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
   }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-  static std::atomic<unsigned> next_slot[64];  // a device's launches take its ticket counters in turn (any thread)
-  p.slot = (int)(next_slot[dev].fetch_add(1u, std::memory_order_relaxed) % TICKET_SLOTS);
+  p.slot = (int)(next_ticket_slot(dev) % TICKET_SLOTS);
   // rows cut into chunks make tiles of two stages or more, the last of which ends the launch late: fixed shares there
   p.tickets = p.chunks == 1;
 #define CASE(M, P, E) \

@@ -96,6 +96,63 @@ __global__ void delta_rule_kernel(float* out, const float* __restrict__ state, f
   }
 }
 
+// The state once through shared memory: a CTA a (value head, DR_COLS columns); the columns of every row of the head's
+// state staged by 16-byte asynchronous copies (read once), then thread j makes column j's chains in the reference's
+// order (rows ascending, every operation rounded alone) for each of count tokens in turn, the state staying in shared
+// memory between them; the last token's state written to next (written once). Token t's inputs at c + t c_stride,
+// its gates and delta at work + t work_stride, its outputs at out + t out_stride (floats).
+constexpr int DR_COLS = 16;
+__device__ __forceinline__ void dr_cp16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__global__ void __launch_bounds__(128) delta_rule_tile_kernel(float* out, long long out_stride,
+                                                              const float* __restrict__ state, float* __restrict__ next,
+                                                              const float* __restrict__ c, long long c_stride,
+                                                              float* work, long long work_stride, int count, int kh,
+                                                              int kd, int vd, int vh, int h0) {
+  extern __shared__ __align__(16) float tile[];  // [kd][DR_COLS]
+  const int h = h0 + blockIdx.x, j0 = blockIdx.y * DR_COLS, j = threadIdx.x;
+  const int key = h / (vh / kh);
+  const float* from = state + (long long)h * kd * vd + j0;
+  float* to = next + (long long)h * kd * vd + j0;
+  constexpr int P = DR_COLS / 4;  // 16-byte pieces a row of the tile
+  for (int e = threadIdx.x; e < kd * P; e += blockDim.x) {
+    const int i = e / P, p = e % P;
+    dr_cp16(tile + i * DR_COLS + 4 * p, from + (long long)i * vd + 4 * p);
+  }
+  asm volatile("cp.async.commit_group;\ncp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  if (j < DR_COLS) {
+    for (int t = 0; t < count; t++) {
+      const float* ct = c + t * c_stride;
+      const float* q = ct + (long long)key * kd;
+      const float* k = ct + (long long)(kh + key) * kd;
+      const float* v = ct + (long long)(2 * kh) * kd + (long long)h * vd;
+      float* wt = work + t * work_stride;
+      const float beta = wt[h], decay = wt[vh + h];
+      float d = 0.0f;
+#pragma unroll 8
+      for (int i = 0; i < kd; i++) d = __fadd_rn(d, __fmul_rn(k[i], __fmul_rn(tile[i * DR_COLS + j], decay)));
+      d = __fmul_rn(__fsub_rn(v[j0 + j], d), beta);
+      wt[2 * (long long)vh + (long long)h * vd + j0 + j] = d;
+      float acc = 0.0f;
+#pragma unroll 8
+      for (int i = 0; i < kd; i++) {
+        const float s = __fadd_rn(__fmul_rn(tile[i * DR_COLS + j], decay), __fmul_rn(k[i], d));
+        tile[i * DR_COLS + j] = s;
+        acc = __fadd_rn(acc, __fmul_rn(q[i], s));
+      }
+      out[t * out_stride + (long long)h * vd + j0 + j] = acc;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < kd * P; e += blockDim.x) {
+    const int i = e / P, p = e % P;
+    *reinterpret_cast<float4*>(to + (long long)i * vd + 4 * p) = *reinterpret_cast<const float4*>(tile + i * DR_COLS + 4 * p);
+  }
+}
+
 __global__ void embed_q8_kernel(float* x, const int8_t* __restrict__ emb, const float* __restrict__ scales,
                                 const int32_t* __restrict__ tokens, int token, int dim, long long stride) {
   const long long t = tokens ? tokens[blockIdx.y] : token;
@@ -104,6 +161,21 @@ __global__ void embed_q8_kernel(float* x, const int8_t* __restrict__ emb, const 
     const long long at = t * dim + i;
     xo[i] = __fmul_rn((float)emb[at], scales[at / 32]);
   }
+}
+
+void launch_delta_tiles(uint64_t out, long long out_stride, uint64_t state, uint64_t next, uint64_t c,
+                        long long c_stride, uint64_t work, long long work_stride, int count, int kh, int kd, int vd,
+                        int vh, int h0, int h1) {
+  const size_t smem = (size_t)kd * DR_COLS * 4;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(delta_rule_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+    pllm_fail(PLLM_ECUDA, "delta_rule: %zu bytes of shared memory", smem);
+    return;
+  }
+  delta_rule_tile_kernel<<<dim3(h1 - h0, vd / DR_COLS), 128, smem, pllm_stream()>>>(
+      dptr<float>(out), out_stride, dptr<const float>(state), dptr<float>(next), dptr<const float>(c), c_stride,
+      dptr<float>(work), work_stride, count, kh, kd, vd, vh, h0);
+  PLLM_LAUNCHED("delta_rule");
 }
 
 unsigned grid_of(int n) {
@@ -173,11 +245,29 @@ PLLM_API void delta_rule(uint64_t out, uint64_t state, uint64_t next, uint64_t c
   PLLM_REQUIRE(h0 >= 0 && h1 >= h0 && h1 <= vh, "delta_rule: heads %d..%d of %d", h0, h1, vh);
   PLLM_REQUIRE(state != next, "delta_rule: state and next must be apart (the reference writes next only)");
   if (h1 == h0) return;
-  const int threads = vd >= 256 ? 256 : ((vd + 31) / 32) * 32;
+  if (vd % DR_COLS == 0 && !(state & 15) && !(next & 15) && (size_t)kd * DR_COLS * 4 <= 200 * 1024) {
+    launch_delta_tiles(out, 0, state, next, c, 0, work, 0, 1, kh, kd, vd, vh, h0, h1);
+    return;
+  }
+  const int threads = vd >= 256 ? 256 : ((vd + 31) / 32) * 32;  // other widths: a block a head, the state read twice
   delta_rule_kernel<<<h1 - h0, threads, 0, pllm_stream()>>>(dptr<float>(out), dptr<const float>(state),
                                                            dptr<float>(next), dptr<const float>(c), dptr<float>(work),
                                                            kh, kd, vd, vh, h0);
   PLLM_LAUNCHED("delta_rule");
+}
+
+// count tokens of the recurrence in one launch (a prompt's block): token t's inputs at c + t c_stride floats, its
+// gates, delta and outputs at work / out + t (work_stride, out_stride) floats; state is read once and the state after
+// the last token written to next once (the states between stay on the chip). Every token's numbers are delta_rule's.
+PLLM_API void pllm_delta_rule_block(uint64_t out, int64_t out_stride, uint64_t state, uint64_t next, uint64_t c,
+                                    int64_t c_stride, uint64_t work, int64_t work_stride, int32_t count, int32_t kh,
+                                    int32_t kd, int32_t vd, int32_t vh, int32_t h0, int32_t h1) {
+  PLLM_REQUIRE(kh > 0 && vh > 0 && vh % kh == 0 && kd > 0 && vd > 0 && count >= 1 && vd % DR_COLS == 0 &&
+                   !(state & 15) && !(next & 15) && state != next && (size_t)kd * DR_COLS * 4 <= 200 * 1024 &&
+                   h0 >= 0 && h1 >= h0 && h1 <= vh,
+               "pllm_delta_rule_block: kh %d vh %d kd %d vd %d count %d heads %d..%d", kh, vh, kd, vd, count, h0, h1);
+  if (h1 == h0) return;
+  launch_delta_tiles(out, out_stride, state, next, c, c_stride, work, work_stride, count, kh, kd, vd, vh, h0, h1);
 }
 
 // count tokens' embedding rows (tokens: device int32[count], or 0 to take token) into x, stride floats apart

@@ -126,14 +126,20 @@ class Engine:
 
     SPLIT = 128  # positions a slice of the split-KV attention (two tiles of 64 a CTA, double-buffered)
 
-    def __init__(self, cfg, host=None, seed=0, device=0, graphs=True, pdl=True, exchange=None, exact=False):
+    def __init__(self, cfg, host=None, seed=0, device=0, graphs=True, pdl=True, exchange=None, exact=False, batch=1):
         """exact: every step in the reference kernels' own order of float32 operations (pllm_exact_*: the oracle's
         logits to the bit, several times slower); else the fused kernels (the same integers, float32 within
-        rounding). One rank only."""
+        rounding). One rank only.
+        batch: sequences decoded together, a token each a step (forward_batch / next_tokens), each with its own cache
+        and position: every product streams its weights once for all of them (up to 16 a pass), the attention takes
+        them in one launch. One rank, the fused kernels, a float16 cache."""
         init(device)
         if exact and exchange:
             raise ValueError("the reference-order step runs on one rank")
+        if batch > 1 and (exact or exchange or not cfg.half_kv):
+            raise ValueError("a batch of sequences runs on one rank, with the fused kernels and a float16 cache")
         self.exact = exact
+        self.batch = nb = int(batch)
         self.xg = exchange
         self.shard = s = Shard(cfg, exchange.rank, exchange.world) if exchange else Shard(cfg)
         if os.environ.get("PLLM_STAGE_BUDGET"):  # the bulk-copy product's stage ring, bytes (a tuning knob)
@@ -166,20 +172,25 @@ class Engine:
         B["cos_t"] = Buffer(c.seq_len * c.head_size // 2 * 4)
         B["sin_t"] = Buffer(c.seq_len * c.head_size // 2 * 4)
         E = 2 if c.half_kv else 4
-        B["kc"] = Buffer(c.layers * c.seq_len * s.kvdim * E).zero()
-        B["vc"] = Buffer(c.layers * c.seq_len * s.kvdim * E).zero()
-        # activations
-        B["x"] = Buffer(c.dim * 4)
+        # the caches: [layer][sequence][position][kv heads x head size]
+        B["kc"] = Buffer(c.layers * nb * c.seq_len * s.kvdim * E).zero()
+        B["vc"] = Buffer(c.layers * nb * c.seq_len * s.kvdim * E).zero()
+        # activations (a row a sequence)
+        B["x"] = Buffer(nb * c.dim * 4)
         B["x1"] = Buffer(c.dim * 4) if exchange else None  # the residual's other buffer (tensor-parallel)
-        B["qkv"] = Buffer(self.rows_qkv * 4)
-        B["att"] = Buffer(s.qdim * 4)
-        B["hb"] = Buffer(s.hidden * 4)
-        B["logits"] = Buffer(s.vocab * 4)
-        B["tp"] = Buffer(8).zero()      # the token and the position, read by the kernels
+        B["qkv"] = Buffer(nb * self.rows_qkv * 4)
+        B["att"] = Buffer(nb * s.qdim * 4)
+        B["hb"] = Buffer(nb * s.hidden * 4)
+        B["logits"] = Buffer(nb * s.vocab * 4)
+        B["tp"] = Buffer(8 * nb).zero()  # the tokens, then the positions, read by the kernels
         B["bad"] = Buffer(4).zero()     # non-finite keys / values written to a float16 cache (halves.ts:35)
         B["next"] = Buffer(4)           # the greedy step's token (pllm_argmax_dev) and its scratch
         B["amx"] = Buffer(16).zero()
-        B["scratch"] = Buffer(L.pllm_attention_scratch_bytes(s.heads, c.head_size, c.seq_len, self.SPLIT)).zero()
+        self.scratch_bytes = (L.pllm_attention_scratch_bytes(s.heads, c.head_size, c.seq_len, self.SPLIT) + 255) & ~255
+        B["scratch"] = Buffer(nb * self.scratch_bytes).zero()
+        if nb > 1:  # w2's input quantized for its product (K too long to quantize in shared memory for 16 tokens)
+            B["hq"], B["hq_scales"] = Buffer(nb * s.hidden), Buffer(nb * s.hidden // 8)
+            B["nexts"] = Buffer(4 * nb)
         if exact:  # the reference-order step's quantized activations, w1 / w3 rows and attention scores
             wide = max(c.dim, c.qdim, c.hidden)
             B["xq"], B["xs"] = Buffer(wide), Buffer(wide // 8)
@@ -190,9 +201,9 @@ class Engine:
         else:
             self.synthesize(seed)
         self.stream = L.pllm_stream_create()
-        self.tp_host = Pinned(2, np.int32)
-        self.logits_host = Pinned(s.vocab, np.float32)
-        self.next_host = Pinned(1, np.int32)
+        self.tp_host = Pinned(2 * nb, np.int32)
+        self.logits_host = Pinned(nb * s.vocab, np.float32)
+        self.next_host = Pinned(nb, np.int32)
         self.graph = 0
         check("Engine")
 
@@ -297,6 +308,8 @@ class Engine:
         norms, RoPE, the cache write and its slices' combine inside; the wo, w1/w3 and w2 products), the classifier."""
         if self.exact:
             return 3 + 11 * self.cfg.layers
+        if self.batch > 1:  # the attention's slices combined by a second kernel where clusters do not take it
+            return 2 + 6 * self.cfg.layers
         return 2 + 5 * self.cfg.layers + (1 if self.xg else 0)
 
     def _enqueue_exact_step(self, need_logits=True):
@@ -334,7 +347,46 @@ class Engine:
             L.pllm_exact_prepare(xq, xs, 0, x, B["final_norm"].ptr, c.dim, c.eps, self.bias, 1)
             L.pllm_exact_product(B["logits"].ptr, 0, xq, xs, B["cls"].ptr, B["cls_s"].ptr, c.dim, c.vocab, rel)
 
+    def _enqueue_batch_step(self, need_logits=True):
+        """A step of the batch's sequences: every product over all of them at once (the batched tensor-core form of
+        pllm_gemv, count = batch), the attention of all of them in one launch (pllm_attention_step_batch: each
+        sequence its own cache and position)."""
+        c, B, nb = self.cfg, self.B, self.batch
+        toks, poss = B["tp"].ptr, B["tp"].ptr + 4 * nb
+        E, pdl = 2, int(self.pdl)
+        x, qkv, att, hb = B["x"].ptr, B["qkv"].ptr, B["att"].ptr, B["hb"].ptr
+        R = self.rows_qkv
+        L.pllm_embed_q8(x, B["emb"].ptr, B["emb_s"].ptr, toks, 0, c.dim, nb, c.dim)
+
+        def gemv(out, ldo, xin, ldx, norm, wq, ws, rows, k, pro, epi, pair=0, xq=0, xs=0):
+            L.pllm_gemv(out, ldo, xq, xs, k if xq else 0, k // 8 if xq else 0, xin, ldx, norm, c.eps, self.bias, wq, ws,
+                        F_Q8, k, 0, rows, nb, pro, epi, pair, pdl)
+        layer_cache = nb * c.seq_len * c.kvdim * E
+        for l in range(c.layers):
+            gemv(qkv, R, x, c.dim, B["att_norm"].ptr + l * c.dim * 4, B["wqkv"].ptr + l * R * c.dim,
+                 B["sqkv"].ptr + l * R * (c.dim // 32) * 4, R, c.dim, PRO_RMS, EPI_STORE)
+            qn = B["q_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
+            kn = B["k_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
+            L.pllm_attention_step_batch(att, c.qdim, qkv, R, B["kc"].ptr + l * layer_cache,
+                                        B["vc"].ptr + l * layer_cache, c.seq_len * c.kvdim * E, B["scratch"].ptr, poss,
+                                        nb, c.seq_len, c.heads, c.kv_heads, c.head_size, 0.0, self.SPLIT, qn, kn,
+                                        B["cos_t"].ptr, B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, pdl)
+            gemv(x, c.dim, att, c.qdim, 0, B["wo"].ptr + l * c.dim * c.qdim,
+                 B["so"].ptr + l * c.dim * (c.qdim // 32) * 4, c.dim, c.qdim, PRO_QUANT, EPI_ADD)
+            gemv(hb, c.hidden, x, c.dim, B["ffn_norm"].ptr + l * c.dim * 4, B["w13"].ptr + l * 2 * c.hidden * c.dim,
+                 B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.hidden, c.dim, PRO_RMS, EPI_SWIGLU,
+                 pair=c.hidden)
+            # w2's K (the hidden width) is quantized first, its activations then read from global memory
+            L.pllm_quantize_tokens(B["hq"].ptr, B["hq_scales"].ptr, hb, c.hidden, self.bias, nb)
+            gemv(x, c.dim, 0, 0, 0, B["w2"].ptr + l * c.dim * c.hidden, B["s2"].ptr + l * c.dim * (c.hidden // 32) * 4,
+                 c.dim, c.hidden, PRO_Q, EPI_ADD, xq=B["hq"].ptr, xs=B["hq_scales"].ptr)
+        if need_logits:
+            gemv(B["logits"].ptr, c.vocab, x, c.dim, B["final_norm"].ptr, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim,
+                 PRO_RMS, EPI_STORE)
+
     def _enqueue_step(self, need_logits=True):
+        if self.batch > 1:
+            return self._enqueue_batch_step(need_logits)
         if self.exact:
             return self._enqueue_exact_step(need_logits)
         if self.xg:
@@ -444,6 +496,8 @@ class Engine:
     def forward(self, token, pos, need_logits=True):
         """One token at pos; the logits (a copy) when asked for."""
         c = self.cfg
+        if self.batch > 1:
+            raise ValueError("a batch engine steps with forward_batch")
         if not (0 <= pos < c.seq_len and 0 <= token < c.vocab):
             raise ValueError(f"token {token} at {pos}: out of range")
         L.pllm_set_stream(self.stream)
@@ -489,6 +543,47 @@ class Engine:
         check("next_token")
         return int(self.next_host.array[0])
 
+    def _batch_in(self, tokens, positions):
+        c, nb = self.cfg, self.batch
+        tokens, positions = np.asarray(tokens, np.int64), np.asarray(positions, np.int64)
+        if tokens.shape != (nb,) or positions.shape != (nb,):
+            raise ValueError(f"a step of the batch takes {nb} tokens and {nb} positions")
+        if (positions < 0).any() or (positions >= c.seq_len).any() or (tokens < 0).any() or (tokens >= c.vocab).any():
+            raise ValueError("a token or a position out of range")
+        L.pllm_set_stream(self.stream)
+        self.tp_host.array[:nb] = tokens
+        self.tp_host.array[nb:] = positions
+        L.pllm_h2d(self.B["tp"].ptr, self.tp_host.ptr, 8 * nb)
+
+    def forward_batch(self, tokens, positions, need_logits=True):
+        """One step of the batch: sequence i's token at its position (each sequence its own cache); the logits, a
+        row a sequence (a copy), when asked for."""
+        if self.batch < 2:
+            raise ValueError("forward_batch is the batch engine's step (Engine(batch=B), B > 1)")
+        self._batch_in(tokens, positions)
+        self.launch_step()
+        n = self.batch * self.shard.vocab
+        if need_logits:
+            L.pllm_d2h(self.logits_host.ptr, self.B["logits"].ptr, n * 4)
+        L.pllm_sync()
+        check("forward_batch")
+        return self.logits_host.array[:n].reshape(self.batch, -1).copy() if need_logits else None
+
+    def next_tokens(self, tokens, positions):
+        """The batch's greedy step: the next token of every sequence (argmax on the device, sample.ts:6-10), 8 bytes
+        a sequence in and 4 back."""
+        if self.batch < 2:
+            raise ValueError("next_tokens is the batch engine's step (Engine(batch=B), B > 1)")
+        self._batch_in(tokens, positions)
+        self.launch_step()
+        V = self.shard.vocab
+        for i in range(self.batch):
+            L.pllm_argmax_dev(self.B["nexts"].ptr + 4 * i, self.B["logits"].ptr + 4 * i * V, V, self.B["amx"].ptr)
+        L.pllm_d2h(self.next_host.ptr, self.B["nexts"].ptr, 4 * self.batch)
+        L.pllm_sync()
+        check("next_tokens")
+        return self.next_host.array[:self.batch].copy()
+
     def forward_many(self, tokens, pos):
         """Tokens at pos, pos + 1, ...: each computed as it would be alone (engine.ts:590); the last one's logits.
         Where the shapes suit the tensor-core prefill (can_prefill) the tokens go through it at once, else one by
@@ -532,12 +627,14 @@ class Engine:
             P["M"] = M
         return P
 
-    def prefill(self, tokens, pos=0, need_logits=True):
+    def prefill(self, tokens, pos=0, need_logits=True, seq=0):
         """tokens at positions pos.. through every layer at once (the products on the tensor cores, pllm_gemm_q8; the
         attention of all of them at once, pllm_attention_prefill), the cache filled for them; the last token's logits
-        (the decode step's classifier)."""
+        (the decode step's classifier). seq: a batch engine's sequence whose cache they fill."""
         c, sh, B = self.cfg, self.shard, self.B
         M = len(tokens)
+        if not 0 <= seq < self.batch:
+            raise ValueError(f"sequence {seq} of {self.batch}")
         if not (M >= 1 and 0 <= pos and pos + M <= c.seq_len):
             raise ValueError(f"{M} tokens at {pos}: out of range")
         if not self.can_prefill():
@@ -554,8 +651,8 @@ class Engine:
             tqkv = P["tsqkv"].ptr + l * self.rows_qkv * (c.dim // 32) * 4
             L.pllm_norm_quantize_rows(XQ, XS, X, c.dim, B["att_norm"].ptr + l * c.dim * 4, c.eps, c.dim, M, bias)
             L.pllm_gemm_q8(QKV, self.rows_qkv, XQ, XS, wqkv, tqkv, M, self.rows_qkv, c.dim, self.rows_qkv, 0, 0)
-            kc = B["kc"].ptr + l * c.seq_len * sh.kvdim * E
-            vc = B["vc"].ptr + l * c.seq_len * sh.kvdim * E
+            kc = B["kc"].ptr + (l * self.batch + seq) * c.seq_len * sh.kvdim * E
+            vc = B["vc"].ptr + (l * self.batch + seq) * c.seq_len * sh.kvdim * E
             qn = B["q_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
             kn = B["k_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
             L.pllm_qk_rope_cache_rows(QKV, self.rows_qkv, qn, kn, B["cos_t"].ptr, B["sin_t"].ptr, pos, M, kc, vc,
@@ -576,13 +673,14 @@ class Engine:
             L.pllm_sync()
             check("prefill")
             return None
-        L.pllm_d2d(B["x"].ptr, X + (M - 1) * c.dim * 4, c.dim * 4)
-        self._gemv(B["logits"].ptr, B["cls"].ptr, B["cls_s"].ptr, sh.vocab, c.dim, B["x"].ptr, B["final_norm"].ptr,
+        x_row, logits_row = B["x"].ptr + seq * c.dim * 4, B["logits"].ptr + seq * sh.vocab * 4
+        L.pllm_d2d(x_row, X + (M - 1) * c.dim * 4, c.dim * 4)
+        self._gemv(logits_row, B["cls"].ptr, B["cls_s"].ptr, sh.vocab, c.dim, x_row, B["final_norm"].ptr,
                    PRO_RMS, EPI_STORE, pdl=False)
-        L.pllm_d2h(self.logits_host.ptr, B["logits"].ptr, sh.vocab * 4)
+        L.pllm_d2h(self.logits_host.ptr, logits_row, sh.vocab * 4)
         L.pllm_sync()
         check("prefill")
-        return self.logits_host.array.copy()
+        return self.logits_host.array[:sh.vocab].copy()
 
     def close(self):
         if self.graph:

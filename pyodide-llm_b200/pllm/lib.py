@@ -90,6 +90,8 @@ SIGNATURES = {
     "pllm_attention_step": ([U64, U64, U64, U64, U64, U64, I32, I32, I32, I32, I32, F32, I32, U64, U64, U64, U64, I32,
                              F32, U64, I32], None),
     "pllm_attention_dev": ([U64, U64, U64, U64, U64, U64, I32, I32, I32, I32, I32, F32, I32, I32], None),
+    "pllm_attention_step_batch": ([U64, I64, U64, I64, U64, U64, I64, U64, U64, I32, I32, I32, I32, I32, F32, I32, U64,
+                                   U64, U64, U64, I32, F32, U64, I32], None),
     "pllm_device_status": ([], I32),
     "pllm_set_gemv_mode": ([I32], I32),
     "pllm_set_stage_budget": ([I32], I32),
@@ -123,6 +125,7 @@ SIGNATURES = {
     "pllm_sample_dev": ([U64, U64, I32, F32, F32, U64, U64, U64, I32, F32], None),
     "pllm_gemv_tp": ([U64, U64, U64, U64, F32, I32, U64, U64, I32, I32, I32, I32, I64, I32, U64, I32], None),
     "pllm_synth_t2": ([U64, U64, I64, I32, U64, F32, F32], None),
+    "pllm_delta_rule_block": ([U64, I64, U64, U64, U64, I64, U64, I64, I32, I32, I32, I32, I32, I32, I32], None),
     "pllm_exact_prepare": ([U64, U64, U64, U64, U64, I32, F32, I32, I32], None),
     "pllm_exact_product": ([U64, U64, U64, U64, U64, U64, I32, I32, I32], None),
     "pllm_exact_qk_rope_cache": ([U64, U64, U64, U64, U64, U64, I32, U64, U64, I32, I32, I32, F32, I32, U64], None),

@@ -414,6 +414,41 @@ def test_delta_rule_bit_exact(kh, vh, kd, vd):
     assert np.array_equal(get(S, np.float32), state)
 
 
+@pytest.mark.parametrize("count", [1, 64])
+def test_delta_rule_block_is_the_tokens_one_by_one(count):
+    """pllm_delta_rule_block: count tokens of the recurrence in one launch (the state on the chip between them) give
+    each token's outputs, gates' delta and the last state of delta_rule called a token at a time, to the bit; the
+    SURVEY's micro-configuration (kh 16, vh 32, kd = vd = 128); a head range writes only its heads."""
+    kh, vh, kd, vd = 16, 32, 128, 128
+    rng = np.random.default_rng(count)
+    state = rng.normal(0, 0.5, vh * kd * vd).astype(np.float32)
+    cw = 2 * kh * kd + vh * vd
+    c = rng.normal(0, 0.3, (count, cw)).astype(np.float32)
+    ww = 2 * vh + vh * vd
+    work = np.zeros((count, ww), np.float32)
+    work[:, :vh] = rng.uniform(0.1, 0.9, (count, vh))
+    work[:, vh:2 * vh] = rng.uniform(0.5, 1.0, (count, vh))
+    outs, s = [], state
+    for t in range(count):
+        o, s, w = O.delta_rule(s, c[t], work[t], kh, kd, vd, vh)
+        outs.append(o)
+        work_t = w
+    for h0, h1 in ((0, vh), (4, 20)):
+        out = dev(np.full(count * vh * vd, -7, np.float32))
+        S, N, C, W = dev(state), dev(np.zeros_like(state)), dev(c), dev(work)
+        L.pllm_delta_rule_block(out.ptr, vh * vd, S.ptr, N.ptr, C.ptr, cw, W.ptr, ww, count, kh, kd, vd, vh, h0, h1)
+        check("pllm_delta_rule_block")
+        got = get(out, np.float32).reshape(count, vh, vd)
+        want = np.stack(outs).reshape(count, vh, vd)
+        assert np.array_equal(bits(got[:, h0:h1]), bits(want[:, h0:h1]))
+        assert np.all(got[:, :h0] == -7) and np.all(got[:, h1:] == -7)
+        nxt = get(N, np.float32).reshape(vh, kd, vd)
+        assert np.array_equal(bits(nxt[h0:h1]), bits(s.reshape(vh, kd, vd)[h0:h1]))
+        last = get(W, np.float32).reshape(count, ww)[-1]
+        delta = last[2 * vh:].reshape(vh, vd)
+        assert np.array_equal(bits(delta[h0:h1]), bits(work_t[2 * vh:].reshape(vh, vd)[h0:h1]))
+
+
 # ---------------------------------------------------------------- the contract's refusals
 
 def test_bad_arguments_launch_nothing():
