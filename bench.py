@@ -120,6 +120,163 @@ def gemm_tops(eng, cfg, M, timed):
             "peak_kind": kind, "frac": round(tops / peak, 4)}
 
 
+SWEEP_SHAPES = [(1024, 1024), (1024, 4608), (4096, 4096), (4096, 12288), (12288, 4096)]  # (K, N): configs[1]
+
+
+def product_sweep(timed, Ms=(1, 4, 16, 128, 512, 2048)):
+    """the isolated products at (K, N) x M, every launch of a measurement on another window of
+    a 512 MB weight arena (so that no launch finds its weights in the 126 MB L2). M <= 16: the decode products
+    (pllm_gemv: int8 on the bulk-copy pipeline -- 1..2 tokens dp4a, 3..16 the tensor-core form; int6 and ternary on the
+    register kernel), their algorithmic bytes (SURVEY: weights N K (1 + 1/8) int8, (3/4 + 1/8) int6, (1/4 + 2/128)
+    ternary, plus the activations and outputs) over the CUDA-event time, against the measured HBM copy rate. M >= 128:
+    the int8 tensor-core product (pllm_gemm_q8, tcgen05 kind::i8), 2 M N K operations against twice the measured bf16
+    dense rate (int6 and ternary checkpoints are widened to int8 for it, so their prefill is this product)."""
+    from pllm.device import Buffer
+    from pllm.lib import L, check
+    hbm, _ = peaks()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tpeak = 2 * float(json.load(f)["bf16_tflops"])
+    except Exception:
+        tpeak = 2 * 1590.0
+    ARENA = 512 << 20
+    wq, ws = Buffer(ARENA), Buffer(ARENA // 8)
+    L.pllm_synth_q8(wq.ptr, ws.ptr, ARENA // 4096, 4096, 7, 0.02)
+    t2, t2s = Buffer(ARENA // 4), Buffer(ARENA // 64)  # ternary: codes of ARENA weights and their float16 scales
+    L.pllm_synth_t2(t2.ptr, t2s.ptr, ARENA // 4096, 4096, 8, 0.02, 0.002)
+    kmax, mmax = 12288, 2048
+    xq, xs = Buffer(mmax * kmax), Buffer(mmax * kmax // 8 * 2)
+    L.pllm_synth_q8(xq.ptr, xs.ptr, mmax, kmax, 9, 1.0)
+    out = Buffer(mmax * 12288 * 4)
+    wt = Buffer(12288 * 4096 // 8 * 4)
+    ev = {}
+    fmts = {"q8": (0, 1.0, 32), "q6": (1, 0.75, 32), "t2": (2, 0.25, 128)}
+    for name, (fmt, vb, gk) in fmts.items():
+        ev[name] = {}
+        for K, N in SWEEP_SHAPES:
+            row = {}
+            wbytes = int(N * K * vb)
+            sbytes = N * (K // gk) * (2 if fmt == 2 else 4)
+            arena, sarena = (t2, t2s) if fmt == 2 else (wq, ws)
+            windows = max(4, min(40, (256 << 20) // max(wbytes, 1)))
+            span = arena.nbytes - wbytes
+            for M in Ms:
+                if M > 16 and fmt != 0:
+                    continue
+                offs = [((i * 7919 * 4096) % max(span, 1)) & ~4095 for i in range(windows)]
+                if M <= 16:
+                    def run():
+                        for i, o in enumerate(offs):
+                            so = (i * sbytes) % max(sarena.nbytes - sbytes, 1) & ~255
+                            L.pllm_gemv(out.ptr, N, xq.ptr, xs.ptr, K, K // 8 * (2 if fmt == 2 else 1), 0, 0, 0, 0.0,
+                                        0, arena.ptr + o, sarena.ptr + so, fmt, K, 0, N, M, 0, 0, 0, 0)
+                    launches = windows
+                else:
+                    L.pllm_transpose_scales(wt.ptr, ws.ptr, N, K // 32)
+
+                    def run():
+                        for o in offs[:4]:
+                            L.pllm_gemm_q8(out.ptr, N, xq.ptr, xs.ptr, wq.ptr + o, wt.ptr, M, N, K, N, 0, 0)
+                    launches = 4
+                run()
+                ms = timed(lambda: [run() for _ in range(3)]) / (3 * launches)
+                check(f"sweep {name} {K}x{N} M {M}")
+                if M <= 16:
+                    byts = wbytes + sbytes + M * K * (1 + 4 / 32) + 4 * M * N
+                    gbs = byts / (ms / 1000) / 1e9
+                    row[str(M)] = {"us": round(ms * 1000, 2), "gbs": round(gbs, 1), "frac": round(gbs / hbm, 3)}
+                else:
+                    tops = 2.0 * M * N * K / (ms / 1000) / 1e12
+                    row[str(M)] = {"us": round(ms * 1000, 2), "tops": round(tops, 1), "frac": round(tops / tpeak, 4)}
+            ev[name][f"K{K}_N{N}"] = row
+    for b in (wq, ws, t2, t2s, xq, xs, out, wt):
+        b.free()
+    return {"shapes": "K x N (configs[1]); M tokens", "l2": "every launch on another window of a 512 MB arena",
+            "gbs_peak": hbm, "tops_peak": tpeak, "products": ev}
+
+
+def batch_decode(cfg, nb, prompt, warmup, steps, timed, hbm):
+    """configs[3] at batch nb: nb sequences, each its own 2048-token prompt (the tensor-core prefill, a sequence at a
+    time) and cache, then decode steps of all of them at once (one CUDA graph a step: the products over the nb tokens on
+    the batched tensor-core form, the attention of all sequences in one launch). tok/s of the whole batch; the step's
+    algorithmic bytes are the weights (8.51 GB) plus every sequence's cache read (2 x layers x (pos + 1) x kvdim x 2
+    bytes). e2e: Engine.next_tokens (8 bytes a sequence in, 4 back)."""
+    from pllm.device import Buffer
+    from pllm.forward import Engine
+    from pllm.lib import L
+    eng = Engine(cfg, seed=0, batch=nb)
+    L.pllm_set_stream(eng.stream)
+    rng = np.random.default_rng(3)
+    ids = rng.integers(0, cfg.vocab, (nb, prompt + warmup + 2 * steps)).astype(np.int32)
+    for i in range(nb):
+        eng.prefill(ids[i, :prompt], 0, need_logits=False, seq=i)
+    eng.capture()
+    total = warmup + 2 * steps
+    tp = np.zeros((total, 2 * nb), np.int32)
+    for s in range(total):
+        tp[s, :nb] = ids[:, prompt + s]
+        tp[s, nb:] = prompt + s
+    staged = Buffer.of(tp)
+
+    def device_steps(first, count):
+        for s in range(first, first + count):
+            L.pllm_d2d(eng.B["tp"].ptr, staged.ptr + 8 * nb * s, 8 * nb)
+            L.pllm_graph_launch(eng.graph)
+
+    device_steps(0, warmup)
+    ms = timed(lambda: device_steps(warmup, steps))
+    kv = 2 * cfg.layers * cfg.kvdim * 2 * nb * sum(prompt + warmup + s + 1 for s in range(steps)) / steps
+    byts = cfg.weight_bytes() + kv
+    e2e_ms = timed(lambda: [eng.next_tokens(ids[:, prompt + warmup + steps + s], tp[warmup + steps + s, nb:])
+                            for s in range(steps)])
+    eng.close()
+    staged.free()
+    tps = nb * steps / (ms / 1000)
+    return {"batch": nb, "value": tps, "unit": "tok/s", "ms_per_step": ms / steps, "steps": steps,
+            "positions": f"{prompt}..{prompt + warmup + steps}", "bytes_per_step": byts,
+            "hbm_frac": byts / (ms / steps / 1000) / 1e9 / hbm,
+            "e2e": {"value": nb * steps / (e2e_ms / 1000), "unit": "tok/s", "h2d_bytes_per_step": 8 * nb,
+                    "d2h_bytes_per_step": 4 * nb, "call": "Engine.next_tokens (greedy: argmax on the device)"},
+            "method": "Engine(batch=16): batched tensor-core products (mma m16n8k32 int8 groups in the bulk-copy "
+                      "pipeline), the batch's attention in one launch"}
+
+
+def ternary_decode(prompt, warmup, steps, timed, hbm):
+    """the 27B-class ternary decoder (5120 hidden, 62 layers, 32 / 16 heads of 128, 21504
+    FFN, 262144 vocab; every matrix packed ternary, 0.2656 bytes a weight: 6.83 GB a token), seeded synthetic codes
+    and float16 row scales; its prompt through the decode step (the tensor-core prefill takes int8 matrices), then
+    batch-1 decode steps (one CUDA graph a step). tok/s; the step's algorithmic bytes are the matrices' plus the cache
+    read."""
+    from pllm.device import Buffer
+    from pllm.forward import TERNARY_27B, Engine
+    from pllm.lib import L
+    cfg = TERNARY_27B
+    eng = Engine(cfg, seed=0)
+    L.pllm_set_stream(eng.stream)
+    eng.capture()
+    ids = np.random.default_rng(5).integers(0, cfg.vocab, prompt + warmup + steps).astype(np.int32)
+    staged = Buffer.of(np.stack([ids, np.arange(ids.size, dtype=np.int32)], axis=1).reshape(-1))
+
+    def device_steps(first, count):
+        for i in range(first, first + count):
+            L.pllm_d2d(eng.B["tp"].ptr, staged.ptr + 8 * i, 8)
+            L.pllm_graph_launch(eng.graph)
+
+    prompt_ms = timed(lambda: device_steps(0, prompt))
+    device_steps(prompt, warmup)
+    ms = timed(lambda: device_steps(prompt + warmup, steps))
+    kv = 2 * cfg.layers * cfg.kvdim * 2 * sum(prompt + warmup + s + 1 for s in range(steps)) / steps
+    byts = cfg.weight_bytes() + kv
+    eng.close()
+    staged.free()
+    return {"config": "configs[4]: 27B-class ternary (5120 hidden, 62 layers, 32/16 heads x 128, 21504 FFN, "
+                      "262144 vocab), packed ternary matrices", "value": steps / (ms / 1000), "unit": "tok/s",
+            "ms_per_step": ms / steps, "positions": f"{prompt}..{prompt + warmup + steps}",
+            "weight_bytes": cfg.weight_bytes(), "bytes_per_step": byts, "hbm_frac": byts / (ms / steps / 1000) / 1e9 / hbm,
+            "prompt": {"tokens": prompt, "tok_s": prompt / (prompt_ms / 1000), "method": "the decode step a token"},
+            "method": "gemv_tma_t2_kernel: bulk-copy stages of 2-bit codes and float16 scales, unpacked in registers"}
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -280,6 +437,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="profiling only: launch each kernel (no CUDA graph, no PDL)")
     ap.add_argument("--no-micro", action="store_true", help="profiling only: skip the per-kernel timings")
+    ap.add_argument("--no-sweep", action="store_true", help="skip configs[1]'s product sweep (N = 1 only)")
+    ap.add_argument("--batch", type=int, default=16, help="configs[3]'s batched decode (N = 1 only; 0: skip)")
+    ap.add_argument("--no-ternary", action="store_true", help="skip configs[4]'s ternary decode (N = 1 only)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: the same shapes with fewer layers (a small case for ncu captures)")
     ap.add_argument("--kernel", choices=["gemm", "attention", "gemv"],
@@ -453,6 +613,11 @@ def main():
         attention = {"us_per_layer": round(att_ms * 1000, 2), "position": last_pos,
                      "gbs": round(att_bytes / (att_ms / 1000) / 1e9, 1)}
 
+    sweep = None
+    if world == 1 and not args.no_sweep and not args.no_micro:
+        sweep = product_sweep(timed)
+        L.pllm_set_stream(eng.stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         W = eng.host_weights()
@@ -491,11 +656,22 @@ def main():
         "gpu_launches": eng.launches_per_step * steps * world,
         "clocks": clock,
     }
+    if sweep:
+        line["sweep"] = sweep
+    if world == 1 and args.batch > 1:
+        eng.close()
+        bsteps = min(64, (cfg.seq_len - prompt - warmup) // 2)
+        line["decode_batch"] = batch_decode(cfg, args.batch, prompt, warmup, bsteps, timed, peak)
+    if world == 1 and not args.no_ternary:
+        if not (args.batch > 1):
+            eng.close()
+        line["decode_ternary_27b"] = ternary_decode(1024, warmup, 128, timed, peak)
     if cpu:
         line["cpu_baseline"] = cpu
     if rank == 0:
         print(json.dumps(line), flush=True)
-    eng.close()
+    if not (world == 1 and (args.batch > 1 or not args.no_ternary)):
+        eng.close()
     if xg:
         xg.close()
     if dist:

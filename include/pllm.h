@@ -214,6 +214,23 @@ void pllm_quantize_tokens(uint64_t xq, uint64_t xs, uint64_t x, int32_t n, int32
 void pllm_to_f16_async(uint64_t out, uint64_t x, int32_t n, uint64_t bad);
 /* rmsnorm of rows rows of n floats, stride floats apart, one weight (Qwen3's per-head q / k norms) */
 void pllm_rmsnorm_rows(uint64_t out, uint64_t x, uint64_t w, int32_t n, float eps, int32_t rows, int64_t stride);
+/* the reference engine's memory touches between kernel calls (JavaScript over its WASM memory, double precision then
+ * stored as float32), as device kernels: */
+/* an LFM2 convolution layer's step between its products (convolution.ts:51-60), a batch of sequences: per sequence z
+ * (its rows at rows + z rows_stride, its [B | C | z] at mixed + z mixed_stride, its output at out + z out_stride,
+ * floats) the rows move up one (at position pos_dev[z] == 0 from zeros, as clear() leaves them; pos_dev 0: never),
+ * the newest row is B z, and out = C sum_j taps[j] rows[j]: shift_rows then short_conv, to the bit; count <= 8 */
+void pllm_conv_step(uint64_t out, int64_t out_stride, uint64_t taps, uint64_t rows, int64_t rows_stride,
+                    uint64_t mixed, int64_t mixed_stride, int32_t n, int32_t count, uint64_t pos_dev, int32_t batch);
+/* linear.ts:160-161, convolution.ts:57: rows 1..count-1 of n floats move up one row (copyWithin); the last stays */
+void pllm_shift_rows(uint64_t rows, int32_t n, int32_t count);
+/* linear.ts:151-158: per value head h, work[h] = 1 / (1 + exp(-work[h])) (beta) and work[vh + h] = exp(decays[h]
+ * softplus(work[vh + h] + dt_bias[h])) (decay), softplus(s) = s past 20, else log1p(exp(s)) */
+void pllm_delta_gates(uint64_t work, uint64_t decays, uint64_t dt_bias, int32_t vh);
+/* engine.ts:452-455: count rows of n floats (stride floats apart) times the float at scale (a layer's layerScale) */
+void pllm_scale_rows(uint64_t x, int32_t n, int32_t count, int64_t stride, uint64_t scale);
+/* engine.ts:467-470: x = cap tanh(x / cap), the quotient, its tanh and the product each rounded to float32 */
+void pllm_softcap(uint64_t x, int32_t n, float cap);
 /* count tokens' int8 embedding rows (tokens: device int32[count], or 0 to take token), as tensors.ts:154-160 */
 void pllm_embed_q8(uint64_t x, uint64_t emb, uint64_t scales, uint64_t tokens, int32_t token, int32_t dim, int32_t count,
                    int64_t stride);

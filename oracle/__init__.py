@@ -143,6 +143,19 @@ def matmul_q8r(xq, xs, wq, ws, wc=None, r0=0, r1=None):
     return out
 
 
+def matmul_q8r_tile(frames, wq, ws, n, r0, r1, count, os_, frame, xs_at=4096):
+    """relaxed/int8.ts:147-166: count tokens, token t's activations at byte t frame of frames (its scales xs_at bytes
+    further), its outputs os bytes apart -> (count, rows) outputs (rows r0..r1 written, the rest zero)."""
+    wq = _c(wq, np.int8).reshape(-1, n)
+    rows = wq.shape[0]
+    frames = _c(frames, np.uint8)
+    out = np.zeros(count * os_ // 4, np.float32)
+    base = frames.ctypes.data
+    lib().or_matmul_q8r_tile(_p(out), ctypes.c_void_p(base), ctypes.c_void_p(base + xs_at), _p(wq),
+                             _p(_c(ws, np.float32)), None, n, r0, r1, count, os_, frame)
+    return out.reshape(count, os_ // 4)[:, :rows]
+
+
 def matmul_q6(xq, xs, w6, ws, n, r0=0, r1=None):
     w6 = _c(w6, np.uint8)
     rows = w6.size // (n // 32 * 24)

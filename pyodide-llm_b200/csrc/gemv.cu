@@ -244,10 +244,14 @@ void launch_fmt(int fmt, const GemvArgs& a, bool pdl) {
     case F_Q8: launch_tokens<F_Q8, PRO, EPI>(a, pdl); break;
     case F_Q6: launch_tokens<F_Q6, PRO, EPI>(a, pdl); break;
     default:
-      // ternary and binary take interleaved activations, made by the caller (pllm_gemv refuses the others)
+      // ternary and binary take interleaved activations, made by the caller; ternary from float32 activations is the
+      // bulk-copy form's alone
       if constexpr (PRO == PRO_Q) {
         if (fmt == F_T2) launch_tokens<F_T2, PRO, EPI>(a, pdl);
         else launch_tokens<F_B1, PRO, EPI>(a, pdl);
+      } else {
+        pllm_fail(PLLM_EINVAL, "pllm_gemv: ternary weights from float32 activations need the bulk-copy form (K %% 128, "
+                               "K / 128 a multiple of 8, 16-byte aligned weights and scales)");
       }
       break;
   }
@@ -431,7 +435,8 @@ PLLM_API void pllm_gemv(uint64_t out, int64_t out_stride, uint64_t xq, uint64_t 
   PLLM_REQUIRE(fmt >= 0 && fmt <= 3 && pro >= 0 && pro <= 2 && epi >= 0 && epi <= 2, "pllm_gemv: fmt %d pro %d epi %d",
                fmt, pro, epi);
   if (!check_rows("pllm_gemv", n, r0, r1, fmt >= F_T2 ? 128 : 32) || r0 == r1 || count <= 0) return;
-  PLLM_REQUIRE(!(fmt >= F_T2 && pro != PRO_Q), "pllm_gemv: ternary / binary take interleaved activations (pro 0)");
+  PLLM_REQUIRE(!(fmt == F_B1 && pro != PRO_Q) && !(fmt == F_T2 && pro != PRO_Q && count != 1),
+               "pllm_gemv: binary (and ternary past one token) take interleaved activations (pro 0)");
   PLLM_REQUIRE(bias == 0 || bias == 64, "pllm_gemv: bias %d", bias);
   GemvArgs a = {};
   a.out = dptr<float>(out);

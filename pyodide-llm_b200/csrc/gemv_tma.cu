@@ -511,6 +511,197 @@ bool launch_mma(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl) {
   return true;
 }
 
+// ---- ternary weights at one token (the 27B-class decoder's products): the same pipeline, a stage TRP rows of K / 4
+// bytes of 2-bit codes (ternary.ts:25-33: weight j's code w + 1 at bits 2 (j & 3) of byte j / 4) and then the rows'
+// float16 scales a group of 128; tiles dealt by tickets. The consumers unpack the codes in registers against the
+// activations in the interleave's layout (matmul.ts:106-146: byte 16 p + c of a block of 64 is activation 4 c + p, so
+// (word >> 2 p) & 0x03030303 holds four codes whose activations are four consecutive bytes; ternary_group), each
+// group of 32's exact sum of codes times activations plus the group's minus-sum (the + 1 of the codes taken out) times
+// its scale, times the group of 128's scale (relaxed/signs.ts:28-55). A unit of 128 activations is 8 chunks of 16
+// bytes, chunk c of unit u stored at slot c ^ (u & 7): the lanes' reads of consecutive units do not share banks.
+constexpr int T2_STAGES = 16;
+
+template <int PHASES>
+__device__ __forceinline__ void produce_t2(const GemvArgs& a, const TmaPlan& p, uint64_t* full, uint64_t* empty,
+                                           int* hdr, uint8_t* stage0) {
+  const int S = p.stages, K = a.K, units = K / 128;
+  const int cb = K / 4, sb = units * 2;  // a row's code bytes and scale bytes
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  const unsigned tiles = (unsigned)((a.r1 - a.r0 + TRP - 1) / TRP);
+  unsigned* ticket = g_tickets + p.slot;
+  unsigned next = atomicAdd(ticket, 1u);
+  long long it = 0;
+  while (next < tiles) {
+    const long long t = a.r0 + (long long)next * TRP;
+    next = atomicAdd(ticket, 1u);
+    const int n = (int)min((long long)TRP, a.r1 - t);
+    for (int ph = 0; ph < PHASES; ph++, it++) {
+      const long long row0 = t + (ph ? a.pair : 0);
+      const int slot = (int)(it % S);
+      if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
+      uint8_t* w = stage0 + (size_t)slot * p.stage_bytes;
+      hdr[slot] = (int)(((t - a.r0) << 4) | n);
+      mbar_expect_tx(&full[slot], (unsigned)(n * (cb + sb)));
+      bulk_copy(w, a.wq + row0 * cb, (unsigned)(n * cb), &full[slot], policy);
+      bulk_copy(w + (size_t)TRP * cb, reinterpret_cast<const uint8_t*>(a.ws) + row0 * sb, (unsigned)(n * sb),
+                &full[slot], policy);
+    }
+  }
+  const int slot = (int)(it % S);
+  if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
+  hdr[slot] = -1;
+  mbar_arrive(&full[slot]);
+  if (next == tiles + gridDim.x - 1) atomicExch(ticket, 0u);
+}
+
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_t2_kernel(const GemvArgs a, const TmaPlan p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int S = p.stages, K = a.K, ng = K / 32, units = K / 128, cb = K / 4;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + S;
+  int* hdr = reinterpret_cast<int*>(smem + 16 * S);
+  uint8_t* act = smem + ((20 * T2_STAGES + 127) & ~127);
+  int8_t* sq = reinterpret_cast<int8_t*>(act);            // [K] the prologue's activations, in order
+  uint8_t* si = act + K;                                   // [K] interleaved, chunks swizzled
+  float* ss = reinterpret_cast<float*>(act + 2 * (size_t)K);  // [ng] scales
+  int* sm = reinterpret_cast<int*>(ss + ng);                  // [ng] minus-sums
+  uint8_t* stage0 = act + p.act_bytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  constexpr int PHASES = EPI == EPI_SWIGLU ? 2 : 1;
+  if (tid == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NC);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == NC) {
+    if (lane == 0) produce_t2<PHASES>(a, p, full, empty, hdr, stage0);
+    return;
+  }
+  pdl_wait();
+  if (PRO == PRO_Q) {  // the caller's interleaved activations, their scales, then their minus-sums (interleave())
+    for (int e = tid; e < K / 16; e += NC * 32) {
+      const int u = e >> 3, c = e & 7;
+      *reinterpret_cast<int4*>(si + (size_t)u * 128 + 16 * (c ^ (u & 7))) = reinterpret_cast<const int4*>(a.xq)[e];
+    }
+    for (int i = tid; i < ng; i += NC * 32) {
+      ss[i] = a.xs[i];
+      sm[i] = reinterpret_cast<const int*>(a.xs + ng)[i];
+    }
+  } else {  // RMSNorm / quantize_x of float32 x, then the interleave and each group's minus-sum here
+    load_activations<F_Q8, 1, PRO, ConsumerSync>(a, sq, ss, nullptr, nullptr);
+    consumer_sync();
+    for (int b = tid; b < K / 64; b += NC * 32) {
+      uint32_t v[16];
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int4 q = reinterpret_cast<const int4*>(sq + 64 * (size_t)b)[k];
+        v[4 * k] = (uint32_t)q.x;
+        v[4 * k + 1] = (uint32_t)q.y;
+        v[4 * k + 2] = (uint32_t)q.z;
+        v[4 * k + 3] = (uint32_t)q.w;
+      }
+      int s0 = 0, s1 = 0;
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        s0 = __dp4a((int)v[k], 0x01010101, s0);
+        s1 = __dp4a((int)v[8 + k], 0x01010101, s1);
+      }
+      sm[2 * b] = -s0;
+      sm[2 * b + 1] = -s1;
+      // plane p, byte c = activation 4 c + p = byte p of word c: plane word q from byte p of words 4 q .. 4 q + 3
+      const int u = b >> 1, h = b & 1;
+#pragma unroll
+      for (int pl = 0; pl < 4; pl++) {
+        const unsigned sel = (unsigned)pl | ((unsigned)(pl + 4) << 4);
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+          o[q] = __byte_perm(__byte_perm(v[4 * q], v[4 * q + 1], sel), __byte_perm(v[4 * q + 2], v[4 * q + 3], sel),
+                             0x5410);
+        const int c = 4 * h + pl;
+        *reinterpret_cast<uint4*>(si + (size_t)u * 128 + 16 * (c ^ (u & 7))) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  consumer_sync();
+  pdl_launch_dependents();
+  float h1 = 0.0f;
+  long long it = 0;
+  for (;;) {
+    for (int ph = 0; ph < PHASES; ph++, it++) {
+      const int slot = (int)(it % S);
+      if (!mbar_wait(&full[slot], (unsigned)(it / S) & 1)) return;
+      const int tile = hdr[slot];
+      if (tile < 0) return;
+      const bool mine = warp < (tile & 15);
+      float acc = 0.0f;
+      if (mine) {
+        const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * cb;
+        const uint16_t* d16 = reinterpret_cast<const uint16_t*>(stage0 + (size_t)slot * p.stage_bytes +
+                                                                (size_t)TRP * cb) + (size_t)warp * units;
+        for (int u = lane; u < units; u += 32) {
+          uint32_t wv[8];
+          const uint4 w0 = *reinterpret_cast<const uint4*>(w + (size_t)u * 32);
+          const uint4 w1 = *reinterpret_cast<const uint4*>(w + (size_t)u * 32 + 16);
+          wv[0] = w0.x; wv[1] = w0.y; wv[2] = w0.z; wv[3] = w0.w;
+          wv[4] = w1.x; wv[5] = w1.y; wv[6] = w1.z; wv[7] = w1.w;
+          int4 av[8];
+#pragma unroll
+          for (int c = 0; c < 8; c++) av[c] = *reinterpret_cast<const int4*>(si + (size_t)u * 128 + 16 * (c ^ (u & 7)));
+          int g4[4] = {0, 0, 0, 0};
+          ternary_group(wv, av, g4);
+          const float d = half_bits_to_float(d16[u]);
+          const int4 mins = *reinterpret_cast<const int4*>(sm + 4 * u);
+          const float4 xs4 = *reinterpret_cast<const float4*>(ss + 4 * u);
+          float r = __fmul_rn(__fmul_rn((float)(g4[0] + mins.x), xs4.x), d);
+          r += __fmul_rn(__fmul_rn((float)(g4[1] + mins.y), xs4.y), d);
+          r += __fmul_rn(__fmul_rn((float)(g4[2] + mins.z), xs4.z), d);
+          r += __fmul_rn(__fmul_rn((float)(g4[3] + mins.w), xs4.w), d);
+          acc += r;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (!mine) continue;
+      const float v = warp_sum(acc);
+      if (lane != 0) continue;
+      const long long row = a.r0 + (tile >> 4) + warp;
+      if (EPI == EPI_SWIGLU) {
+        if (ph == 0) h1 = v;
+        else a.out[row] = (h1 / (1.0f + expf(-h1))) * v;
+      } else if (EPI == EPI_ADD) {
+        a.out[row] += v;
+      } else {
+        a.out[row] = v;
+      }
+    }
+  }
+}
+
+template <int PRO, int EPI>
+bool launch_t2(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl) {
+  auto kernel = gemv_tma_t2_kernel<PRO, EPI>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return false;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)gemv_tma_grid(a.r1 - a.r0, EPI));
+  cfg.blockDim = dim3(TMA_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = pllm_stream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a, p);
+  if (e != cudaSuccess) pllm_fail(PLLM_ECUDA, "gemv_tma (ternary) launch: %s", cudaGetErrorString(e));
+  return true;
+}
+
 template <int MT, int PRO, int EPI>
 bool launch(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl, const Xchg& xg) {
   auto kernel = gemv_tma_kernel<MT, PRO, EPI>;
@@ -618,11 +809,43 @@ bool gemv_tma_batched(const GemvArgs& a, int pro, int epi, bool pdl) {
   return false;
 }
 
-// The bulk-copy product for int8 weights at 1 to 16 tokens; false where it does not apply (the caller then takes the
-// register-streaming kernel).
+// The ternary form at one token: whole rows a stage (K / 4 code bytes and K / 128 float16 scales a row, the scales'
+// rows whole 16-byte pieces), up to 16 stages.
+bool gemv_tma_t2(const GemvArgs& a, int pro, int epi, bool pdl) {
+  const int K = a.K, units = K / 128;
+  if (K % 128 || K > 65536 || (units * 2) % 16 || epi > EPI_SWIGLU || ((uintptr_t)a.wq & 15) || ((uintptr_t)a.ws & 15))
+    return false;
+  if (pro == PRO_Q && (((uintptr_t)a.xq & 15) || ((uintptr_t)a.xs & 15))) return false;
+  TmaPlan p = {};
+  p.chunks = 1;
+  p.ks = K;
+  p.stage_bytes = (TRP * (K / 4) + TRP * units * 2 + 127) & ~127;
+  p.act_bytes = (int)((2 * (size_t)K + 2 * (size_t)(K / 32) * 4 + 127) & ~127);
+  const int head = (20 * T2_STAGES + 127) & ~127;
+  int S = (g_tma_budget - head - p.act_bytes) / p.stage_bytes;
+  if (S > T2_STAGES) S = T2_STAGES;
+  if (S < 2) return false;
+  p.stages = S;
+  const size_t smem = (size_t)head + p.act_bytes + (size_t)S * p.stage_bytes;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  p.slot = (int)(next_ticket_slot(dev) % TICKET_SLOTS);
+  p.tickets = 1;
+#define CASE(P, E) \
+  if (pro == P && epi == E) return launch_t2<P, E>(a, p, smem, pdl);
+  CASE(PRO_Q, EPI_STORE) CASE(PRO_Q, EPI_ADD) CASE(PRO_Q, EPI_SWIGLU)
+  CASE(PRO_RMS, EPI_STORE) CASE(PRO_RMS, EPI_ADD) CASE(PRO_RMS, EPI_SWIGLU)
+  CASE(PRO_QUANT, EPI_STORE) CASE(PRO_QUANT, EPI_ADD) CASE(PRO_QUANT, EPI_SWIGLU)
+#undef CASE
+  return false;
+}
+
+// The bulk-copy product for int8 weights at 1 to 16 tokens and ternary weights at one; false where it does not apply
+// (the caller then takes the register-streaming kernel).
 bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg* xg) {
   const bool tp = pro == PRO_RMS_SUM || epi == EPI_SEND;
   if (tp != (xg != nullptr)) return false;
+  if (fmt == F_T2 && !tp && a.count == 1 && g_gemv_mode != 1) return gemv_tma_t2(a, pro, epi, pdl);
   if (g_gemv_mode == 1 || fmt != F_Q8 || a.count < 1 || (tp && a.count != 1)) return false;
   const int K = a.K;
   if (K % 128 || ((uintptr_t)a.wq & 15) || ((uintptr_t)a.ws & 15)) return false;

@@ -178,6 +178,73 @@ void launch_delta_tiles(uint64_t out, long long out_stride, uint64_t state, uint
   PLLM_LAUNCHED("delta_rule");
 }
 
+// The memory touches of the reference's engine between kernel calls, as device kernels (it read and wrote its WASM
+// memory from JavaScript): each the same numbers as the JavaScript, whose arithmetic is in double precision and then
+// stored as float32 (Math.exp, Math.log1p, Math.tanh are CUDA's double functions here).
+// linear.ts:160-161 / convolution.ts:57: rows 1..count-1 of n floats move up one (copyWithin); the last is left
+__global__ void shift_rows_kernel(float* rows, int n, int count) {
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < n; c += gridDim.x * blockDim.x) {
+    float v = rows[(long long)(count - 1) * n + c];
+    for (int j = count - 2; j >= 0; j--) {  // from the top: each value read before its row is written
+      const float below = rows[(long long)j * n + c];
+      rows[(long long)j * n + c] = v;
+      v = below;
+    }
+  }
+}
+// linear.ts:151-158: per value head, beta = 1 / (1 + exp(-b)) and decay = exp(A softplus(g + dt_bias)), softplus(s) =
+// s past 20, else log1p(exp(s)); b at work[h], g at work[vh + h] (each overwritten)
+__global__ void delta_gates_kernel(float* work, const float* decays, const float* dt_bias, int vh) {
+  const int h = blockIdx.x * blockDim.x + threadIdx.x;
+  if (h >= vh) return;
+  const double b = work[h], step = (double)work[vh + h] + (double)dt_bias[h];
+  work[h] = (float)(1.0 / (1.0 + exp(-b)));
+  work[vh + h] = (float)exp((double)decays[h] * (step > 20.0 ? step : log1p(exp(step))));
+}
+// engine.ts:452-455: count rows of n floats (stride apart) times a layer's scale (read from device memory)
+__global__ void scale_rows_kernel(float* x, int n, int count, long long stride, const float* scale) {
+  const float s = *scale;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)n * count;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long t = i / n, c = i % n;
+    x[t * stride + c] = __fmul_rn(x[t * stride + c], s);
+  }
+}
+// engine.ts:467-470: logits = cap tanh(logits / cap), the quotient, its tanh and the product each rounded to float32
+__global__ void softcap_kernel(float* x, int n, float cap) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float q = (float)((double)x[i] / (double)cap);
+    const float t = (float)tanh((double)q);
+    x[i] = (float)((double)cap * (double)t);
+  }
+}
+
+// An LFM2 convolution layer's step between its two products, for a batch of sequences (grid y): the rows move up one
+// (convolution.ts:57's copyWithin; at position 0 the rows before are zero, as clear() leaves them), the newest row is
+// B z, and out = C times the taps' sum over the rows, oldest first (stateful.ts:70-86's short_conv): the same float32
+// operations in the same order, so the reference's numbers to the bit. mixed: [B | C | z] a sequence.
+__global__ void conv_step_kernel(float* out, const float* __restrict__ taps, float* rows, const float* __restrict__ mixed,
+                                 int n, int count, const int* pos_dev, long long rows_stride, long long mixed_stride,
+                                 long long out_stride) {
+  const int z = blockIdx.y;
+  rows += z * rows_stride;
+  mixed += z * mixed_stride;
+  out += z * out_stride;
+  const bool fresh = pos_dev && pos_dev[z] == 0;
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < n; c += gridDim.x * blockDim.x) {
+    float r[8];
+    for (int j = 0; j + 1 < count; j++) r[j] = fresh ? 0.0f : rows[(long long)(j + 1) * n + c];
+    r[count - 1] = __fmul_rn(mixed[c], mixed[2 * (long long)n + c]);
+    float acc = __fmul_rn(taps[c], r[0]);
+    rows[c] = r[0];
+    for (int j = 1; j < count; j++) {
+      rows[(long long)j * n + c] = r[j];
+      acc = __fadd_rn(acc, __fmul_rn(taps[(long long)j * n + c], r[j]));
+    }
+    out[c] = __fmul_rn(mixed[(long long)n + c], acc);
+  }
+}
+
 unsigned grid_of(int n) {
   unsigned g = cdiv((unsigned)(n > 0 ? n : 1), 256u);
   const unsigned most = (unsigned)pllm_num_sms() * 4;
@@ -268,6 +335,41 @@ PLLM_API void pllm_delta_rule_block(uint64_t out, int64_t out_stride, uint64_t s
                "pllm_delta_rule_block: kh %d vh %d kd %d vd %d count %d heads %d..%d", kh, vh, kd, vd, count, h0, h1);
   if (h1 == h0) return;
   launch_delta_tiles(out, out_stride, state, next, c, c_stride, work, work_stride, count, kh, kd, vd, vh, h0, h1);
+}
+
+PLLM_API void pllm_conv_step(uint64_t out, int64_t out_stride, uint64_t taps, uint64_t rows, int64_t rows_stride,
+                              uint64_t mixed, int64_t mixed_stride, int32_t n, int32_t count, uint64_t pos_dev,
+                              int32_t batch) {
+  PLLM_REQUIRE(out && taps && rows && mixed && n > 0 && count >= 1 && count <= 8 && batch >= 1 && batch <= 65535,
+               "pllm_conv_step: n %d count %d batch %d", n, count, batch);
+  conv_step_kernel<<<dim3(cdiv(n, 256), batch), 256, 0, pllm_stream()>>>(
+      dptr<float>(out), dptr<const float>(taps), dptr<float>(rows), dptr<const float>(mixed), n, count,
+      dptr<const int>(pos_dev), rows_stride, mixed_stride, out_stride);
+  PLLM_LAUNCHED("pllm_conv_step");
+}
+
+PLLM_API void pllm_shift_rows(uint64_t rows, int32_t n, int32_t count) {
+  PLLM_REQUIRE(rows && n > 0 && count >= 1, "pllm_shift_rows: n %d count %d", n, count);
+  if (count < 2) return;
+  shift_rows_kernel<<<grid_of(n), 256, 0, pllm_stream()>>>(dptr<float>(rows), n, count);
+  PLLM_LAUNCHED("pllm_shift_rows");
+}
+PLLM_API void pllm_delta_gates(uint64_t work, uint64_t decays, uint64_t dt_bias, int32_t vh) {
+  PLLM_REQUIRE(work && decays && dt_bias && vh > 0, "pllm_delta_gates: vh %d", vh);
+  delta_gates_kernel<<<cdiv(vh, 128), 128, 0, pllm_stream()>>>(dptr<float>(work), dptr<const float>(decays),
+                                                               dptr<const float>(dt_bias), vh);
+  PLLM_LAUNCHED("pllm_delta_gates");
+}
+PLLM_API void pllm_scale_rows(uint64_t x, int32_t n, int32_t count, int64_t stride, uint64_t scale) {
+  PLLM_REQUIRE(x && scale && n > 0 && count > 0 && stride >= n, "pllm_scale_rows: n %d count %d", n, count);
+  scale_rows_kernel<<<grid_of(n * count), 256, 0, pllm_stream()>>>(dptr<float>(x), n, count, stride,
+                                                                    dptr<const float>(scale));
+  PLLM_LAUNCHED("pllm_scale_rows");
+}
+PLLM_API void pllm_softcap(uint64_t x, int32_t n, float cap) {
+  PLLM_REQUIRE(x && n > 0 && cap > 0.0f, "pllm_softcap: n %d cap %g", n, (double)cap);
+  softcap_kernel<<<grid_of(n), 256, 0, pllm_stream()>>>(dptr<float>(x), n, cap);
+  PLLM_LAUNCHED("pllm_softcap");
 }
 
 // count tokens' embedding rows (tokens: device int32[count], or 0 to take token) into x, stride floats apart

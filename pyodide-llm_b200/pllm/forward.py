@@ -35,7 +35,7 @@ from .device import Buffer, Pinned, init
 from .lib import L, check
 from .tp import Shard
 
-F_Q8 = 0
+F_Q8, F_T2 = 0, 2
 PRO_Q, PRO_RMS, PRO_QUANT, PRO_RMS_SUM = 0, 1, 2, 3
 EPI_STORE, EPI_ADD, EPI_SWIGLU, EPI_SEND = 0, 1, 2, 3
 
@@ -55,6 +55,7 @@ class Config:
     eps: float = 1e-5
     relaxed: bool = False     # matmul_q8r's activations (bias 64, qmax 63) in place of matmul_q8's (qmax 127)
     half_kv: bool = True      # a float16 cache (to_f16 / attention_f16), as engine.ts:191 chooses for int8 models
+    weights: str = "q8"       # the matrices' format: "q8" int8 groups of 32, "t2" packed ternary (ternary.ts)
 
     @property
     def qdim(self):
@@ -64,16 +65,24 @@ class Config:
     def kvdim(self):
         return self.kv_heads * self.head_size
 
+    @property
+    def bytes_per_weight(self):
+        """int8: the value and 4 / 32 of a float32 scale; ternary: 2 bits and 2 / 128 of a float16 scale."""
+        return 1.125 if self.weights == "q8" else 0.25 + 2 / 128
+
     def weight_bytes(self):
-        """The bytes a decode step reads of the int8 matrices (values and float32 scales, 1.125 bytes a weight)."""
+        """The bytes a decode step reads of the matrices (values and scales)."""
         per_layer = (self.qdim + 2 * self.kvdim) * self.dim + self.dim * self.qdim + 3 * self.hidden * self.dim
-        return int((self.layers * per_layer + self.vocab * self.dim) * 1.125)
+        return int((self.layers * per_layer + self.vocab * self.dim) * self.bytes_per_weight)
 
 
 # the BASELINE configurations (synthetic weights of these shapes)
 STORIES15M = Config(dim=288, hidden=768, layers=6, heads=6, kv_heads=6, head_size=48, vocab=32000, seq_len=256)
 QWEN3_8B = Config(dim=4096, hidden=12288, layers=36, heads=32, kv_heads=8, head_size=128, vocab=151936, seq_len=2560,
                   qk_norm=True, rope_theta=1e6, eps=1e-6)
+# configs[4]: the 27B-class ternary decoder (every matrix ternary, the classifier too); 1024 + 256 positions
+TERNARY_27B = Config(dim=5120, hidden=21504, layers=62, heads=32, kv_heads=16, head_size=128, vocab=262144,
+                     seq_len=1280, weights="t2")
 
 
 def rope_tables(cfg):
@@ -92,14 +101,39 @@ def quantize_rows(w):
     return np.rint(g * inv[:, None]).astype(np.int8).reshape(w.shape), scales.reshape(w.shape[:-1] + (-1,))
 
 
+def pack_ternary(w):
+    """int8 weights in {-1, 0, +1} (rows of k) -> codes w + 1 four to a byte, weight j at bits 2 (j & 3) of byte j / 4
+    (kernels/ternary.ts:25-33, engine/packing.py:100-136)."""
+    c = (w.astype(np.int16) + 1).astype(np.uint8).reshape(w.shape[:-1] + (-1, 4))
+    return (c[..., 0] | (c[..., 1] << 2) | (c[..., 2] << 4) | (c[..., 3] << 6)).astype(np.uint8)
+
+
+def widen_ternary(packed, scales16):
+    """Packed ternary rows and their float16 scales a group of 128 -> the same weights as int8 groups of 32 (the code
+    less 1) with their group of 128's scale each: the same integers of every group of 32 and the same products within
+    float32 rounding (the checkpoint reader's widening, engine/packing.py:48-53 for the int6 analogue)."""
+    p = packed.astype(np.uint8)
+    codes = np.stack([(p >> (2 * j)) & 3 for j in range(4)], axis=-1).reshape(p.shape[:-1] + (-1,))
+    w = (codes.astype(np.int16) - 1).astype(np.int8)
+    s = np.repeat(scales16.view(np.float16).astype(np.float32), 4, axis=-1)
+    return np.ascontiguousarray(w), np.ascontiguousarray(s)
+
+
 def synthetic_host_weights(cfg, seed=0, std=0.02):
     """Host weights of a small model in the reference's int8 format (N(0, std) quantized; norms N(1, 0.1) as
-    tests/made_up.py:42 makes them): a dict by the oracle's field names."""
+    tests/made_up.py:42 makes them), or (cfg.weights "t2") packed ternary (codes uniform on {-1, 0, +1}, a row's
+    scale N(std, std / 10) rounded to float16 for each of its groups of 128): a dict by the oracle's field names."""
     rng = np.random.default_rng(seed)
     Lr, d, h, q, kv = cfg.layers, cfg.dim, cfg.hidden, cfg.qdim, cfg.kvdim
     W = {}
 
     def mat(name, shape):
+        if cfg.weights == "t2":
+            w = rng.integers(-1, 2, shape).astype(np.int8)
+            s = rng.normal(std, std / 10, shape[:-1] + (1,)).astype(np.float16)
+            W["w" + name] = pack_ternary(w)
+            W["s" + name] = np.repeat(s, shape[-1] // 128, axis=-1).view(np.uint16)
+            return
         w, s = quantize_rows(rng.normal(0, std, shape).astype(np.float32))
         W["w" + name], W["s" + name] = w, s
 
@@ -111,7 +145,8 @@ def synthetic_host_weights(cfg, seed=0, std=0.02):
     mat("2", (Lr, d, h))
     mat("3", (Lr, h, d))
     W["emb"], W["emb_s"] = quantize_rows(rng.normal(0, 1.0, (cfg.vocab, d)).astype(np.float32))
-    W["cls"], W["cls_s"] = quantize_rows(rng.normal(0, std, (cfg.vocab, d)).astype(np.float32))
+    mat("cls", (cfg.vocab, d))
+    W["cls"], W["cls_s"] = W.pop("wcls"), W.pop("scls")
     W["att_norm"] = rng.normal(1, 0.1, (Lr, d)).astype(np.float32)
     W["ffn_norm"] = rng.normal(1, 0.1, (Lr, d)).astype(np.float32)
     W["final_norm"] = rng.normal(1, 0.1, d).astype(np.float32)
@@ -138,6 +173,9 @@ class Engine:
             raise ValueError("the reference-order step runs on one rank")
         if batch > 1 and (exact or exchange or not cfg.half_kv):
             raise ValueError("a batch of sequences runs on one rank, with the fused kernels and a float16 cache")
+        if cfg.weights not in ("q8", "t2") or (cfg.weights == "t2" and (exact or exchange or batch > 1)):
+            raise ValueError("ternary matrices run the fused single-sequence step on one rank")
+        self.fmt = F_T2 if cfg.weights == "t2" else F_Q8
         self.exact = exact
         self.batch = nb = int(batch)
         self.xg = exchange
@@ -152,18 +190,19 @@ class Engine:
         B = {}
         ng = lambda cols: cols // 32  # noqa: E731
         # the matrices (this rank's share), a layer's after another; q, k, v rows in one, w1 rows then w3 rows in one
-        B["wqkv"] = Buffer(c.layers * self.rows_qkv * c.dim)
-        B["sqkv"] = Buffer(c.layers * self.rows_qkv * ng(c.dim) * 4)
-        B["wo"] = Buffer(c.layers * c.dim * s.qdim)
-        B["so"] = Buffer(c.layers * c.dim * ng(s.qdim) * 4)
-        B["w13"] = Buffer(c.layers * 2 * s.hidden * c.dim)
-        B["s13"] = Buffer(c.layers * 2 * s.hidden * ng(c.dim) * 4)
-        B["w2"] = Buffer(c.layers * c.dim * s.hidden)
-        B["s2"] = Buffer(c.layers * c.dim * ng(s.hidden) * 4)
+        wb, sb = self.wb, self.sb
+        B["wqkv"] = Buffer(c.layers * self.rows_qkv * wb(c.dim))
+        B["sqkv"] = Buffer(c.layers * self.rows_qkv * sb(c.dim))
+        B["wo"] = Buffer(c.layers * c.dim * wb(s.qdim))
+        B["so"] = Buffer(c.layers * c.dim * sb(s.qdim))
+        B["w13"] = Buffer(c.layers * 2 * s.hidden * wb(c.dim))
+        B["s13"] = Buffer(c.layers * 2 * s.hidden * sb(c.dim))
+        B["w2"] = Buffer(c.layers * c.dim * wb(s.hidden))
+        B["s2"] = Buffer(c.layers * c.dim * sb(s.hidden))
         B["emb"] = Buffer(c.vocab * c.dim)
         B["emb_s"] = Buffer(c.vocab * ng(c.dim) * 4)
-        B["cls"] = Buffer(s.vocab * c.dim)
-        B["cls_s"] = Buffer(s.vocab * ng(c.dim) * 4)
+        B["cls"] = Buffer(s.vocab * wb(c.dim))
+        B["cls_s"] = Buffer(s.vocab * sb(c.dim))
         B["att_norm"] = Buffer(c.layers * c.dim * 4)
         B["ffn_norm"] = Buffer(c.layers * c.dim * 4)
         B["final_norm"] = Buffer(c.dim * 4)
@@ -208,6 +247,14 @@ class Engine:
         check("Engine")
 
     # ---- weights
+    def wb(self, k):
+        """Bytes of a row of k weights' values: int8 k, ternary k / 4 (four codes a byte)."""
+        return k if self.fmt == F_Q8 else k // 4
+
+    def sb(self, k):
+        """Bytes of a row of k weights' scales: int8 a float32 a group of 32, ternary a float16 a group of 128."""
+        return k // 8 if self.fmt == F_Q8 else k // 64
+
     def load(self, W):
         """Host weights (synthetic_host_weights' dict, the reference's int8 layout) into the device layout (this rank's
         share of them with an exchange)."""
@@ -235,7 +282,13 @@ class Engine:
         N(1, 0.1), the RoPE tables of the configuration."""
         c, B = self.cfg, self.B
         s = seed * 1000
-        if self.xg:
+        if self.fmt == F_T2:  # codes uniform on {-1, 0, +1}, a row's scale N(0.02, 0.002) rounded to float16
+            for i, (w, sc, rows, cols) in enumerate([
+                    ("wqkv", "sqkv", c.layers * self.rows_qkv, c.dim), ("wo", "so", c.layers * c.dim, c.qdim),
+                    ("w13", "s13", c.layers * 2 * c.hidden, c.dim), ("w2", "s2", c.layers * c.dim, c.hidden),
+                    ("cls", "cls_s", c.vocab, c.dim)]):
+                L.pllm_synth_t2(B[w].ptr, B[sc].ptr, rows, cols, s + i, 0.02, 0.002)
+        elif self.xg:
             self._synthesize_share(s)
         else:
             for i, (w, sc, rows, cols) in enumerate([
@@ -274,8 +327,11 @@ class Engine:
         blk("cls", "cls_s", 0, sh.vocab, c.dim, sh.vocab_rows().start, 0, c.dim, s + 4)
 
     def host_weights(self):
-        """The device weights back in the oracle's layout (for the CPU baseline and the checks)."""
+        """The device weights back in the oracle's layout (for the CPU baseline and the checks); ternary matrices
+        widened to int8 groups of 32 (widen_ternary: the same integers)."""
         c, B, sh = self.cfg, self.B, self.shard
+        if self.fmt == F_T2:
+            return self._host_weights_t2()
         d = lambda k, dt: B[k].download(dt)  # noqa: E731
         W = {}
         qkv = d("wqkv", np.int8).reshape(c.layers, self.rows_qkv, c.dim)
@@ -296,11 +352,36 @@ class Engine:
         W["k_norm"] = d("k_norm", np.float32) if c.qk_norm else None
         return {k: (np.ascontiguousarray(v) if v is not None else None) for k, v in W.items()}
 
+    def _host_weights_t2(self):
+        c, B = self.cfg, self.B
+        d = lambda k, dt: B[k].download(dt)  # noqa: E731
+        W = {}
+
+        def mat(key, skey, rows, k):
+            return widen_ternary(d(key, np.uint8).reshape(rows, k // 4), d(skey, np.uint16).reshape(rows, k // 128))
+        qkv, sqkv = mat("wqkv", "sqkv", c.layers * self.rows_qkv, c.dim)
+        qkv, sqkv = qkv.reshape(c.layers, self.rows_qkv, -1), sqkv.reshape(c.layers, self.rows_qkv, -1)
+        W["wq"], W["wk"], W["wv"] = np.split(qkv, [c.qdim, c.qdim + c.kvdim], axis=1)
+        W["sq"], W["sk"], W["sv"] = np.split(sqkv, [c.qdim, c.qdim + c.kvdim], axis=1)
+        W["wo"], W["so"] = mat("wo", "so", c.layers * c.dim, c.qdim)
+        w13, s13 = mat("w13", "s13", c.layers * 2 * c.hidden, c.dim)
+        w13, s13 = w13.reshape(c.layers, 2 * c.hidden, -1), s13.reshape(c.layers, 2 * c.hidden, -1)
+        W["w1"], W["w3"] = w13[:, :c.hidden], w13[:, c.hidden:]
+        W["s1"], W["s3"] = s13[:, :c.hidden], s13[:, c.hidden:]
+        W["w2"], W["s2"] = mat("w2", "s2", c.layers * c.dim, c.hidden)
+        W["cls"], W["cls_s"] = mat("cls", "cls_s", c.vocab, c.dim)
+        for k, dt in (("emb", np.int8), ("emb_s", np.float32), ("att_norm", np.float32), ("ffn_norm", np.float32),
+                      ("final_norm", np.float32), ("cos_t", np.float32), ("sin_t", np.float32)):
+            W[k] = d(k, dt)
+        W["q_norm"] = d("q_norm", np.float32) if c.qk_norm else None
+        W["k_norm"] = d("k_norm", np.float32) if c.qk_norm else None
+        return {k: (np.ascontiguousarray(v) if v is not None else None) for k, v in W.items()}
+
     # ---- one step
     def _gemv(self, out, wq, ws, rows, n, x, norm, pro, epi, pair=0, pdl=True):
         c = self.cfg
-        L.pllm_gemv(out, 0, 0, 0, 0, 0, x, 0, norm, c.eps, self.bias, wq, ws, F_Q8, n, 0, rows, 1, pro, epi, pair,
-                    int(pdl and self.pdl))
+        L.pllm_gemv(out, 0, 0, 0, 0, 0, x, 0, norm, c.eps, self.bias, wq, ws, self.fmt, n, 0, rows, 1, pro, epi,
+                    pair, int(pdl and self.pdl))
 
     @property
     def launches_per_step(self):
@@ -394,10 +475,11 @@ class Engine:
         c, B = self.cfg, self.B
         tok, pos = B["tp"].ptr, B["tp"].ptr + 4
         E = 2 if c.half_kv else 4
+        wb, sb = self.wb, self.sb
         L.pllm_embed_q8(B["x"].ptr, B["emb"].ptr, B["emb_s"].ptr, tok, 0, c.dim, 1, c.dim)
         for l in range(c.layers):
-            wqkv = B["wqkv"].ptr + l * self.rows_qkv * c.dim
-            sqkv = B["sqkv"].ptr + l * self.rows_qkv * (c.dim // 32) * 4
+            wqkv = B["wqkv"].ptr + l * self.rows_qkv * wb(c.dim)
+            sqkv = B["sqkv"].ptr + l * self.rows_qkv * sb(c.dim)
             self._gemv(B["qkv"].ptr, wqkv, sqkv, self.rows_qkv, c.dim, B["x"].ptr, B["att_norm"].ptr + l * c.dim * 4,
                        PRO_RMS, EPI_STORE)
             kc = B["kc"].ptr + l * c.seq_len * c.kvdim * E
@@ -407,12 +489,12 @@ class Engine:
             L.pllm_attention_step(B["att"].ptr, B["qkv"].ptr, kc, vc, B["scratch"].ptr, pos, c.seq_len, c.heads,
                                   c.kv_heads, c.head_size, int(c.half_kv), 0.0, self.SPLIT, qn, kn, B["cos_t"].ptr,
                                   B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, int(self.pdl))
-            self._gemv(B["x"].ptr, B["wo"].ptr + l * c.dim * c.qdim, B["so"].ptr + l * c.dim * (c.qdim // 32) * 4,
+            self._gemv(B["x"].ptr, B["wo"].ptr + l * c.dim * wb(c.qdim), B["so"].ptr + l * c.dim * sb(c.qdim),
                        c.dim, c.qdim, B["att"].ptr, 0, PRO_QUANT, EPI_ADD)
-            self._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * c.hidden * c.dim,
-                       B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.hidden, c.dim, B["x"].ptr,
+            self._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * c.hidden * wb(c.dim),
+                       B["s13"].ptr + l * 2 * c.hidden * sb(c.dim), c.hidden, c.dim, B["x"].ptr,
                        B["ffn_norm"].ptr + l * c.dim * 4, PRO_RMS, EPI_SWIGLU, pair=c.hidden)
-            self._gemv(B["x"].ptr, B["w2"].ptr + l * c.dim * c.hidden, B["s2"].ptr + l * c.dim * (c.hidden // 32) * 4,
+            self._gemv(B["x"].ptr, B["w2"].ptr + l * c.dim * wb(c.hidden), B["s2"].ptr + l * c.dim * sb(c.hidden),
                        c.dim, c.hidden, B["hb"].ptr, 0, PRO_QUANT, EPI_ADD)
         if need_logits:
             self._gemv(B["logits"].ptr, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim, B["x"].ptr, B["final_norm"].ptr,
@@ -599,7 +681,7 @@ class Engine:
     def can_prefill(self):
         """The tensor-core prefill's shapes: products with K and rows in whole 128s, a float16 cache, one rank."""
         c, sh = self.cfg, self.shard
-        return (not self.xg and not self.exact and c.half_kv and c.head_size <= 128 and all(
+        return (not self.xg and not self.exact and self.fmt == F_Q8 and c.half_kv and c.head_size <= 128 and all(
             v % 128 == 0 for v in (c.dim, sh.qdim, sh.hidden, self.rows_qkv)))
 
     def _prefill_buffers(self, M):

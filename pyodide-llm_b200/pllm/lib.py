@@ -126,6 +126,11 @@ SIGNATURES = {
     "pllm_gemv_tp": ([U64, U64, U64, U64, F32, I32, U64, U64, I32, I32, I32, I32, I64, I32, U64, I32], None),
     "pllm_synth_t2": ([U64, U64, I64, I32, U64, F32, F32], None),
     "pllm_delta_rule_block": ([U64, I64, U64, U64, U64, I64, U64, I64, I32, I32, I32, I32, I32, I32, I32], None),
+    "pllm_shift_rows": ([U64, I32, I32], None),
+    "pllm_conv_step": ([U64, I64, U64, U64, I64, U64, I64, I32, I32, U64, I32], None),
+    "pllm_delta_gates": ([U64, U64, U64, I32], None),
+    "pllm_scale_rows": ([U64, I32, I32, I64, U64], None),
+    "pllm_softcap": ([U64, I32, F32], None),
     "pllm_exact_prepare": ([U64, U64, U64, U64, U64, I32, F32, I32, I32], None),
     "pllm_exact_product": ([U64, U64, U64, U64, U64, U64, I32, I32, I32], None),
     "pllm_exact_qk_rope_cache": ([U64, U64, U64, U64, U64, U64, I32, U64, U64, I32, I32, I32, F32, I32, U64], None),

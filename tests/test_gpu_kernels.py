@@ -175,7 +175,8 @@ def test_int8_int6_products(golden, ng):
 
 def test_q8r_tile_equals_token_kernel(golden):
     """relaxed/int8.ts:60-65: each (row, token) of the tile is matmul_q8r's number (here: to the bit on the GPU too),
-    for 1..9, 16 and 21 tokens, rows off the fours; nothing written outside the rows and tokens."""
+    for 1..9, 16 and 21 tokens, rows off the fours; nothing written outside the rows and tokens; and every (row,
+    token) within the products' bound of the oracle's matmul_q8r_tile."""
     k = "int8_ng13_"
     n, frame, os_ = 13 * 32, 8192, 64
     w8h = golden[k + "w8"]
@@ -202,6 +203,13 @@ def test_q8r_tile_equals_token_kernel(golden):
                     L.matmul_q8r(alone.ptr, frames.ptr + t * frame, frames.ptr + t * frame + 4096, w8.ptr, ws.ptr,
                                  wc.ptr, n, r0, r1)
                 assert np.array_equal(bits(got[t]), bits(get(alone, np.float32))), (count, r0, r1, t)
+            if r1 > r0:  # the oracle's tile (relaxed/int8.ts:147-166) on the same frames
+                want = O.matmul_q8r_tile(qr, w8h, golden[k + "ws"], n, r0, r1, count, os_, frame)
+                for t in range(count):
+                    xq_t, xs_t = qr[t, :n], qr[t, 4096:4096 + 13 * 4].view(np.float32)
+                    G = O.group_sums_q8(xq_t, w8h, 64).reshape(13, -1)
+                    b = product_bound(G, golden[k + "ws"].reshape(13, -1), xs_t)
+                    assert np.all(np.abs(got[t, r0:r1].astype(np.float64) - want[t, r0:r1]) <= b[r0:r1]), (count, t)
 
 
 # ---------------------------------------------------------------- ternary / binary
@@ -268,6 +276,13 @@ def test_signs_tiles_equal_token_kernel(golden):
                     getattr(L, one)(alone.ptr, frames.ptr + t * frame, frames.ptr + t * frame + 2048, w.ptr, halves.ptr,
                                     n, 1, 12, code)
                 assert np.array_equal(bits(got[t]), bits(get(alone, np.float32))), (tile, count, t)
+                if t < count:  # and against the oracle's signs product (relaxed/signs.ts:77-120) on the token's frame
+                    il, ext = buf[t, :n], buf[t, 2048:2048 + n // 4].view(np.float32)
+                    want = O.matmul_signs(il, ext, packed, golden[k + "halves"], n, binary, 1, 12)
+                    G = O.group_sums_signs(il, ext, packed, n, binary).astype(np.float64)
+                    d = np.repeat(O.from_f16(golden[k + "halves"]).reshape(-1, n // 128), 4, axis=1)
+                    b = 8 * (n // 32) * EPS * (np.abs(G) * ext[: n // 32][None, :] * d).sum(axis=1) + 1e-37
+                    assert np.all(np.abs(got[t, 1:12].astype(np.float64) - want[1:12]) <= b[1:12]), (tile, count, t)
 
 
 # ---------------------------------------------------------------- model-sized products (size-independent properties)
@@ -753,3 +768,49 @@ def test_sums_x_and_signed_dots():
     L.signed_dots(out.ptr, dev(a).ptr, dev(b).ptr)
     check("signed_dots")
     assert np.array_equal(get(out, np.int32), (a.astype(np.int32) * b).reshape(4, 4).sum(axis=1))
+
+
+# ---------------------------------------------------------------- the engine's memory touches as device kernels
+
+def test_memory_touches_are_the_javascripts():
+    """pllm_shift_rows (convolution.ts:57's copyWithin), pllm_scale_rows (engine.ts:452-455), pllm_delta_gates
+    (linear.ts:151-158: JavaScript's double-precision exp / log1p, stored as float32) and pllm_softcap
+    (engine.ts:467-470: each step rounded to float32) against the same arithmetic in NumPy (float64, then float32):
+    the moves and products to the bit, the transcendental ones within one float32 step."""
+    rng = np.random.default_rng(12)
+    n, count = 1000, 3
+    rows = rng.normal(0, 1, (count, n)).astype(np.float32)
+    R = dev(rows)
+    L.pllm_shift_rows(R.ptr, n, count)
+    check("pllm_shift_rows")
+    want = rows.copy()
+    want[:-1] = rows[1:]
+    assert np.array_equal(get(R, np.float32).reshape(count, n), want)
+    x = rng.normal(0, 1, (4, 640)).astype(np.float32)
+    X, S = dev(x), dev(np.array([0.37], np.float32))
+    L.pllm_scale_rows(X.ptr, 600, 4, 640, S.ptr)
+    check("pllm_scale_rows")
+    want = x.copy()
+    want[:, :600] = x[:, :600] * np.float32(0.37)
+    assert np.array_equal(get(X, np.float32).reshape(4, 640), want)
+    vh = 32
+    work = np.concatenate([rng.normal(0, 3, vh), rng.normal(0, 12, vh)]).astype(np.float32)
+    work[vh + 3] = 30.0  # past softplus's 20
+    decays = -np.exp(rng.normal(0, 1, vh)).astype(np.float32)
+    dt = rng.normal(0, 1, vh).astype(np.float32)
+    W = dev(work)
+    L.pllm_delta_gates(W.ptr, dev(decays).ptr, dev(dt).ptr, vh)
+    check("pllm_delta_gates")
+    b, step = work[:vh].astype(np.float64), work[vh:].astype(np.float64) + dt.astype(np.float64)
+    soft = np.where(step > 20, step, np.log1p(np.exp(np.minimum(step, 20))))
+    want = np.concatenate([1.0 / (1.0 + np.exp(-b)), np.exp(decays.astype(np.float64) * soft)]).astype(np.float32)
+    got = get(W, np.float32)
+    assert np.all(np.abs(got.view(np.int32) - want.view(np.int32)) <= 1), (got, want)
+    logits = rng.normal(0, 40, 5000).astype(np.float32)
+    G = dev(logits)
+    L.pllm_softcap(G.ptr, logits.size, 30.0)
+    check("pllm_softcap")
+    q = (logits.astype(np.float64) / 30.0).astype(np.float32)
+    want = (30.0 * np.tanh(q.astype(np.float64)).astype(np.float32).astype(np.float64)).astype(np.float32)
+    got = get(G, np.float32)
+    assert np.all(np.abs(got.view(np.int32) - want.view(np.int32)) <= 1)
