@@ -65,6 +65,30 @@ def kernel_case(which):
         for _ in range(3):
             L.pllm_gemv(out.ptr, 0, 0, 0, 0, 0, x.ptr, 0, norm.ptr, 1e-6, 0, w.ptr, ws.ptr, F_Q8, K, 0, hidden, 1, 1, 2,
                         hidden, 0)
+    elif which == "gemv16":  # the batch-16 step's w1/w3 product (the batched tensor-core form), 16 tokens
+        hidden, K, M = 12288, 4096, 16
+        w, ws = Buffer(2 * hidden * K), Buffer(2 * hidden * K // 8)
+        x, norm, out = Buffer(M * K * 4), Buffer(K * 4), Buffer(M * hidden * 4)
+        bufs += [w, ws, x, norm, out]
+        L.pllm_synth_q8(w.ptr, ws.ptr, 2 * hidden, K, 1, 0.02)
+        L.pllm_synth_f32(x.ptr, M * K, 2, 0.0, 1.0)
+        L.pllm_synth_f32(norm.ptr, K, 3, 1.0, 0.1)
+        for _ in range(3):
+            L.pllm_gemv(out.ptr, hidden, 0, 0, 0, 0, x.ptr, K, norm.ptr, 1e-6, 0, w.ptr, ws.ptr, 0, K, 0, hidden, M, 1, 2,
+                        hidden, 0)
+    elif which == "t2":  # configs[4]'s w1/w3 product (ternary, 2 x 21504 rows, K 5120), three copies: none in L2
+        hidden, K = 21504, 5120
+        ws_ = [(Buffer(2 * hidden * K // 4), Buffer(2 * hidden * K // 64)) for _ in range(3)]
+        x, norm, out = Buffer(K * 4), Buffer(K * 4), Buffer(hidden * 4)
+        bufs += [b for pair in ws_ for b in pair] + [x, norm, out]
+        for i, (w, ws) in enumerate(ws_):
+            L.pllm_synth_t2(w.ptr, ws.ptr, 2 * hidden, K, 1 + i, 0.02, 0.002)
+        L.pllm_synth_f32(x.ptr, K, 2, 0.0, 1.0)
+        L.pllm_synth_f32(norm.ptr, K, 3, 1.0, 0.1)
+        for i in range(3):
+            w, ws = ws_[i]
+            L.pllm_gemv(out.ptr, 0, 0, 0, 0, 0, x.ptr, 0, norm.ptr, 1e-6, 0, w.ptr, ws.ptr, 2, K, 0, hidden, 1, 1, 2,
+                        hidden, 0)
     elif which == "gemm":
         M, N, K = 512, 4096, 4096
         xq, xs, w, ws, wt, out = (Buffer(n) for n in (M * K, M * K // 8, N * K, N * K // 8, N * K // 8, M * N * 4))
@@ -277,6 +301,79 @@ def ternary_decode(prompt, warmup, steps, timed, hbm):
             "method": "gemv_tma_t2_kernel: bulk-copy stages of 2-bit codes and float16 scales, unpacked in registers"}
 
 
+def lfm2_decode(nb, prompt, warmup, steps, timed, hbm):
+    """the LFM2-350M-shaped hybrid (1024 hidden, 16 layers: 10 short-convolution layers of 3
+    taps among 6 grouped-query attention layers of 16 / 8 heads of 64, 4608 FFN, 65536 vocab), seeded synthetic int8
+    weights, at batch nb: every sequence's 512-token prompt through the decode step (all the batch's at once), then
+    decode steps (one CUDA graph a step). tok/s of the batch; the step's bytes are the matrices' (0.40 GB) plus the
+    caches read."""
+    from pllm.device import Buffer
+    from pllm.forward import LFM2_350M, Engine
+    from pllm.lib import L
+    cfg = LFM2_350M
+    eng = Engine(cfg, seed=0, batch=nb)
+    L.pllm_set_stream(eng.stream)
+    eng.capture()
+    total = prompt + warmup + steps
+    ids = np.random.default_rng(11).integers(0, cfg.vocab, (total, nb)).astype(np.int32)
+    tp = np.concatenate([ids, np.repeat(np.arange(total, dtype=np.int32)[:, None], nb, axis=1)], axis=1)
+    staged = Buffer.of(tp)
+
+    def device_steps(first, count):
+        for s in range(first, first + count):
+            L.pllm_d2d(eng.B["tp"].ptr, staged.ptr + 8 * nb * s, 8 * nb)
+            L.pllm_graph_launch(eng.graph)
+
+    prompt_ms = timed(lambda: device_steps(0, prompt))
+    device_steps(prompt, warmup)
+    ms = timed(lambda: device_steps(prompt + warmup, steps))
+    attn = sum(1 for k in cfg.kinds if k == "a")
+    kv = 2 * attn * cfg.kvdim * 2 * nb * sum(prompt + warmup + s + 1 for s in range(steps)) / steps
+    byts = cfg.weight_bytes() + kv
+    eng.close()
+    staged.free()
+    return {"batch": nb, "value": nb * steps / (ms / 1000), "unit": "tok/s", "ms_per_step": ms / steps,
+            "positions": f"{prompt}..{prompt + warmup + steps}", "bytes_per_step": byts,
+            "hbm_frac": byts / (ms / steps / 1000) / 1e9 / hbm,
+            "prompt": {"tokens": prompt, "tok_s": nb * prompt / (prompt_ms / 1000), "method": "the decode step"}}
+
+
+def delta_rule_micro(timed, hbm):
+    """The delta rule's micro-configuration (no BASELINE config has the layer): kh 16, vh 32, kd = vd = 128, one token
+    (delta_rule: the state read and the next written, 2 x 2 MB) and a block of 64 tokens (pllm_delta_rule_block: the
+    state read once and written once for all 64); its HBM bytes over the CUDA-event time. Each launch on another of 40
+    state pairs (160 MB: none in L2)."""
+    from pllm.device import Buffer
+    from pllm.lib import L
+    kh, vh, kd, vd, n = 16, 32, 128, 128, 40
+    sbytes = vh * kd * vd * 4
+    states = Buffer(2 * n * sbytes)
+    L.pllm_synth_f32(states.ptr, 2 * n * sbytes // 4, 31, 0.0, 0.5)
+    cw, ww = 2 * kh * kd + vh * vd, 2 * vh + vh * vd
+    c, work, out = Buffer(64 * cw * 4), Buffer(64 * ww * 4), Buffer(64 * vh * vd * 4)
+    L.pllm_synth_f32(c.ptr, 64 * cw, 32, 0.0, 0.3)
+    L.pllm_synth_f32(work.ptr, 64 * ww, 33, 0.5, 0.1)
+    res = {}
+    for name, count in (("token", 1), ("block64", 64)):
+        def run():
+            for i in range(n):
+                s0 = states.ptr + 2 * i * sbytes
+                if count == 1:
+                    L.delta_rule(out.ptr, s0, s0 + sbytes, c.ptr, work.ptr, kh, kd, vd, vh, 0, vh)
+                else:
+                    L.pllm_delta_rule_block(out.ptr, vh * vd, s0, s0 + sbytes, c.ptr, cw, work.ptr, ww, count, kh,
+                                            kd, vd, vh, 0, vh)
+        run()
+        ms = timed(lambda: [run() for _ in range(3)]) / (3 * n)
+        byts = 2 * sbytes + count * (cw + ww + vh * vd) * 4
+        res[name] = {"tokens": count, "us": round(ms * 1000, 2), "gbs": round(byts / (ms / 1000) / 1e9, 1),
+                     "frac": round(byts / (ms / 1000) / 1e9 / hbm, 3), "us_per_token": round(ms * 1000 / count, 3)}
+    for b in (states, c, work, out):
+        b.free()
+    res["config"] = "kh 16, vh 32, kd = vd = 128 (the state 2 MB a layer)"
+    return res
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -440,9 +537,10 @@ def main():
     ap.add_argument("--no-sweep", action="store_true", help="skip configs[1]'s product sweep (N = 1 only)")
     ap.add_argument("--batch", type=int, default=16, help="configs[3]'s batched decode (N = 1 only; 0: skip)")
     ap.add_argument("--no-ternary", action="store_true", help="skip configs[4]'s ternary decode (N = 1 only)")
+    ap.add_argument("--no-lfm2", action="store_true", help="skip configs[2]'s hybrid decode (N = 1 only)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: the same shapes with fewer layers (a small case for ncu captures)")
-    ap.add_argument("--kernel", choices=["gemm", "attention", "gemv"],
+    ap.add_argument("--kernel", choices=["gemm", "attention", "gemv", "gemv16", "t2"],
                     help="profiling only: three launches of one kernel's small case (for ncu), then exit")
     args = ap.parse_args()
 
@@ -616,6 +714,7 @@ def main():
     sweep = None
     if world == 1 and not args.no_sweep and not args.no_micro:
         sweep = product_sweep(timed)
+        sweep["delta_rule"] = delta_rule_micro(timed, peaks()[0])
         L.pllm_set_stream(eng.stream)
 
     cpu = None
@@ -666,11 +765,15 @@ def main():
         if not (args.batch > 1):
             eng.close()
         line["decode_ternary_27b"] = ternary_decode(1024, warmup, 128, timed, peak)
+    if world == 1 and not args.no_lfm2:
+        if args.batch <= 1 and args.no_ternary:
+            eng.close()
+        line["decode_lfm2_350m"] = [lfm2_decode(nb, 512, warmup, 256, timed, peak) for nb in (1, 8)]
     if cpu:
         line["cpu_baseline"] = cpu
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if not (world == 1 and (args.batch > 1 or not args.no_ternary)):
+    if not (world == 1 and (args.batch > 1 or not args.no_ternary or not args.no_lfm2)):
         eng.close()
     if xg:
         xg.close()

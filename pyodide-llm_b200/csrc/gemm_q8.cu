@@ -199,9 +199,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else if (warp >= 2) {  // ---- the epilogue
     const int q = warp & 3, h = (warp - 2) >> 2;
     const int m = 32 * q + lane;
-    float acc[64];
+    float2 acc2[32];  // column pairs (2 c, 2 c + 1): the packed float32 operations take two columns an instruction
 #pragma unroll
-    for (int c = 0; c < 64; c++) acc[c] = 0.0f;
+    for (int c = 0; c < 32; c++) acc2[c] = make_float2(0.0f, 0.0f);
     bool ok = true;
     for (int g = 0; g < ngroups; g++) {
       const int b = g % NBUF, kb = g / GPS, j = g % GPS, s = kb % STAGES;
@@ -218,17 +218,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (ok) {
         const uint8_t* st = stage(s);
         const float xsv = reinterpret_cast<const float*>(st + A_BYTES + B_BYTES)[m * GPS + j];
+        const float2 xs2 = make_float2(xsv, xsv), off2 = make_float2(-12582912.0f, -12582912.0f);
         const float4* wsv =
             reinterpret_cast<const float4*>(st + A_BYTES + B_BYTES + XS_BYTES + h * (WS_BYTES / 2)) + j * 16;
 #pragma unroll
         for (int c4 = 0; c4 < 16; c4++) {
           const float4 w = wsv[c4];
-          const float ws4[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-          for (int u = 0; u < 4; u++) {
-            const int c = 4 * c4 + u;
-            const float G = __int_as_float((int)r[c] + 0x4B400000) - 12582912.0f;  // exact: |G| < 2^22
-            acc[c] = fmaf(G, __fmul_rn(ws4[u], xsv), acc[c]);
+          for (int u = 0; u < 2; u++) {
+            const int c = 4 * c4 + 2 * u;
+            // exact: |G| < 2^22, its bits added to those of 1.5 x 2^23 and that taken off (two columns at once)
+            const float2 G = __fadd2_rn(make_float2(__int_as_float((int)r[c] + 0x4B400000),
+                                                    __int_as_float((int)r[c + 1] + 0x4B400000)), off2);
+            const float2 s = __fmul2_rn(u ? make_float2(w.z, w.w) : make_float2(w.x, w.y), xs2);
+            acc2[c / 2] = __ffma2_rn(G, s, acc2[c / 2]);
           }
         }
       }
@@ -238,6 +241,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
     // the tile out
+    float acc[64];
+#pragma unroll
+    for (int c = 0; c < 32; c++) {
+      acc[2 * c] = acc2[c].x;
+      acc[2 * c + 1] = acc2[c].y;
+    }
     const int row = m0 + m;
     if (EPI == GE_SWIGLU) {
       float* sw = reinterpret_cast<float*>(smem);  // [BM][65]: the w3 rows' results (the stages are done)

@@ -91,6 +91,8 @@ struct TmaPlan {
   int act_bytes;    // activations and their scales, 128-aligned
   int slot;         // this launch's ticket counter (g_tickets)
   int tickets;      // 1: tiles dealt by tickets; 0: each CTA its own share of the rows (rows cut into chunks)
+  int nred;         // the batched form's buffers of the warps' parts (stages + 2)
+  int rw;           // the ternary form's rows a consumer warp (a tile NC rw rows)
 };
 
 // this CTA's rows: [lo, hi) of [r0, r1), near-equal shares
@@ -313,12 +315,11 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
 // rows is one tensor-core product (mma.sync m16n8k32, int8 x int8 -> int32, 16 tokens x 8 rows), whose int32 are the
 // exact group sums (the same integers as every other form; tokens past count are zeros), each scaled by ws x xs and
 // summed in float32. The consumer warps split a stage's groups (warp w: groups w, w + 8, ...), so each holds a part of
-// the tile's 16 x 8 sums; at the end of a tile's phase they add their parts in shared memory, in warp order, behind a
-// bounded barrier, and 128 threads write the outputs. Activations: ASMEM, all tokens in shared memory (rows padded by
+// the tile's 16 x 8 sums; at the end of a tile's phase each posts its part in shared memory and the last to post adds
+// them (in warp order) and writes the outputs. Activations: ASMEM, all tokens in shared memory (rows padded by
 // 16 bytes: conflict-free fragment reads), made by the prologue; else (K too long for shared memory) the caller's
 // quantized activations read from global memory (L2) fragment by fragment.
 constexpr int MB = 16;                      // tokens of the batched form
-constexpr int RED_BYTES = 2 * NC * 128 * 4;  // two buffers of the warps' parts
 
 __device__ __forceinline__ void mma_s8(int c[4], const uint32_t a[4], const uint32_t b[2]) {
   asm volatile(
@@ -339,45 +340,57 @@ __device__ __forceinline__ float exact_float(int v) {
   return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
 }
 
-// the consumer warps' barrier, bounded: false (and the status word set) past the bound. bar: [0] arrivals, [1] the
-// generation.
-__device__ __forceinline__ bool consumers_meet(unsigned* bar) {
-  __syncwarp();
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) {
-    volatile unsigned* gen = bar + 1;
-    const unsigned g0 = *gen;
-    __threadfence_block();
-    if (atomicAdd(bar, 1u) == NC - 1) {
-      bar[0] = 0;
-      __threadfence_block();
-      atomicAdd(bar + 1, 1u);
+// The batched kernel's shared memory: the barriers, headers and the phase-ends' arrival counts in the first 512
+// bytes, then nred buffers of the warps' parts (NC x 128 floats each), nred buffers of w1's results (EPI_SWIGLU, 128
+// floats each), the activations, the stages.
+constexpr int MMA_HEAD = 512;
+constexpr int RED_FLOATS = NC * 128;
+
+// one group of 32 of the stage (its u-th): the tokens' fragment (shared memory, or the caller's activations in global
+// memory), the weights' fragment, the tensor-core product, its exact int32 scaled into the lane's four sums
+template <bool ASMEM>
+__device__ __forceinline__ void mma_group(float acc[4], const int8_t* sq, int AS, const float* sst, int uu, int a_tok,
+                                          int a_off, int g, const uint8_t* xg0, const uint8_t* xg1, const float* xs0,
+                                          const float* xs1, bool tok0, bool tok1, unsigned bias4, const uint8_t* brow,
+                                          float w0, float w1, int t4, uint32_t af[4], uint32_t bf[2], float& x0,
+                                          float& x1, bool load) {
+  if (load) {
+    if (ASMEM) {
+      ldsm_x4(af, sq + (size_t)a_tok * AS + (size_t)uu * 32 + a_off);
+      x0 = sst[uu * MB + g];
+      x1 = sst[uu * MB + g + 8];
     } else {
-      long long i = 0;
-      while (*gen == g0)
-        if (++i > WAIT_BOUND) {
-          atomicExch(&g_pllm_status, PLLM_ETIMEOUT);
-          ok = 0;
-          break;
-        }
+      const long long o = (long long)uu * 32 + 4 * t4;
+      af[0] = tok0 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg0 + o)), bias4) : 0u;
+      af[1] = tok1 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg1 + o)), bias4) : 0u;
+      af[2] = tok0 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg0 + o + 16)), bias4) : 0u;
+      af[3] = tok1 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg1 + o + 16)), bias4) : 0u;
+      x0 = tok0 ? __ldg(xs0 + uu) : 0.0f;
+      x1 = tok1 ? __ldg(xs1 + uu) : 0.0f;
     }
-    __threadfence_block();
+    ldsm_x2(bf, brow);
+    return;
   }
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
+  int cf[4] = {0, 0, 0, 0};
+  mma_s8(cf, af, bf);
+  acc[0] = fmaf(exact_float(cf[0]), __fmul_rn(w0, x0), acc[0]);
+  acc[1] = fmaf(exact_float(cf[1]), __fmul_rn(w1, x0), acc[1]);
+  acc[2] = fmaf(exact_float(cf[2]), __fmul_rn(w0, x1), acc[2]);
+  acc[3] = fmaf(exact_float(cf[3]), __fmul_rn(w1, x1), acc[3]);
 }
 
 template <int PRO, int EPI, bool ASMEM>
 __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_mma_kernel(const GemvArgs a, const TmaPlan p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages, KS = p.ks, chunks = p.chunks, K = a.K, ng = K / 32, RS = KS + 16, AS = K + 16;
+  const int NRED = p.nred;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
   int* hdr = reinterpret_cast<int*>(smem + 16 * S);
-  unsigned* bar = reinterpret_cast<unsigned*>(smem + 20 * S);  // [2]
-  float* red = reinterpret_cast<float*>(smem + ((20 * S + 8 + 127) & ~127));
-  uint8_t* act = reinterpret_cast<uint8_t*>(red) + RED_BYTES;
+  int* cnt = reinterpret_cast<int*>(smem + 20 * S);  // [NRED] the warps arrived at a phase-end
+  float* red = reinterpret_cast<float*>(smem + MMA_HEAD);  // [NRED][NC][128]
+  float* hsave = red + NRED * RED_FLOATS;                     // [NRED][128]
+  uint8_t* act = reinterpret_cast<uint8_t*>(hsave + NRED * 128);
   int8_t* sq = reinterpret_cast<int8_t*>(act);                         // ASMEM: [MB][AS]
   float* ss = reinterpret_cast<float*>(act + (size_t)MB * AS);         //        [MB][ng]
   float* sst = ss + MB * ng;                                           //        [ng][MB]: by group
@@ -390,7 +403,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_mma_kernel(const Gemv
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NC);
     }
-    bar[0] = bar[1] = 0;
+    for (int i = 0; i < NRED; i++) cnt[i] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -419,12 +432,10 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_mma_kernel(const Gemv
       reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(a.xs) + (long long)(g + 8) * a.xs_stride);
   const bool tok0 = g < a.count, tok1 = g + 8 < a.count;
   const unsigned bias4 = a.bias ? 0x40404040u : 0u;
-  float h1 = 0.0f;  // EPI_SWIGLU: thread tid < 128's w1 result
-  int buf = 0;
-  long long it = 0;
+  long long it = 0, pe = 0;  // stages taken, phase-ends passed (the same sequence in every warp)
   for (;;) {
     int tile = 0;
-    for (int ph = 0; ph < PHASES; ph++) {
+    for (int ph = 0; ph < PHASES; ph++, pe++) {
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (int c = 0; c < chunks; c++, it++) {
         const int slot = (int)(it % S);
@@ -436,50 +447,57 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_mma_kernel(const Gemv
         const int gs = KS / 32, u0 = c * gs;
         const float* ws0 = sc + (2 * t4) * gs;
         const float* ws1 = ws0 + gs;
-        for (int u = warp; u < gs; u += NC) {
-          uint32_t af[4], bf[2];
-          float x0, x1;
-          if (ASMEM) {
-            ldsm_x4(af, sq + (size_t)a_tok * AS + (size_t)(u0 + u) * 32 + a_off);
-            x0 = sst[(u0 + u) * MB + g];
-            x1 = sst[(u0 + u) * MB + g + 8];
-          } else {
-            const long long o = (long long)(u0 + u) * 32 + 4 * t4;
-            af[0] = tok0 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg0 + o)), bias4) : 0u;
-            af[1] = tok1 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg1 + o)), bias4) : 0u;
-            af[2] = tok0 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg0 + o + 16)), bias4) : 0u;
-            af[3] = tok1 ? __vsub4(__ldg(reinterpret_cast<const unsigned*>(xg1 + o + 16)), bias4) : 0u;
-            x0 = tok0 ? __ldg(xs0 + u0 + u) : 0.0f;
-            x1 = tok1 ? __ldg(xs1 + u0 + u) : 0.0f;
-          }
-          ldsm_x2(bf, w + (size_t)b_row * RS + (size_t)u * 32 + b_off);
-          int cf[4] = {0, 0, 0, 0};
-          mma_s8(cf, af, bf);
-          const float w0 = ws0[u], w1 = ws1[u];
-          acc[0] = fmaf(exact_float(cf[0]), __fmul_rn(w0, x0), acc[0]);
-          acc[1] = fmaf(exact_float(cf[1]), __fmul_rn(w1, x0), acc[1]);
-          acc[2] = fmaf(exact_float(cf[2]), __fmul_rn(w0, x1), acc[2]);
-          acc[3] = fmaf(exact_float(cf[3]), __fmul_rn(w1, x1), acc[3]);
+        const uint8_t* brow = w + (size_t)b_row * RS + b_off;
+        // two groups an iteration: both groups' fragments loaded before either product
+        for (int u = warp; u < gs; u += 2 * NC) {
+          const bool two = u + NC < gs;
+          uint32_t af0[4], af1[4], bf0[2], bf1[2];
+          float x00 = 0.0f, x01 = 0.0f, x10 = 0.0f, x11 = 0.0f;
+          mma_group<ASMEM>(acc, sq, AS, sst, u0 + u, a_tok, a_off, g, xg0, xg1, xs0, xs1, tok0, tok1, bias4,
+                           brow + (size_t)u * 32, 0.0f, 0.0f, t4, af0, bf0, x00, x01, true);
+          if (two)
+            mma_group<ASMEM>(acc, sq, AS, sst, u0 + u + NC, a_tok, a_off, g, xg0, xg1, xs0, xs1, tok0, tok1, bias4,
+                             brow + (size_t)(u + NC) * 32, 0.0f, 0.0f, t4, af1, bf1, x10, x11, true);
+          mma_group<ASMEM>(acc, sq, AS, sst, 0, a_tok, a_off, g, xg0, xg1, xs0, xs1, tok0, tok1, bias4, brow,
+                           ws0[u], ws1[u], t4, af0, bf0, x00, x01, false);
+          if (two)
+            mma_group<ASMEM>(acc, sq, AS, sst, 0, a_tok, a_off, g, xg0, xg1, xs0, xs1, tok0, tok1, bias4, brow,
+                             ws0[u + NC], ws1[u + NC], t4, af1, bf1, x10, x11, false);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
       }
-      // the tile's phase is done: the warps' parts added in warp order, a thread an output
-      float* rb = red + buf * (NC * 128);
+      // the tile's phase is done: this warp's part posted; the last warp to post adds the parts in warp order and
+      // writes the outputs (no warp waits for another). A warp runs at most S stages ahead of the slowest, so the
+      // nred = S + 2 buffers are not reused while read.
+      const int b = (int)(pe % NRED);
+      float* rb = red + b * RED_FLOATS;
       *reinterpret_cast<float4*>(rb + warp * 128 + 4 * lane) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      if (!consumers_meet(bar)) return;
-      if (tid < 128) {
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        __threadfence_block();
+        last = atomicAdd(&cnt[b], 1) == NC - 1;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      __threadfence_block();
+      for (int e = lane; e < 128; e += 32) {
         float v = 0.0f;
 #pragma unroll
-        for (int w2 = 0; w2 < NC; w2++) v += rb[w2 * 128 + tid];
-        const int el = tid >> 2, i = tid & 3;
+        for (int w2 = 0; w2 < NC; w2++) v += rb[w2 * 128 + e];
+        const int el = e >> 2, i = e & 3;
         const int token = (el >> 2) + (i >= 2 ? 8 : 0), r = 2 * (el & 3) + (i & 1);
+        if (EPI == EPI_SWIGLU && ph == 0) {
+          hsave[b * 128 + e] = v;  // w1's result, read by the phase that follows (its last warp)
+          continue;
+        }
         if (r < (tile & 15) && token < a.count) {
           const long long row = a.r0 + (tile >> 4) + r;
           float* o = a.out + token * a.out_stride + row;
           if (EPI == EPI_SWIGLU) {
-            if (ph == 0) h1 = v;
-            else *o = (h1 / (1.0f + expf(-h1))) * v;
+            const float h1 = hsave[(int)((pe - 1) % NRED) * 128 + e];
+            *o = (h1 / (1.0f + expf(-h1))) * v;
           } else if (EPI == EPI_ADD) {
             *o += v;
           } else {
@@ -487,7 +505,11 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_mma_kernel(const Gemv
           }
         }
       }
-      buf ^= 1;
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        cnt[b] = 0;
+      }
     }
   }
 }
@@ -524,27 +546,27 @@ constexpr int T2_STAGES = 16;
 template <int PHASES>
 __device__ __forceinline__ void produce_t2(const GemvArgs& a, const TmaPlan& p, uint64_t* full, uint64_t* empty,
                                            int* hdr, uint8_t* stage0) {
-  const int S = p.stages, K = a.K, units = K / 128;
+  const int S = p.stages, K = a.K, units = K / 128, T = NC * p.rw;
   const int cb = K / 4, sb = units * 2;  // a row's code bytes and scale bytes
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-  const unsigned tiles = (unsigned)((a.r1 - a.r0 + TRP - 1) / TRP);
+  const unsigned tiles = (unsigned)((a.r1 - a.r0 + T - 1) / T);
   unsigned* ticket = g_tickets + p.slot;
   unsigned next = atomicAdd(ticket, 1u);
   long long it = 0;
   while (next < tiles) {
-    const long long t = a.r0 + (long long)next * TRP;
+    const long long t = a.r0 + (long long)next * T;
     next = atomicAdd(ticket, 1u);
-    const int n = (int)min((long long)TRP, a.r1 - t);
+    const int n = (int)min((long long)T, a.r1 - t);
     for (int ph = 0; ph < PHASES; ph++, it++) {
       const long long row0 = t + (ph ? a.pair : 0);
       const int slot = (int)(it % S);
       if (!mbar_wait(&empty[slot], ((unsigned)(it / S) & 1) ^ 1)) return;
       uint8_t* w = stage0 + (size_t)slot * p.stage_bytes;
-      hdr[slot] = (int)(((t - a.r0) << 4) | n);
+      hdr[slot] = (int)(((t - a.r0) << 6) | n);
       mbar_expect_tx(&full[slot], (unsigned)(n * (cb + sb)));
       bulk_copy(w, a.wq + row0 * cb, (unsigned)(n * cb), &full[slot], policy);
-      bulk_copy(w + (size_t)TRP * cb, reinterpret_cast<const uint8_t*>(a.ws) + row0 * sb, (unsigned)(n * sb),
+      bulk_copy(w + (size_t)T * cb, reinterpret_cast<const uint8_t*>(a.ws) + row0 * sb, (unsigned)(n * sb),
                 &full[slot], policy);
     }
   }
@@ -630,7 +652,9 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_t2_kernel(const GemvA
   }
   consumer_sync();
   pdl_launch_dependents();
-  float h1 = 0.0f;
+  constexpr int RWM = 4;  // the most rows a warp
+  const int rw = p.rw, T = NC * rw;
+  float h1[RWM] = {0.0f, 0.0f, 0.0f, 0.0f};  // EPI_SWIGLU: this warp's rows' w1 results
   long long it = 0;
   for (;;) {
     for (int ph = 0; ph < PHASES; ph++, it++) {
@@ -638,46 +662,56 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_t2_kernel(const GemvA
       if (!mbar_wait(&full[slot], (unsigned)(it / S) & 1)) return;
       const int tile = hdr[slot];
       if (tile < 0) return;
-      const bool mine = warp < (tile & 15);
-      float acc = 0.0f;
-      if (mine) {
-        const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * cb;
+      const int mine = min(rw, (tile & 63) - warp * rw);  // this warp's rows of the tile
+      float acc[RWM] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (mine > 0) {
+        const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * rw * cb;
         const uint16_t* d16 = reinterpret_cast<const uint16_t*>(stage0 + (size_t)slot * p.stage_bytes +
-                                                                (size_t)TRP * cb) + (size_t)warp * units;
-        for (int u = lane; u < units; u += 32) {
-          uint32_t wv[8];
-          const uint4 w0 = *reinterpret_cast<const uint4*>(w + (size_t)u * 32);
-          const uint4 w1 = *reinterpret_cast<const uint4*>(w + (size_t)u * 32 + 16);
-          wv[0] = w0.x; wv[1] = w0.y; wv[2] = w0.z; wv[3] = w0.w;
-          wv[4] = w1.x; wv[5] = w1.y; wv[6] = w1.z; wv[7] = w1.w;
-          int4 av[8];
+                                                                (size_t)T * cb) + (size_t)warp * rw * units;
+        // half units of 64 weights (16 code bytes; one block of the interleave), lane after lane along the row: the
+        // block's activations read once for the warp's rows
+        for (int hu = lane; hu < 2 * units; hu += 32) {
+          const int u = hu >> 1, h = hu & 1;
+          int4 av[4];
 #pragma unroll
-          for (int c = 0; c < 8; c++) av[c] = *reinterpret_cast<const int4*>(si + (size_t)u * 128 + 16 * (c ^ (u & 7)));
-          int g4[4] = {0, 0, 0, 0};
-          ternary_group(wv, av, g4);
-          const float d = half_bits_to_float(d16[u]);
-          const int4 mins = *reinterpret_cast<const int4*>(sm + 4 * u);
-          const float4 xs4 = *reinterpret_cast<const float4*>(ss + 4 * u);
-          float r = __fmul_rn(__fmul_rn((float)(g4[0] + mins.x), xs4.x), d);
-          r += __fmul_rn(__fmul_rn((float)(g4[1] + mins.y), xs4.y), d);
-          r += __fmul_rn(__fmul_rn((float)(g4[2] + mins.z), xs4.z), d);
-          r += __fmul_rn(__fmul_rn((float)(g4[3] + mins.w), xs4.w), d);
-          acc += r;
+          for (int pl = 0; pl < 4; pl++)
+            av[pl] = *reinterpret_cast<const int4*>(si + (size_t)u * 128 + 16 * ((4 * h + pl) ^ (u & 7)));
+          const int m0 = sm[4 * u + 2 * h], m1 = sm[4 * u + 2 * h + 1];
+          const float x0 = ss[4 * u + 2 * h], x1 = ss[4 * u + 2 * h + 1];
+#pragma unroll
+          for (int r = 0; r < RWM; r++) {
+            if (r >= mine) break;
+            const uint4 cw = *reinterpret_cast<const uint4*>(w + (size_t)r * cb + (size_t)u * 32 + 16 * h);
+            int g0 = 0, g1 = 0;
+#pragma unroll
+            for (int pl = 0; pl < 4; pl++) {
+              const unsigned sh = 2 * pl;
+              g0 = __dp4a((int)((cw.x >> sh) & 0x03030303u), av[pl].x, g0);
+              g0 = __dp4a((int)((cw.y >> sh) & 0x03030303u), av[pl].y, g0);
+              g1 = __dp4a((int)((cw.z >> sh) & 0x03030303u), av[pl].z, g1);
+              g1 = __dp4a((int)((cw.w >> sh) & 0x03030303u), av[pl].w, g1);
+            }
+            const float d = half_bits_to_float(d16[(size_t)r * units + u]);
+            acc[r] += __fmul_rn(__fmul_rn((float)(g0 + m0), x0), d) + __fmul_rn(__fmul_rn((float)(g1 + m1), x1), d);
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
-      if (!mine) continue;
-      const float v = warp_sum(acc);
-      if (lane != 0) continue;
-      const long long row = a.r0 + (tile >> 4) + warp;
-      if (EPI == EPI_SWIGLU) {
-        if (ph == 0) h1 = v;
-        else a.out[row] = (h1 / (1.0f + expf(-h1))) * v;
-      } else if (EPI == EPI_ADD) {
-        a.out[row] += v;
-      } else {
-        a.out[row] = v;
+#pragma unroll
+      for (int r = 0; r < RWM; r++) {
+        if (r >= mine) break;
+        const float v = warp_sum(acc[r]);
+        if (lane != 0) continue;
+        const long long row = a.r0 + (tile >> 6) + warp * rw + r;
+        if (EPI == EPI_SWIGLU) {
+          if (ph == 0) h1[r] = v;
+          else a.out[row] = (h1[r] / (1.0f + expf(-h1[r]))) * v;
+        } else if (EPI == EPI_ADD) {
+          a.out[row] += v;
+        } else {
+          a.out[row] = v;
+        }
       }
     }
   }
@@ -779,20 +813,21 @@ bool gemv_tma_batched(const GemvArgs& a, int pro, int epi, bool pdl) {
   while (K % (p.chunks * 128)) p.chunks++;
   p.ks = K / p.chunks;
   p.stage_bytes = (TRP * (p.ks + 16) + TRP * (p.ks / 32) * 4 + 127) & ~127;
-  const int head = (20 * 8 + 8 + 127) & ~127;  // the barriers, headers and meeting counts of up to 8 stages
   const int most = 227 * 1024;
+  const int per_red = (RED_FLOATS + 128) * 4;  // a buffer of the warps' parts and one of w1's results
   int act = (int)(((size_t)MB * (K + 16) + 2 * (size_t)MB * (K / 32) * 4 + 127) & ~127);
-  const bool asmem = head + RED_BYTES + act + 2 * p.stage_bytes <= most;
+  const bool asmem = MMA_HEAD + 4 * per_red + act + 2 * p.stage_bytes <= most;
   if (!asmem) {
     if (pro != PRO_Q || (a.xq_stride & 3) || (a.xs_stride & 3)) return false;
     act = 0;
   }
   p.act_bytes = act;
-  int S = (most - head - RED_BYTES - act) / p.stage_bytes;
+  int S = (most - MMA_HEAD - 2 * per_red - act) / (p.stage_bytes + per_red);  // S stages and S + 2 buffers
   if (S > 8) S = 8;
   if (S < 2) return false;
   p.stages = S;
-  const size_t smem = (size_t)head + RED_BYTES + act + (size_t)S * p.stage_bytes;
+  p.nred = S + 2;
+  const size_t smem = (size_t)MMA_HEAD + (size_t)p.nred * per_red + act + (size_t)S * p.stage_bytes;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
   p.slot = (int)(next_ticket_slot(dev) % TICKET_SLOTS);
@@ -819,10 +854,14 @@ bool gemv_tma_t2(const GemvArgs& a, int pro, int epi, bool pdl) {
   TmaPlan p = {};
   p.chunks = 1;
   p.ks = K;
-  p.stage_bytes = (TRP * (K / 4) + TRP * units * 2 + 127) & ~127;
+  const int row_bytes = K / 4 + units * 2;
+  p.rw = 45056 / (NC * row_bytes);  // a stage of about 44 KB: up to 4 rows a warp (the shorter rows)
+  if (p.rw > 4) p.rw = 4;
+  if (p.rw < 1) p.rw = 1;
+  p.stage_bytes = (NC * p.rw * row_bytes + 127) & ~127;
   p.act_bytes = (int)((2 * (size_t)K + 2 * (size_t)(K / 32) * 4 + 127) & ~127);
   const int head = (20 * T2_STAGES + 127) & ~127;
-  int S = (g_tma_budget - head - p.act_bytes) / p.stage_bytes;
+  int S = (227 * 1024 - head - p.act_bytes) / p.stage_bytes;
   if (S > T2_STAGES) S = T2_STAGES;
   if (S < 2) return false;
   p.stages = S;

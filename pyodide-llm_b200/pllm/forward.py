@@ -56,6 +56,11 @@ class Config:
     relaxed: bool = False     # matmul_q8r's activations (bias 64, qmax 63) in place of matmul_q8's (qmax 127)
     half_kv: bool = True      # a float16 cache (to_f16 / attention_f16), as engine.ts:191 chooses for int8 models
     weights: str = "q8"       # the matrices' format: "q8" int8 groups of 32, "t2" packed ternary (ternary.ts)
+    kinds: str = ""           # an LFM2's layers, a letter each: "c" a convolution layer, "a" attention ("": all "a")
+    taps: int = 3             # a convolution layer's taps (conv_L_cache)
+
+    def kind(self, l):
+        return self.kinds[l] if self.kinds else "a"
 
     @property
     def qdim(self):
@@ -72,14 +77,20 @@ class Config:
 
     def weight_bytes(self):
         """The bytes a decode step reads of the matrices (values and scales)."""
-        per_layer = (self.qdim + 2 * self.kvdim) * self.dim + self.dim * self.qdim + 3 * self.hidden * self.dim
-        return int((self.layers * per_layer + self.vocab * self.dim) * self.bytes_per_weight)
+        attn = (self.qdim + 2 * self.kvdim) * self.dim + self.dim * self.qdim
+        conv = 3 * self.dim * self.dim + self.dim * self.dim
+        total = sum((conv if self.kind(l) == "c" else attn) + 3 * self.hidden * self.dim for l in range(self.layers))
+        return int((total + self.vocab * self.dim) * self.bytes_per_weight)
 
 
 # the BASELINE configurations (synthetic weights of these shapes)
 STORIES15M = Config(dim=288, hidden=768, layers=6, heads=6, kv_heads=6, head_size=48, vocab=32000, seq_len=256)
 QWEN3_8B = Config(dim=4096, hidden=12288, layers=36, heads=32, kv_heads=8, head_size=128, vocab=151936, seq_len=2560,
                   qk_norm=True, rope_theta=1e6, eps=1e-6)
+# configs[2]: the LFM2-350M-shaped hybrid: 10 short-convolution layers (3 taps) among 6 grouped-query attention layers
+# (16 q / 8 kv heads of 64, QK-norm), SwiGLU FFN 4608, 65536 vocab (the classifier the embedding's rows)
+LFM2_350M = Config(dim=1024, hidden=4608, layers=16, heads=16, kv_heads=8, head_size=64, vocab=65536, seq_len=768,
+                   qk_norm=True, rope_theta=1e6, eps=1e-5, kinds="ccaccaccacacacac", taps=3)
 # configs[4]: the 27B-class ternary decoder (every matrix ternary, the classifier too); 1024 + 256 positions
 TERNARY_27B = Config(dim=5120, hidden=21504, layers=62, heads=32, kv_heads=16, head_size=128, vocab=262144,
                      seq_len=1280, weights="t2")
@@ -175,6 +186,9 @@ class Engine:
             raise ValueError("a batch of sequences runs on one rank, with the fused kernels and a float16 cache")
         if cfg.weights not in ("q8", "t2") or (cfg.weights == "t2" and (exact or exchange or batch > 1)):
             raise ValueError("ternary matrices run the fused single-sequence step on one rank")
+        self.hybrid = "c" in cfg.kinds
+        if self.hybrid and (exact or exchange or cfg.weights != "q8" or not cfg.half_kv):
+            raise ValueError("convolution layers run the fused int8 step on one rank (one sequence or a batch)")
         self.fmt = F_T2 if cfg.weights == "t2" else F_Q8
         self.exact = exact
         self.batch = nb = int(batch)
@@ -203,6 +217,12 @@ class Engine:
         B["emb_s"] = Buffer(c.vocab * ng(c.dim) * 4)
         B["cls"] = Buffer(s.vocab * wb(c.dim))
         B["cls_s"] = Buffer(s.vocab * sb(c.dim))
+        if self.hybrid:  # a convolution layer's in (3 dim rows: B, C, x) and out matrices, its taps, its sequences' rows
+            B["win"], B["swin"] = Buffer(c.layers * 3 * c.dim * c.dim), Buffer(c.layers * 3 * c.dim * c.dim // 8)
+            B["wout"], B["swout"] = Buffer(c.layers * c.dim * c.dim), Buffer(c.layers * c.dim * c.dim // 8)
+            B["taps"] = Buffer(c.layers * c.taps * c.dim * 4)
+            B["rows"] = Buffer(c.layers * nb * c.taps * c.dim * 4).zero()
+            B["mixed"] = Buffer(nb * 3 * c.dim * 4)
         B["att_norm"] = Buffer(c.layers * c.dim * 4)
         B["ffn_norm"] = Buffer(c.layers * c.dim * 4)
         B["final_norm"] = Buffer(c.dim * 4)
@@ -218,7 +238,8 @@ class Engine:
         B["x"] = Buffer(nb * c.dim * 4)
         B["x1"] = Buffer(c.dim * 4) if exchange else None  # the residual's other buffer (tensor-parallel)
         B["qkv"] = Buffer(nb * self.rows_qkv * 4)
-        B["att"] = Buffer(nb * s.qdim * 4)
+        self.att_stride = max(s.qdim, c.dim) if self.hybrid else s.qdim  # a convolution layer's output too
+        B["att"] = Buffer(nb * self.att_stride * 4)
         B["hb"] = Buffer(nb * s.hidden * 4)
         B["logits"] = Buffer(nb * s.vocab * 4)
         B["tp"] = Buffer(8 * nb).zero()  # the tokens, then the positions, read by the kernels
@@ -271,6 +292,9 @@ class Engine:
         B["s2"].upload(W["s2"])
         for k in ("emb", "emb_s", "cls", "cls_s", "att_norm", "ffn_norm", "final_norm", "cos_t", "sin_t"):
             B[k].upload(W[k])
+        if self.hybrid:
+            for k in ("win", "swin", "wout", "swout", "taps"):
+                B[k].upload(W[k])
         if c.qk_norm:
             B["q_norm"].upload(W["q_norm"])
             B["k_norm"].upload(W["k_norm"])
@@ -296,6 +320,10 @@ class Engine:
                     ("w13", "s13", c.layers * 2 * c.hidden, c.dim), ("w2", "s2", c.layers * c.dim, c.hidden),
                     ("cls", "cls_s", c.vocab, c.dim)]):
                 L.pllm_synth_q8(B[w].ptr, B[sc].ptr, rows, cols, s + i, 0.02)
+        if self.hybrid:
+            L.pllm_synth_q8(B["win"].ptr, B["swin"].ptr, c.layers * 3 * c.dim, c.dim, s + 5, 0.02)
+            L.pllm_synth_q8(B["wout"].ptr, B["swout"].ptr, c.layers * c.dim, c.dim, s + 6, 0.02)
+            L.pllm_synth_f32(B["taps"].ptr, c.layers * c.taps * c.dim, s + 7, 0.0, 0.3)
         L.pllm_synth_q8(B["emb"].ptr, B["emb_s"].ptr, c.vocab, c.dim, s + 10, 1.0)
         for i, k in enumerate(("att_norm", "ffn_norm", "final_norm", "q_norm", "k_norm")):
             if B[k] is not None:
@@ -350,6 +378,12 @@ class Engine:
             W[k] = d(k, dt)
         W["q_norm"] = d("q_norm", np.float32) if c.qk_norm else None
         W["k_norm"] = d("k_norm", np.float32) if c.qk_norm else None
+        if self.hybrid:
+            W["win"] = d("win", np.int8).reshape(c.layers, 3 * c.dim, c.dim)
+            W["swin"] = d("swin", np.float32).reshape(c.layers, 3 * c.dim, c.dim // 32)
+            W["wout"] = d("wout", np.int8).reshape(c.layers, c.dim, c.dim)
+            W["swout"] = d("swout", np.float32).reshape(c.layers, c.dim, c.dim // 32)
+            W["taps"] = d("taps", np.float32).reshape(c.layers, c.taps, c.dim)
         return {k: (np.ascontiguousarray(v) if v is not None else None) for k, v in W.items()}
 
     def _host_weights_t2(self):
@@ -443,27 +477,42 @@ class Engine:
             L.pllm_gemv(out, ldo, xq, xs, k if xq else 0, k // 8 if xq else 0, xin, ldx, norm, c.eps, self.bias, wq, ws,
                         F_Q8, k, 0, rows, nb, pro, epi, pair, pdl)
         layer_cache = nb * c.seq_len * c.kvdim * E
+        A, d = self.att_stride, c.dim
         for l in range(c.layers):
+            if c.kind(l) == "c":  # the convolution layer of every sequence: its rows at rows + (l nb + z) taps dim
+                gemv(B["mixed"].ptr, 3 * d, x, d, B["att_norm"].ptr + l * d * 4, B["win"].ptr + l * 3 * d * d,
+                     B["swin"].ptr + l * 3 * d * (d // 32) * 4, 3 * d, d, PRO_RMS, EPI_STORE)
+                L.pllm_conv_step(att, A, B["taps"].ptr + l * c.taps * d * 4, B["rows"].ptr + l * nb * c.taps * d * 4,
+                                 c.taps * d, B["mixed"].ptr, 3 * d, d, c.taps, poss, nb)
+                gemv(x, d, att, A, 0, B["wout"].ptr + l * d * d, B["swout"].ptr + l * d * (d // 32) * 4, d, d,
+                     PRO_QUANT, EPI_ADD)
+                self._enqueue_batch_ffn(l, gemv)
+                continue
             gemv(qkv, R, x, c.dim, B["att_norm"].ptr + l * c.dim * 4, B["wqkv"].ptr + l * R * c.dim,
                  B["sqkv"].ptr + l * R * (c.dim // 32) * 4, R, c.dim, PRO_RMS, EPI_STORE)
             qn = B["q_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
             kn = B["k_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
-            L.pllm_attention_step_batch(att, c.qdim, qkv, R, B["kc"].ptr + l * layer_cache,
+            L.pllm_attention_step_batch(att, A, qkv, R, B["kc"].ptr + l * layer_cache,
                                         B["vc"].ptr + l * layer_cache, c.seq_len * c.kvdim * E, B["scratch"].ptr, poss,
                                         nb, c.seq_len, c.heads, c.kv_heads, c.head_size, 0.0, self.SPLIT, qn, kn,
                                         B["cos_t"].ptr, B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, pdl)
-            gemv(x, c.dim, att, c.qdim, 0, B["wo"].ptr + l * c.dim * c.qdim,
+            gemv(x, c.dim, att, A, 0, B["wo"].ptr + l * c.dim * c.qdim,
                  B["so"].ptr + l * c.dim * (c.qdim // 32) * 4, c.dim, c.qdim, PRO_QUANT, EPI_ADD)
-            gemv(hb, c.hidden, x, c.dim, B["ffn_norm"].ptr + l * c.dim * 4, B["w13"].ptr + l * 2 * c.hidden * c.dim,
-                 B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.hidden, c.dim, PRO_RMS, EPI_SWIGLU,
-                 pair=c.hidden)
-            # w2's K (the hidden width) is quantized first, its activations then read from global memory
-            L.pllm_quantize_tokens(B["hq"].ptr, B["hq_scales"].ptr, hb, c.hidden, self.bias, nb)
-            gemv(x, c.dim, 0, 0, 0, B["w2"].ptr + l * c.dim * c.hidden, B["s2"].ptr + l * c.dim * (c.hidden // 32) * 4,
-                 c.dim, c.hidden, PRO_Q, EPI_ADD, xq=B["hq"].ptr, xs=B["hq_scales"].ptr)
+            self._enqueue_batch_ffn(l, gemv)
         if need_logits:
             gemv(B["logits"].ptr, c.vocab, x, c.dim, B["final_norm"].ptr, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim,
                  PRO_RMS, EPI_STORE)
+
+    def _enqueue_batch_ffn(self, l, gemv):
+        """Layer l's gated FFN of the batch's sequences; w2's K (the hidden width) quantized first, its activations then
+        read from global memory by the batched product."""
+        c, B, nb = self.cfg, self.B, self.batch
+        x, hb = B["x"].ptr, B["hb"].ptr
+        gemv(hb, c.hidden, x, c.dim, B["ffn_norm"].ptr + l * c.dim * 4, B["w13"].ptr + l * 2 * c.hidden * c.dim,
+             B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.hidden, c.dim, PRO_RMS, EPI_SWIGLU, pair=c.hidden)
+        L.pllm_quantize_tokens(B["hq"].ptr, B["hq_scales"].ptr, hb, c.hidden, self.bias, nb)
+        gemv(x, c.dim, 0, 0, 0, B["w2"].ptr + l * c.dim * c.hidden, B["s2"].ptr + l * c.dim * (c.hidden // 32) * 4,
+             c.dim, c.hidden, PRO_Q, EPI_ADD, xq=B["hq"].ptr, xs=B["hq_scales"].ptr)
 
     def _enqueue_step(self, need_logits=True):
         if self.batch > 1:
@@ -478,6 +527,10 @@ class Engine:
         wb, sb = self.wb, self.sb
         L.pllm_embed_q8(B["x"].ptr, B["emb"].ptr, B["emb_s"].ptr, tok, 0, c.dim, 1, c.dim)
         for l in range(c.layers):
+            if c.kind(l) == "c":
+                self._enqueue_conv(l, pos)
+                self._enqueue_ffn(l)
+                continue
             wqkv = B["wqkv"].ptr + l * self.rows_qkv * wb(c.dim)
             sqkv = B["sqkv"].ptr + l * self.rows_qkv * sb(c.dim)
             self._gemv(B["qkv"].ptr, wqkv, sqkv, self.rows_qkv, c.dim, B["x"].ptr, B["att_norm"].ptr + l * c.dim * 4,
@@ -491,14 +544,30 @@ class Engine:
                                   B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, int(self.pdl))
             self._gemv(B["x"].ptr, B["wo"].ptr + l * c.dim * wb(c.qdim), B["so"].ptr + l * c.dim * sb(c.qdim),
                        c.dim, c.qdim, B["att"].ptr, 0, PRO_QUANT, EPI_ADD)
-            self._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * c.hidden * wb(c.dim),
-                       B["s13"].ptr + l * 2 * c.hidden * sb(c.dim), c.hidden, c.dim, B["x"].ptr,
-                       B["ffn_norm"].ptr + l * c.dim * 4, PRO_RMS, EPI_SWIGLU, pair=c.hidden)
-            self._gemv(B["x"].ptr, B["w2"].ptr + l * c.dim * wb(c.hidden), B["s2"].ptr + l * c.dim * sb(c.hidden),
-                       c.dim, c.hidden, B["hb"].ptr, 0, PRO_QUANT, EPI_ADD)
+            self._enqueue_ffn(l)
         if need_logits:
             self._gemv(B["logits"].ptr, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim, B["x"].ptr, B["final_norm"].ptr,
                        PRO_RMS, EPI_STORE)
+
+    def _enqueue_ffn(self, l):
+        """Layer l's gated FFN of one sequence: x += w2 . quantize_x(silu(w1 . h) * (w3 . h)), h = RMSNorm(x)."""
+        c, B, wb, sb = self.cfg, self.B, self.wb, self.sb
+        self._gemv(B["hb"].ptr, B["w13"].ptr + l * 2 * c.hidden * wb(c.dim), B["s13"].ptr + l * 2 * c.hidden * sb(c.dim),
+                   c.hidden, c.dim, B["x"].ptr, B["ffn_norm"].ptr + l * c.dim * 4, PRO_RMS, EPI_SWIGLU, pair=c.hidden)
+        self._gemv(B["x"].ptr, B["w2"].ptr + l * c.dim * wb(c.hidden), B["s2"].ptr + l * c.dim * sb(c.hidden), c.dim,
+                   c.hidden, B["hb"].ptr, 0, PRO_QUANT, EPI_ADD)
+
+    def _enqueue_conv(self, l, pos):
+        """An LFM2 convolution layer of one sequence (forward/convolution.ts:51-60): mixed = win . quantize_x(RMSNorm
+        (x)) ([B | C | z]), the rows' shift and the causal convolution (pllm_conv_step), x += wout . quantize_x(it)."""
+        c, B = self.cfg, self.B
+        d = c.dim
+        self._gemv(B["mixed"].ptr, B["win"].ptr + l * 3 * d * d, B["swin"].ptr + l * 3 * d * (d // 32) * 4, 3 * d, d,
+                   B["x"].ptr, B["att_norm"].ptr + l * d * 4, PRO_RMS, EPI_STORE)
+        L.pllm_conv_step(B["att"].ptr, 0, B["taps"].ptr + l * c.taps * d * 4, B["rows"].ptr + l * c.taps * d * 4, 0,
+                         B["mixed"].ptr, 0, d, c.taps, pos, 1)
+        self._gemv(B["x"].ptr, B["wout"].ptr + l * d * d, B["swout"].ptr + l * d * (d // 32) * 4, d, d, B["att"].ptr, 0,
+                   PRO_QUANT, EPI_ADD)
 
     def _enqueue_tp_step(self, need_logits=True):
         """One tensor-parallel step: reduction 2 l after layer l's wo (summed into x1 by its w1/w3 product), 2 l + 1
@@ -681,7 +750,7 @@ class Engine:
     def can_prefill(self):
         """The tensor-core prefill's shapes: products with K and rows in whole 128s, a float16 cache, one rank."""
         c, sh = self.cfg, self.shard
-        return (not self.xg and not self.exact and self.fmt == F_Q8 and c.half_kv and c.head_size <= 128 and all(
+        return (not self.xg and not self.exact and not self.hybrid and self.fmt == F_Q8 and c.half_kv and c.head_size <= 128 and all(
             v % 128 == 0 for v in (c.dim, sh.qdim, sh.hidden, self.rows_qkv)))
 
     def _prefill_buffers(self, M):

@@ -114,3 +114,21 @@ def test_prefill_equals_token_by_token_at_8b_width():
     assert same0 > 0.995 and rel1 < 2e-2
     a.close()
     b.close()
+
+
+def test_8b_width_prefill_matches_oracle():
+    """Qwen3-8B's widths, two layers, a 64-token prompt through the tensor-core prefill against the oracle's forward
+    of the same tokens (the reference kernels' arithmetic, token after token, on the device's weights), at the int8
+    engine's line (2e-2 of the largest logit); then two decode steps on the cache the prefill wrote, at the same line."""
+    cfg = replace(QWEN3_8B, layers=2, seq_len=96)
+    eng = Engine(cfg, seed=4)
+    W = eng.host_weights()
+    prompt = np.random.default_rng(6).integers(0, cfg.vocab, 64)
+    got = eng.prefill(prompt, 0)
+    want, A = oracle_run(cfg, W, prompt)
+    close(got, want, "8B-width prefill of 64 tokens against the oracle")
+    for i, t in enumerate([17, 40001]):
+        got = eng.forward(t, 64 + i)
+        want, _ = oracle_run(cfg, W, [t], 64 + i, A)
+        close(got, want, f"decode at {64 + i} after the prefill")
+    eng.close()
