@@ -283,8 +283,10 @@ void pllm_delta_rule_block(uint64_t out, int64_t out_stride, uint64_t state, uin
                            int64_t c_stride, uint64_t work, int64_t work_stride, int32_t count, int32_t kh, int32_t kd,
                            int32_t vd, int32_t vh, int32_t h0, int32_t h1);
 
-/* a bounded device-side wait (an mbarrier of the bulk-copy product) gave up since the last call: PLLM_ETIMEOUT (3),
- * else 0; reading it clears it (and, after a wait that gave up, puts the products' tile counters back to zero) */
+/* a bounded device-side wait (an mbarrier of the bulk-copy product) gave up since the last call: PLLM_ETIMEOUT (3);
+ * or the attention step read a position from device memory outside its cache (held at the cache's edge, so that
+ * nothing is read or written outside it): PLLM_ERANGE (5); else 0. Reading it clears it (and, after a wait that gave
+ * up, puts the products' tile counters back to zero) */
 int32_t pllm_device_status(void);
 /* which decode-product kernel: 0 the bulk-copy pipeline where it applies (int8 weights, 1 or 2 tokens), 1 the
  * register-streaming kernel always; returns the previous mode */

@@ -20,6 +20,10 @@
 
 #include "pllm_common.cuh"
 
+namespace gemvk {
+int* status_word();  // the device status word's address on the current device (gemv_tma.cu)
+}
+
 namespace {
 
 constexpr int ATT_THREADS = 128, ATT_WARPS = ATT_THREADS / 32;
@@ -42,7 +46,20 @@ struct AttArgs {
   // words), and its position is pos_dev[z]
   int batch;
   long long z_out, z_q, z_kv, z_part;
+  int capacity;         // the cache's positions (a device position past them is held at the last: see position())
+  int* status;          // the device status word (PLLM_ERANGE: a device position out of the cache)
 };
+
+// the call's position: the host's, or the one in device memory held inside the cache (a position below 0 or past the
+// cache's capacity is taken as the first or last row and reported in the status word as PLLM_ERANGE, so that no
+// read or write leaves the cache or the rope tables)
+__device__ __forceinline__ int position(const AttArgs& a) {
+  if (!a.pos_dev) return a.pos;
+  const int pos = *a.pos_dev;
+  if (pos >= 0 && pos < a.capacity) return pos;
+  if (a.status && threadIdx.x == 0) atomicExch(a.status, PLLM_ERANGE);
+  return pos < 0 ? 0 : a.capacity - 1;
+}
 
 // sequence z's arguments (grid z) from sequence 0's, each array assigned from the launch's own argument
 __device__ __forceinline__ AttArgs sequence_of(const AttArgs& a0, int z) {
@@ -240,7 +257,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_f32_kernel(const AttArg
   __shared__ float sM[KVM], sL[KVM], sScale[KVM];
   pdl_launch_dependents();  // the next kernel waits for this one's completion; its CTAs may take the SMs this one leaves
   // the position: written by the host before the step's first kernel, so readable before the dependency wait
-  const int pos = a.pos_dev ? *a.pos_dev : a.pos;
+  const int pos = position(a);
   const int count = pos + 1;
   const int kvh = blockIdx.x, split = blockIdx.y;
   const int nsplit = a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
@@ -454,7 +471,7 @@ __global__ void __launch_bounds__(32 * W, 1) attention_chunk_kernel(const AttArg
   if constexpr (CL) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   pdl_launch_dependents();  // the next kernel waits for this one's completion; its CTAs may take the SMs this one leaves
   // the position: written by the host before the step's first kernel, so readable before the dependency wait
-  const int pos = a.pos_dev ? *a.pos_dev : a.pos;
+  const int pos = position(a);
   const int count = pos + 1;
   const int kvh = CL ? blockIdx.y : blockIdx.x, split = CL ? 0 : blockIdx.y;
   const int rank = CL ? blockIdx.x : 0;  // the CTA's rank in its cluster
@@ -766,7 +783,7 @@ __global__ void __launch_bounds__(32 * W, 1) attention_chunk_kernel(const AttArg
 __global__ void attention_combine_kernel(const AttArgs a0) {
   const AttArgs a = sequence_of(a0, blockIdx.z);
   pdl_wait();
-  const int pos = a.pos_dev ? *a.pos_dev : a.pos;
+  const int pos = position(a);
   const int count = pos + 1;
   const int nsplit = a.pos_dev ? (count + a.split_len - 1) / a.split_len : a.nsplit;
   const int h = a.h0 + blockIdx.x;
@@ -1410,6 +1427,8 @@ PLLM_API void pllm_attention_dev(uint64_t out, uint64_t q, uint64_t kc, uint64_t
   a.nsplit = (capacity + split_len - 1) / split_len;
   a.cap = cap;
   a.counters = dptr<int>(scratch + partial_bytes(nh, hs, capacity, split_len));
+  a.capacity = capacity;
+  a.status = gemvk::status_word();
   run_attention("pllm_attention_dev", a, half != 0, pdl != 0);
 }
 
@@ -1439,6 +1458,8 @@ PLLM_API void pllm_attention_step(uint64_t out, uint64_t qkv, uint64_t kc, uint6
   a.nsplit = (capacity + split_len - 1) / split_len;
   a.cap = cap;
   a.counters = dptr<int>(scratch + partial_bytes(nh, hs, capacity, split_len));
+  a.capacity = capacity;
+  a.status = gemvk::status_word();
   Fuse f = {};
   f.k = dptr<const float>(qkv) + (long long)nh * hs;
   f.v = f.k + (long long)nkv * hs;
@@ -1490,6 +1511,8 @@ PLLM_API void pllm_attention_step_batch(uint64_t out, int64_t out_stride, uint64
   a.z_q = qkv_stride;
   a.z_kv = cache_stride;
   a.z_part = (long long)(per / 4);
+  a.capacity = capacity;
+  a.status = gemvk::status_word();
   Fuse f = {};
   f.k = dptr<const float>(qkv) + (long long)nh * hs;
   f.v = f.k + (long long)nkv * hs;

@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const GemvArgs a) {
       for (int t = 1; t < MT; t++)
         if (lane == t) v = acc[t];
       float* o = a.out + lane * a.out_stride + row;
-      if (EPI == EPI_ADD) *o += v;
+      if (EPI == EPI_ADD) add_once(o, v);
       else *o = v;
     }
   }

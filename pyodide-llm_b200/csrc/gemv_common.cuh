@@ -160,6 +160,11 @@ __device__ __forceinline__ void quantize_pair(const GemvArgs& a, const float4* x
 struct CtaSync {
   __device__ __forceinline__ void operator()() const { __syncthreads(); }
 };
+// out += v where a launch adds to each output once: red.global.add.f32, the same rounded sum as a load and a store
+// without the consumer warp waiting on the load (measured on the Qwen3-8B decode step: 2.009 -> 1.965 ms); the add
+// flushes a subnormal sum to zero
+__device__ __forceinline__ void add_once(float* o, float v) { atomicAdd(o, v); }
+
 // x's float4 number i of token t: PRO_RMS_SUM adds the ranks' partials in rank order (waiting for their slots) and
 // CTA 0 stores the sum to x_out
 template <int PRO>

@@ -18,7 +18,11 @@
 //
 // The rows are dealt as tiles of 8 from a ticket counter, not as fixed shares: each CTA's producer takes the next
 // tile's ticket while the current tile streams, so the CTAs that start early (on SMs the kernel ahead leaves first)
-// stream more of the matrix and none waits at the end for a late one's fixed share. A tile is all its stages in a row
+// stream more of the matrix and none waits at the end for a late one's fixed share. Until its consumers have their
+// activations a CTA takes no more than its even share of the tiles (Dealer): one that starts early would fill its
+// whole ring while the kernel ahead still runs, then consume those tiles one after another while the CTAs that start
+// later find none (measured on the 4096 x 4096 product after attention: 6 tiles on 68 CTAs, none on 18). A tile is
+// all its stages in a row
 // (EPI_SWIGLU: its w1 rows, then the same rows of w3; K cut into chunks: a stage a chunk), and the producer writes the
 // tile's first row and row count into the stage's header before the copies' barrier completes, so a consumer warp
 // reads it after its wait, with no barrier among the consumers. Every CTA's producer takes exactly one ticket past the
@@ -95,6 +99,23 @@ struct TmaPlan {
   int rw;           // the ternary form's rows a consumer warp (a tile NC rw rows)
 };
 
+// The ticket dealing of one CTA's producer (see the file's head). started: set by the consumers once they have their
+// activations.
+struct Dealer {
+  unsigned* ticket;
+  unsigned fair, taken;
+  const volatile int* started;
+  __device__ Dealer(unsigned* t, unsigned tiles, const int* st)
+      : ticket(t), fair((tiles + gridDim.x - 1) / gridDim.x), taken(0), started(st) {}
+  // the next ticket; past an even share, not before the consumers have started (a bounded wait: a hint only)
+  __device__ __forceinline__ unsigned take() {
+    if (taken >= fair)
+      for (long long i = 0; !*started && i < WAIT_BOUND; i++) __nanosleep(32);
+    taken++;
+    return atomicAdd(ticket, 1u);
+  }
+};
+
 // this CTA's rows: [lo, hi) of [r0, r1), near-equal shares
 __device__ __forceinline__ void cta_rows(const GemvArgs& a, long long& lo, long long& hi) {
   const long long rows = a.r1 - a.r0, G = gridDim.x, c = blockIdx.x;
@@ -123,7 +144,7 @@ __device__ __forceinline__ int group_dot(const uint8_t* w, int swz, const int4 x
 // consumer's fragment reads are then free of bank conflicts), the scales after TRP such rows.
 template <int PHASES, bool PAD>
 __device__ __forceinline__ void produce(const GemvArgs& a, const TmaPlan& p, uint64_t* full, uint64_t* empty, int* hdr,
-                                        uint8_t* stage0) {
+                                        uint8_t* stage0, const int* started) {
   const int S = p.stages, KS = p.ks, chunks = p.chunks, K = a.K, ng = K / 32;
   const int RS = PAD ? KS + 16 : KS;
   uint64_t policy;
@@ -132,14 +153,15 @@ __device__ __forceinline__ void produce(const GemvArgs& a, const TmaPlan& p, uin
   unsigned* ticket = g_tickets + p.slot;
   long long lo = a.r0, hi = a.r1;  // the rows this CTA streams: all of them by tickets, or its own share
   if (!p.tickets) cta_rows(a, lo, hi);
-  unsigned next = p.tickets ? atomicAdd(ticket, 1u) : 0u;
+  Dealer deal(ticket, tiles, started);
+  unsigned next = p.tickets ? deal.take() : 0u;
   long long it = 0;
   for (long long ts = lo;;) {
     long long t;
     if (p.tickets) {
       if (next >= tiles) break;
       t = a.r0 + (long long)next * TRP;
-      next = atomicAdd(ticket, 1u);  // the following tile's ticket, on its way while this tile streams
+      next = deal.take();  // the following tile's ticket, on its way while this tile streams
     } else {
       if (ts >= hi) break;
       t = ts;
@@ -184,6 +206,20 @@ __device__ __forceinline__ void produce(const GemvArgs& a, const TmaPlan& p, uin
   if (p.tickets && next == tiles + gridDim.x - 1) atomicExch(ticket, 0u);  // the last ticket of the launch
 }
 
+// a finished row's value of token t: stored, added, or sent to the ranks' exchange slots
+template <int EPI>
+__device__ __forceinline__ void emit(const GemvArgs& a, const Xchg& xg, int t, long long row, float v) {
+  float* o = a.out + t * a.out_stride + row;
+  if (EPI == EPI_SEND) {
+    const unsigned mark = xchg_mark(xg);
+    for (int r = 0; r < xg.world; r++) st_slot(xg.dst[r] + row, v, mark);
+  } else if (EPI == EPI_ADD) {
+    add_once(o, v);
+  } else {
+    *o = v;
+  }
+}
+
 template <int MT, int PRO, int EPI>
 __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs a, const TmaPlan p, const Xchg xg) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -191,7 +227,8 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
   int* hdr = reinterpret_cast<int*>(smem + 16 * S);  // [S] a stage's tile: its first row from r0 x 16 + its rows; -1: the end
-  uint8_t* act = smem + ((20 * S + 127) & ~127);
+  int* started = hdr + S;                            // the consumers have their activations
+  uint8_t* act = smem + ((20 * S + 4 + 127) & ~127);
   int8_t* sq = reinterpret_cast<int8_t*>(act);
   float* ss = reinterpret_cast<float*>(act + (size_t)MT * K);
   uint8_t* stage0 = act + p.act_bytes;
@@ -206,12 +243,13 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NC);
     }
+    *started = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
   if (warp == NC) {  // ---- the producer
-    if (lane == 0) produce<PHASES, false>(a, p, full, empty, hdr, stage0);
+    if (lane == 0) produce<PHASES, false>(a, p, full, empty, hdr, stage0, started);
     return;
   }
 
@@ -219,6 +257,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
   pdl_wait();
   load_activations<F_Q8, MT, PRO, ConsumerSync>(a, sq, ss, nullptr, &xg);
   consumer_sync();
+  if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(started) = 1;
   pdl_launch_dependents();
   const int swz = (lane >> 2) & 1;  // which half of its 32 bytes a lane reads first: no bank conflicts
   // one token and rows of at most 32 x RG groups in one chunk: a lane's activation groups (the same for every row) and
@@ -297,15 +336,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_kernel(const GemvArgs
         if (ph == 0) h1 = v;
         else a.out[lane * a.out_stride + row] = (h1 / (1.0f + expf(-h1))) * v;
       } else {
-        float* o = a.out + lane * a.out_stride + row;
-        if (EPI == EPI_SEND) {
-          const unsigned mark = xchg_mark(xg);
-          for (int r = 0; r < xg.world; r++) st_slot(xg.dst[r] + row, v, mark);
-        } else if (EPI == EPI_ADD) {
-          *o += v;
-        } else {
-          *o = v;
-        }
+        emit<EPI>(a, xg, lane, row, v);
       }
     }
   }
@@ -388,6 +419,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_mma_kernel(const Gemv
   uint64_t* empty = full + S;
   int* hdr = reinterpret_cast<int*>(smem + 16 * S);
   int* cnt = reinterpret_cast<int*>(smem + 20 * S);  // [NRED] the warps arrived at a phase-end
+  int* started = cnt + NRED;                         // the consumers have their activations
   float* red = reinterpret_cast<float*>(smem + MMA_HEAD);  // [NRED][NC][128]
   float* hsave = red + NRED * RED_FLOATS;                     // [NRED][128]
   uint8_t* act = reinterpret_cast<uint8_t*>(hsave + NRED * 128);
@@ -404,11 +436,12 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_mma_kernel(const Gemv
       mbar_init(&empty[s], NC);
     }
     for (int i = 0; i < NRED; i++) cnt[i] = 0;
+    *started = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   if (warp == NC) {
-    if (lane == 0) produce<PHASES, true>(a, p, full, empty, hdr, stage0);
+    if (lane == 0) produce<PHASES, true>(a, p, full, empty, hdr, stage0, started);
     return;
   }
   pdl_wait();
@@ -418,6 +451,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_mma_kernel(const Gemv
     for (int i = tid; i < MB * ng; i += NC * 32) sst[(i % ng) * MB + i / ng] = ss[i];
     consumer_sync();
   }
+  if (tid == 0) *reinterpret_cast<volatile int*>(started) = 1;
   pdl_launch_dependents();
   const int g = lane >> 2, t4 = lane & 3;
   // ldmatrix rows: A (tokens (lane & 7) + 8 ((lane >> 3) & 1), bytes 16 (lane >> 4) of a group), B (weight rows lane & 7,
@@ -499,7 +533,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_mma_kernel(const Gemv
             const float h1 = hsave[(int)((pe - 1) % NRED) * 128 + e];
             *o = (h1 / (1.0f + expf(-h1))) * v;
           } else if (EPI == EPI_ADD) {
-            *o += v;
+            add_once(o, v);
           } else {
             *o = v;
           }
@@ -543,20 +577,28 @@ bool launch_mma(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl) {
 // bytes, chunk c of unit u stored at slot c ^ (u & 7): the lanes' reads of consecutive units do not share banks.
 constexpr int T2_STAGES = 16;
 
+// four unsigned bytes of a times four signed bytes of b, plus c (dp4a.u32.s32)
+__device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 template <int PHASES>
 __device__ __forceinline__ void produce_t2(const GemvArgs& a, const TmaPlan& p, uint64_t* full, uint64_t* empty,
-                                           int* hdr, uint8_t* stage0) {
+                                           int* hdr, uint8_t* stage0, const int* started) {
   const int S = p.stages, K = a.K, units = K / 128, T = NC * p.rw;
   const int cb = K / 4, sb = units * 2;  // a row's code bytes and scale bytes
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
   const unsigned tiles = (unsigned)((a.r1 - a.r0 + T - 1) / T);
   unsigned* ticket = g_tickets + p.slot;
-  unsigned next = atomicAdd(ticket, 1u);
+  Dealer deal(ticket, tiles, started);
+  unsigned next = deal.take();
   long long it = 0;
   while (next < tiles) {
     const long long t = a.r0 + (long long)next * T;
-    next = atomicAdd(ticket, 1u);
+    next = deal.take();
     const int n = (int)min((long long)T, a.r1 - t);
     for (int ph = 0; ph < PHASES; ph++, it++) {
       const long long row0 = t + (ph ? a.pair : 0);
@@ -584,7 +626,8 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_t2_kernel(const GemvA
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
   int* hdr = reinterpret_cast<int*>(smem + 16 * S);
-  uint8_t* act = smem + ((20 * T2_STAGES + 127) & ~127);
+  int* started = hdr + S;  // the consumers have their activations
+  uint8_t* act = smem + ((20 * T2_STAGES + 4 + 127) & ~127);
   int8_t* sq = reinterpret_cast<int8_t*>(act);            // [K] the prologue's activations, in order
   uint8_t* si = act + K;                                   // [K] interleaved, chunks swizzled
   float* ss = reinterpret_cast<float*>(act + 2 * (size_t)K);  // [ng] scales
@@ -597,11 +640,12 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_t2_kernel(const GemvA
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NC);
     }
+    *started = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   if (warp == NC) {
-    if (lane == 0) produce_t2<PHASES>(a, p, full, empty, hdr, stage0);
+    if (lane == 0) produce_t2<PHASES>(a, p, full, empty, hdr, stage0, started);
     return;
   }
   pdl_wait();
@@ -651,6 +695,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_t2_kernel(const GemvA
     }
   }
   consumer_sync();
+  if (tid == 0) *reinterpret_cast<volatile int*>(started) = 1;
   pdl_launch_dependents();
   constexpr int RWM = 4;  // the most rows a warp
   const int rw = p.rw, T = NC * rw;
@@ -682,15 +727,19 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_t2_kernel(const GemvA
           for (int r = 0; r < RWM; r++) {
             if (r >= mine) break;
             const uint4 cw = *reinterpret_cast<const uint4*>(w + (size_t)r * cb + (size_t)u * 32 + 16 * h);
-            int g0 = 0, g1 = 0;
+            // plane p's codes left in place (times 4^p, unsigned bytes up to 192) against the signed activations: 4^p
+            // times the plane's sum, exactly; the planes' sums shifted back and added
+            int q0[4], q1[4];
 #pragma unroll
             for (int pl = 0; pl < 4; pl++) {
-              const unsigned sh = 2 * pl;
-              g0 = __dp4a((int)((cw.x >> sh) & 0x03030303u), av[pl].x, g0);
-              g0 = __dp4a((int)((cw.y >> sh) & 0x03030303u), av[pl].y, g0);
-              g1 = __dp4a((int)((cw.z >> sh) & 0x03030303u), av[pl].z, g1);
-              g1 = __dp4a((int)((cw.w >> sh) & 0x03030303u), av[pl].w, g1);
+              const unsigned m = 0x03030303u << (2 * pl);
+              q0[pl] = dp4a_us(cw.x & m, av[pl].x, 0);
+              q0[pl] = dp4a_us(cw.y & m, av[pl].y, q0[pl]);
+              q1[pl] = dp4a_us(cw.z & m, av[pl].z, 0);
+              q1[pl] = dp4a_us(cw.w & m, av[pl].w, q1[pl]);
             }
+            const int g0 = q0[0] + (q0[1] >> 2) + (q0[2] >> 4) + (q0[3] >> 6);
+            const int g1 = q1[0] + (q1[1] >> 2) + (q1[2] >> 4) + (q1[3] >> 6);
             const float d = half_bits_to_float(d16[(size_t)r * units + u]);
             acc[r] += __fmul_rn(__fmul_rn((float)(g0 + m0), x0), d) + __fmul_rn(__fmul_rn((float)(g1 + m1), x1), d);
           }
@@ -708,7 +757,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_t2_kernel(const GemvA
           if (ph == 0) h1[r] = v;
           else a.out[row] = (h1[r] / (1.0f + expf(-h1[r]))) * v;
         } else if (EPI == EPI_ADD) {
-          a.out[row] += v;
+          add_once(a.out + row, v);
         } else {
           a.out[row] = v;
         }
@@ -860,7 +909,7 @@ bool gemv_tma_t2(const GemvArgs& a, int pro, int epi, bool pdl) {
   if (p.rw < 1) p.rw = 1;
   p.stage_bytes = (NC * p.rw * row_bytes + 127) & ~127;
   p.act_bytes = (int)((2 * (size_t)K + 2 * (size_t)(K / 32) * 4 + 127) & ~127);
-  const int head = (20 * T2_STAGES + 127) & ~127;
+  const int head = (20 * T2_STAGES + 4 + 127) & ~127;
   int S = (227 * 1024 - head - p.act_bytes) / p.stage_bytes;
   if (S > T2_STAGES) S = T2_STAGES;
   if (S < 2) return false;
@@ -911,7 +960,7 @@ bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg
   const int MT = a.count;
   p.stage_bytes = (TRP * p.ks + TRP * (p.ks / 32) * 4 + 127) & ~127;
   p.act_bytes = (int)((MT * (size_t)K + MT * (size_t)(K / 32) * 4 + 127) & ~127);
-  const int head = (20 * 8 + 127) & ~127;  // the barriers and headers of up to 8 stages
+  const int head = (20 * 8 + 4 + 127) & ~127;  // the barriers, headers and started flag of up to 8 stages
   int S = (g_tma_budget - p.act_bytes - head) / p.stage_bytes;
   if (S > 8) S = 8;
   if (S < 2) return false;

@@ -28,6 +28,7 @@ enum PllmError {
   PLLM_ECUDA = 2,      // a CUDA call or launch failed
   PLLM_ETIMEOUT = 3,   // a bounded device-side wait gave up
   PLLM_ENOMEM = 4,
+  PLLM_ERANGE = 5,     // a position read from device memory lay outside the cache (held at its edge)
 };
 
 // check the launch that was just enqueued

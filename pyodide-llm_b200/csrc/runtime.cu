@@ -57,6 +57,10 @@ static int check(cudaError_t e, const char* what) {
 }
 
 // ---- device and errors
+namespace gemvk {
+int* status_word();  // gemv_tma.cu
+}
+
 PLLM_API int32_t pllm_init(int32_t device) {
   if (check(cudaSetDevice(device), "cudaSetDevice")) return -1;
   g_device = device;
@@ -69,7 +73,10 @@ PLLM_API int32_t pllm_init(int32_t device) {
               major, minor);
     return -1;
   }
-  return check(cudaFree(nullptr), "context");
+  if (check(cudaFree(nullptr), "context")) return -1;
+  // the device status word's address, looked up here once, outside any stream capture (the kernels that report
+  // through it take it at launch)
+  return gemvk::status_word() ? 0 : -1;
 }
 
 PLLM_API int32_t pllm_last_error(char* buf, int32_t len) {

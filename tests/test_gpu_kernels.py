@@ -610,6 +610,52 @@ def test_attention_step(half, nh, nkv, hs, qk):
     assert np.all(counts == 0)
 
 
+@pytest.mark.parametrize("mode", [1, 0], ids=["clusters", "slices"])
+@pytest.mark.parametrize("written", [307, -3])
+def test_attention_step_holds_a_device_position_in_the_cache(mode, written):
+    """A position in device memory outside the cache (the host's calls check theirs; a graph reads what is there):
+    the step takes the cache's last (or first) row instead, reads and writes nothing outside the cache, and reports
+    PLLM_ERANGE (5) in the device status word, which reading clears."""
+    nh, nkv, hs, cap, split, eps = 8, 2, 128, 300, 64, 1e-6
+    held = cap - 1 if written >= cap else 0
+    rng = np.random.default_rng(cap)
+    kvdim = nkv * hs
+    kc0 = O.to_f16(rng.normal(0, 1, (cap, kvdim)).astype(np.float32))[0].reshape(cap, kvdim)
+    vc0 = O.to_f16(rng.normal(0, 1, (cap, kvdim)).astype(np.float32))[0].reshape(cap, kvdim)
+    ang = np.outer(np.arange(cap), 1.0 / 1e4 ** (np.arange(0, hs, 2) / hs))
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    # guard rows around the cache: a write outside it would show there
+    pad = 4 * kvdim
+    KC = dev(np.concatenate([np.full(pad, 0x7777, np.uint16), kc0.reshape(-1), np.full(pad, 0x7777, np.uint16)]))
+    VC = dev(np.concatenate([np.full(pad, 0x7777, np.uint16), vc0.reshape(-1), np.full(pad, 0x7777, np.uint16)]))
+    scratch = dev(np.zeros(L.pllm_attention_scratch_bytes(nh, hs, cap, split) // 4 + 1, np.float32))
+    qkv = rng.normal(0, 1, (nh + 2 * nkv) * hs).astype(np.float32)
+    out, bad = dev(np.zeros(nh * hs, np.float32)), dev(np.zeros(1, np.int32))
+    P = dev(np.array([0, written], np.int32))
+    old = L.pllm_set_attention_mode(mode)
+    try:
+        assert L.pllm_device_status() == 0
+        L.pllm_attention_step(out.ptr, dev(qkv).ptr, KC.ptr + 2 * pad, VC.ptr + 2 * pad, scratch.ptr, P.ptr + 4, cap,
+                              nh, nkv, hs, 1, 0.0, split, 0, 0, dev(cos).ptr, dev(sin).ptr, 0, eps, bad.ptr, 0)
+        check("pllm_attention_step")
+        assert L.pllm_device_status() == 5
+        assert L.pllm_device_status() == 0
+    finally:
+        L.pllm_set_attention_mode(old)
+    k, v = qkv[nh * hs: nh * hs + kvdim], qkv[nh * hs + kvdim:]
+    q = O.rope(qkv[: nh * hs], cos[held], sin[held], nh, hs)
+    k = O.rope(k, cos[held], sin[held], nkv, hs)
+    kc, vc = kc0.copy(), vc0.copy()
+    kc[held], vc[held] = O.to_f16(k)[0], O.to_f16(v)[0]
+    got_k, got_v = get(KC, np.uint16), get(VC, np.uint16)
+    assert np.all(got_k[:pad] == 0x7777) and np.all(got_k[-pad:] == 0x7777)
+    assert np.all(got_v[:pad] == 0x7777) and np.all(got_v[-pad:] == 0x7777)
+    assert np.array_equal(got_k[pad:-pad].reshape(cap, kvdim), kc)
+    assert np.array_equal(got_v[pad:-pad].reshape(cap, kvdim), vc)
+    want, _ = O.attention(q, kc[: held + 1], vc[: held + 1], held, nh, nkv, hs, half=True)
+    np.testing.assert_allclose(get(out, np.float32), want, rtol=1e-4, atol=2e-5)
+
+
 @pytest.mark.parametrize("n", [1, 7, 1000, 151936])
 def test_argmax_and_penalize(n):
     """sample.ts's argmax (device, both forms) and penalize against the oracle's walks: NaNs, ties, -inf."""
