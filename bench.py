@@ -65,6 +65,20 @@ def kernel_case(which):
         for _ in range(3):
             L.pllm_gemv(out.ptr, 0, 0, 0, 0, 0, x.ptr, 0, norm.ptr, 1e-6, 0, w.ptr, ws.ptr, F_Q8, K, 0, hidden, 1, 1, 2,
                         hidden, 0)
+    elif which in ("qkv", "wo", "w2"):  # the step's other int8 products at the Qwen3-8B shape, one token
+        # qkv: rows 6144, K 4096, RMSNorm prologue; wo: rows 4096, K 4096 and w2: rows 4096, K 12288, quantize_x
+        # prologue and the residual add
+        rows, K, pro, epi = {"qkv": (6144, 4096, 1, 0), "wo": (4096, 4096, 2, 1), "w2": (4096, 12288, 2, 1)}[which]
+        w, ws = Buffer(rows * K), Buffer(rows * K // 8)
+        x, norm, out = Buffer(K * 4), Buffer(K * 4), Buffer(rows * 4)
+        bufs += [w, ws, x, norm, out]
+        L.pllm_synth_q8(w.ptr, ws.ptr, rows, K, 1, 0.02)
+        L.pllm_synth_f32(x.ptr, K, 2, 0.0, 1.0)
+        L.pllm_synth_f32(norm.ptr, K, 3, 1.0, 0.1)
+        L.pllm_synth_f32(out.ptr, rows, 4, 0.0, 1.0)
+        for _ in range(3):
+            L.pllm_gemv(out.ptr, 0, 0, 0, 0, 0, x.ptr, 0, norm.ptr if pro == 1 else 0, 1e-6, 0, w.ptr, ws.ptr, 0, K, 0,
+                        rows, 1, pro, epi, 0, 0)
     elif which == "gemv16":  # the batch-16 step's w1/w3 product (the batched tensor-core form), 16 tokens
         hidden, K, M = 12288, 4096, 16
         w, ws = Buffer(2 * hidden * K), Buffer(2 * hidden * K // 8)
@@ -540,7 +554,7 @@ def main():
     ap.add_argument("--no-lfm2", action="store_true", help="skip configs[2]'s hybrid decode (N = 1 only)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: the same shapes with fewer layers (a small case for ncu captures)")
-    ap.add_argument("--kernel", choices=["gemm", "attention", "gemv", "gemv16", "t2"],
+    ap.add_argument("--kernel", choices=["gemm", "attention", "gemv", "qkv", "wo", "w2", "gemv16", "t2"],
                     help="profiling only: three launches of one kernel's small case (for ncu), then exit")
     args = ap.parse_args()
 
