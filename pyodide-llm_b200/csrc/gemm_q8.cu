@@ -14,10 +14,11 @@
 //
 // A CTA: warp 0 issues the TMA copies (activations [128 tokens][128 bytes of K], weights [2 x 64 rows][128 bytes],
 // their scales) into a ring of 4 stages; warp 1 allocates TMEM and one thread issues the MMAs (4 groups a stage) into
-// 4 accumulator buffers of 128 columns; warps 2..9 take a buffer each group (warp w: TMEM lanes 32 (w % 4)..+31 =
-// tokens, columns 64 h..+63 with h = (w - 2) / 4), convert (exact: the int32 plus 2^23 + 2^22 read as a float32,
-// minus that), scale and accumulate, then store the tile with the epilogue's operation (store, add into the residual,
-// or the gated FFN's silu(w1 row) x (w3 row), the two halves of the weight tile being w1's and w3's rows).
+// 4 accumulator buffers of 128 columns; warps 2..17 take a buffer each group (warp w: TMEM lanes 32 (w % 4)..+31 =
+// tokens, columns 32 h..+31 with h = (w - 2) / 4: four warps on each SM sub-partition, so that one's latency is
+// another's issue), convert (exact: the int32 plus 2^23 + 2^22 read as a float32, minus that), scale and accumulate,
+// then store the tile with the epilogue's operation (store, add into the residual, or the gated FFN's silu(w1 row) x
+// (w3 row), the two halves of the weight tile being w1's and w3's rows).
 // Every mbarrier wait is bounded: past the bound the kernel records PLLM_ETIMEOUT, stops issuing work, and still
 // frees its TMEM before it returns.
 #include <cuda.h>
@@ -34,7 +35,7 @@ namespace {
 constexpr int BM = 128, BN = 128, BKB = 128;  // a tile's tokens and weight rows; K bytes a stage
 constexpr int GPS = BKB / 32;                 // groups a stage
 constexpr int STAGES = 4, NBUF = 4;           // shared-memory stages; TMEM accumulator buffers of BN columns
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 16;                 // four a TMEM lane quarter, 32 columns each
 constexpr int GEMM_THREADS = (2 + EPI_WARPS) * 32;
 constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB;
 constexpr int XS_BYTES = BM * GPS * 4, WS_BYTES = BN * GPS * 4;
@@ -197,20 +198,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     mma_commit(done);  // every MMA issued has completed once this arrives
     mbar_wait(done, 0, a.status);
   } else if (warp >= 2) {  // ---- the epilogue
+    // warp w: TMEM lanes 32 (w % 4).. (tokens) and columns 32 h..+31 with h = (w - 2) / 4 (h 0, 1: the weight tile's
+    // first half, w1's rows for the gated FFN; 2, 3: its second half, w3's)
     const int q = warp & 3, h = (warp - 2) >> 2;
     const int m = 32 * q + lane;
-    float2 acc2[32];  // column pairs (2 c, 2 c + 1): the packed float32 operations take two columns an instruction
+    float2 acc2[16];  // column pairs (2 c, 2 c + 1): the packed float32 operations take two columns an instruction
 #pragma unroll
-    for (int c = 0; c < 32; c++) acc2[c] = make_float2(0.0f, 0.0f);
+    for (int c = 0; c < 16; c++) acc2[c] = make_float2(0.0f, 0.0f);
     bool ok = true;
     for (int g = 0; g < ngroups; g++) {
       const int b = g % NBUF, kb = g / GPS, j = g % GPS, s = kb % STAGES;
       if (ok) ok = mbar_wait(&accf[b], (g / NBUF) & 1, a.status);
       fence_after();
-      uint32_t r[64];
-      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BN + 64 * h);
+      uint32_t r[32];
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BN + 32 * h);
       tmem_ld32(taddr, r);
-      tmem_ld32(taddr + 32, r + 32);
       tmem_wait_ld();
       fence_before();
       __syncwarp();
@@ -219,10 +221,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const uint8_t* st = stage(s);
         const float xsv = reinterpret_cast<const float*>(st + A_BYTES + B_BYTES)[m * GPS + j];
         const float2 xs2 = make_float2(xsv, xsv), off2 = make_float2(-12582912.0f, -12582912.0f);
-        const float4* wsv =
-            reinterpret_cast<const float4*>(st + A_BYTES + B_BYTES + XS_BYTES + h * (WS_BYTES / 2)) + j * 16;
+        const float4* wsv = reinterpret_cast<const float4*>(st + A_BYTES + B_BYTES + XS_BYTES +
+                                                            (h >> 1) * (WS_BYTES / 2)) + j * 16 + (h & 1) * 8;
 #pragma unroll
-        for (int c4 = 0; c4 < 16; c4++) {
+        for (int c4 = 0; c4 < 8; c4++) {
           const float4 w = wsv[c4];
 #pragma unroll
           for (int u = 0; u < 2; u++) {
@@ -241,37 +243,37 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
     // the tile out
-    float acc[64];
+    float acc[32];
 #pragma unroll
-    for (int c = 0; c < 32; c++) {
+    for (int c = 0; c < 16; c++) {
       acc[2 * c] = acc2[c].x;
       acc[2 * c + 1] = acc2[c].y;
     }
     const int row = m0 + m;
     if (EPI == GE_SWIGLU) {
       float* sw = reinterpret_cast<float*>(smem);  // [BM][65]: the w3 rows' results (the stages are done)
-      if (h == 1)
+      if (h >= 2)
 #pragma unroll
-        for (int c = 0; c < 64; c++) sw[m * 65 + c] = acc[c];
+        for (int c = 0; c < 32; c++) sw[m * 65 + 32 * (h - 2) + c] = acc[c];
       epi_sync();
-      if (h == 0 && row < a.M) {
-        float* o = a.out + (long long)row * a.ldo + blockIdx.y * (BN / 2);
+      if (h < 2 && row < a.M) {
+        float* o = a.out + (long long)row * a.ldo + blockIdx.y * (BN / 2) + 32 * h;
 #pragma unroll
-        for (int c = 0; c < 64; c += 4) {
+        for (int c = 0; c < 32; c += 4) {
           float4 v;
           const float h1[4] = {acc[c], acc[c + 1], acc[c + 2], acc[c + 3]};
           float res[4];
 #pragma unroll
-          for (int u = 0; u < 4; u++) res[u] = (h1[u] / (1.0f + expf(-h1[u]))) * sw[m * 65 + c + u];
+          for (int u = 0; u < 4; u++) res[u] = (h1[u] / (1.0f + expf(-h1[u]))) * sw[m * 65 + 32 * h + c + u];
           v = make_float4(res[0], res[1], res[2], res[3]);
           *reinterpret_cast<float4*>(o + c) = v;
         }
       }
     } else if (row < a.M) {
-      const int n0 = blockIdx.y * BN + 64 * h;
+      const int n0 = blockIdx.y * BN + 32 * h;
       float* o = a.out + (long long)row * a.ldo + n0;
 #pragma unroll
-      for (int c = 0; c < 64; c += 4) {
+      for (int c = 0; c < 32; c += 4) {
         if (n0 + c >= a.N) break;
         float4 v = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
         if (EPI == GE_ADD) {
