@@ -79,6 +79,25 @@ def kernel_case(which):
         for _ in range(3):
             L.pllm_gemv(out.ptr, 0, 0, 0, 0, 0, x.ptr, 0, norm.ptr if pro == 1 else 0, 1e-6, 0, w.ptr, ws.ptr, 0, K, 0,
                         rows, 1, pro, epi, 0, 0)
+    elif which == "attention_prefill":  # the prefill's attention: 2,048 tokens at positions 0.., 32 / 8 heads of 128
+        M, nh, nkv, hs = 2048, 32, 8, 128
+        rows = (nh + 2 * nkv) * hs
+        rng = np.random.default_rng(0)
+        qkv = Buffer.of(rng.normal(0, 1, M * rows).astype(np.float32))
+        kc = Buffer.of(rng.normal(0, 1, M * nkv * hs).astype(np.float16).view(np.uint16))
+        vc = Buffer.of(rng.normal(0, 1, M * nkv * hs).astype(np.float16).view(np.uint16))
+        out = Buffer(M * nh * hs * 4)
+        bufs += [qkv, kc, vc, out]
+        for _ in range(3):
+            L.pllm_attention_prefill(out.ptr, nh * hs, qkv.ptr, rows, kc.ptr, vc.ptr, 0, M, nh, nkv, hs)
+    elif which == "prefill":  # the whole prefill of configs[3]: 2,048 tokens through 36 layers, twice (the launch list)
+        from pllm.forward import QWEN3_8B, Engine
+        eng = Engine(QWEN3_8B, seed=0)
+        ids = np.random.default_rng(1).integers(0, QWEN3_8B.vocab, 2048).astype(np.int32)
+        for _ in range(2):
+            eng.prefill(ids, 0, need_logits=False)
+        L.pllm_sync()
+        eng.close()
     elif which == "gemv16":  # the batch-16 step's w1/w3 product (the batched tensor-core form), 16 tokens
         hidden, K, M = 12288, 4096, 16
         w, ws = Buffer(2 * hidden * K), Buffer(2 * hidden * K // 8)
@@ -554,7 +573,8 @@ def main():
     ap.add_argument("--no-lfm2", action="store_true", help="skip configs[2]'s hybrid decode (N = 1 only)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: the same shapes with fewer layers (a small case for ncu captures)")
-    ap.add_argument("--kernel", choices=["gemm", "attention", "gemv", "qkv", "wo", "w2", "gemv16", "t2"],
+    ap.add_argument("--kernel", choices=["gemm", "attention", "attention_prefill", "prefill", "gemv", "qkv", "wo", "w2",
+                                         "gemv16", "t2"],
                     help="profiling only: three launches of one kernel's small case (for ncu), then exit")
     args = ap.parse_args()
 
