@@ -10,15 +10,16 @@ reference's group-of-32 format); the prompt is seeded random ids. Prints one JSO
               position already in device memory; the 8.5 GB of weights (> the 126 MB L2) stream from HBM every step
   e2e         the same through the engine's public call: at N = 1 Engine.next_token(token, pos), the greedy step (the
               token and position copied from pinned host memory, 8 bytes, and the next token back, 4 bytes, every
-              step: the argmax runs on the device); at N > 1 Engine.forward (each rank's vocab slice of the logits
-              back every step)
+              step: the argmax runs on the device); at N > 1 the same call on every rank (each rank's vocab slice
+              gives its largest as a key; the keys' max is an NCCL all-reduce on the devices; 4 bytes back a rank)
   roofline    the dominant kernel (the fused w1/w3 product: 2 x 12288 x 4096 int8 + scales, SwiGLU epilogue), its
               algorithmic bytes a launch over its CUDA-event duration, against MEASURED_PEAKS.json's HBM copy GB/s
   cpu_baseline  the CPU oracle (the reference kernels' arithmetic in C, OpenMP over rows) decoding the same model
               on the host cores, a bounded sample of tokens (rank 0, N = 1)
 Under torchrun (N > 1) the ranks decode one stream together, tensor-parallel (pllm.tp: each GPU holds 1/N of every
-matrix and its heads' cache; the two reductions a layer go over NVLink in the products' epilogues and prologues):
-scaling "strong" (the work of a token is fixed), value = tokens / the slowest rank's time.
+matrix and its heads' cache; the two reductions a layer go over NVLink in the products' epilogues and prologues;
+the prompt's prefill on the tensor cores, its row-parallel partials summed by NCCL all-reduces): scaling "strong" (the
+work of a token is fixed), value = tokens / the slowest rank's time.
 
 --impl reference: the reference's CPU implementation of the path, timed on the host cores: its kernels are
 AssemblyScript compiled to WASM and cannot run on this image (no Node, Bun or AssemblyScript), so the oracle's C
@@ -670,12 +671,10 @@ def main():
     e2e_first = prompt + warmup + steps
     if e2e_steps < 8:  # rewind into the decode range (the cache's later positions are rewritten, as a new request)
         e2e_first, e2e_steps = prompt + warmup, steps
-    if world == 1:  # the greedy step's public call: the token and position in, the next token out
-        e2e_ms = timed(lambda: [eng.next_token(int(ids[i % ids.size]), i) for i in range(e2e_first, e2e_first + e2e_steps)])
-        d2h_step = 4
-    else:  # a rank's vocab slice of the logits out
-        e2e_ms = timed(lambda: [eng.forward(int(ids[i % ids.size]), i) for i in range(e2e_first, e2e_first + e2e_steps)])
-        d2h_step = sh.vocab * 4 * world
+    # the greedy step's public call: the token and position in, the next token out (N > 1: every rank's vocab slice
+    # gives its largest as a key, the keys meet in an NCCL max on the devices, each rank gets the token back)
+    e2e_ms = timed(lambda: [eng.next_token(int(ids[i % ids.size]), i) for i in range(e2e_first, e2e_first + e2e_steps)])
+    d2h_step = 4 * world
     e2e = e2e_steps / (e2e_ms / 1000)
 
     gemv, gemv_us, attention, achieved, w13_bytes = {}, {}, {}, None, None
@@ -774,7 +773,8 @@ def main():
                    "l2": "no flush: every step streams 8.51 GB of weights (> 126 MB L2)"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * world,  # every rank's copies
                 "d2h_bytes_per_step": d2h_step,
-                "call": "Engine.next_token (greedy: argmax on the device)" if world == 1 else "Engine.forward"},
+                "call": "Engine.next_token (greedy: argmax on the device)" if world == 1 else
+                        "Engine.next_token (greedy: the ranks' argmax keys' NCCL max on the devices)"},
         "prefill": {"value": prefill_tps, "unit": "tok/s", "tokens": prompt, "ms": prefill_ms, "method": prefill_method,
                     "gemm": gemm},
         "gemv_gbs": gemv,

@@ -244,6 +244,12 @@ void pllm_gemv(uint64_t out, int64_t out_stride, uint64_t xq, uint64_t xs, int64
 /* argmax into device memory (out: one int32) without waiting: the forward driver's greedy step; scratch: 16 bytes of
  * device memory, zero before the first call (every call leaves it at zero); a scratch's calls must not overlap */
 void pllm_argmax_dev(uint64_t out, uint64_t x, int32_t n, uint64_t scratch);
+/* the tensor-parallel greedy step (no counterpart in the reference: one memory holds its vocabulary): a rank's slice of
+ * n logits starting at token offset gives its largest as a 64-bit key (ordered float bits, complement of the global
+ * token) at key; the integer max of the ranks' keys (an all-reduce) names argmax's token over the whole vocabulary,
+ * and pllm_key_token_dev turns it into the token (one int32 at out); scratch as pllm_argmax_dev's */
+void pllm_argmax_key_dev(uint64_t key, uint64_t x, int32_t n, int64_t offset, uint64_t scratch);
+void pllm_key_token_dev(uint64_t out, uint64_t key);
 /* sample into device memory (out: one int32) without waiting, the random number a double at random_dev (written
  * before the launch runs: a recorded step's) */
 void pllm_sample_dev(uint64_t out, uint64_t logits, int32_t n, float temperature, float topp, uint64_t random_dev,

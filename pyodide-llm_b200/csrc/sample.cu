@@ -22,7 +22,11 @@ __device__ __forceinline__ unsigned ordered(float v) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-__global__ void argmax_kernel(const float* __restrict__ x, int n, unsigned long long* key, unsigned* count, int* out) {
+// key_out (the tensor-parallel form): instead of the index, the slice's key with its global index (offset + i), for the
+// ranks' largest key to be taken by a max across the ranks; the slice that starts the vocabulary (offset 0) with a NaN
+// first gives the largest key of all, which names index 0 (the reference's walk: nothing is greater than a NaN start)
+__global__ void argmax_kernel(const float* __restrict__ x, int n, unsigned long long* key, unsigned* count, int* out,
+                              unsigned long long* key_out = nullptr, long long offset = 0) {
   unsigned long long best = 0;  // no element (every one a NaN): key 0
   for (long long i = blockIdx.x * (long long)AM_THREADS + threadIdx.x; i < n; i += (long long)gridDim.x * AM_THREADS) {
     const float v = x[i];
@@ -51,9 +55,23 @@ __global__ void argmax_kernel(const float* __restrict__ x, int n, unsigned long 
   const unsigned long long k = atomicExch(key, 0ull);
   int idx = k ? (int)(0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFu)) : 0;
   const float x0 = x[0];
+  if (key_out) {
+    unsigned long long g = k ? (k & 0xFFFFFFFF00000000ull) | (0xFFFFFFFFu - (unsigned)(offset + idx)) : 0ull;
+    if (offset == 0 && x0 != x0) g = ~0ull;
+    *key_out = g;
+    *count = 0;
+    return;
+  }
   if (x0 != x0) idx = 0;  // the walk starts from a NaN: nothing is greater
   *out = idx;
   *count = 0;
+}
+
+// the token of the ranks' largest key (after a max across the ranks): its global index, 0 where no rank had a
+// number (every logit a NaN)
+__global__ void key_token_kernel(int* out, const unsigned long long* key) {
+  const unsigned long long k = *key;
+  *out = k ? (int)(0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFu)) : 0;
 }
 
 __global__ void penalize_kernel(float* logits, const int* tokens, int count, float penalty, float presence) {
@@ -112,6 +130,26 @@ PLLM_API void pllm_argmax_dev(uint64_t out, uint64_t x, int32_t n, uint64_t scra
   argmax_kernel<<<grid_for(n), AM_THREADS, 0, pllm_stream()>>>(
       dptr<const float>(x), n, dptr<unsigned long long>(scratch), dptr<unsigned>(scratch + 8), dptr<int>(out));
   PLLM_LAUNCHED("pllm_argmax_dev");
+}
+
+// The tensor-parallel greedy step (no counterpart in the reference, which holds the whole vocabulary in one memory):
+// rank r's slice of n logits at x starts at token offset; key (8 bytes of device memory) gets the slice's largest
+// as (ordered float bits, complement of the global token), so that the largest key across the ranks (an integer max,
+// e.g. an all-reduce) names the reference argmax's token (sample.ts:6: the first index of the largest, a NaN skipped,
+// index 0 where the walk starts from a NaN); scratch as pllm_argmax_dev's
+PLLM_API void pllm_argmax_key_dev(uint64_t key, uint64_t x, int32_t n, int64_t offset, uint64_t scratch) {
+  PLLM_REQUIRE(key && !(key & 7) && x && n > 0 && offset >= 0 && offset + n <= 0x7FFFFFFFll && scratch && !(scratch & 7),
+               "pllm_argmax_key_dev: n %d offset %lld", n, (long long)offset);
+  argmax_kernel<<<grid_for(n), AM_THREADS, 0, pllm_stream()>>>(
+      dptr<const float>(x), n, dptr<unsigned long long>(scratch), dptr<unsigned>(scratch + 8), nullptr,
+      dptr<unsigned long long>(key), offset);
+  PLLM_LAUNCHED("pllm_argmax_key_dev");
+}
+// the token (one int32 at out) that the largest of the ranks' keys names
+PLLM_API void pllm_key_token_dev(uint64_t out, uint64_t key) {
+  PLLM_REQUIRE(out && key && !(key & 7), "pllm_key_token_dev: addresses");
+  key_token_kernel<<<1, 1, 0, pllm_stream()>>>(dptr<int>(out), dptr<const unsigned long long>(key));
+  PLLM_LAUNCHED("pllm_key_token_dev");
 }
 
 // penalize (sample.ts:16): the logits of the distinct tokens of tokens[0..count)

@@ -193,6 +193,7 @@ class Engine:
         self.exact = exact
         self.batch = nb = int(batch)
         self.xg = exchange
+        self.device = device
         self.shard = s = Shard(cfg, exchange.rank, exchange.world) if exchange else Shard(cfg)
         if os.environ.get("PLLM_STAGE_BUDGET"):  # the bulk-copy product's stage ring, bytes (a tuning knob)
             L.pllm_set_stage_budget(int(os.environ["PLLM_STAGE_BUDGET"]))
@@ -667,10 +668,13 @@ class Engine:
         temperature 0: the most probable (argmax, sample.ts:6-10); else drawn (sample.ts:248-337) from
         softmax(logits / temperature) by random in [0, 1) (the caller's generator's, as the reference's engine hands
         Python's), of the topk most probable (0: all), then their nucleus (0 < topp < 1), then without those below minp
-        times the most probable. -1: the logits' largest is no finite number."""
+        times the most probable. -1: the logits' largest is no finite number.
+        With tensor parallelism (every rank calls it with the same token and position): greedy only; each rank's
+        vocab slice gives its largest as a key (pllm_argmax_key_dev), the ranks' keys meet in an NCCL max, and every
+        rank gets the same token, 4 bytes back (the logits stay on the devices)."""
         c = self.cfg
-        if self.xg:
-            raise NotImplementedError("next_token takes one rank: with tensor parallelism gather the logits' slices")
+        if self.xg and temperature > 0:
+            raise NotImplementedError("with tensor parallelism next_token is greedy: draw from the gathered logits")
         if not (0 <= pos < c.seq_len and 0 <= token < c.vocab):
             raise ValueError(f"token {token} at {pos}: out of range")
         if temperature > 0 and not (random is not None and 0.0 <= random < 1.0):
@@ -687,6 +691,15 @@ class Engine:
             L.pllm_h2d(self.B["random"].ptr, self.random_host.ptr, 8)
             L.pllm_sample_dev(self.B["next"].ptr, self.B["logits"].ptr, c.vocab, temperature, topp,
                               self.B["random"].ptr, self.B["probs"].ptr, self.B["index"].ptr, topk, minp)
+        elif self.xg:
+            sh = self.shard
+            if "key" not in self.B:
+                self.B["key"] = Buffer(8)
+                self.xg.collectives(self.device)
+            L.pllm_argmax_key_dev(self.B["key"].ptr, self.B["logits"].ptr, sh.vocab, sh.rank * sh.vocab,
+                                  self.B["amx"].ptr)
+            self.xg.all_reduce(self.B["key"].ptr, 1, "i8", self.stream, op="max")
+            L.pllm_key_token_dev(self.B["next"].ptr, self.B["key"].ptr)
         else:
             L.pllm_argmax_dev(self.B["next"].ptr, self.B["logits"].ptr, c.vocab, self.B["amx"].ptr)
         L.pllm_d2h(self.next_host.ptr, self.B["next"].ptr, 4)
@@ -748,9 +761,9 @@ class Engine:
 
     # ---- prefill: many tokens at once on the tensor cores
     def can_prefill(self):
-        """The tensor-core prefill's shapes: products with K and rows in whole 128s, a float16 cache, one rank."""
+        """The tensor-core prefill's shapes: products with K and rows in whole 128s, a float16 cache."""
         c, sh = self.cfg, self.shard
-        return (not self.xg and not self.exact and not self.hybrid and self.fmt == F_Q8 and c.half_kv and c.head_size <= 128 and all(
+        return (not self.exact and not self.hybrid and self.fmt == F_Q8 and c.half_kv and c.head_size <= 128 and all(
             v % 128 == 0 for v in (c.dim, sh.qdim, sh.hidden, self.rows_qkv)))
 
     def _prefill_buffers(self, M):
@@ -768,20 +781,25 @@ class Engine:
                 P["t" + w] = t
             self.P = P
         if P["M"] < M:
-            for k in ("X", "QKV", "ATT", "HB", "XQ", "XS", "TOK"):
+            for k in ("X", "QKV", "ATT", "HB", "XQ", "XS", "TOK", "PART"):
                 if k in P:
                     P[k].free()
             wide = max(c.dim, sh.qdim, sh.hidden, self.rows_qkv)
             P["X"], P["QKV"] = Buffer(M * c.dim * 4), Buffer(M * self.rows_qkv * 4)
             P["ATT"], P["HB"] = Buffer(M * sh.qdim * 4), Buffer(M * sh.hidden * 4)
             P["XQ"], P["XS"], P["TOK"] = Buffer(M * wide), Buffer(M * wide // 8), Buffer(M * 4)
+            if self.xg:  # the row-parallel products' partials, reduced over the ranks
+                P["PART"] = Buffer(M * c.dim * 4)
             P["M"] = M
         return P
 
     def prefill(self, tokens, pos=0, need_logits=True, seq=0):
         """tokens at positions pos.. through every layer at once (the products on the tensor cores, pllm_gemm_q8; the
         attention of all of them at once, pllm_attention_prefill), the cache filled for them; the last token's logits
-        (the decode step's classifier). seq: a batch engine's sequence whose cache they fill."""
+        (the decode step's classifier). seq: a batch engine's sequence whose cache they fill.
+        With tensor parallelism (every rank calls it with the same tokens): each rank's products over its shares, its
+        heads' attention and cache; wo and w2 make partials of every row, summed over the ranks by an NCCL all-reduce
+        (pllm.tp.Exchange.all_reduce) and added to the residual; the logits returned are the rank's vocab slice."""
         c, sh, B = self.cfg, self.shard, self.B
         M = len(tokens)
         if not 0 <= seq < self.batch:
@@ -795,6 +813,9 @@ class Engine:
         P["TOK"].upload(np.asarray(tokens, np.int32))
         E = 2
         X, QKV, ATT, HB, XQ, XS = (P[k].ptr for k in ("X", "QKV", "ATT", "HB", "XQ", "XS"))
+        PART = P["PART"].ptr if self.xg else 0
+        if self.xg:
+            self.xg.collectives(self.device)
         L.pllm_embed_q8(X, B["emb"].ptr, B["emb_s"].ptr, P["TOK"].ptr, 0, c.dim, M, c.dim)
         bias = self.bias
         for l in range(c.layers):
@@ -811,15 +832,27 @@ class Engine:
             L.pllm_attention_prefill(ATT, sh.qdim, QKV, self.rows_qkv, kc, vc, pos, M, sh.heads, sh.kv_heads,
                                      c.head_size)
             L.pllm_norm_quantize_rows(XQ, XS, ATT, sh.qdim, 0, c.eps, sh.qdim, M, bias)
-            L.pllm_gemm_q8(X, c.dim, XQ, XS, B["wo"].ptr + l * c.dim * sh.qdim,
-                           P["tso"].ptr + l * c.dim * (sh.qdim // 32) * 4, M, c.dim, sh.qdim, c.dim, 1, 0)
+            if self.xg:  # row-parallel: this rank's partial over its heads' groups, summed over the ranks, then added
+                L.pllm_gemm_q8(PART, c.dim, XQ, XS, B["wo"].ptr + l * c.dim * sh.qdim,
+                               P["tso"].ptr + l * c.dim * (sh.qdim // 32) * 4, M, c.dim, sh.qdim, c.dim, 0, 0)
+                self.xg.all_reduce(PART, M * c.dim, "f4", self.stream)
+                L.add_inplace(X, PART, M * c.dim)
+            else:
+                L.pllm_gemm_q8(X, c.dim, XQ, XS, B["wo"].ptr + l * c.dim * sh.qdim,
+                               P["tso"].ptr + l * c.dim * (sh.qdim // 32) * 4, M, c.dim, sh.qdim, c.dim, 1, 0)
             L.pllm_norm_quantize_rows(XQ, XS, X, c.dim, B["ffn_norm"].ptr + l * c.dim * 4, c.eps, c.dim, M, bias)
             L.pllm_gemm_q8(HB, sh.hidden, XQ, XS, B["w13"].ptr + l * 2 * sh.hidden * c.dim,
                            P["ts13"].ptr + l * 2 * sh.hidden * (c.dim // 32) * 4, M, sh.hidden, c.dim,
                            2 * sh.hidden, 2, sh.hidden)
             L.pllm_norm_quantize_rows(XQ, XS, HB, sh.hidden, 0, c.eps, sh.hidden, M, bias)
-            L.pllm_gemm_q8(X, c.dim, XQ, XS, B["w2"].ptr + l * c.dim * sh.hidden,
-                           P["ts2"].ptr + l * c.dim * (sh.hidden // 32) * 4, M, c.dim, sh.hidden, c.dim, 1, 0)
+            if self.xg:  # row-parallel over this rank's hidden rows
+                L.pllm_gemm_q8(PART, c.dim, XQ, XS, B["w2"].ptr + l * c.dim * sh.hidden,
+                               P["ts2"].ptr + l * c.dim * (sh.hidden // 32) * 4, M, c.dim, sh.hidden, c.dim, 0, 0)
+                self.xg.all_reduce(PART, M * c.dim, "f4", self.stream)
+                L.add_inplace(X, PART, M * c.dim)
+            else:
+                L.pllm_gemm_q8(X, c.dim, XQ, XS, B["w2"].ptr + l * c.dim * sh.hidden,
+                               P["ts2"].ptr + l * c.dim * (sh.hidden // 32) * 4, M, c.dim, sh.hidden, c.dim, 1, 0)
         if not need_logits:
             L.pllm_sync()
             check("prefill")

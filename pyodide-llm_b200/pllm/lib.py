@@ -113,6 +113,8 @@ SIGNATURES = {
     "argmax": ([U64, I32], I32),
     "penalize": ([U64, U64, I32, F32, F32], None),
     "pllm_argmax_dev": ([U64, U64, I32, U64], None),
+    "pllm_argmax_key_dev": ([U64, U64, I32, I64, U64], None),
+    "pllm_key_token_dev": ([U64, U64], None),
     "sb_tables": ([U64, U64], I32),
     "sums_x": ([U64, U64, I32], None),
     "matmul_sb": ([U64, U64, U64, U64, U64, I32, I32, I32, I32], None),

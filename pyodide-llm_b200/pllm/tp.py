@@ -119,6 +119,29 @@ class Exchange:
             import torch.distributed as dist
             dist.barrier(group=self.group)
 
+    def collectives(self, device):
+        """The ranks' NCCL group for the prefill's reductions and the greedy step's key (made on first use: every rank
+        reaches it in the same call, in the same order)."""
+        if getattr(self, "_nccl", None) is None:
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(device)
+            self._nccl = dist.new_group(list(range(self.world)), backend="nccl")
+            self._device = device
+        return self._nccl
+
+    def all_reduce(self, ptr, count, dtype, stream, op="sum"):
+        """count elements (float32 or int64) of the library's device memory at ptr, summed (or their max) over the
+        ranks in place, NCCL over NVLink, in order on the library's stream (its kernels before, after)."""
+        import torch
+        import torch.distributed as dist
+        group = self.collectives(self._device if getattr(self, "_device", None) is not None else 0)
+        typestr = {"f4": "<f4", "i8": "<i8"}[dtype]
+        view = _DeviceView(ptr, count, typestr)
+        t = torch.as_tensor(view, device=f"cuda:{self._device}")
+        with torch.cuda.stream(torch.cuda.ExternalStream(stream, device=f"cuda:{self._device}")):
+            dist.all_reduce(t, op=dist.ReduceOp.SUM if op == "sum" else dist.ReduceOp.MAX, group=group)
+
     def close(self):
         """Every rank stops using the exchange, then each unmaps the others' regions and frees its own."""
         if self.h:
@@ -126,6 +149,14 @@ class Exchange:
             self.barrier()
             L.pllm_tp_close(self.h)
             self.h = 0
+
+
+class _DeviceView:
+    """The CUDA array interface of count elements of the library's device memory (no copy; torch reads the pointer)."""
+
+    def __init__(self, ptr, count, typestr):
+        self.__cuda_array_interface__ = {"shape": (count,), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "stream": None}
 
 
 def gather_logits(local, shard, group=None):

@@ -97,3 +97,8 @@ def test_ranks_against_one_gpu(world, tmp_path):
         print(f"{world} ranks, position {row['pos']}: relative {row['rel']:.2e}, peak {row['peak']:.2e}, "
               f"argmax {row['argmax']}")
         assert row["rel"] <= 2e-2 and row["peak"] <= 2e-2, row
+    for row in res["prefill_rows"]:  # the tensor-core prefill across the ranks, then decode steps after it
+        print(f"{world} ranks, {row['pos']}: relative {row['rel']:.2e}, peak {row['peak']:.2e}, argmax {row['argmax']}")
+        assert row["rel"] <= 2e-2 and row["peak"] <= 2e-2, row
+    # every rank's greedy token (the keys' max across the ranks) is the gathered logits' argmax
+    assert all(t == res["gathered_argmax"] for t in res["greedy"]), res
