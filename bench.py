@@ -99,6 +99,12 @@ def kernel_case(which):
             eng.prefill(ids, 0, need_logits=False)
         L.pllm_sync()
         eng.close()
+    elif which == "decode16":  # configs[3] at batch 16: two steps of the batch engine, eager (its launch list)
+        from pllm.forward import QWEN3_8B, Engine
+        eng = Engine(QWEN3_8B, seed=0, batch=16, graphs=False, pdl=False)
+        for s in range(2):
+            eng.forward_batch(np.arange(16) + 5 + s, np.full(16, 2048 + s), need_logits=False)
+        eng.close()
     elif which == "gemv16":  # the batch-16 step's w1/w3 product (the batched tensor-core form), 16 tokens
         hidden, K, M = 12288, 4096, 16
         w, ws = Buffer(2 * hidden * K), Buffer(2 * hidden * K // 8)
@@ -574,8 +580,8 @@ def main():
     ap.add_argument("--no-lfm2", action="store_true", help="skip configs[2]'s hybrid decode (N = 1 only)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: the same shapes with fewer layers (a small case for ncu captures)")
-    ap.add_argument("--kernel", choices=["gemm", "attention", "attention_prefill", "prefill", "gemv", "qkv", "wo", "w2",
-                                         "gemv16", "t2"],
+    ap.add_argument("--kernel", choices=["gemm", "attention", "attention_prefill", "prefill", "decode16", "gemv", "qkv",
+                                         "wo", "w2", "gemv16", "t2"],
                     help="profiling only: three launches of one kernel's small case (for ncu), then exit")
     args = ap.parse_args()
 
