@@ -474,9 +474,18 @@ class Engine:
         R = self.rows_qkv
         L.pllm_embed_q8(x, B["emb"].ptr, B["emb_s"].ptr, toks, 0, c.dim, nb, c.dim)
 
-        def gemv(out, ldo, xin, ldx, norm, wq, ws, rows, k, pro, epi, pair=0, xq=0, xs=0):
-            L.pllm_gemv(out, ldo, xq, xs, k if xq else 0, k // 8 if xq else 0, xin, ldx, norm, c.eps, self.bias, wq, ws,
-                        F_Q8, k, 0, rows, nb, pro, epi, pair, pdl)
+        def gemv(out, ldo, xin, ldx, norm, wq, ws, rows, k, pro, epi, pair=0, xq=0, xs=0, bias=None):
+            L.pllm_gemv(out, ldo, xq, xs, k if xq else 0, k // 8 if xq else 0, xin, ldx, norm, c.eps,
+                        self.bias if bias is None else bias, wq, ws, F_Q8, k, 0, rows, nb, pro, epi, pair, pdl)
+
+        def quantized(xin, ldx, norm, k):
+            """The batch's activations (RMSNorm with norm, or none: 0) quantized once, signed int8 (the bias taken
+            off) into hq: a product over them loads them as they are, where every CTA of a product that quantizes in
+            its own prologue makes all the batch's tokens again (measured at batch 16: the products' prologues took
+            most of the step)."""
+            L.pllm_norm_quantize_rows(B["hq"].ptr, B["hq_scales"].ptr, xin, ldx, norm, c.eps, k, nb, self.bias)
+            return {"xq": B["hq"].ptr, "xs": B["hq_scales"].ptr, "bias": 0}
+        self._quantized = quantized
         layer_cache = nb * c.seq_len * c.kvdim * E
         A, d = self.att_stride, c.dim
         for l in range(c.layers):
@@ -489,28 +498,29 @@ class Engine:
                      PRO_QUANT, EPI_ADD)
                 self._enqueue_batch_ffn(l, gemv)
                 continue
-            gemv(qkv, R, x, c.dim, B["att_norm"].ptr + l * c.dim * 4, B["wqkv"].ptr + l * R * c.dim,
-                 B["sqkv"].ptr + l * R * (c.dim // 32) * 4, R, c.dim, PRO_RMS, EPI_STORE)
+            gemv(qkv, R, 0, 0, 0, B["wqkv"].ptr + l * R * c.dim, B["sqkv"].ptr + l * R * (c.dim // 32) * 4, R,
+                 c.dim, PRO_Q, EPI_STORE, **quantized(x, c.dim, B["att_norm"].ptr + l * c.dim * 4, c.dim))
             qn = B["q_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
             kn = B["k_norm"].ptr + l * c.head_size * 4 if c.qk_norm else 0
             L.pllm_attention_step_batch(att, A, qkv, R, B["kc"].ptr + l * layer_cache,
                                         B["vc"].ptr + l * layer_cache, c.seq_len * c.kvdim * E, B["scratch"].ptr, poss,
                                         nb, c.seq_len, c.heads, c.kv_heads, c.head_size, 0.0, self.SPLIT, qn, kn,
                                         B["cos_t"].ptr, B["sin_t"].ptr, 0, c.eps, B["bad"].ptr, pdl)
-            gemv(x, c.dim, att, A, 0, B["wo"].ptr + l * c.dim * c.qdim,
-                 B["so"].ptr + l * c.dim * (c.qdim // 32) * 4, c.dim, c.qdim, PRO_QUANT, EPI_ADD)
+            gemv(x, c.dim, 0, 0, 0, B["wo"].ptr + l * c.dim * c.qdim, B["so"].ptr + l * c.dim * (c.qdim // 32) * 4,
+                 c.dim, c.qdim, PRO_Q, EPI_ADD, **quantized(att, A, 0, c.qdim))
             self._enqueue_batch_ffn(l, gemv)
         if need_logits:
-            gemv(B["logits"].ptr, c.vocab, x, c.dim, B["final_norm"].ptr, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim,
-                 PRO_RMS, EPI_STORE)
+            gemv(B["logits"].ptr, c.vocab, 0, 0, 0, B["cls"].ptr, B["cls_s"].ptr, c.vocab, c.dim, PRO_Q, EPI_STORE,
+                 **quantized(x, c.dim, B["final_norm"].ptr, c.dim))
 
     def _enqueue_batch_ffn(self, l, gemv):
-        """Layer l's gated FFN of the batch's sequences; w2's K (the hidden width) quantized first, its activations then
-        read from global memory by the batched product."""
+        """Layer l's gated FFN of the batch's sequences: the activations of each product quantized once first (w1/w3:
+        RMSNorm and quantize_x; w2's K, the hidden width, then read from global memory by the batched product)."""
         c, B, nb = self.cfg, self.B, self.batch
         x, hb = B["x"].ptr, B["hb"].ptr
-        gemv(hb, c.hidden, x, c.dim, B["ffn_norm"].ptr + l * c.dim * 4, B["w13"].ptr + l * 2 * c.hidden * c.dim,
-             B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.hidden, c.dim, PRO_RMS, EPI_SWIGLU, pair=c.hidden)
+        gemv(hb, c.hidden, 0, 0, 0, B["w13"].ptr + l * 2 * c.hidden * c.dim,
+             B["s13"].ptr + l * 2 * c.hidden * (c.dim // 32) * 4, c.hidden, c.dim, PRO_Q, EPI_SWIGLU, pair=c.hidden,
+             **self._quantized(x, c.dim, B["ffn_norm"].ptr + l * c.dim * 4, c.dim))
         L.pllm_quantize_tokens(B["hq"].ptr, B["hq_scales"].ptr, hb, c.hidden, self.bias, nb)
         gemv(x, c.dim, 0, 0, 0, B["w2"].ptr + l * c.dim * c.hidden, B["s2"].ptr + l * c.dim * (c.hidden // 32) * 4,
              c.dim, c.hidden, PRO_Q, EPI_ADD, xq=B["hq"].ptr, xs=B["hq_scales"].ptr)
