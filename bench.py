@@ -105,6 +105,67 @@ def kernel_case(which):
         for s in range(2):
             eng.forward_batch(np.arange(16) + 5 + s, np.full(16, 2048 + s), need_logits=False)
         eng.close()
+    elif which == "cls":  # the classifier product: 151,936 rows, K 4096, RMSNorm prologue (171 MB: > L2)
+        rows, K = 151936, 4096
+        w, ws = Buffer(rows * K), Buffer(rows * K // 8)
+        x, norm, out = Buffer(K * 4), Buffer(K * 4), Buffer(rows * 4)
+        bufs += [w, ws, x, norm, out]
+        L.pllm_synth_q8(w.ptr, ws.ptr, rows, K, 1, 0.02)
+        L.pllm_synth_f32(x.ptr, K, 2, 0.0, 1.0)
+        L.pllm_synth_f32(norm.ptr, K, 3, 1.0, 0.1)
+        for _ in range(3):
+            L.pllm_gemv(out.ptr, 0, 0, 0, 0, 0, x.ptr, 0, norm.ptr, 1e-6, 0, w.ptr, ws.ptr, 0, K, 0, rows, 1, 1, 0, 0, 0)
+    elif which in ("q6r", "b1r"):  # the registry's int6 / binary products (register streaming), 16,384 x 4096
+        rows, K = 16384, 4096
+        rng = np.random.default_rng(7)
+        wbytes = rows * K * 6 // 8 if which == "q6r" else rows * K // 8
+        w = Buffer.of(rng.integers(0, 256, wbytes, dtype=np.uint8))
+        out = Buffer(rows * 4)
+        xq = Buffer.of(rng.integers(0, 128, K, dtype=np.uint8))
+        bufs += [w, out, xq]
+        if which == "q6r":
+            ws = Buffer.of(rng.normal(0.02, 0.002, rows * K // 32).astype(np.float32))
+            wc = Buffer.of(rng.integers(-2000, 2000, rows * K // 32).astype(np.int32))
+            xs = Buffer.of(rng.normal(0.02, 0.002, K // 32).astype(np.float32))
+            bufs += [ws, wc, xs]
+            for _ in range(3):
+                L.matmul_q6r(out.ptr, xq.ptr, xs.ptr, w.ptr, ws.ptr, wc.ptr, K, 0, rows)
+        else:
+            halves = Buffer.of(rng.normal(0.02, 0.002, rows * K // 128).astype(np.float16).view(np.uint16))
+            ext = Buffer.of(np.concatenate([rng.normal(0.02, 0.002, K // 32).astype(np.float32).view(np.int32),
+                                            rng.integers(-2000, 2000, K // 32).astype(np.int32)]))
+            bufs += [halves, ext]
+            for _ in range(3):
+                L.matmul_b1r(out.ptr, xq.ptr, ext.ptr, w.ptr, halves.ptr, K, 0, rows, 2)
+    elif which in ("delta1", "delta64"):  # the delta rule's micro-configuration: kh 16, vh 32, kd = vd = 128
+        kh, vh, kd, vd = 16, 32, 128, 128
+        count = 1 if which == "delta1" else 64
+        sbytes = vh * kd * vd * 4
+        states = Buffer(2 * 3 * sbytes)  # three state pairs (12 MB), one a launch
+        cw, ww = 2 * kh * kd + vh * vd, 2 * vh + vh * vd
+        c, work, out = Buffer(64 * cw * 4), Buffer(64 * ww * 4), Buffer(64 * vh * vd * 4)
+        bufs += [states, c, work, out]
+        L.pllm_synth_f32(states.ptr, 2 * 3 * sbytes // 4, 31, 0.0, 0.5)
+        L.pllm_synth_f32(c.ptr, 64 * cw, 32, 0.0, 0.3)
+        L.pllm_synth_f32(work.ptr, 64 * ww, 33, 0.5, 0.1)
+        for i in range(3):
+            s0 = states.ptr + 2 * i * sbytes
+            if count == 1:
+                L.delta_rule(out.ptr, s0, s0 + sbytes, c.ptr, work.ptr, kh, kd, vd, vh, 0, vh)
+            else:
+                L.pllm_delta_rule_block(out.ptr, vh * vd, s0, s0 + sbytes, c.ptr, cw, work.ptr, ww, count, kh, kd, vd,
+                                        vh, 0, vh)
+    elif which == "sample":  # the greedy step's argmax and a draw (temperature 0.8, top-p 0.9) over 151,936 logits
+        n = 151936
+        logits = Buffer(n * 4)
+        L.pllm_synth_f32(logits.ptr, n, 5, 0.0, 3.0)
+        nxt, amx, probs, index, rnd = Buffer(4), Buffer(16).zero(), Buffer(4 * n), Buffer(4 * n), Buffer.of(
+            np.array([0.37], np.float64))
+        bufs += [logits, nxt, amx, probs, index, rnd]
+        for _ in range(3):
+            L.pllm_argmax_dev(nxt.ptr, logits.ptr, n, amx.ptr)
+        for _ in range(3):
+            L.pllm_sample_dev(nxt.ptr, logits.ptr, n, 0.8, 0.9, rnd.ptr, probs.ptr, index.ptr, 0, 0.0)
     elif which == "gemv16":  # the batch-16 step's w1/w3 product (the batched tensor-core form), 16 tokens
         hidden, K, M = 12288, 4096, 16
         w, ws = Buffer(2 * hidden * K), Buffer(2 * hidden * K // 8)
@@ -581,7 +642,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: the same shapes with fewer layers (a small case for ncu captures)")
     ap.add_argument("--kernel", choices=["gemm", "attention", "attention_prefill", "prefill", "decode16", "gemv", "qkv",
-                                         "wo", "w2", "gemv16", "t2"],
+                                         "wo", "w2", "cls", "q6r", "b1r", "delta1", "delta64", "sample", "gemv16",
+                                         "t2"],
                     help="profiling only: three launches of one kernel's small case (for ncu), then exit")
     args = ap.parse_args()
 
