@@ -166,6 +166,22 @@ def kernel_case(which):
             L.pllm_argmax_dev(nxt.ptr, logits.ptr, n, amx.ptr)
         for _ in range(3):
             L.pllm_sample_dev(nxt.ptr, logits.ptr, n, 0.8, 0.9, rnd.ptr, probs.ptr, index.ptr, 0, 0.0)
+    elif which in ("sbq4k", "sbiq2xs"):  # super-block products (matmul_sbr) over 16,384 x 4096: Q4_K, IQ2_XS
+        t, size, halves = {"sbq4k": (12, 144, (0, 2)), "sbiq2xs": (17, 74, (0,))}[which]
+        rows, n = 16384, 4096
+        rng = np.random.default_rng(t)
+        raw = rng.integers(0, 256, (rows * n // 256, size), dtype=np.uint8)  # any bytes are blocks
+        for at in halves:  # finite float16 scales of a model's size
+            raw[:, at:at + 2] = rng.uniform(0.002, 0.05, raw.shape[0]).astype("<f2").view(np.uint8).reshape(-1, 2)
+        books = np.load(os.path.join(ROOT, "tests", "golden", "superblocks.npz"))["codebooks"]
+        W, tab, bk = Buffer.of(raw.reshape(-1)), Buffer(34992), Buffer.of(books)
+        X = Buffer.of(np.concatenate([rng.integers(0, 128, n, dtype=np.uint8),
+                                      rng.normal(0, 0.02, n // 8).astype(np.float32).view(np.uint8)]))
+        out = Buffer(rows * 4)
+        bufs += [W, tab, bk, X, out]
+        L.sb_tables(tab.ptr, bk.ptr)
+        for _ in range(3):
+            L.matmul_sbr(out.ptr, X.ptr, X.ptr + n, W.ptr, tab.ptr, n, 0, rows, t)
     elif which == "gemv16":  # the batch-16 step's w1/w3 product (the batched tensor-core form), 16 tokens
         hidden, K, M = 12288, 4096, 16
         w, ws = Buffer(2 * hidden * K), Buffer(2 * hidden * K // 8)
@@ -642,8 +658,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: the same shapes with fewer layers (a small case for ncu captures)")
     ap.add_argument("--kernel", choices=["gemm", "attention", "attention_prefill", "prefill", "decode16", "gemv", "qkv",
-                                         "wo", "w2", "cls", "q6r", "b1r", "delta1", "delta64", "sample", "gemv16",
-                                         "t2"],
+                                         "wo", "w2", "cls", "q6r", "b1r", "delta1", "delta64", "sample", "sbq4k",
+                                         "sbiq2xs", "gemv16", "t2"],
                     help="profiling only: three launches of one kernel's small case (for ncu), then exit")
     args = ap.parse_args()
 
