@@ -300,12 +300,125 @@ __global__ void sums_x_kernel(float* xs, const int8_t* xq, int n) {
   }
 }
 
+// The same products with a row's blocks staged in shared memory: a warp takes two rows (half a warp a row, a lane
+// its blocks hl, hl + 16, ...), copies both rows' bytes with 16-byte loads (4-byte where the rows are not 16-byte
+// aligned) into its own buffer, then decodes from there; every block's integers and its float32 part as sb_kernel's,
+// the lanes' parts added in another order (a lane 16 apart, a half-warp's reduction). (sb_kernel read each block's
+// fields from global memory one at a time, 50 to 144 bytes from its neighbour lane's, with half the lanes idle at K
+// 4096: 2 % of the copy rate.)
+template <int TYPE>
+__global__ void __launch_bounds__(SB_WARPS * 32) sb_staged_kernel(float* out, const int8_t* xq, const float* xs,
+                                                                   const uint8_t* w, const uint8_t* tabg, int n, int r0,
+                                                                   int r1, long long os, long long frame) {
+  extern __shared__ __align__(16) uint8_t sb_smem[];
+  constexpr int SIZE = block_bytes(TYPE);
+  constexpr bool KQ = TYPE == 10 || TYPE == 12;
+  const int blocks = n / 256, rowbytes = blocks * SIZE;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane >> 4, hl = lane & 15;
+  uint8_t* tab = sb_smem;                                                   // TABLES bytes
+  int8_t* sx = reinterpret_cast<int8_t*>(sb_smem + ((TABLES + 15) & ~15));  // n activations
+  float* ss = reinterpret_cast<float*>(sx + n);                             // n / 32 scales
+  uint8_t* wbuf = reinterpret_cast<uint8_t*>(ss + n / 32) + (size_t)warp * 2 * ((rowbytes + 15) & ~15);
+  const int t = blockIdx.y;
+  const int8_t* xt = reinterpret_cast<const int8_t*>(reinterpret_cast<const uint8_t*>(xq) + t * frame);
+  const float* st = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(xs) + t * frame);
+  for (int i = threadIdx.x; i < TABLES; i += blockDim.x) tab[i] = tabg[i];
+  for (int i = threadIdx.x; i < n / 4; i += blockDim.x) reinterpret_cast<int*>(sx)[i] = reinterpret_cast<const int*>(xt)[i];
+  for (int i = threadIdx.x; i < n / 32; i += blockDim.x) ss[i] = st[i];
+  __syncthreads();
+  const int rb16 = (rowbytes + 15) & ~15;
+  const bool v16 = (rowbytes & 15) == 0 && (((uintptr_t)w) & 15) == 0;
+  float* o = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(out) + t * os);
+  for (int pr = r0 + 2 * (blockIdx.x * SB_WARPS + warp); pr < r1; pr += 2 * gridDim.x * SB_WARPS) {
+    const int nr = pr + 1 < r1 ? 2 : 1;  // rows of this pair
+    __syncwarp();  // the buffer's last pair is decoded
+    for (int h = 0; h < nr; h++) {
+      const uint8_t* src = w + (size_t)(pr + h) * rowbytes;
+      uint8_t* dst = wbuf + h * rb16;
+      if (v16) {
+        for (int i = lane; i < rowbytes / 16; i += 32)
+          reinterpret_cast<int4*>(dst)[i] = __ldg(reinterpret_cast<const int4*>(src) + i);
+      } else if ((((uintptr_t)w) & 1) == 0) {  // rows a multiple of 2 bytes (every block's size is even)
+        for (int i = lane; i < rowbytes / 2; i += 32)
+          reinterpret_cast<uint16_t*>(dst)[i] = __ldg(reinterpret_cast<const unsigned short*>(src) + i);
+      } else {
+        for (int i = lane; i < rowbytes; i += 32) dst[i] = __ldg(src + i);
+      }
+    }
+    __syncwarp();
+    const int row = pr + half;
+    float facc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (half < nr) {
+      const uint8_t* wr = wbuf + half * rb16;
+      for (int b = hl; b < blocks; b += 16) {
+        const uint8_t* p = wr + (size_t)b * SIZE;
+        const int8_t* x = sx + 256 * b;
+        int G[8], M[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) G[k] = M[k] = 0;
+#pragma unroll 1
+        for (int u = 0; u < 16; u++) {
+          int W[16], S, m;
+          unit_of<TYPE>(p, u, tab, W, S, m);
+          const int* xa = reinterpret_cast<const int*>(x + 16 * u);
+          int d = 0, s16 = 0;
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            d = __dp4a(pack4(W + 4 * q), xa[q], d);
+            if (KQ) s16 = __dp4a(0x01010101, xa[q], s16);
+          }
+          G[u >> 1] += S * d;
+          if (KQ) M[u >> 1] += m * s16;
+        }
+        const float* s = ss + 8 * b;
+        const float F = block_F<TYPE>(p);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          float part = __fmul_rn(__fadd_rn(__fmul_rn((float)G[j], s[j]), __fmul_rn((float)G[j + 4], s[j + 4])), F);
+          if (KQ)
+            part = __fsub_rn(part, __fmul_rn(__fadd_rn(__fmul_rn((float)M[j], s[j]), __fmul_rn((float)M[j + 4], s[j + 4])),
+                                             block_Fm<TYPE>(p)));
+          facc[j] = __fadd_rn(facc[j], part);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) facc[j] += __shfl_xor_sync(0xffffffffu, facc[j], off);
+    if (half < nr && hl == 0) o[row] = ((facc[0] + facc[1]) + facc[2]) + facc[3];
+  }
+}
+
 bool known(int type) { return block_bytes(type) != 0; }
 
 bool launch_products(float* out, const int8_t* xq, const float* xs, const uint8_t* w, const uint8_t* tab, int n, int r0,
                      int r1, int count, long long os, long long frame, int type) {
   const size_t smem = ((TABLES + 15) & ~15) + (size_t)n + (size_t)n / 8;
   const int rows = r1 - r0;
+  // the staged form where every warp's two rows fit beside the tables and the activations
+  const size_t rb16 = ((size_t)(n / 256) * block_bytes(type) + 15) & ~(size_t)15;
+  const size_t staged = smem + (size_t)SB_WARPS * 2 * rb16;
+  if (staged <= 200 * 1024) {
+    int pairs = (rows + 2 * SB_WARPS - 1) / (2 * SB_WARPS);
+    const int most_s = 4 * pllm_num_sms();
+    pairs = pairs > most_s ? most_s : pairs;
+    const dim3 grid_s(pairs < 1 ? 1 : pairs, count);
+#define SB_STAGED(T)                                                                                            \
+  case T: {                                                                                                     \
+    if (cudaFuncSetAttribute(sb_staged_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)staged) != \
+        cudaSuccess)                                                                                            \
+      return false;                                                                                             \
+    sb_staged_kernel<T><<<grid_s, SB_WARPS * 32, staged, pllm_stream()>>>(out, xq, xs, w, tab, n, r0, r1, os, frame); \
+    return true;                                                                                                \
+  }
+    switch (type) {
+      SB_STAGED(10) SB_STAGED(12) SB_STAGED(16) SB_STAGED(17) SB_STAGED(18) SB_STAGED(19) SB_STAGED(21) SB_STAGED(22)
+      SB_STAGED(23) SB_STAGED(29)
+    }
+#undef SB_STAGED
+    return false;
+  }
   int ctas = (rows + SB_WARPS - 1) / SB_WARPS;
   const int most = 4 * pllm_num_sms();
   ctas = ctas > most ? most : ctas;
