@@ -177,7 +177,8 @@ PLLM_API void penalize(uint64_t logits, uint64_t tokens, int32_t count, float pe
 // differs only where the random number falls within about 1e-15 of a boundary.
 namespace {
 
-constexpr int SP_THREADS = 256, SP_FINAL = 1024, SP_MAX_CTAS = 1024, SP_CHUNK = 1024;
+// SP_CHUNK: the keys the final kernel sorts at once, in its dynamic shared memory (128 KB)
+constexpr int SP_THREADS = 256, SP_FINAL = 1024, SP_MAX_CTAS = 1024, SP_CHUNK = 16384;
 
 struct SampleScratch {
   float part_max[SP_MAX_CTAS];
@@ -365,8 +366,8 @@ __device__ unsigned long long sp_select(const float* probs, const int* index, in
   return prefix;
 }
 
-// the elements of the set with lo <= key < upper (at most SP_CHUNK of them) into shared memory, sorted descending;
-// returns how many
+// the elements of the set with lo <= key < upper (at most SP_CHUNK of them) into shared memory, sorted descending
+// (a bitonic sort of the next power of two of them); returns how many
 template <typename In>
 __device__ int sp_chunk(const float* probs, const int* index, int count, In in, unsigned long long lo,
                         unsigned long long upper, unsigned long long* keys, int* fill) {
@@ -382,11 +383,13 @@ __device__ int sp_chunk(const float* probs, const int* index, int count, In in, 
   }
   __syncthreads();
   const int m = min(*fill, SP_CHUNK);
-  for (int i = m + threadIdx.x; i < SP_CHUNK; i += SP_FINAL) keys[i] = 0;  // padding sorts last
+  int width = 32;
+  while (width < m) width <<= 1;
+  for (int i = m + threadIdx.x; i < width; i += SP_FINAL) keys[i] = 0;  // padding sorts last
   __syncthreads();
-  for (int size = 2; size <= SP_CHUNK; size <<= 1)  // bitonic sort, descending
+  for (int size = 2; size <= width; size <<= 1)  // bitonic sort, descending
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < SP_CHUNK; i += SP_FINAL) {
+      for (int i = threadIdx.x; i < width; i += SP_FINAL) {
         const int j = i ^ stride;
         if (j > i) {
           const bool down = (i & size) == 0;
@@ -411,7 +414,7 @@ __global__ void __launch_bounds__(SP_FINAL) sample_final_kernel(int ctas, float 
   __shared__ double red[33];
   __shared__ float redf[33];
   __shared__ unsigned hist[256];
-  __shared__ unsigned long long keys[SP_CHUNK];
+  extern __shared__ unsigned long long keys[];  // [SP_CHUNK]
   __shared__ int fill, result;
   const float best = sp_best(ctas);
   if (!isfinite(best)) {
@@ -460,10 +463,76 @@ __global__ void __launch_bounds__(SP_FINAL) sample_final_kernel(int ctas, float 
       return (!narrowed || sp_key(p, index[i]) >= kth) && (double)p >= cutoff && p >= least;
     };
     const double limit = nucleus ? (double)topp * total : INFINITY;
-    // pass 1: the nucleus's mass and its last key, chunk by chunk from the most probable
     __shared__ double mass;
     __shared__ unsigned long long last_key;
     __shared__ bool done;
+    // The walk's keys at once where they fit in one chunk: a histogram of the set's mass by probability (the float's
+    // top 11 bits), summed from the most probable bin down to the first bin where the mass passes the limit (by a
+    // relative 1e-9 more than the walk's own sums could differ by), names a floor that holds every key the walk can
+    // reach; the keys at or above it, sorted once, are walked for both passes in the same descending order as the
+    // chunk-by-chunk walk below, so the same sums, the same token (each of those chunks is a full scan of the
+    // candidates: a draw with a wide nucleus took ~100 scans).
+    {
+      __shared__ double hmass[1024];
+      __shared__ unsigned hcount[1024];
+      __shared__ int lo_bin, fits;
+      for (int b = threadIdx.x; b < 1024; b += SP_FINAL) {
+        hmass[b] = 0.0;
+        hcount[b] = 0;
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < count; i += SP_FINAL) {
+        if (!in(i)) continue;
+        const float p = probs[i];
+        const int b = (int)(__float_as_uint(p) >> 21) & 1023;  // p >= 0: its bits' order is its order
+        atomicAdd(&hmass[b], (double)p);
+        atomicAdd(&hcount[b], 1u);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        double cum = 0.0;
+        unsigned n = 0;
+        int lo = 0;
+        for (int b = 1023; b >= 0; b--) {
+          cum += hmass[b];
+          n += hcount[b];
+          if (cum >= limit * (1.0 + 1e-9)) {
+            lo = b;
+            break;
+          }
+        }
+        lo_bin = lo;
+        fits = n <= (unsigned)SP_CHUNK;
+      }
+      __syncthreads();
+      if (fits) {
+        const unsigned long long lo_key = (unsigned long long)((unsigned)lo_bin << 21) << 32;
+        const int m = sp_chunk(probs, index, count, in, lo_key, ~0ull, keys, &fill);
+        if (threadIdx.x == 0) {
+          double walked = 0.0;
+          unsigned long long last = 0;
+          for (int k = 0; k < m; k++) {  // pass 1: the nucleus's mass and its last key
+            walked += sp_prob(keys[k]);
+            last = keys[k];
+            if (walked >= limit) break;
+          }
+          const double target = random * walked;  // pass 2: the first whose cumulative sum passes random x mass
+          int pick = sp_token(last);
+          double cumulative = 0.0;
+          for (int k = 0; k < m; k++) {
+            cumulative += sp_prob(keys[k]);
+            if (cumulative > target) {
+              pick = sp_token(keys[k]);
+              break;
+            }
+            if (keys[k] == last) break;
+          }
+          *out = pick;
+        }
+        return;
+      }
+    }
+    // pass 1: the nucleus's mass and its last key, chunk by chunk from the most probable
     if (threadIdx.x == 0) {
       mass = 0.0;
       last_key = 0;
@@ -575,7 +644,17 @@ bool sample_enqueue(const float* x, int n, float temperature, float topp, const 
   sample_max_kernel<<<ctas, SP_THREADS, 0, s>>>(x, n);
   sample_count_kernel<<<ctas, SP_THREADS, 0, s>>>(x, n, temperature, topp);
   sample_scatter_kernel<<<ctas, SP_THREADS, 0, s>>>(x, n, temperature, topp, probs, index);
-  sample_final_kernel<<<1, SP_FINAL, 0, s>>>(ctas, temperature, topp, random_dev, random, topk, minp, probs, index, out);
+  static bool sized[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (!sized[dev]) {  // the key buffer's dynamic shared memory, set once a device (outside any stream capture)
+    if (cudaFuncSetAttribute(sample_final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SP_CHUNK * (int)sizeof(unsigned long long)) != cudaSuccess)
+      return false;
+    sized[dev] = true;
+  }
+  sample_final_kernel<<<1, SP_FINAL, SP_CHUNK * sizeof(unsigned long long), s>>>(ctas, temperature, topp, random_dev,
+                                                                               random, topk, minp, probs, index, out);
   return cudaGetLastError() == cudaSuccess;
 }
 
