@@ -122,12 +122,20 @@ __global__ void __launch_bounds__(128) delta_rule_tile_kernel(float* out, long l
     dr_cp16(tile + i * DR_COLS + 4 * p, from + (long long)i * vd + 4 * p);
   }
   asm volatile("cp.async.commit_group;\ncp.async.wait_all;" ::: "memory");
-  __syncthreads();
-  if (j < DR_COLS) {
-    for (int t = 0; t < count; t++) {
-      const float* ct = c + t * c_stride;
-      const float* q = ct + (long long)key * kd;
-      const float* k = ct + (long long)(kh + key) * kd;
+  // each token's q and k rows (kd floats each) through shared memory, loaded by the whole CTA: the chains' operands
+  // then come from shared memory (read from global memory inside the chains, a load a step held every step)
+  float* sqk = tile + kd * DR_COLS;  // [2][kd]
+  for (int t = 0; t < count; t++) {
+    const float* ct = c + t * c_stride;
+    __syncthreads();  // the tile is staged; the last token's q and k are read
+    for (int e = threadIdx.x; e < kd; e += blockDim.x) {
+      sqk[e] = ct[(long long)key * kd + e];
+      sqk[kd + e] = ct[(long long)(kh + key) * kd + e];
+    }
+    __syncthreads();
+    if (j < DR_COLS) {
+      const float* q = sqk;
+      const float* k = sqk + kd;
       const float* v = ct + (long long)(2 * kh) * kd + (long long)h * vd;
       float* wt = work + t * work_stride;
       const float beta = wt[h], decay = wt[vh + h];
@@ -166,7 +174,7 @@ __global__ void embed_q8_kernel(float* x, const int8_t* __restrict__ emb, const 
 void launch_delta_tiles(uint64_t out, long long out_stride, uint64_t state, uint64_t next, uint64_t c,
                         long long c_stride, uint64_t work, long long work_stride, int count, int kh, int kd, int vd,
                         int vh, int h0, int h1) {
-  const size_t smem = (size_t)kd * DR_COLS * 4;
+  const size_t smem = (size_t)kd * DR_COLS * 4 + 2 * (size_t)kd * 4;  // the tile, then a token's q and k
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(delta_rule_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
     pllm_fail(PLLM_ECUDA, "delta_rule: %zu bytes of shared memory", smem);
