@@ -1,5 +1,5 @@
 // gemv_tma.cu: the decode product as a bulk-copy pipeline (the forward driver's and the registry's int8 products at
-// one or two tokens).
+// one to sixteen tokens, int6 and ternary products at one).
 //
 // One CTA an SM, warp-specialized: a producer warp streams the CTA's rows of weights and their scales from HBM into
 // a ring of shared-memory stages with cp.async.bulk (the TMA's bulk engine; completion counted on an mbarrier per
@@ -584,11 +584,14 @@ __device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
   return d;
 }
 
-template <int PHASES>
-__device__ __forceinline__ void produce_t2(const GemvArgs& a, const TmaPlan& p, uint64_t* full, uint64_t* empty,
-                                           int* hdr, uint8_t* stage0, const int* started) {
-  const int S = p.stages, K = a.K, units = K / 128, T = NC * p.rw;
-  const int cb = K / 4, sb = units * 2;  // a row's code bytes and scale bytes
+// a tile's whole rows a stage: the rows' codes, then their scales (ternary: K / 4 code bytes and a float16 scale a
+// group of 128; int6: K / 32 x 24 code bytes and a float32 scale a group of 32)
+template <int FMT, int PHASES>
+__device__ __forceinline__ void produce_rows(const GemvArgs& a, const TmaPlan& p, uint64_t* full, uint64_t* empty,
+                                             int* hdr, uint8_t* stage0, const int* started) {
+  const int S = p.stages, K = a.K, T = NC * p.rw;
+  const int cb = FMT == F_Q6 ? K / 32 * 24 : K / 4;        // a row's code bytes
+  const int sb = FMT == F_Q6 ? K / 32 * 4 : K / 128 * 2;  // and its scale bytes
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
   const unsigned tiles = (unsigned)((a.r1 - a.r0 + T - 1) / T);
@@ -645,7 +648,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_t2_kernel(const GemvA
   }
   __syncthreads();
   if (warp == NC) {
-    if (lane == 0) produce_t2<PHASES>(a, p, full, empty, hdr, stage0, started);
+    if (lane == 0) produce_rows<F_T2, PHASES>(a, p, full, empty, hdr, stage0, started);
     return;
   }
   pdl_wait();
@@ -782,6 +785,116 @@ bool launch_t2(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl) {
   cfg.numAttrs = pdl ? 1 : 0;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a, p);
   if (e != cudaSuccess) pllm_fail(PLLM_ECUDA, "gemv_tma (ternary) launch: %s", cudaGetErrorString(e));
+  return true;
+}
+
+// ---- int6 weights at one token (matmul.ts:227, relaxed/six.ts:16): the same pipeline, a stage NC rw whole rows of
+// K / 32 x 24 bytes of codes (a group of 32: the low nibbles of its 32 values in 16 bytes, their top two bits in 8)
+// and then the rows' float32 scales a group of 32; tiles dealt by tickets. A lane takes a row's groups lane, lane +
+// 32, ... in order and widens each group's 24 bytes to eight words of int8 (widen6_regs: 4 v) against the group's
+// activations: the register kernel's order of every sum, so the same bits as matmul_q6 / q6r there.
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_q6_kernel(const GemvArgs a, const TmaPlan p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int S = p.stages, K = a.K, ng = K / 32, cb = ng * 24;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + S;
+  int* hdr = reinterpret_cast<int*>(smem + 16 * S);
+  int* started = hdr + S;  // the consumers have their activations
+  uint8_t* act = smem + ((20 * T2_STAGES + 4 + 127) & ~127);
+  int8_t* sq = reinterpret_cast<int8_t*>(act);          // [K] signed activations
+  float* ss = reinterpret_cast<float*>(act + (size_t)K);  // [ng] their scales
+  uint8_t* stage0 = act + p.act_bytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  constexpr int PHASES = EPI == EPI_SWIGLU ? 2 : 1;
+  if (tid == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NC);
+    }
+    *started = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == NC) {
+    if (lane == 0) produce_rows<F_Q6, PHASES>(a, p, full, empty, hdr, stage0, started);
+    return;
+  }
+  pdl_wait();
+  load_activations<F_Q6, 1, PRO, ConsumerSync>(a, sq, ss, nullptr, nullptr);
+  consumer_sync();
+  if (tid == 0) *reinterpret_cast<volatile int*>(started) = 1;
+  pdl_launch_dependents();
+  constexpr int RWM = 4;  // the most rows a warp
+  const int rw = p.rw, T = NC * rw;
+  float h1[RWM] = {0.0f, 0.0f, 0.0f, 0.0f};  // EPI_SWIGLU: this warp's rows' w1 results
+  long long it = 0;
+  for (;;) {
+    for (int ph = 0; ph < PHASES; ph++, it++) {
+      const int slot = (int)(it % S);
+      if (!mbar_wait(&full[slot], (unsigned)(it / S) & 1)) return;
+      const int tile = hdr[slot];
+      if (tile < 0) return;
+      const int mine = min(rw, (tile & 63) - warp * rw);  // this warp's rows of the tile
+      float acc[RWM] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (mine > 0) {
+        const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * rw * cb;
+        const float* d32 = reinterpret_cast<const float*>(stage0 + (size_t)slot * p.stage_bytes + (size_t)T * cb) +
+                           (size_t)warp * rw * ng;
+        for (int g = lane; g < ng; g += 32) {  // the group's activations read once for the warp's rows
+          const int4 a0 = *reinterpret_cast<const int4*>(sq + 32 * (size_t)g);
+          const int4 a1 = *reinterpret_cast<const int4*>(sq + 32 * (size_t)g + 16);
+          const float xs = ss[g];
+#pragma unroll
+          for (int r = 0; r < RWM; r++) {
+            if (r >= mine) break;
+            const uint8_t* c = w + (size_t)r * cb + 24 * (size_t)g;
+            const uint2 v0 = *reinterpret_cast<const uint2*>(c), v1 = *reinterpret_cast<const uint2*>(c + 8),
+                        v2 = *reinterpret_cast<const uint2*>(c + 16);
+            uint32_t wd[8];
+            widen6_regs(v0.x, v0.y, v1.x, v1.y, v2.x, v2.y, wd);
+            const int G = dot32_words(wd, a0, a1);
+            acc[r] = fmaf((float)G, __fmul_rn(d32[(size_t)r * ng + g], xs), acc[r]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+#pragma unroll
+      for (int r = 0; r < RWM; r++) {
+        if (r >= mine) break;
+        const float v = warp_sum(acc[r]);
+        if (lane != 0) continue;
+        const long long row = a.r0 + (tile >> 6) + warp * rw + r;
+        if (EPI == EPI_SWIGLU) {
+          if (ph == 0) h1[r] = v;
+          else a.out[row] = (h1[r] / (1.0f + expf(-h1[r]))) * v;
+        } else if (EPI == EPI_ADD) {
+          add_once(a.out + row, v);
+        } else {
+          a.out[row] = v;
+        }
+      }
+    }
+  }
+}
+
+template <int PRO, int EPI>
+bool launch_q6(const GemvArgs& a, const TmaPlan& p, size_t smem, bool pdl) {
+  auto kernel = gemv_tma_q6_kernel<PRO, EPI>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return false;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)gemv_tma_grid(a.r1 - a.r0, EPI));
+  cfg.blockDim = dim3(TMA_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = pllm_stream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, a, p);
+  if (e != cudaSuccess) pllm_fail(PLLM_ECUDA, "gemv_tma (int6) launch: %s", cudaGetErrorString(e));
   return true;
 }
 
@@ -928,12 +1041,48 @@ bool gemv_tma_t2(const GemvArgs& a, int pro, int epi, bool pdl) {
   return false;
 }
 
-// The bulk-copy product for int8 weights at 1 to 16 tokens and ternary weights at one; false where it does not apply
+// The int6 form at one token: whole rows a stage (K / 32 x 24 code bytes and K / 32 float32 scales a row), up to 16
+// stages.
+bool gemv_tma_q6(const GemvArgs& a, int pro, int epi, bool pdl) {
+  const int K = a.K, ng = K / 32;
+  if (K % 128 || K > 65536 || epi > EPI_SWIGLU || ((uintptr_t)a.wq & 15) || ((uintptr_t)a.ws & 15)) return false;
+  if (pro == PRO_Q && (((uintptr_t)a.xq & 15) || ((uintptr_t)a.xs & 15))) return false;
+  TmaPlan p = {};
+  p.chunks = 1;
+  p.ks = K;
+  const int row_bytes = ng * 24 + ng * 4;
+  p.rw = 45056 / (NC * row_bytes);  // a stage of about 44 KB: up to 4 rows a warp (the shorter rows)
+  if (p.rw > 4) p.rw = 4;
+  if (p.rw < 1) p.rw = 1;
+  p.stage_bytes = (NC * p.rw * row_bytes + 127) & ~127;
+  p.act_bytes = (int)(((size_t)K + (size_t)ng * 4 + 127) & ~127);
+  const int head = (20 * T2_STAGES + 4 + 127) & ~127;
+  int S = (227 * 1024 - head - p.act_bytes) / p.stage_bytes;
+  if (S > T2_STAGES) S = T2_STAGES;
+  if (S < 2) return false;
+  p.stages = S;
+  const size_t smem = (size_t)head + p.act_bytes + (size_t)S * p.stage_bytes;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  p.slot = (int)(next_ticket_slot(dev) % TICKET_SLOTS);
+  p.tickets = 1;
+#define CASE(P, E) \
+  if (pro == P && epi == E) return launch_q6<P, E>(a, p, smem, pdl);
+  CASE(PRO_Q, EPI_STORE) CASE(PRO_Q, EPI_ADD) CASE(PRO_Q, EPI_SWIGLU)
+  CASE(PRO_RMS, EPI_STORE) CASE(PRO_RMS, EPI_ADD) CASE(PRO_RMS, EPI_SWIGLU)
+  CASE(PRO_QUANT, EPI_STORE) CASE(PRO_QUANT, EPI_ADD) CASE(PRO_QUANT, EPI_SWIGLU)
+#undef CASE
+  return false;
+}
+
+// The bulk-copy product for int8 weights at 1 to 16 tokens and int6 and ternary weights at one; false where it does not
+// apply
 // (the caller then takes the register-streaming kernel).
 bool gemv_tma(const GemvArgs& a, int fmt, int pro, int epi, bool pdl, const Xchg* xg) {
   const bool tp = pro == PRO_RMS_SUM || epi == EPI_SEND;
   if (tp != (xg != nullptr)) return false;
   if (fmt == F_T2 && !tp && a.count == 1 && g_gemv_mode != 1) return gemv_tma_t2(a, pro, epi, pdl);
+  if (fmt == F_Q6 && !tp && a.count == 1 && g_gemv_mode != 1) return gemv_tma_q6(a, pro, epi, pdl);
   if (g_gemv_mode == 1 || fmt != F_Q8 || a.count < 1 || (tp && a.count != 1)) return false;
   const int K = a.K;
   if (K % 128 || ((uintptr_t)a.wq & 15) || ((uintptr_t)a.ws & 15)) return false;

@@ -555,6 +555,44 @@ def test_registry_products_both_kernels(golden, mode):
         L.pllm_set_gemv_mode(old)
 
 
+@pytest.mark.parametrize("K,N", [(4096, 1000), (12288, 520), (384, 77)])
+@pytest.mark.parametrize("pro", [0, 1, 2])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_int6_bulk_copy_is_the_register_kernel(K, N, pro, epi):
+    """pllm_gemv on int6 weights (fmt 1) at one token: the bulk-copy form (whole rows a stage, tiles by tickets) and
+    the register kernel take every lane's groups of 32 in the same order, so their outputs are the same bits, for every
+    prologue (the caller's activations, plain and relaxed; RMSNorm + quantize_x; quantize_x) and epilogue (store,
+    residual add, SwiGLU of a row pair). The register kernel's numbers are the oracle's within float32 rounding
+    (test_int8_int6_products)."""
+    rng = np.random.default_rng(K + N + 5 * pro + epi)
+    ng = K // 32
+    rows = 2 * N if epi == 2 else N
+    w6 = dev(rng.integers(0, 256, (rows, ng * 24), dtype=np.uint8))
+    ws = dev(rng.uniform(1e-3, 2e-2, (rows, ng)).astype(np.float32))
+    x = dev(rng.normal(0, 1, K).astype(np.float32))
+    norm = dev(rng.normal(1, 0.1, K).astype(np.float32))
+    init = rng.normal(0, 1, N).astype(np.float32)
+    for bias in ((0, 64) if pro == 0 else (0,)):
+        lo = 0 if bias else -127
+        xq = dev(rng.integers(lo, 128, K).astype(np.int8).view(np.uint8))
+        xs = dev(rng.uniform(1e-3, 1e-2, ng).astype(np.float32))
+        results = []
+        for mode in (0, 1):
+            old = L.pllm_set_gemv_mode(mode)
+            try:
+                out = dev(init)
+                L.pllm_gemv(out.ptr, N, xq.ptr if pro == 0 else 0, xs.ptr if pro == 0 else 0, 0, 0,
+                            x.ptr if pro else 0, K, norm.ptr if pro == 1 else 0, 1e-6, bias, w6.ptr, ws.ptr, 1, K, 0, N,
+                            1, pro, epi, N if epi == 2 else 0, 0)
+                check("pllm_gemv int6")
+                results.append(get(out, np.float32))
+            finally:
+                L.pllm_set_gemv_mode(old)
+        assert np.isfinite(results[0]).all()
+        assert np.array_equal(bits(results[0]), bits(results[1])), (bias, np.abs(results[0] - results[1]).max())
+    assert L.pllm_device_status() == 0
+
+
 @pytest.mark.parametrize("half", [True, False])
 @pytest.mark.parametrize("nh,nkv,hs,qk", [(8, 2, 128, True), (6, 6, 48, False), (16, 8, 64, False)])
 def test_attention_step(half, nh, nkv, hs, qk):
