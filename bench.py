@@ -115,7 +115,7 @@ def kernel_case(which):
         L.pllm_synth_f32(norm.ptr, K, 3, 1.0, 0.1)
         for _ in range(3):
             L.pllm_gemv(out.ptr, 0, 0, 0, 0, 0, x.ptr, 0, norm.ptr, 1e-6, 0, w.ptr, ws.ptr, 0, K, 0, rows, 1, 1, 0, 0, 0)
-    elif which in ("q6r", "b1r"):  # the registry's int6 (bulk-copy form) / binary (register streaming) products, 16,384 x 4096
+    elif which in ("q6r", "b1r"):  # the registry's int6 (bulk-copy) and binary (register) products, 16,384 x 4096
         rows, K = 16384, 4096
         rng = np.random.default_rng(7)
         wbytes = rows * K * 6 // 8 if which == "q6r" else rows * K // 8
