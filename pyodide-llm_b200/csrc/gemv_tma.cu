@@ -841,20 +841,32 @@ __global__ void __launch_bounds__(TMA_THREADS, 1) gemv_tma_q6_kernel(const GemvA
         const uint8_t* w = stage0 + (size_t)slot * p.stage_bytes + (size_t)warp * rw * cb;
         const float* d32 = reinterpret_cast<const float*>(stage0 + (size_t)slot * p.stage_bytes + (size_t)T * cb) +
                            (size_t)warp * rw * ng;
-        for (int g = lane; g < ng; g += 32) {  // the group's activations read once for the warp's rows
+        // two groups a step (g and g + 32: independent loads and products, added in order); the groups' activations
+        // read once for the warp's rows
+        for (int g = lane; g < ng; g += 64) {
+          const bool two = g + 32 < ng;
+          const int h = two ? g + 32 : g;
           const int4 a0 = *reinterpret_cast<const int4*>(sq + 32 * (size_t)g);
           const int4 a1 = *reinterpret_cast<const int4*>(sq + 32 * (size_t)g + 16);
-          const float xs = ss[g];
+          const int4 b0 = *reinterpret_cast<const int4*>(sq + 32 * (size_t)h);
+          const int4 b1 = *reinterpret_cast<const int4*>(sq + 32 * (size_t)h + 16);
+          const float xs = ss[g], xt = ss[h];
 #pragma unroll
           for (int r = 0; r < RWM; r++) {
             if (r >= mine) break;
             const uint8_t* c = w + (size_t)r * cb + 24 * (size_t)g;
+            const uint8_t* e = w + (size_t)r * cb + 24 * (size_t)h;
             const uint2 v0 = *reinterpret_cast<const uint2*>(c), v1 = *reinterpret_cast<const uint2*>(c + 8),
                         v2 = *reinterpret_cast<const uint2*>(c + 16);
-            uint32_t wd[8];
+            const uint2 u0 = *reinterpret_cast<const uint2*>(e), u1 = *reinterpret_cast<const uint2*>(e + 8),
+                        u2 = *reinterpret_cast<const uint2*>(e + 16);
+            const float s0 = d32[(size_t)r * ng + g], s1 = d32[(size_t)r * ng + h];
+            uint32_t wd[8], wu[8];
             widen6_regs(v0.x, v0.y, v1.x, v1.y, v2.x, v2.y, wd);
-            const int G = dot32_words(wd, a0, a1);
-            acc[r] = fmaf((float)G, __fmul_rn(d32[(size_t)r * ng + g], xs), acc[r]);
+            widen6_regs(u0.x, u0.y, u1.x, u1.y, u2.x, u2.y, wu);
+            const int G = dot32_words(wd, a0, a1), H = dot32_words(wu, b0, b1);
+            const float f = fmaf((float)G, __fmul_rn(s0, xs), acc[r]);
+            acc[r] = two ? fmaf((float)H, __fmul_rn(s1, xt), f) : f;
           }
         }
       }
@@ -1046,13 +1058,16 @@ bool gemv_tma_t2(const GemvArgs& a, int pro, int epi, bool pdl) {
 bool gemv_tma_q6(const GemvArgs& a, int pro, int epi, bool pdl) {
   const int K = a.K, ng = K / 32;
   if (K % 128 || K > 65536 || epi > EPI_SWIGLU || ((uintptr_t)a.wq & 15) || ((uintptr_t)a.ws & 15)) return false;
+  // below ~32 M weights the register kernel is as fast or faster (measured, one launch after another: 4096 x 4096
+  // 6.0-6.4 us against 8.3, 1024 x 1024 the same; from 12,288 x 4096 up the bulk-copy form is 10-12 % faster)
+  if ((long long)(a.r1 - a.r0) * K < (1ll << 25)) return false;
   if (pro == PRO_Q && (((uintptr_t)a.xq & 15) || ((uintptr_t)a.xs & 15))) return false;
   TmaPlan p = {};
   p.chunks = 1;
   p.ks = K;
   const int row_bytes = ng * 24 + ng * 4;
-  p.rw = 45056 / (NC * row_bytes);  // a stage of about 44 KB: up to 4 rows a warp (the shorter rows)
-  if (p.rw > 4) p.rw = 4;
+  p.rw = 90112 / (NC * row_bytes);  // a stage of about 88 KB, up to 4 rows a warp (measured: 4.0 TB/s at 16,384 x
+  if (p.rw > 4) p.rw = 4;            // 4096 against 3.1 with 28 KB stages of a row a warp)
   if (p.rw < 1) p.rw = 1;
   p.stage_bytes = (NC * p.rw * row_bytes + 127) & ~127;
   p.act_bytes = (int)(((size_t)K + (size_t)ng * 4 + 127) & ~127);

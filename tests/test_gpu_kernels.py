@@ -555,15 +555,15 @@ def test_registry_products_both_kernels(golden, mode):
         L.pllm_set_gemv_mode(old)
 
 
-@pytest.mark.parametrize("K,N", [(4096, 1000), (12288, 520), (384, 77)])
+@pytest.mark.parametrize("K,N", [(4096, 8192), (12288, 2731), (128, 262144)])
 @pytest.mark.parametrize("pro", [0, 1, 2])
 @pytest.mark.parametrize("epi", [0, 1, 2])
 def test_int6_bulk_copy_is_the_register_kernel(K, N, pro, epi):
-    """pllm_gemv on int6 weights (fmt 1) at one token: the bulk-copy form (whole rows a stage, tiles by tickets) and
-    the register kernel take every lane's groups of 32 in the same order, so their outputs are the same bits, for every
-    prologue (the caller's activations, plain and relaxed; RMSNorm + quantize_x; quantize_x) and epilogue (store,
-    residual add, SwiGLU of a row pair). The register kernel's numbers are the oracle's within float32 rounding
-    (test_int8_int6_products)."""
+    """pllm_gemv on int6 weights (fmt 1) at one token: the bulk-copy form (whole rows a stage, tiles by tickets; it
+    serves products of 2^25 weights and more, as these) and the register kernel take every lane's groups of 32 in the
+    same order, so their outputs are the same bits, for every prologue (the caller's activations, plain and relaxed;
+    RMSNorm + quantize_x; quantize_x) and epilogue (store, residual add, SwiGLU of a row pair). The register kernel's
+    numbers are the oracle's within float32 rounding (test_int8_int6_products)."""
     rng = np.random.default_rng(K + N + 5 * pro + epi)
     ng = K // 32
     rows = 2 * N if epi == 2 else N
