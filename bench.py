@@ -866,7 +866,7 @@ def main():
         "attention": attention,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if achieved else None,
-                     "peak_kind": peak_kind, "kernel": "gemv_kernel<int8, 1 token, RMSNorm prologue, SwiGLU epilogue>",
+                     "peak_kind": peak_kind, "kernel": "gemv_tma_kernel<1, 1, 2> (w1/w3: int8, 1 token, RMSNorm, SwiGLU)",
                      "bytes_per_launch": w13_bytes,  # a rank's launch: its 1/N of the rows
                      "traffic": (profile_traffic("gemv_q8_w13_qwen3-8b") or 0) / world or None},
         "decode_roofline_frac": (c.weight_bytes() / (decode_ms / steps / 1000) / 1e9) / (peak * world),
