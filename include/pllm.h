@@ -294,8 +294,9 @@ void pllm_delta_rule_block(uint64_t out, int64_t out_stride, uint64_t state, uin
  * nothing is read or written outside it): PLLM_ERANGE (5); else 0. Reading it clears it (and, after a wait that gave
  * up, puts the products' tile counters back to zero) */
 int32_t pllm_device_status(void);
-/* which decode-product kernel: 0 the bulk-copy pipeline where it applies (int8 weights, 1 or 2 tokens), 1 the
- * register-streaming kernel always; returns the previous mode */
+/* which decode-product kernel: 0 the bulk-copy pipeline where it applies (int8 weights at 1 to 16 tokens; int6
+ * weights at one token in products of 2^25 weights and more; ternary weights at one token), 1 the register-streaming
+ * kernel always; returns the previous mode */
 int32_t pllm_set_gemv_mode(int32_t mode);
 /* the shared-memory bytes the bulk-copy product's ring of stages may take (32 KB..227 KB; default 180 KB) */
 int32_t pllm_set_stage_budget(int32_t bytes);
