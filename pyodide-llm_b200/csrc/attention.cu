@@ -505,12 +505,16 @@ __global__ void __launch_bounds__(32 * W, 1) attention_chunk_kernel(const AttArg
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  for (int i = 0; i < ring && i < mine; i++) load_chunk(i);
+  const bool holds_pos = FUSE && (CL ? (pos / CHUNK) % TW / W == rank : p1 == count);
+  // CL: the warps of the q / k / v prologue issue their chunks' copies after it, the others at once (a CTA's copies
+  // take microseconds to issue, the memory being busy with them: the prologue need not wait behind them)
+  const bool late = CL && warp < KVM + (holds_pos ? 2 : 0);
+  if (!late)
+    for (int i = 0; i < ring && i < mine; i++) load_chunk(i);
   for (int e = tid; e < (HP - KVM) * qst; e += (32 * W)) {  // the padded heads' q: zero
     sqh[KVM * qst + e] = __float2half_rn(0.0f);
     sql[KVM * qst + e] = __float2half_rn(0.0f);
   }
-  const bool holds_pos = FUSE && (CL ? (pos / CHUNK) % TW / W == rank : p1 == count);
   // the head norms' weights and the RoPE tables' row of pos (not the previous kernel's output): read before the wait
   const int turned = f.rot > 0 && f.rot < hs ? f.rot : hs;
   float wq[DL], wk[DL], cs[DL], sn[DL];
@@ -579,6 +583,8 @@ __global__ void __launch_bounds__(32 * W, 1) attention_chunk_kernel(const AttArg
       if (local && f.bad) atomicAdd(f.bad, local);
     }
   }
+  if (late)
+    for (int i = 0; i < ring && i < mine; i++) load_chunk(i);
   __syncthreads();
   float M0 = -INFINITY, M1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // heads j0, j1: running max and (lane-partial) sum
   float oc[MBM][4];
@@ -704,17 +710,29 @@ __global__ void __launch_bounds__(32 * W, 1) attention_chunk_kernel(const AttArg
   // part's maxima and sums into every CTA's
   namespace cg = cooperative_groups;
   const int per = CL ? (KVM * hs + ncta - 1) / ncta : 1, RS = per + 2 * KVM;  // CL: the pairs a CTA makes; a slot
+  // each head's largest warp maximum, then each (warp, head)'s weight, once (a head's pairs share them)
+  __shared__ float s_mx[KVM], s_wt[W * KVM];
+  if (tid < KVM) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < W; w++) mx = fmaxf(mx, sml[(w * KVM + tid) * 2]);
+    s_mx[tid] = mx;
+  }
+  __syncthreads();
+  if (tid < W * KVM) {
+    const int w = tid / KVM, j = tid % KVM;
+    const float base = s_mx[j] == -INFINITY ? 0.0f : s_mx[j];
+    s_wt[tid] = expf(sml[(w * KVM + j) * 2] - base);  // 0 for a warp without chunks
+  }
+  __syncthreads();
   if constexpr (CL) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA has started
   for (int e = tid; e < KVM * hs; e += (32 * W)) {
     const int j = e / hs, d = e % hs, h = hbase + j;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < W; w++) mx = fmaxf(mx, sml[(w * KVM + j) * 2]);
-    const float base = mx == -INFINITY ? 0.0f : mx;
+    const float mx = s_mx[j];
     float o = 0.0f, l = 0.0f;
 #pragma unroll
     for (int w = 0; w < W; w++) {
-      const float wt = expf(sml[(w * KVM + j) * 2] - base);  // 0 for a warp without chunks
+      const float wt = s_wt[w * KVM + j];
       o = fmaf(reinterpret_cast<const float*>(att_smem + (size_t)w * ring * chunkb)[j * (hs + 4) + d], wt, o);
       l = fmaf(sml[(w * KVM + j) * 2 + 1], wt, l);
     }
@@ -746,30 +764,31 @@ __global__ void __launch_bounds__(32 * W, 1) attention_chunk_kernel(const AttArg
     // in its receive buffer (no CTA reads another's shared memory after the barrier, so none waits to leave)
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();  // every part stored (release / acquire)
+    // each head's largest CTA maximum, then each (CTA, head)'s weight, once
+    __shared__ float c_mx[KVM], c_wt[CS_MAX * KVM];
+    if (tid < KVM) {
+      float mx = -INFINITY;
+      for (int c = 0; c < ncta; c++) mx = fmaxf(mx, rcv[c * RS + per + tid]);
+      c_mx[tid] = mx;
+    }
+    __syncthreads();
+    if (tid < ncta * KVM) {
+      const int c = tid / KVM, j = tid % KVM;
+      const float base = c_mx[j] == -INFINITY ? 0.0f : c_mx[j];
+      c_wt[tid] = expf(rcv[c * RS + per + j] - base);  // 0 for a CTA without chunks
+    }
+    __syncthreads();
     const int e = rank * per + tid;
     if (tid < per && e < KVM * hs) {
       const int j = e / hs, d = e % hs;
-      float m[CS_MAX], l[CS_MAX], o[CS_MAX];
-#pragma unroll
-      for (int c = 0; c < CS_MAX; c++) {
-        if (c >= ncta) break;
-        const float* src = rcv + c * RS;
-        m[c] = src[per + j];
-        l[c] = src[per + KVM + j];
-        o[c] = src[tid];
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < CS_MAX; c++)
-        if (c < ncta) mx = fmaxf(mx, m[c]);
-      const float base = mx == -INFINITY ? 0.0f : mx;
       float os = 0.0f, ls = 0.0f;
 #pragma unroll
       for (int c = 0; c < CS_MAX; c++) {
         if (c >= ncta) break;
-        const float wt = expf(m[c] - base);  // 0 for a CTA without chunks
-        os = fmaf(o[c], wt, os);
-        ls = fmaf(l[c], wt, ls);
+        const float* src = rcv + c * RS;
+        const float wt = c_wt[c * KVM + j];
+        os = fmaf(src[tid], wt, os);
+        ls = fmaf(src[per + KVM + j], wt, ls);
       }
       a.out[(long long)(hbase + j) * hs + d] = os / ls;
     }
