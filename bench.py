@@ -267,9 +267,10 @@ SWEEP_SHAPES = [(1024, 1024), (1024, 4608), (4096, 4096), (4096, 12288), (12288,
 def product_sweep(timed, Ms=(1, 4, 16, 128, 512, 2048)):
     """the isolated products at (K, N) x M, every launch of a measurement on another window of
     a 512 MB weight arena (so that no launch finds its weights in the 126 MB L2). M <= 16: the decode products
-    (pllm_gemv: int8 on the bulk-copy pipeline -- 1..2 tokens dp4a, 3..16 the tensor-core form; int6 and ternary on the
-    register kernel), their algorithmic bytes (SURVEY: weights N K (1 + 1/8) int8, (3/4 + 1/8) int6, (1/4 + 2/128)
-    ternary, plus the activations and outputs) over the CUDA-event time, against the measured HBM copy rate. M >= 128:
+    (pllm_gemv: int8 on the bulk-copy pipeline -- 1..2 tokens dp4a, 3..16 the tensor-core form; int6 and ternary at one
+    token on their bulk-copy forms (int6 from 2^25 weights up), past one token on the register kernel), their
+    algorithmic bytes (weights N K (1 + 1/8) int8, (3/4 + 1/8) int6, (1/4 + 2/128) ternary, plus the activations and
+    outputs) over the CUDA-event time, against the measured HBM copy rate. M >= 128:
     the int8 tensor-core product (pllm_gemm_q8, tcgen05 kind::i8), 2 M N K operations against twice the measured bf16
     dense rate (int6 and ternary checkpoints are widened to int8 for it, so their prefill is this product)."""
     from pllm.device import Buffer

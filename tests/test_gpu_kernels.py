@@ -433,7 +433,7 @@ def test_delta_rule_bit_exact(kh, vh, kd, vd):
 def test_delta_rule_block_is_the_tokens_one_by_one(count):
     """pllm_delta_rule_block: count tokens of the recurrence in one launch (the state on the chip between them) give
     each token's outputs, gates' delta and the last state of delta_rule called a token at a time, to the bit; the
-    SURVEY's micro-configuration (kh 16, vh 32, kd = vd = 128); a head range writes only its heads."""
+    delta rule's micro-configuration (kh 16, vh 32, kd = vd = 128); a head range writes only its heads."""
     kh, vh, kd, vd = 16, 32, 128, 128
     rng = np.random.default_rng(count)
     state = rng.normal(0, 0.5, vh * kd * vd).astype(np.float32)
